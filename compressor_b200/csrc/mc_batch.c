@@ -1,0 +1,1330 @@
+/*
+ * mc_batch.c -- grouped batch compress and batch decompress engines.
+ *
+ * Compress follows the reference grouped path
+ * (momentum_compressor_openmp_simd_final.c build_batch_pipeline :2566-2675,
+ * process_batch_group :2710-2814, commit_grouped_batch_results :2869-2952):
+ * the host plans every item (group key, local step chain, direct / momentum /
+ * generic mode, which earlier input is its previous gradient), the GPU runs
+ * the numeric passes for the whole batch, and the state maps are updated only
+ * after every device step succeeded (all-or-nothing).
+ *
+ * Decompress follows decompress_batch (:4707-4838) -> decompress_layer
+ * (:3476-3598) -> decompress_momentum_predicted_layer (:3186-3474), with the
+ * per-item early exits of the reference decided on the host before launch
+ * (or, for device-resident bitmaps, from the device-computed predicted count
+ * before commit).
+ */
+#define _GNU_SOURCE
+#include <stdlib.h>
+#include <string.h>
+
+#include "mc_internal.h"
+
+#define ALIGN_UP(x, a) (((x) + ((a)-1)) & ~((size_t)(a)-1))
+#define SLOT_ALIGN 256
+#define TILE_ELEMS 8192
+
+enum { MODE_DIRECT = 0, MODE_MOMENTUM = 1, MODE_GENERIC = 2 };
+
+/* device scratch slots of an instance */
+enum {
+    SD_TABLES = 0,   /* item tables, tile lists, frame jobs */
+    SD_RESULTS,      /* per-item results */
+    SD_TILES,        /* per-tile partials */
+    SD_POFF,         /* per-tile predicted offsets */
+    SD_WORDS,        /* bitmap / dominant / dense-sign words */
+    SD_INPUT,        /* staged host inputs */
+    SD_PAYLOAD,      /* payload arena when payloads return to the host */
+    SD_FSIZE,        /* frame sizes written by the device */
+    SD_DSTAGE,       /* decoder: staged payload bytes */
+    SD_DOUT,         /* decoder: contiguous decoded output before the host copy */
+    SD_DCONTENT,     /* decoder: frame contents expanded on the device */
+};
+enum { SH_TABLES = 0, SH_RESULTS, SH_STAGE };
+
+/* ================================================================ compress */
+typedef struct {
+    char hkey[MAX_KEY_LENGTH];
+    char lkey[MAX_KEY_LENGTH];
+    int group;
+    int mode;
+    int local_step;
+    int kind;
+    int dcodec;
+    const char *codec_tag;
+    int wave;
+    int prev_item;
+    mc_tensor *prev_t;
+    int use_lossy;
+    int candidate;
+    DataType dt;
+    size_t n, bytes, K, ks;
+    const NDArray *g;
+    int src_dev;
+    const void *dev_in;
+    mc_tensor *hist;
+    size_t off_data, cap_data, off_bm, cap_bm, off_sg, cap_sg;
+    size_t words_off;    /* in SD_WORDS, units of uint32 */
+    size_t kwords;
+    int tile_base, ntiles, tile_param;
+    size_t fs_bm, fs_sg, fs_data;   /* indices into the frame-size array, or (size_t)-1 */
+} cplan;
+
+typedef struct {
+    char key[MAX_KEY_LENGTH];
+    mc_tensor *mem_committed;
+    mc_tensor *mem_new;
+    int n_mom;
+} cgroup;
+
+static int layout_equal(const NDArray *a, DataType dt, size_t ndim, const size_t *shape, size_t n) {
+    if (a->dtype != dt || a->ndim != ndim || a->total_size != n) return 0;
+    for (size_t i = 0; i < ndim; i++)
+        if (a->shape[i] != shape[i]) return 0;
+    return 1;
+}
+
+static int dcodec_of(int codec) {
+    switch (codec) {
+        case MC_CODEC_INT4: return MC_DC_INT4;
+        case MC_CODEC_RAW: return MC_DC_RAW;
+        case MC_CODEC_Q8_RAW: return MC_DC_Q8_RAW;
+        case MC_CODEC_INT4_RAW: return MC_DC_INT4_RAW;
+        default: return MC_DC_Q8;
+    }
+}
+
+static size_t residual_bytes(int dcodec, size_t n) {
+    switch (dcodec) {
+        case MC_DC_Q8: return 4 + n;
+        case MC_DC_INT4: return 4 + (n + 1) / 2;
+        default: return 4 * n;
+    }
+}
+
+static const char *codec_tag_of(int dcodec) {
+    switch (dcodec) {
+        case MC_DC_Q8: return "q8";
+        case MC_DC_INT4: return "int4";
+        default: return "sz3_memcpy";
+    }
+}
+
+static int tile_kernels_for(size_t ks) {
+    size_t tk = TILE_ELEMS / (ks ? ks : 1);
+    tk = tk / 32 * 32;
+    if (tk < 32) tk = 32;
+    if (tk > 8192) tk = 8192;
+    return (int)tk;
+}
+
+static void free_plan_tensors(MomentumCompressor *mc, cplan *P, size_t n, cgroup *G, size_t ng) {
+    for (size_t i = 0; i < n; i++) {
+        if (P[i].hist) tensor_drop(P[i].hist);
+        P[i].hist = NULL;
+    }
+    for (size_t g = 0; g < ng; g++) {
+        if (G[g].mem_new) tensor_drop(G[g].mem_new);
+        G[g].mem_new = NULL;
+    }
+    (void)mc;
+}
+
+int mc_compress_grouped(MomentumCompressor *mc, BatchItem *items, size_t n, const char *client,
+                        int payload_loc, int allow_fault) {
+    int rc = ERROR_NONE;
+    cplan *P = (cplan *)calloc(n, sizeof(cplan));
+    cgroup *G = (cgroup *)calloc(n, sizeof(cgroup));
+    if (!P || !G) {
+        free(P);
+        free(G);
+        return ERROR_ALLOCATION;
+    }
+    size_t ng = 0;
+    const size_t thr = mc->config.param_count_threshold;
+
+    /* ---------------------------------------------------- validation / meta */
+    for (size_t i = 0; i < n; i++) {
+        items[i].compressed = NULL;
+        items[i].error = ERROR_NONE;
+    }
+    for (size_t i = 0; i < n; i++) {
+        const NDArray *g = items[i].gradient;
+        if (!g || !items[i].layer_name) {
+            items[i].error = ERROR_INVALID_PARAM;
+            mc_set_error(mc, "Batch compress: item[%zu] has NULL gradient or layer_name", i);
+            rc = ERROR_INVALID_PARAM;
+            goto out;
+        }
+        size_t elem = mc_dtype_size(g->dtype);
+        size_t prod = 1;
+        int bad = g->ndim < MIN_NDIM || g->ndim > MAX_NDIM || !g->shape || !g->data || elem == 0;
+        for (size_t d = 0; !bad && d < g->ndim; d++) prod *= g->shape[d];
+        if (bad || prod == 0 || prod != g->total_size) {
+            items[i].error = ERROR_INVALID_PARAM;
+            mc_set_error(mc, "Batch compress: item[%zu] '%s' has an invalid array descriptor", i,
+                         items[i].layer_name);
+            rc = ERROR_INVALID_PARAM;
+            goto out;
+        }
+        cplan *p = &P[i];
+        p->g = g;
+        p->dt = g->dtype;
+        p->n = g->total_size;
+        p->bytes = p->n * elem;
+        mc_history_key(p->hkey, client, items[i].layer_name);
+        mc_layer_key(p->lkey, sizeof(p->lkey), items[i].layer_name, g->shape, g->ndim, g->dtype);
+        p->use_lossy = mc_should_lossy(items[i].layer_name, p->n, p->dt, thr);
+        p->candidate = g->ndim == 4 && g->dtype == DTYPE_FLOAT32 && p->use_lossy;
+        p->prev_item = -1;
+        p->fs_bm = p->fs_sg = p->fs_data = (size_t)-1;
+    }
+
+    /* ------------------------------------------------ fault injection hook */
+    {
+        const char *fault = allow_fault ? getenv("FALCOM_FAULT_INJECT_COMPRESS_FAIL_AT") : NULL;
+        if (fault && *fault && (size_t)strtoull(fault, NULL, 10) < n) {
+            mc_set_error(mc, "fault injection requested for item[%zu]",
+                         (size_t)strtoull(fault, NULL, 10));
+            for (size_t i = 0; i < n; i++) items[i].error = ERROR_COMPRESSION;
+            rc = ERROR_COMPRESSION;
+            goto out;
+        }
+    }
+
+    /* --------------------------------------------- group keys (:2627-2645) */
+    for (size_t i = 0; i < n; i++) {
+        size_t same = 0;
+        for (size_t j = 0; j < n; j++) same += strcmp(P[i].hkey, P[j].hkey) == 0;
+        const mc_tensor *h0 = (const mc_tensor *)map_get(mc->history, P[i].hkey);
+        char gk[MAX_KEY_LENGTH];
+        if (P[i].candidate && (h0 != NULL || same > 1)) snprintf(gk, sizeof(gk), "%s", P[i].lkey);
+        else if (same > 1) snprintf(gk, sizeof(gk), "%s", P[i].hkey);
+        else snprintf(gk, sizeof(gk), "item:%zu", i);
+        size_t g;
+        for (g = 0; g < ng; g++)
+            if (strcmp(G[g].key, gk) == 0) break;
+        if (g == ng) {
+            snprintf(G[g].key, sizeof(G[g].key), "%s", gk);
+            char mk[2 * MAX_KEY_LENGTH];
+            mc_memory_key(mk, sizeof(mk), client, gk);
+            G[g].mem_committed = (mc_tensor *)map_get(mc->memory, mk);
+            ng++;
+        }
+        P[i].group = (int)g;
+    }
+
+    /* ------------------------ per-group step chains (:2710-2814, in order) */
+    for (size_t g = 0; g < ng; g++) {
+        for (size_t i = 0; i < n; i++) {
+            if (P[i].group != (int)g) continue;
+            /* state of this history key inside the group: last earlier item */
+            int last = -1;
+            for (size_t j = 0; j < i; j++)
+                if (P[j].group == (int)g && strcmp(P[j].hkey, P[i].hkey) == 0) last = (int)j;
+            int step0;
+            if (last >= 0) {
+                step0 = P[last].local_step;
+            } else {
+                step0 = (int)(intptr_t)map_get(mc->steps, P[i].hkey);
+            }
+            P[i].local_step = step0 + 1;
+            const NDArray *g_i = P[i].g;
+            int has_prev = 0, prev_match = 0;
+            if (last >= 0) {
+                has_prev = 1;
+                const NDArray *pg = P[last].g;
+                prev_match = layout_equal(g_i, pg->dtype, pg->ndim, pg->shape, pg->total_size);
+                P[i].prev_item = last;
+            } else {
+                mc_tensor *h = (mc_tensor *)map_get(mc->history, P[i].hkey);
+                if (h) {
+                    has_prev = 1;
+                    prev_match = layout_equal(g_i, h->dtype, h->ndim, h->shape, h->n);
+                    P[i].prev_t = h;
+                }
+            }
+            if (P[i].local_step == 1) P[i].mode = MODE_DIRECT;
+            else if (has_prev && prev_match && P[i].candidate) P[i].mode = MODE_MOMENTUM;
+            else P[i].mode = MODE_GENERIC;
+            if (P[i].mode == MODE_MOMENTUM) {
+                P[i].wave = G[g].n_mom;
+                G[g].n_mom++;
+            }
+        }
+    }
+
+    /* --------------------------------------------- kinds, codecs, tiling */
+    const int dcodec = dcodec_of(mc->residual_codec);
+    int nwaves = 1;
+    int ntiles_total = 0, nframes = 0, nmom = 0;
+    size_t words_total = 0;
+    for (size_t i = 0; i < n; i++) {
+        cplan *p = &P[i];
+        if (p->mode == MODE_MOMENTUM) {
+            p->kind = MC_K_MOMENTUM;
+            p->dcodec = dcodec;
+            p->codec_tag = codec_tag_of(dcodec);
+            p->K = p->g->shape[0] * p->g->shape[1];
+            p->ks = p->g->shape[2] * p->g->shape[3];
+            p->tile_param = tile_kernels_for(p->ks);
+            p->ntiles = (int)((p->K + (size_t)p->tile_param - 1) / (size_t)p->tile_param);
+            p->kwords = (p->K + 31) / 32 + 1;
+            p->words_off = words_total;
+            words_total += 3 * ALIGN_UP(p->kwords, 64);
+            if (p->wave + 1 > nwaves) nwaves = p->wave + 1;
+            nframes += 2;
+            nmom++;
+        } else if (p->use_lossy && p->dt == DTYPE_FLOAT32 && dcodec != MC_DC_RAW) {
+            p->dcodec = dcodec;
+            p->codec_tag = codec_tag_of(dcodec);
+            p->kind = MC_K_QUANT;
+            p->tile_param = TILE_ELEMS;
+            p->ntiles = (int)((p->n + TILE_ELEMS - 1) / TILE_ELEMS);
+        } else if (p->use_lossy) {
+            /* raw residual codec, and float64 lossy tensors: raw copy (the
+             * reference's result when SZ3 is unavailable) */
+            p->kind = MC_K_COPY;
+            p->dcodec = MC_DC_RAW;
+            p->codec_tag = "sz3_memcpy";
+            p->tile_param = TILE_ELEMS * 4;
+            p->ntiles = (int)((p->bytes + (size_t)p->tile_param - 1) / (size_t)p->tile_param);
+        } else {
+            p->kind = MC_K_FRAME;
+            p->codec_tag = "zstd";
+            p->tile_param = TILE_ELEMS * 4;
+            p->ntiles = (int)((p->bytes + (size_t)p->tile_param - 1) / (size_t)p->tile_param);
+            nframes += 1;
+        }
+        p->tile_base = ntiles_total;
+        ntiles_total += p->ntiles;
+    }
+    if (mc->frame_mode == MC_FRAME_LIBZSTD) payload_loc = FALCOM_LOC_HOST;
+
+    /* --------------------------------------------------- payload layout */
+    size_t arena_bytes = 0;
+    for (size_t i = 0; i < n; i++) {
+        cplan *p = &P[i];
+        size_t cap;
+        if (p->kind == MC_K_MOMENTUM || p->kind == MC_K_QUANT) cap = residual_bytes(p->dcodec, p->n);
+        else if (p->kind == MC_K_COPY) cap = p->bytes;
+        else cap = mc->frame_mode == MC_FRAME_LIBZSTD ? p->bytes + p->bytes / 64 + 1024
+                                                      : zf_max_frame_size(p->bytes);
+        p->off_data = arena_bytes;
+        p->cap_data = cap;
+        arena_bytes = ALIGN_UP(arena_bytes + cap, SLOT_ALIGN);
+        if (p->kind == MC_K_MOMENTUM) {
+            size_t c = (p->K + 7) / 8;
+            size_t fc = mc->frame_mode == MC_FRAME_LIBZSTD ? c + c / 64 + 1024 : zf_max_frame_size(c);
+            p->off_bm = arena_bytes;
+            p->cap_bm = fc;
+            arena_bytes = ALIGN_UP(arena_bytes + fc, SLOT_ALIGN);
+            p->off_sg = arena_bytes;
+            p->cap_sg = fc;
+            arena_bytes = ALIGN_UP(arena_bytes + fc, SLOT_ALIGN);
+        }
+    }
+
+    /* --------------------------------------- device memory for this batch */
+    cudaStream_t st = mc->stream;
+    const int dev = mc->device;
+    mc_arena *dev_arena = NULL, *host_arena = NULL;
+    uint8_t *payload_dev;
+    if (payload_loc == FALCOM_LOC_DEVICE) {
+        dev_arena = arena_acquire(arena_bytes, dev);
+        payload_dev = dev_arena ? (uint8_t *)dev_arena->ptr : NULL;
+    } else {
+        payload_dev = (uint8_t *)scratch_dev(&mc->scratch, SD_PAYLOAD, arena_bytes);
+        host_arena = arena_acquire(arena_bytes, -1);
+    }
+    if (!payload_dev || (payload_loc != FALCOM_LOC_DEVICE && !host_arena)) {
+        mc_set_error(mc, "Batch compress: payload allocation failed (%zu bytes)", arena_bytes);
+        rc = ERROR_ALLOCATION;
+        goto fail;
+    }
+
+    /* history tensors, group memories */
+    for (size_t i = 0; i < n; i++) {
+        P[i].hist = tensor_new(P[i].dt, P[i].g->ndim, P[i].g->shape, dev);
+        if (!P[i].hist) {
+            rc = ERROR_ALLOCATION;
+            mc_set_error(mc, "Batch compress: device allocation failed for history");
+            goto fail;
+        }
+    }
+    for (size_t g = 0; g < ng; g++) {
+        if (G[g].n_mom == 0) continue;
+        /* every momentum item of a group has the group's shape */
+        for (size_t i = 0; i < n; i++) {
+            if (P[i].group == (int)g && P[i].mode == MODE_MOMENTUM) {
+                G[g].mem_new = tensor_new(DTYPE_FLOAT32, 4, P[i].g->shape, dev);
+                break;
+            }
+        }
+        if (!G[g].mem_new) {
+            rc = ERROR_ALLOCATION;
+            mc_set_error(mc, "Batch compress: device allocation failed for prediction memory");
+            goto fail;
+        }
+    }
+
+    /* ----------------------------------------------- stage host inputs */
+    {
+        size_t stage_bytes = 0;
+        int any_host = 0;
+        for (size_t i = 0; i < n; i++) {
+            int d = -1;
+            P[i].src_dev = mc_ptr_is_device(P[i].g->data, &d);
+            if (P[i].src_dev && d != dev) P[i].src_dev = 0;   /* another GPU: copy */
+            if (!P[i].src_dev) any_host = 1;
+        }
+        if (any_host) {
+            /* coalesce host inputs that are adjacent in memory (16-byte aligned) */
+            size_t *order = (size_t *)malloc(n * sizeof(size_t));
+            size_t no = 0;
+            for (size_t i = 0; i < n; i++)
+                if (!P[i].src_dev) order[no++] = i;
+            for (size_t a = 1; a < no; a++) { /* insertion sort by address */
+                size_t v = order[a], b = a;
+                while (b > 0 && (uintptr_t)P[order[b - 1]].g->data > (uintptr_t)P[v].g->data) {
+                    order[b] = order[b - 1];
+                    b--;
+                }
+                order[b] = v;
+            }
+            size_t *run_off = (size_t *)malloc(n * sizeof(size_t));
+            for (size_t a = 0; a < no;) {
+                size_t i0 = order[a];
+                uintptr_t base = (uintptr_t)P[i0].g->data, end = base + P[i0].bytes;
+                size_t b = a + 1;
+                while (b < no) {
+                    uintptr_t s = (uintptr_t)P[order[b]].g->data;
+                    if (s != end || (s & 15) || (base & 15)) break;
+                    end = s + P[order[b]].bytes;
+                    b++;
+                }
+                size_t start = stage_bytes;
+                for (size_t c = a; c < b; c++)
+                    run_off[order[c]] = start + ((uintptr_t)P[order[c]].g->data - base);
+                stage_bytes = ALIGN_UP(start + (end - base), SLOT_ALIGN);
+                a = b;
+            }
+            uint8_t *stage = (uint8_t *)scratch_dev(&mc->scratch, SD_INPUT, stage_bytes);
+            if (!stage) {
+                free(order);
+                free(run_off);
+                rc = ERROR_ALLOCATION;
+                mc_set_error(mc, "Batch compress: input staging allocation failed");
+                goto fail;
+            }
+            for (size_t a = 0; a < no;) {
+                size_t i0 = order[a];
+                uintptr_t base = (uintptr_t)P[i0].g->data, end = base + P[i0].bytes;
+                size_t b = a + 1;
+                while (b < no) {
+                    uintptr_t s = (uintptr_t)P[order[b]].g->data;
+                    if (s != end || (s & 15) || (base & 15)) break;
+                    end = s + P[order[b]].bytes;
+                    b++;
+                }
+                if (cudaMemcpyAsync(stage + run_off[i0], (const void *)base, end - base,
+                                    cudaMemcpyHostToDevice, st) != cudaSuccess) {
+                    free(order);
+                    free(run_off);
+                    rc = ERROR_COMPRESSION;
+                    mc_set_error(mc, "Batch compress: host-to-device copy failed");
+                    goto fail;
+                }
+                for (size_t c = a; c < b; c++) P[order[c]].dev_in = stage + run_off[order[c]];
+                a = b;
+            }
+            free(order);
+            free(run_off);
+        }
+        for (size_t i = 0; i < n; i++)
+            if (P[i].src_dev) P[i].dev_in = P[i].g->data;
+    }
+
+    /* ------------------------------------------------------ scratch sizes */
+    uint32_t *words = NULL;
+    if (words_total) {
+        words = (uint32_t *)scratch_dev(&mc->scratch, SD_WORDS, words_total * 4);
+        if (!words) {
+            rc = ERROR_ALLOCATION;
+            goto fail;
+        }
+        cudaMemsetAsync(words, 0, words_total * 4, st);
+    }
+    mc_enc_result *results = (mc_enc_result *)scratch_dev(&mc->scratch, SD_RESULTS,
+                                                          n * sizeof(mc_enc_result));
+    mc_enc_tile *tiles = (mc_enc_tile *)scratch_dev(&mc->scratch, SD_TILES,
+                                                    (size_t)(ntiles_total + 1) * sizeof(mc_enc_tile));
+    int64_t *poff = (int64_t *)scratch_dev(&mc->scratch, SD_POFF, (size_t)(ntiles_total + 1) * 8);
+    int64_t *fsize = (int64_t *)scratch_dev(&mc->scratch, SD_FSIZE, (size_t)(nframes + 1) * 8);
+    if (!results || !tiles || !poff || !fsize) {
+        rc = ERROR_ALLOCATION;
+        goto fail;
+    }
+
+    /* ------------------------------------------------ build device tables */
+    /* layout: [items][tile_item by tile id][per wave: all-tile list, momentum-tile list][frames] */
+    size_t tab_items = ALIGN_UP(n * sizeof(mc_enc_item), 256);
+    size_t tab_tiles = ALIGN_UP((size_t)(ntiles_total + 1) * 4, 256);
+    size_t tab_lists = 2 * tab_tiles * (size_t)nwaves;
+    size_t tab_frames = ALIGN_UP((size_t)(nframes + 1) * sizeof(mc_frame_job), 256);
+    size_t tab_total = tab_items + tab_tiles + tab_lists + tab_frames;
+    uint8_t *htab = (uint8_t *)scratch_host(&mc->scratch, SH_TABLES, tab_total);
+    uint8_t *dtab = (uint8_t *)scratch_dev(&mc->scratch, SD_TABLES, tab_total);
+    if (!htab || !dtab) {
+        rc = ERROR_ALLOCATION;
+        goto fail;
+    }
+    /* the pinned table buffer is reused by every call: wait for the previous
+     * upload from it to finish before rewriting it */
+    cudaStreamSynchronize(st);
+    memset(htab, 0, tab_total);
+    mc_enc_item *hit = (mc_enc_item *)htab;
+    int32_t *h_tile_item = (int32_t *)(htab + tab_items);
+    mc_frame_job *hfr = (mc_frame_job *)(htab + tab_items + tab_tiles + tab_lists);
+    mc_frame_job *dfr = (mc_frame_job *)(dtab + tab_items + tab_tiles + tab_lists);
+    int fj = 0;
+    for (size_t i = 0; i < n; i++) {
+        cplan *p = &P[i];
+        mc_enc_item *I = &hit[i];
+        I->cur = p->dev_in;
+        I->hist_out = p->hist->dev;
+        I->data_out = payload_dev + p->off_data;
+        I->n = (int64_t)p->n;
+        I->kind = p->kind;
+        I->codec = p->dcodec;
+        I->tile_kernels = p->tile_param;
+        I->ntiles = p->ntiles;
+        I->tile_base = p->tile_base;
+        I->elem_bytes = (int32_t)mc_dtype_size(p->dt);
+        I->step = p->local_step;
+        I->lr = mc->config.momentum_lr;
+        I->thr = mc->config.consistency_threshold;
+        for (int t = 0; t < p->ntiles; t++) h_tile_item[p->tile_base + t] = (int32_t)i;
+        if (p->kind == MC_K_MOMENTUM) {
+            cgroup *grp = &G[p->group];
+            if (p->prev_item >= 0) I->prev = (const float *)P[p->prev_item].dev_in;
+            else I->prev = (const float *)p->prev_t->dev;
+            /* the first momentum item of a group reads the committed memory;
+             * later ones continue in the group's new buffer */
+            I->mem_in = p->wave == 0 ? (grp->mem_committed ? (const float *)grp->mem_committed->dev
+                                                           : NULL)
+                                     : (const float *)grp->mem_new->dev;
+            I->mem_out = (float *)grp->mem_new->dev;
+            I->K = (int64_t)p->K;
+            I->ks = (int32_t)p->ks;
+            I->ksdiv = mc_fastdiv_make((uint32_t)p->ks);
+            size_t stride = ALIGN_UP(p->kwords, 64);
+            I->bm_words = words + p->words_off;
+            I->dom_words = words + p->words_off + stride;
+            I->sign_words = words + p->words_off + 2 * stride;
+            if (mc->frame_mode == MC_FRAME_GPU) {
+                mc_frame_job *J = &hfr[fj];
+                J->src = (const uint8_t *)I->bm_words;
+                J->size = (int64_t)((p->K + 7) / 8);
+                J->dst = payload_dev + p->off_bm;
+                J->size_out = fsize + fj;
+                p->fs_bm = (size_t)fj++;
+                J = &hfr[fj];
+                J->src = (const uint8_t *)I->sign_words;
+                J->size = -1;
+                J->P_src = &results[i].P;
+                J->dst = payload_dev + p->off_sg;
+                J->size_out = fsize + fj;
+                p->fs_sg = (size_t)fj++;
+            }
+        } else if (p->kind == MC_K_FRAME || p->kind == MC_K_COPY) {
+            I->n = (int64_t)p->bytes;   /* byte tiles */
+            if (p->kind == MC_K_FRAME && mc->frame_mode == MC_FRAME_GPU) {
+                mc_frame_job *J = &hfr[fj];
+                J->src = (const uint8_t *)p->dev_in;
+                J->size = (int64_t)p->bytes;
+                J->dst = payload_dev + p->off_data;
+                J->size_out = fsize + fj;
+                p->fs_data = (size_t)fj++;
+            }
+        }
+    }
+    /* per-wave tile lists: direct items run in wave 0, momentum items in the
+     * wave of their position in the group's memory chain */
+    int *wave_na = (int *)calloc((size_t)nwaves, sizeof(int));
+    int *wave_nm = (int *)calloc((size_t)nwaves, sizeof(int));
+    if (!wave_na || !wave_nm) {
+        free(wave_na);
+        free(wave_nm);
+        rc = ERROR_ALLOCATION;
+        goto fail;
+    }
+    for (int w = 0; w < nwaves; w++) {
+        int32_t *la = (int32_t *)(htab + tab_items + tab_tiles + 2 * tab_tiles * (size_t)w);
+        int32_t *lm = la + tab_tiles / 4;
+        int na = 0, nm = 0;
+        for (size_t i = 0; i < n; i++) {
+            cplan *p = &P[i];
+            int in_wave = p->kind == MC_K_MOMENTUM ? p->wave == w : w == 0;
+            if (!in_wave) continue;
+            for (int t = 0; t < p->ntiles; t++) {
+                la[na++] = p->tile_base + t;
+                if (p->kind == MC_K_MOMENTUM) lm[nm++] = p->tile_base + t;
+            }
+        }
+        wave_na[w] = na;
+        wave_nm[w] = nm;
+    }
+    if (cudaMemcpyAsync(dtab, htab, tab_total, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+        cudaMemsetAsync(results, 0, n * sizeof(mc_enc_result), st) != cudaSuccess) {
+        free(wave_na);
+        free(wave_nm);
+        rc = ERROR_COMPRESSION;
+        goto fail;
+    }
+
+    /* ---------------------------------------------------------- launch */
+    mc->last_launches = 0;
+    for (int w = 0; w < nwaves; w++) {
+        uint8_t *dl = dtab + tab_items + tab_tiles + 2 * tab_tiles * (size_t)w;
+        mc_enc_launch L;
+        memset(&L, 0, sizeof(L));
+        L.items = (const mc_enc_item *)dtab;
+        L.results = results;
+        L.nitems = (int32_t)n;
+        L.tile_item = (const int32_t *)(dtab + tab_items);
+        L.all_tiles = (const int32_t *)dl;
+        L.nall_tiles = wave_na[w];
+        L.mom_tiles = (const int32_t *)(dl + tab_tiles);
+        L.nmom_tiles = wave_nm[w];
+        L.tiles = tiles;
+        L.tile_poff = poff;
+        L.frames = (w == nwaves - 1) ? dfr : NULL;
+        L.nframes = (w == nwaves - 1) ? fj : 0;
+        int k = mc_launch_encode(&L, st);
+        if (k < 0) {
+            free(wave_na);
+            free(wave_nm);
+            rc = ERROR_COMPRESSION;
+            mc_set_error(mc, "Batch compress: kernel launch failed: %s",
+                         cudaGetErrorString(cudaGetLastError()));
+            goto fail;
+        }
+        mc->last_launches += k;
+    }
+    free(wave_na);
+    free(wave_nm);
+    mc->total_launches += mc->last_launches;
+
+    /* ------------------------------------------------- results to host */
+    mc_enc_result *hres = (mc_enc_result *)scratch_host(&mc->scratch, SH_RESULTS,
+                                                        n * sizeof(mc_enc_result) + (size_t)(fj + 1) * 8);
+    int64_t *hfs = (int64_t *)((uint8_t *)hres + n * sizeof(mc_enc_result));
+    cudaMemcpyAsync(hres, results, n * sizeof(mc_enc_result), cudaMemcpyDeviceToHost, st);
+    if (fj) cudaMemcpyAsync(hfs, fsize, (size_t)fj * 8, cudaMemcpyDeviceToHost, st);
+    if (host_arena)
+        cudaMemcpyAsync(host_arena->ptr, payload_dev, arena_bytes, cudaMemcpyDeviceToHost, st);
+    cudaError_t e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) {
+        rc = ERROR_COMPRESSION;
+        mc_set_error(mc, "Batch compress: device execution failed: %s", cudaGetErrorString(e));
+        goto fail;
+    }
+
+    /* libzstd frame mode: frames written on the host from device contents */
+    if (mc->frame_mode == MC_FRAME_LIBZSTD) {
+        if (!zf_libzstd_available()) {
+            rc = ERROR_COMPRESSION;
+            mc_set_error(mc, "Batch compress: libzstd frame mode requested but libzstd.so.1 is missing");
+            goto fail;
+        }
+        size_t need = 0;
+        for (size_t i = 0; i < n; i++) {
+            if (P[i].kind == MC_K_MOMENTUM) need += 2 * ((P[i].K + 7) / 8) + 8;
+            else if (P[i].kind == MC_K_FRAME) need += P[i].bytes + 8;
+        }
+        uint8_t *hb = (uint8_t *)malloc(need ? need : 1);
+        if (!hb) {
+            rc = ERROR_ALLOCATION;
+            goto fail;
+        }
+        size_t o = 0;
+        for (size_t i = 0; i < n; i++) {
+            if (P[i].kind == MC_K_MOMENTUM) {
+                size_t c = (P[i].K + 7) / 8;
+                cudaMemcpy(hb + o, hit[i].bm_words, c, cudaMemcpyDeviceToHost);
+                cudaMemcpy(hb + o + c, hit[i].sign_words, c, cudaMemcpyDeviceToHost);
+                o += 2 * c + 8;
+            } else if (P[i].kind == MC_K_FRAME) {
+                cudaMemcpy(hb + o, P[i].dev_in, P[i].bytes, cudaMemcpyDeviceToHost);
+                o += P[i].bytes + 8;
+            }
+        }
+        o = 0;
+        uint8_t *ha = (uint8_t *)host_arena->ptr;
+        for (size_t i = 0; i < n; i++) {
+            cplan *p = &P[i];
+            if (p->kind == MC_K_MOMENTUM) {
+                size_t c = (p->K + 7) / 8;
+                size_t sb = (size_t)(hres[i].P + 7) / 8;
+                size_t a = zf_libzstd_compress(ha + p->off_bm, p->cap_bm, hb + o, c, 10);
+                size_t b = hres[i].P ? zf_libzstd_compress(ha + p->off_sg, p->cap_sg, hb + o + c, sb, 10) : 0;
+                if (!a || (hres[i].P && !b)) {
+                    free(hb);
+                    rc = ERROR_COMPRESSION;
+                    goto fail;
+                }
+                p->fs_bm = a;   /* reuse as sizes */
+                p->fs_sg = b;
+                o += 2 * c + 8;
+            } else if (p->kind == MC_K_FRAME) {
+                size_t a = zf_libzstd_compress(ha + p->off_data, p->cap_data, hb + o, p->bytes, 10);
+                if (!a) {
+                    free(hb);
+                    rc = ERROR_COMPRESSION;
+                    goto fail;
+                }
+                p->fs_data = a;
+                o += p->bytes + 8;
+            }
+        }
+        free(hb);
+    }
+
+    /* -------------------------------------------- CompressedLayerData out */
+    {
+        mc_arena *arena = dev_arena ? dev_arena : host_arena;
+        uint8_t *base = (uint8_t *)arena->ptr;
+        CompressedLayerData **outs = (CompressedLayerData **)calloc(n, sizeof(*outs));
+        if (!outs) {
+            rc = ERROR_ALLOCATION;
+            goto fail;
+        }
+        for (size_t i = 0; i < n; i++) {
+            outs[i] = (CompressedLayerData *)calloc(1, sizeof(CompressedLayerData));
+            if (!outs[i]) {
+                for (size_t j = 0; j < i; j++) free(outs[j]);
+                free(outs);
+                rc = ERROR_ALLOCATION;
+                goto fail;
+            }
+        }
+        const int libz = mc->frame_mode == MC_FRAME_LIBZSTD;
+        for (size_t i = 0; i < n; i++) {
+            cplan *p = &P[i];
+            CompressedLayerData *c = outs[i];
+            const mc_enc_result *r = &hres[i];
+            snprintf(c->type, sizeof(c->type), "%s",
+                     p->mode == MODE_DIRECT ? "direct"
+                                            : (p->mode == MODE_MOMENTUM ? "momentum_predicted"
+                                                                        : "direct_generic"));
+            snprintf(c->codec, sizeof(c->codec), "%s", p->codec_tag);
+            c->ndim = p->g->ndim;
+            memcpy(c->shape, p->g->shape, p->g->ndim * sizeof(size_t));
+            snprintf(c->original_dtype, sizeof(c->original_dtype), "%s", mc_dtype_name(p->dt));
+            snprintf(c->stored_dtype, sizeof(c->stored_dtype), "%s", mc_dtype_name(p->dt));
+            c->step = p->local_step;
+            c->data = base + p->off_data;
+            if (p->kind == MC_K_MOMENTUM || p->kind == MC_K_QUANT) c->data_size = residual_bytes(p->dcodec, p->n);
+            else if (p->kind == MC_K_COPY) c->data_size = p->bytes;
+            else c->data_size = libz ? p->fs_data : (size_t)hfs[p->fs_data];
+            if (p->kind == MC_K_MOMENTUM) {
+                c->bitmap = base + p->off_bm;
+                c->bitmap_size = libz ? p->fs_bm : (size_t)hfs[p->fs_bm];
+                size_t sgs = libz ? p->fs_sg : (size_t)hfs[p->fs_sg];
+                c->dominant_signs = sgs ? base + p->off_sg : NULL;
+                c->dominant_signs_size = sgs;
+                c->num_predicted_kernels = (int)r->P;
+                c->prediction_ratio = (float)r->P / (float)p->K;
+                int64_t pel = r->P * (int64_t)p->ks;
+                c->sign_mismatch_ratio = pel > 0 ? (float)r->mism / (float)pel : 0.0f;
+                c->current_mean = r->cm;
+                c->current_std = r->cs;
+                c->prev_mean = r->pm;
+                c->prev_std = r->ps;
+                c->global_min = r->gmin;
+                c->global_max = r->gmax;
+            }
+        }
+        /* ------------------------------------------------------- commit */
+        for (size_t g = 0; g < ng; g++) {
+            if (!G[g].mem_new) continue;
+            char mk[2 * MAX_KEY_LENGTH];
+            mc_memory_key(mk, sizeof(mk), client, G[g].key);
+            mc_tensor *old = (mc_tensor *)map_get(mc->memory, mk);
+            map_put(mc->memory, mk, G[g].mem_new);
+            G[g].mem_new = NULL;
+            if (old) tensor_drop(old);
+            map_put(mc->mem_clients, client, (void *)1);
+        }
+        for (size_t i = 0; i < n; i++) {
+            intptr_t s = (intptr_t)map_get(mc->steps, P[i].hkey);
+            map_put(mc->steps, P[i].hkey, (void *)(s + 1));
+            mc_tensor *old = (mc_tensor *)map_get(mc->history, P[i].hkey);
+            map_put(mc->history, P[i].hkey, P[i].hist);
+            P[i].hist = NULL;
+            if (old) tensor_drop(old);
+            mc_record_stats(mc, outs[i]);
+            items[i].compressed = outs[i];
+            items[i].error = ERROR_NONE;
+            registry_add(outs[i], arena);
+        }
+        arena_retain(arena, (int)n - 1);
+        free(outs);
+        if (n == 0) arena_release(arena);
+    }
+    rc = ERROR_NONE;
+    goto out;
+
+fail:
+    free_plan_tensors(mc, P, n, G, ng);
+    if (dev_arena) arena_release(dev_arena);
+    if (host_arena) arena_release(host_arena);
+    for (size_t i = 0; i < n; i++) {
+        items[i].compressed = NULL;
+        if (items[i].error == ERROR_NONE) items[i].error = rc;
+    }
+out:
+    free(P);
+    free(G);
+    return rc;
+}
+
+/* ============================================================== decompress */
+typedef struct {
+    int ok;               /* planned successfully */
+    int kind;             /* MC_D_* */
+    int dcodec;
+    DataType dt;
+    size_t ndim, shape[MAX_NDIM], n, bytes, K, ks;
+    char hkey[MAX_KEY_LENGTH];
+    char mkey[2 * MAX_KEY_LENGTH];
+    mc_tensor *prev;          /* decoder history head (MOMENTUM) */
+    mc_tensor *mem_in;
+    mc_tensor *mem_new;
+    mc_tensor *hist;
+    /* payload sources */
+    const uint8_t *data;      /* data bytes as passed (host or device) */
+    size_t data_size;
+    const uint8_t *bm;
+    size_t bm_size;
+    const uint8_t *sg;
+    size_t sg_size;
+    int data_frame;           /* data is a zstd frame (lossless content) */
+    /* device addresses after staging */
+    const uint8_t *d_data, *d_bm, *d_sg;
+    /* content buffers (device) */
+    size_t c_data_off, c_bm_off, c_sg_off;
+    int j_data, j_bm, j_sg;   /* unframe job indices, -1 when none */
+    size_t out_off;
+    int tile_base, ntiles, tile_param;
+    const char *why;
+} dplan;
+
+typedef struct {
+    const uint8_t *src;
+    size_t len;
+    const uint8_t **dst;      /* where the device address is written */
+} hrange;
+
+static int is_our_device_arena_ptr(const void *p, int dev) {
+    int d = -1;
+    return mc_ptr_is_device(p, &d) && d == dev;
+}
+
+/* Plans one item (reference decompress_layer :3476-3598 validation order). */
+static void dplan_item(MomentumCompressor *mc, dplan *d, const BatchItem *it, const char *client) {
+    const CompressedLayerData *c = it->compressed;
+    d->ok = 0;
+    d->j_data = d->j_bm = d->j_sg = -1;
+    if (!c || !it->layer_name || !*it->layer_name) { d->why = "NULL compressed data or layer name"; return; }
+    if (!c->type[0]) { d->why = "compressed type is empty"; return; }
+    if (c->ndim < MIN_NDIM || c->ndim > MAX_NDIM) { d->why = "invalid ndim"; return; }
+    if (!c->data || c->data_size == 0) { d->why = "compressed data is empty"; return; }
+    if (mc_dtype_parse(c->original_dtype, &d->dt) != 0) { d->why = "unknown original dtype"; return; }
+    d->ndim = c->ndim;
+    d->n = 1;
+    for (size_t i = 0; i < c->ndim; i++) {
+        d->shape[i] = c->shape[i];
+        d->n *= c->shape[i];
+    }
+    if (d->n == 0) { d->why = "empty shape"; return; }
+    d->bytes = d->n * mc_dtype_size(d->dt);
+    mc_history_key(d->hkey, client, it->layer_name);
+    d->data = c->data;
+    d->data_size = c->data_size;
+    const char *codec = c->codec;
+    int is_direct = strcmp(c->type, "direct") == 0 || strcmp(c->type, "direct_generic") == 0;
+    int is_mom = strcmp(c->type, "momentum_predicted") == 0;
+    if (!is_direct && !is_mom) { d->why = "unknown compression type"; return; }
+
+    /* residual / data codec */
+    if (strcmp(codec, "q8") == 0 || strcmp(codec, "int4") == 0) {
+        if (d->dt != DTYPE_FLOAT32) { d->why = "quantised payload for a non-float32 tensor"; return; }
+        d->dcodec = codec[0] == 'q' ? MC_DC_Q8 : MC_DC_INT4;
+        if (c->data_size != residual_bytes(d->dcodec, d->n)) { d->why = "size mismatch"; return; }
+        d->kind = MC_D_QUANT;
+    } else if (strcmp(codec, "sz3_memcpy") == 0) {
+        if (c->data_size != d->bytes) { d->why = "size mismatch"; return; }
+        d->dcodec = MC_DC_RAW;
+        d->kind = MC_D_COPY;
+    } else if (strcmp(codec, "zstd") == 0 || strcmp(codec, "blosc") == 0) {
+        /* blosc is decoded as zstd, as the reference does without USE_BLOSC */
+        d->data_frame = 1;
+        d->dcodec = MC_DC_RAW;
+        d->kind = MC_D_COPY;
+    } else if (strcmp(codec, "pickle") == 0) {
+        /* "PICKLE\0\0" + u64 size + bytes (reference :714-745) */
+        if (c->data_size < 16 || memcmp(c->data, "PICKLE\0\0", 8) != 0) { d->why = "invalid pickle header"; return; }
+        uint64_t sz;
+        memcpy(&sz, c->data + 8, 8);
+        if (sz + 16 != c->data_size || sz != d->bytes) { d->why = "size mismatch"; return; }
+        d->data = c->data + 16;
+        d->data_size = sz;
+        d->dcodec = MC_DC_RAW;
+        d->kind = MC_D_COPY;
+    } else {
+        d->why = "unsupported codec";
+        return;
+    }
+
+    if (is_mom) {
+        if (d->dt != DTYPE_FLOAT32 || d->ndim != 4) { d->why = "momentum layer must be 4-D float32"; return; }
+        d->K = d->shape[0] * d->shape[1];
+        d->ks = d->shape[2] * d->shape[3];
+        if (d->kind == MC_D_COPY && !d->data_frame) d->kind = MC_D_RESIDUAL;  /* raw floats */
+        if (d->kind == MC_D_QUANT) d->kind = MC_D_RESIDUAL;
+        if (d->data_frame) { d->why = "zstd-coded momentum residual is not supported"; return; }
+        d->bm = c->bitmap;
+        d->bm_size = c->bitmap ? c->bitmap_size : 0;
+        d->sg = c->dominant_signs;
+        d->sg_size = c->dominant_signs ? c->dominant_signs_size : 0;
+        mc_tensor *h = (mc_tensor *)map_get(mc->history, d->hkey);
+        int hist_ok = h && h->dtype == DTYPE_FLOAT32 && h->ndim == 4 && h->n == d->n;
+        for (size_t i = 0; hist_ok && i < 4; i++) hist_ok = h->shape[i] == d->shape[i];
+        if (d->bm_size > 0 && hist_ok) {
+            d->kind = MC_D_MOMENTUM;
+            d->prev = h;
+            char lk[MAX_KEY_LENGTH];
+            mc_layer_key(lk, sizeof(lk), it->layer_name, d->shape, d->ndim, d->dt);
+            mc_memory_key(d->mkey, sizeof(d->mkey), client, lk);
+            d->mem_in = (mc_tensor *)map_get(mc->memory, d->mkey);
+        }
+    } else if (d->kind == MC_D_QUANT) {
+        /* direct tensor through the quantiser */
+    }
+    d->ok = 1;
+}
+
+static int dec_segment(MomentumCompressor *mc, const BatchItem *items, size_t n, const char *client,
+                       NDArray **out, int out_loc, size_t *n_ok) {
+    cudaStream_t st = mc->stream;
+    const int dev = mc->device;
+    dplan *D = (dplan *)calloc(n, sizeof(dplan));
+    if (!D) return ERROR_ALLOCATION;
+    int rc = ERROR_NONE;
+    for (size_t i = 0; i < n; i++) {
+        out[i] = NULL;
+        dplan_item(mc, &D[i], &items[i], client);
+        if (!D[i].ok)
+            fprintf(stderr, "[ERROR] Batch decompress: item '%s': %s\n",
+                    items[i].layer_name ? items[i].layer_name : "(null)", D[i].why);
+    }
+
+    /* ---------------------------------------------- payload residency */
+    /* host payload ranges are copied to the device (adjacent ranges merged);
+     * frames with compressed blocks are decoded on the host first */
+    size_t nr = 0;
+    hrange *R = (hrange *)calloc(3 * n + 1, sizeof(hrange));
+    uint8_t **host_dec = (uint8_t **)calloc(3 * n + 1, sizeof(uint8_t *));
+    size_t nhd = 0;
+    if (!R || !host_dec) { rc = ERROR_ALLOCATION; goto done; }
+    for (size_t i = 0; i < n; i++) {
+        dplan *d = &D[i];
+        if (!d->ok) continue;
+        const uint8_t *srcs[3] = {d->data, d->kind == MC_D_MOMENTUM ? d->bm : NULL,
+                                  d->kind == MC_D_MOMENTUM ? d->sg : NULL};
+        size_t lens[3] = {d->data_size, d->bm_size, d->sg_size};
+        const uint8_t **dsts[3] = {&d->d_data, &d->d_bm, &d->d_sg};
+        int is_frame[3] = {d->data_frame, 1, 1};
+        for (int k = 0; k < 3; k++) {
+            if (!srcs[k] || lens[k] == 0) continue;
+            if (is_our_device_arena_ptr(srcs[k], dev)) {
+                *dsts[k] = srcs[k];
+                continue;
+            }
+            const uint8_t *src = srcs[k];
+            size_t len = lens[k];
+            if (is_frame[k] && !zf_is_simple(src, len)) {
+                /* compressed blocks: decode with libzstd on the host */
+                unsigned long long cs = 0;
+                if (zf_content_size(src, len, &cs) != 0 || cs > (1ull << 40)) {
+                    if (k == 0) { d->ok = 0; d->why = "zstd decompression failed"; }
+                    else if (k == 1) d->kind = MC_D_RESIDUAL;
+                    else d->sg = NULL, d->sg_size = 0;
+                    continue;
+                }
+                size_t cap = (size_t)cs + 16;
+                uint8_t *buf = (uint8_t *)malloc(cap);
+                size_t got = 0;
+                if (!buf || zf_decode_host(src, len, buf, cap, &got) != 0) {
+                    free(buf);
+                    if (k == 0) { d->ok = 0; d->why = "zstd decompression failed"; }
+                    else if (k == 1) d->kind = MC_D_RESIDUAL;
+                    else d->sg = NULL, d->sg_size = 0;
+                    continue;
+                }
+                /* re-frame as a raw frame so the device path reads it */
+                uint8_t *fr = (uint8_t *)malloc(zf_max_frame_size(got));
+                if (!fr) { free(buf); rc = ERROR_ALLOCATION; goto done; }
+                size_t fl = zf_write_raw_host(fr, buf, got);
+                free(buf);
+                host_dec[nhd++] = fr;
+                src = fr;
+                len = fl;
+                if (k == 0) d->data_size = fl;
+                else if (k == 1) d->bm_size = fl;
+                else d->sg_size = fl;
+            }
+            R[nr].src = src;
+            R[nr].len = len;
+            R[nr].dst = dsts[k];
+            nr++;
+        }
+    }
+    /* momentum items whose bitmap turned out unusable fall back to residual only */
+    /* stage host ranges */
+    if (nr) {
+        /* sort by address, merge ranges with gaps below 64 KiB */
+        for (size_t a = 1; a < nr; a++) {
+            hrange v = R[a];
+            size_t b = a;
+            while (b > 0 && (uintptr_t)R[b - 1].src > (uintptr_t)v.src) { R[b] = R[b - 1]; b--; }
+            R[b] = v;
+        }
+        size_t total = 0;
+        for (size_t a = 0; a < nr;) {
+            uintptr_t base = (uintptr_t)R[a].src, end = base + R[a].len;
+            size_t b = a + 1;
+            while (b < nr && (uintptr_t)R[b].src <= end + 65536) {
+                uintptr_t e2 = (uintptr_t)R[b].src + R[b].len;
+                if (e2 > end) end = e2;
+                b++;
+            }
+            total = ALIGN_UP(total + (base & 15) + (end - base), SLOT_ALIGN);
+            a = b;
+        }
+        uint8_t *stage = (uint8_t *)scratch_dev(&mc->scratch, SD_DSTAGE, total + 256);
+        if (!stage) { rc = ERROR_ALLOCATION; goto done; }
+        size_t off = 0;
+        for (size_t a = 0; a < nr;) {
+            uintptr_t base = (uintptr_t)R[a].src, end = base + R[a].len;
+            size_t b = a + 1;
+            while (b < nr && (uintptr_t)R[b].src <= end + 65536) {
+                uintptr_t e2 = (uintptr_t)R[b].src + R[b].len;
+                if (e2 > end) end = e2;
+                b++;
+            }
+            /* keep the source's 16-byte phase so 4-byte fields stay aligned */
+            size_t phase = base & 15;
+            uint8_t *dst = stage + off + phase;
+            if (cudaMemcpyAsync(dst, (const void *)base, end - base, cudaMemcpyHostToDevice, st) !=
+                cudaSuccess) { rc = ERROR_DECOMPRESSION; goto done; }
+            for (size_t c = a; c < b; c++) *R[c].dst = dst + ((uintptr_t)R[c].src - base);
+            off = ALIGN_UP(off + phase + (end - base), SLOT_ALIGN);
+            a = b;
+        }
+    }
+
+    /* ------------------------------------------ tiles, contents, outputs */
+    int ntiles = 0, nmom_tiles = 0, njobs = 0;
+    size_t content_bytes = 0, out_bytes = 0;
+    for (size_t i = 0; i < n; i++) {
+        dplan *d = &D[i];
+        if (!d->ok) continue;
+        if (d->kind == MC_D_MOMENTUM) {
+            d->tile_param = tile_kernels_for(d->ks);
+            d->ntiles = (int)((d->K + (size_t)d->tile_param - 1) / (size_t)d->tile_param);
+            nmom_tiles += d->ntiles;
+            size_t wb = ALIGN_UP(((d->K + 31) / 32 + 1) * 4 + 4096, 256);
+            d->c_bm_off = content_bytes;
+            content_bytes += wb;
+            d->j_bm = njobs++;
+            if (d->d_sg) {
+                d->c_sg_off = content_bytes;
+                content_bytes += wb;
+                d->j_sg = njobs++;
+            }
+        } else if (d->kind == MC_D_COPY) {
+            d->tile_param = TILE_ELEMS * 4;
+            d->ntiles = (int)((d->bytes + (size_t)d->tile_param - 1) / (size_t)d->tile_param);
+            if (d->data_frame) {
+                d->c_data_off = content_bytes;
+                content_bytes += ALIGN_UP(d->bytes + 16, 256);
+                d->j_data = njobs++;
+            }
+        } else {
+            d->tile_param = TILE_ELEMS;
+            d->ntiles = (int)((d->n + TILE_ELEMS - 1) / TILE_ELEMS);
+        }
+        d->tile_base = ntiles;
+        ntiles += d->ntiles;
+        d->out_off = out_bytes;
+        out_bytes = ALIGN_UP(out_bytes + d->bytes, SLOT_ALIGN);
+    }
+    uint8_t *content = content_bytes ? (uint8_t *)scratch_dev(&mc->scratch, SD_DCONTENT, content_bytes) : NULL;
+    mc_arena *oarena = NULL;
+    uint8_t *dout;
+    if (out_loc == FALCOM_LOC_DEVICE) {
+        oarena = arena_acquire(out_bytes, dev);
+        dout = oarena ? (uint8_t *)oarena->ptr : NULL;
+    } else {
+        dout = (uint8_t *)scratch_dev(&mc->scratch, SD_DOUT, out_bytes + 256);
+        oarena = arena_acquire(out_bytes, -1);
+    }
+    if ((content_bytes && !content) || !dout || !oarena) { rc = ERROR_ALLOCATION; goto fail_arena; }
+    for (size_t i = 0; i < n; i++) {
+        dplan *d = &D[i];
+        if (!d->ok) continue;
+        d->hist = tensor_new(d->dt, d->ndim, d->shape, dev);
+        if (!d->hist) { rc = ERROR_ALLOCATION; goto fail_arena; }
+        if (d->kind == MC_D_MOMENTUM) {
+            d->mem_new = tensor_new(DTYPE_FLOAT32, 4, d->shape, dev);
+            if (!d->mem_new) { rc = ERROR_ALLOCATION; goto fail_arena; }
+        }
+    }
+
+    /* ------------------------------------------------------- tables */
+    size_t t_items = ALIGN_UP(n * sizeof(mc_dec_item), 256);
+    size_t t_tiles = ALIGN_UP((size_t)(ntiles + 1) * 4, 256);
+    size_t t_jobs = ALIGN_UP((size_t)(njobs + 1) * sizeof(mc_unframe_job), 256);
+    size_t t_lens = ALIGN_UP((size_t)(njobs + 1) * 8, 256);
+    size_t t_res = ALIGN_UP(n * sizeof(mc_dec_result), 256);
+    size_t t_count = ALIGN_UP((size_t)(ntiles + 1) * 4, 256);
+    size_t t_poff = ALIGN_UP((size_t)(ntiles + 1) * 8, 256);
+    size_t tab = t_items + 3 * t_tiles + t_jobs;
+    size_t dyn = t_lens + t_res + t_count + t_poff;
+    uint8_t *ht = (uint8_t *)scratch_host(&mc->scratch, SH_TABLES, tab + t_lens + t_res);
+    uint8_t *dt = (uint8_t *)scratch_dev(&mc->scratch, SD_TABLES, tab + dyn);
+    if (!ht || !dt) { rc = ERROR_ALLOCATION; goto fail_arena; }
+    cudaStreamSynchronize(st);
+    memset(ht, 0, tab);
+    mc_dec_item *hi = (mc_dec_item *)ht;
+    int32_t *h_ti = (int32_t *)(ht + t_items);
+    int32_t *h_all = (int32_t *)(ht + t_items + t_tiles);
+    int32_t *h_mom = (int32_t *)(ht + t_items + 2 * t_tiles);
+    mc_unframe_job *h_jobs = (mc_unframe_job *)(ht + t_items + 3 * t_tiles);
+    int64_t *d_lens = (int64_t *)(dt + tab);
+    mc_dec_result *d_res = (mc_dec_result *)(dt + tab + t_lens);
+    int32_t *d_count = (int32_t *)(dt + tab + t_lens + t_res);
+    int64_t *d_poff = (int64_t *)(dt + tab + t_lens + t_res + t_count);
+    int na = 0, nm = 0;
+    for (size_t i = 0; i < n; i++) {
+        dplan *d = &D[i];
+        if (!d->ok) continue;
+        mc_dec_item *I = &hi[i];
+        I->kind = d->kind;
+        I->codec = d->dcodec;
+        I->n = (int64_t)(d->kind == MC_D_COPY ? d->bytes : d->n);
+        I->tile_kernels = d->tile_param;
+        I->ntiles = d->ntiles;
+        I->tile_base = d->tile_base;
+        I->elem_bytes = (int32_t)mc_dtype_size(d->dt);
+        I->hist_out = d->hist->dev;
+        I->out = dout + d->out_off;
+        if (d->dcodec == MC_DC_Q8 || d->dcodec == MC_DC_INT4) {
+            I->scale_ptr = (const float *)d->d_data;
+            I->data = d->d_data + 4;
+        } else {
+            I->data = d->d_data;
+        }
+        if (d->j_data >= 0) {
+            mc_unframe_job *J = &h_jobs[d->j_data];
+            J->frame = d->d_data;
+            J->frame_size = (int64_t)d->data_size;
+            J->dst = content + d->c_data_off;
+            J->cap = (int64_t)d->bytes;
+            J->content_out = d_lens + d->j_data;
+            I->data = content + d->c_data_off;
+        }
+        if (d->kind == MC_D_MOMENTUM) {
+            const CompressedLayerData *c = items[i].compressed;
+            I->K = (int64_t)d->K;
+            I->ks = (int32_t)d->ks;
+            I->ksdiv = mc_fastdiv_make((uint32_t)d->ks);
+            I->prev = (const float *)d->prev->dev;
+            I->mem_in = d->mem_in ? (const float *)d->mem_in->dev : NULL;
+            I->mem_out = (float *)d->mem_new->dev;
+            I->cm = c->current_mean;
+            I->cs = c->current_std;
+            I->pm = c->prev_mean;
+            I->ps = c->prev_std;
+            I->lr = mc->config.momentum_lr;
+            mc_unframe_job *J = &h_jobs[d->j_bm];
+            J->frame = d->d_bm;
+            J->frame_size = (int64_t)d->bm_size;
+            J->dst = content + d->c_bm_off;
+            J->cap = (int64_t)(((d->K + 31) / 32 + 1) * 4 + 4096);
+            J->content_out = d_lens + d->j_bm;
+            I->bm_words = (const uint32_t *)(content + d->c_bm_off);
+            I->bm_len_ptr = d_lens + d->j_bm;
+            if (d->j_sg >= 0) {
+                J = &h_jobs[d->j_sg];
+                J->frame = d->d_sg;
+                J->frame_size = (int64_t)d->sg_size;
+                J->dst = content + d->c_sg_off;
+                J->cap = (int64_t)(((d->K + 31) / 32 + 1) * 4 + 4096);
+                J->content_out = d_lens + d->j_sg;
+                I->sg_bytes = content + d->c_sg_off;
+                I->sg_len_ptr = d_lens + d->j_sg;
+            }
+        }
+        for (int t = 0; t < d->ntiles; t++) {
+            h_ti[d->tile_base + t] = (int32_t)i;
+            h_all[na++] = d->tile_base + t;
+            if (d->kind == MC_D_MOMENTUM) h_mom[nm++] = d->tile_base + t;
+        }
+    }
+    if (cudaMemcpyAsync(dt, ht, tab, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+        cudaMemsetAsync(d_res, 0, t_res, st) != cudaSuccess) { rc = ERROR_DECOMPRESSION; goto fail_arena; }
+
+    /* ------------------------------------------------------- launch */
+    mc->last_launches = 0;
+    if (njobs) {
+        /* bitmaps must decode into clean zero-padded words */
+        if (content_bytes) cudaMemsetAsync(content, 0, content_bytes, st);
+        int k = mc_launch_unframe((const mc_unframe_job *)(dt + t_items + 3 * t_tiles), njobs, st);
+        if (k < 0) { rc = ERROR_DECOMPRESSION; goto fail_arena; }
+        mc->last_launches += k;
+    }
+    {
+        mc_dec_launch L;
+        memset(&L, 0, sizeof(L));
+        L.items = (const mc_dec_item *)dt;
+        L.results = d_res;
+        L.nitems = (int32_t)n;
+        L.tile_item = (const int32_t *)(dt + t_items);
+        L.all_tiles = (const int32_t *)(dt + t_items + t_tiles);
+        L.nall_tiles = na;
+        L.mom_tiles = (const int32_t *)(dt + t_items + 2 * t_tiles);
+        L.nmom_tiles = nm;
+        L.tile_count = d_count;
+        L.tile_poff = d_poff;
+        int k = mc_launch_decode(&L, st);
+        if (k < 0) { rc = ERROR_DECOMPRESSION; goto fail_arena; }
+        mc->last_launches += k;
+    }
+    mc->total_launches += mc->last_launches;
+
+    /* ------------------------------------------------- back to the host */
+    int64_t *h_lens = (int64_t *)(ht + tab);
+    mc_dec_result *h_res = (mc_dec_result *)(ht + tab + t_lens);
+    if (njobs) cudaMemcpyAsync(h_lens, d_lens, (size_t)njobs * 8, cudaMemcpyDeviceToHost, st);
+    cudaMemcpyAsync(h_res, d_res, n * sizeof(mc_dec_result), cudaMemcpyDeviceToHost, st);
+    if (out_loc != FALCOM_LOC_DEVICE && out_bytes)
+        cudaMemcpyAsync(oarena->ptr, dout, out_bytes, cudaMemcpyDeviceToHost, st);
+    cudaError_t e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) {
+        mc_set_error(mc, "Batch decompress: device execution failed: %s", cudaGetErrorString(e));
+        rc = ERROR_DECOMPRESSION;
+        goto fail_arena;
+    }
+
+    /* ------------------------------------------------------- commit */
+    int handed = 0;
+    for (size_t i = 0; i < n; i++) {
+        dplan *d = &D[i];
+        if (!d->ok) continue;
+        if (d->j_data >= 0 && h_lens[d->j_data] != (int64_t)d->bytes) {
+            fprintf(stderr, "[ERROR] Size mismatch: got %lld, expected %zu\n",
+                    (long long)h_lens[d->j_data], d->bytes);
+            d->ok = 0;
+            continue;
+        }
+        NDArray *a = (NDArray *)calloc(1, sizeof(NDArray));
+        size_t *shp = (size_t *)malloc(d->ndim * sizeof(size_t));
+        if (!a || !shp) { free(a); free(shp); d->ok = 0; continue; }
+        memcpy(shp, d->shape, d->ndim * sizeof(size_t));
+        a->data = (uint8_t *)oarena->ptr + d->out_off;
+        a->shape = shp;
+        a->ndim = d->ndim;
+        a->total_size = d->n;
+        a->dtype = d->dt;
+        out[i] = a;
+        registry_add(a, oarena);
+        handed++;
+        (*n_ok)++;
+        int commit_hist = 1;
+        if (d->kind == MC_D_MOMENTUM) {
+            /* reference :3266-3269: no predicted kernel -> residual returned,
+             * neither memory nor history touched */
+            if (h_res[i].P == 0) commit_hist = 0;
+            else {
+                mc_tensor *old = (mc_tensor *)map_get(mc->memory, d->mkey);
+                map_put(mc->memory, d->mkey, d->mem_new);
+                d->mem_new = NULL;
+                if (old) tensor_drop(old);
+                map_put(mc->mem_clients, client, (void *)1);
+            }
+        } else if (d->kind == MC_D_RESIDUAL) {
+            commit_hist = 0;
+        }
+        if (commit_hist) {
+            mc_tensor *old = (mc_tensor *)map_get(mc->history, d->hkey);
+            map_put(mc->history, d->hkey, d->hist);
+            d->hist = NULL;
+            if (old) tensor_drop(old);
+        }
+    }
+    if (handed > 0) arena_retain(oarena, handed - 1);
+    else arena_release(oarena);
+    oarena = NULL;
+
+fail_arena:
+    if (oarena) arena_release(oarena);
+    for (size_t i = 0; i < n; i++) {
+        if (D[i].hist) tensor_drop(D[i].hist);
+        if (D[i].mem_new) tensor_drop(D[i].mem_new);
+    }
+done:
+    for (size_t i = 0; i < nhd; i++) free(host_dec[i]);
+    free(host_dec);
+    free(R);
+    free(D);
+    return rc;
+}
+
+int mc_decompress_items(MomentumCompressor *mc, const BatchItem *items, size_t n,
+                        const char *client, NDArray **out, int out_loc) {
+    /* Items that share a history key with an earlier item of the call run in
+     * a later segment, after the earlier one's state is committed, so the
+     * serial semantics of the reference decoder hold. */
+    size_t ok = 0;
+    size_t a = 0;
+    int rc = ERROR_NONE;
+    while (a < n) {
+        size_t b = a + 1;
+        for (; b < n; b++) {
+            int clash = 0;
+            for (size_t j = a; j < b && !clash; j++) {
+                if (items[j].layer_name && items[b].layer_name &&
+                    strcmp(items[j].layer_name, items[b].layer_name) == 0)
+                    clash = 1;
+            }
+            if (clash) break;
+        }
+        int r = dec_segment(mc, items + a, b - a, client, out + a, out_loc, &ok);
+        if (r != ERROR_NONE) {
+            rc = r;
+            for (size_t j = a; j < b; j++) {
+                if (out[j]) { ndarray_destroy(out[j]); out[j] = NULL; }
+            }
+        }
+        a = b;
+    }
+    (void)rc;
+    if (ok == 0) return ERROR_DECOMPRESSION;
+    if (ok < n) return -((int)n - (int)ok);
+    return ERROR_NONE;
+}

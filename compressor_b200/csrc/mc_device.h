@@ -1,0 +1,196 @@
+/*
+ * mc_device.h -- plain-C descriptors shared by the host code and the sm_100a
+ * kernels (mc_kernels.cu), plus the extern "C" launchers.
+ *
+ * Work is described per batch as a table of items (one per tensor) cut into
+ * tiles; one CTA processes one tile.  Momentum tiles always hold whole conv
+ * kernels (a multiple of 32 kernels except at the end of a layer), so every
+ * per-kernel decision and every 32-bit word of the bitmap belongs to exactly
+ * one tile.
+ */
+#ifndef MC_DEVICE_H
+#define MC_DEVICE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* q = floor(x / d) for 32-bit x as ((umulhi(x, mul) + x) >> shift). */
+typedef struct {
+    uint32_t mul;
+    uint32_t shift;
+} mc_fastdiv;
+mc_fastdiv mc_fastdiv_make(uint32_t d);
+
+/* item kinds of the encoder table */
+enum {
+    MC_K_MOMENTUM = 0,  /* 4-D momentum layer: stats, bitmap, signs, memory, residual codec */
+    MC_K_QUANT = 1,     /* direct lossy tensor through the residual codec */
+    MC_K_COPY = 2,      /* direct lossy tensor stored raw ("sz3_memcpy") */
+    MC_K_FRAME = 3      /* direct lossless tensor: zstd frame of its bytes */
+};
+
+/* residual codecs on the device */
+enum { MC_DC_Q8 = 0, MC_DC_INT4 = 1, MC_DC_RAW = 2, MC_DC_Q8_RAW = 3, MC_DC_INT4_RAW = 4 };
+
+typedef struct {
+    const void *cur;        /* input (fp32 for MOMENTUM/QUANT/COPY, bytes for FRAME) */
+    const float *prev;      /* MOMENTUM: encoder history head */
+    const float *mem_in;    /* MOMENTUM: committed prediction memory, NULL = zeros */
+    float *mem_out;         /* MOMENTUM: new prediction memory */
+    void *hist_out;         /* copy of the input for the new history head, or NULL */
+    uint8_t *data_out;      /* payload data slot */
+    uint32_t *bm_words;     /* MOMENTUM: bitmap content, ceil(K/32) words */
+    uint32_t *dom_words;    /* MOMENTUM: dominant sign per kernel, ceil(K/32) words */
+    uint32_t *sign_words;   /* MOMENTUM: dense sign content, zeroed, ceil(K/32) words */
+    int64_t n;              /* elements */
+    int64_t K;              /* kernels (MOMENTUM) */
+    int32_t ks;             /* kernel size h*w (MOMENTUM) */
+    int32_t kind;
+    int32_t codec;          /* MC_DC_* */
+    int32_t tile_kernels;   /* MOMENTUM: kernels per tile; others: elements per tile */
+    int32_t ntiles;
+    int32_t tile_base;      /* index of the first tile in the batch tile list */
+    int32_t elem_bytes;     /* bytes per element of the input */
+    int32_t step;
+    mc_fastdiv ksdiv;
+    float lr;
+    float thr;
+} mc_enc_item;
+
+typedef struct {
+    double s_cur, s_prev;   /* sums of |cur|, |prev| */
+    double v_cur, v_prev;   /* sums of squared deviations */
+    float mn, mx, maxr;
+    int32_t P;
+    int64_t mism;
+} mc_enc_tile;
+
+typedef struct {
+    float cm, cs, pm, ps, gmin, gmax;
+    float inv_ps;           /* 1/prev_std when prev_std > 1e-8, else 1 */
+    float scale;            /* residual codec scale */
+    float maxr;
+    float pad0;
+    int64_t P;              /* predicted kernels */
+    int64_t mism;           /* sign mismatches over predicted elements */
+    uint32_t ticket[4];     /* last-CTA election per pass; zeroed before launch */
+    int32_t err;
+    int32_t pad1;
+} mc_enc_result;
+
+/* One zstd frame to write from device content. */
+typedef struct {
+    const uint8_t *src;
+    int64_t size;               /* content bytes, or -1: ceil(P/8) of *P_src */
+    const int64_t *P_src;
+    uint8_t *dst;
+    int64_t *size_out;          /* frame bytes written */
+} mc_frame_job;
+
+typedef struct {
+    const mc_enc_item *items;   /* device */
+    mc_enc_result *results;     /* device, zeroed by the caller before the first wave */
+    int32_t nitems;
+    const int32_t *tile_item;   /* device: item index of every tile id */
+    const int32_t *all_tiles;   /* device: tile ids processed by passes 1 and 4 */
+    int32_t nall_tiles;
+    const int32_t *mom_tiles;   /* device: tile ids of momentum items (passes 2, 3) */
+    int32_t nmom_tiles;
+    mc_enc_tile *tiles;         /* device scratch, one per tile id */
+    int64_t *tile_poff;         /* device scratch, ntiles */
+    const mc_frame_job *frames; /* device */
+    int32_t nframes;
+} mc_enc_launch;
+
+/* ---------------------------------------------------------------- decode */
+enum {
+    MC_D_MOMENTUM = 0,      /* full reconstruction with memory update */
+    MC_D_RESIDUAL = 1,      /* residual only (no usable history / bitmap) */
+    MC_D_QUANT = 2,         /* direct, codes * scale */
+    MC_D_COPY = 3           /* direct, bytes copied (raw floats or lossless content) */
+};
+
+typedef struct {
+    const uint8_t *data;        /* codes (after the scale header), raw floats or content bytes */
+    const uint32_t *bm_words;   /* MOMENTUM: bitmap content (zero padded words) */
+    const uint8_t *sg_bytes;    /* MOMENTUM: sign content, NULL when absent */
+    int64_t sg_len;             /* sign content bytes (when sg_len_ptr is NULL) */
+    const int64_t *sg_len_ptr;  /* device-expanded sign content length, -1 = failed */
+    const int64_t *bm_len_ptr;  /* device-expanded bitmap content length, -1 = failed */
+    const float *prev;          /* MOMENTUM: decoder history head */
+    const float *mem_in;        /* MOMENTUM: decoder memory, NULL = zeros */
+    float *mem_out;
+    void *hist_out;             /* decoded tensor (becomes the history head) */
+    void *out;                  /* optional second copy (device output), NULL */
+    int64_t n;
+    int64_t K;
+    int64_t bm_bits;            /* min(bitmap bytes*8, K) */
+    int32_t ks;
+    int32_t kind;
+    int32_t codec;              /* MC_DC_* for the residual / QUANT data */
+    int32_t tile_kernels;
+    int32_t ntiles;
+    int32_t tile_base;
+    int32_t elem_bytes;
+    int32_t pad;
+    const float *scale_ptr;     /* device pointer to the f32 scale header */
+    mc_fastdiv ksdiv;
+    float cm, cs, pm, ps, lr;
+} mc_dec_item;
+
+typedef struct {
+    int64_t P;
+    uint32_t ticket;
+    int32_t err;
+} mc_dec_result;
+
+/* One device-resident zstd frame to expand into contiguous content. */
+typedef struct {
+    const uint8_t *frame;
+    int64_t frame_size;
+    uint8_t *dst;
+    int64_t cap;                /* bytes available at dst */
+    int64_t *content_out;       /* content bytes produced, -1 on a format error */
+} mc_unframe_job;
+
+typedef struct {
+    const mc_dec_item *items;
+    mc_dec_result *results;     /* zeroed by the caller */
+    int32_t nitems;
+    const int32_t *tile_item;   /* item index of every tile id */
+    const int32_t *all_tiles;   /* tile ids for the reconstruct kernel */
+    int32_t nall_tiles;
+    const int32_t *mom_tiles;   /* tile ids of momentum items (prefix kernel) */
+    int32_t nmom_tiles;
+    int32_t *tile_count;        /* scratch */
+    int64_t *tile_poff;         /* scratch */
+} mc_dec_launch;
+
+/* Launchers: return the number of kernels launched, or a negative value
+ * when a launch failed. */
+int mc_launch_encode(const mc_enc_launch *L, void *stream);
+int mc_launch_decode(const mc_dec_launch *L, void *stream);
+int mc_launch_unframe(const mc_unframe_job *jobs, int njobs, void *stream);
+
+/* Reusable device / pinned scratch owned by one compressor instance. */
+typedef struct {
+    void *ptr;
+    size_t bytes;
+} mc_sbuf;
+typedef struct {
+    mc_sbuf dev[16];
+    mc_sbuf host[8];
+    int device;
+} mc_scratch;
+void *scratch_dev(mc_scratch *s, int slot, size_t bytes);
+void *scratch_host(mc_scratch *s, int slot, size_t bytes);
+void scratch_free(mc_scratch *s);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

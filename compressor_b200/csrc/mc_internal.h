@@ -1,0 +1,141 @@
+/*
+ * mc_internal.h -- shared types of the host side of libmomentum_compressor.so.
+ *
+ * Host code is C11; device work is issued through the launchers declared at
+ * the end of this file (implemented in mc_kernels.cu).
+ */
+#ifndef MC_INTERNAL_H
+#define MC_INTERNAL_H
+
+#include <pthread.h>
+#include <stdint.h>
+#include <stdio.h>
+
+#include <cuda_runtime_api.h>
+
+#include "falcom_b200.h"
+#include "momentum_compressor.h"
+#include "mc_device.h"
+
+#define MC_EXPORT __attribute__((visibility("default")))
+
+/* ------------------------------------------------------------------ maps */
+/* Open-addressing string-keyed hash map (keys are copied). */
+typedef struct mc_map {
+    char **keys;
+    void **vals;
+    size_t cap;   /* power of two */
+    size_t len;
+    size_t tomb;
+} mc_map;
+
+mc_map *map_new(void);
+void map_free(mc_map *m, void (*drop)(void *));
+void *map_get(const mc_map *m, const char *key);
+int map_put(mc_map *m, const char *key, void *val);   /* 0 ok, -1 OOM; replaces */
+void *map_del(mc_map *m, const char *key);            /* returns removed value */
+#define MAP_TOMB ((char *)1)
+#define MAP_LIVE(m, i) ((m)->keys[i] && (m)->keys[i] != MAP_TOMB)
+
+/* ------------------------------------------------------------- buffers */
+/* Arena of library-owned output memory (pinned host or device), reference
+ * counted by the CompressedLayerData / NDArray objects that point into it. */
+typedef struct mc_arena {
+    void *ptr;
+    size_t bytes;
+    int device;      /* -1 for pinned host memory */
+    int refs;
+} mc_arena;
+
+mc_arena *arena_acquire(size_t bytes, int device);   /* refs = 1 */
+void arena_release(mc_arena *a);                      /* refs--, pooled at 0 */
+void arena_retain(mc_arena *a, int n);
+
+/* Ownership registry of returned objects. */
+void registry_add(const void *obj, mc_arena *a);
+mc_arena *registry_take(const void *obj, int *found);
+
+/* Device buffers held by state entries (pooled per device by byte size). */
+void *dbuf_get(int device, size_t bytes);
+void dbuf_put(int device, void *ptr, size_t bytes);
+
+/* ------------------------------------------------------------- state */
+typedef struct {
+    DataType dtype;
+    size_t ndim;
+    size_t shape[MAX_NDIM];
+    size_t n;          /* elements */
+    size_t bytes;
+    void *dev;         /* device copy */
+} mc_tensor;
+
+mc_tensor *tensor_new(DataType dt, size_t ndim, const size_t *shape, int device);
+void tensor_drop(void *t);   /* for map_free */
+
+struct MomentumCompressor {
+    CompressorConfig config;
+    char current_client_id[256];
+    int log_level;
+    int device;
+    cudaStream_t stream;
+    cudaStream_t own_stream;
+    int residual_codec;      /* MC_CODEC_* */
+    int frame_mode;          /* MC_FRAME_GPU / MC_FRAME_LIBZSTD */
+    int payload_loc;
+    int output_loc;
+
+    mc_map *steps;           /* "client:layer" -> (intptr_t) step */
+    mc_map *history;         /* "client:layer" -> mc_tensor* (latest gradient) */
+    mc_map *memory;          /* "client\x1f<layer|dtype|conv_(...)>" -> mc_tensor* */
+    mc_map *mem_clients;     /* clients that own a prediction-memory table */
+
+    struct {
+        size_t total_compressions;
+        float *prediction_ratios;
+        size_t pr_count, pr_cap;
+        float *sign_mismatch_ratios;
+        size_t sm_count, sm_cap;
+    } stats;
+
+    char last_error[256];
+    int last_launches;
+    long long total_launches;
+
+    /* reusable scratch (grown on demand) */
+    mc_scratch scratch;
+};
+
+enum { MC_CODEC_Q8 = 0, MC_CODEC_INT4, MC_CODEC_RAW, MC_CODEC_Q8_RAW, MC_CODEC_INT4_RAW };
+enum { MC_FRAME_GPU = 0, MC_FRAME_LIBZSTD = 1 };
+
+/* ------------------------------------------------------------- helpers */
+size_t mc_dtype_size(DataType dt);
+const char *mc_dtype_name(DataType dt);
+int mc_dtype_parse(const char *s, DataType *out);
+void mc_history_key(char *out, const char *client, const char *layer);
+void mc_layer_key(char *out, size_t cap, const char *layer, const size_t *shape, size_t ndim,
+                  DataType dt);
+void mc_memory_key(char *out, size_t cap, const char *client, const char *layer_key);
+int mc_should_lossy(const char *name, size_t n, DataType dt, size_t threshold);
+int mc_env_flag(const char *name);
+void mc_set_error(MomentumCompressor *mc, const char *fmt, ...);
+void mc_log(const MomentumCompressor *mc, int level, const char *fmt, ...);
+int mc_ptr_is_device(const void *p, int *device);
+void mc_record_stats(MomentumCompressor *mc, const CompressedLayerData *c);
+
+/* zstd frames (mc_wire.c) */
+size_t zf_max_frame_size(size_t content);
+size_t zf_write_raw_host(uint8_t *dst, const uint8_t *src, size_t n);  /* raw/RLE */
+int zf_content_size(const uint8_t *frame, size_t n, unsigned long long *out);
+int zf_decode_host(const uint8_t *frame, size_t n, uint8_t *dst, size_t cap, size_t *out);
+int zf_is_simple(const uint8_t *frame, size_t n);   /* raw/RLE blocks only */
+int zf_libzstd_available(void);
+size_t zf_libzstd_compress(uint8_t *dst, size_t cap, const uint8_t *src, size_t n, int level);
+
+/* batch engines (mc_batch.c) */
+int mc_compress_grouped(MomentumCompressor *mc, BatchItem *items, size_t n, const char *client,
+                        int payload_loc, int allow_fault);
+int mc_decompress_items(MomentumCompressor *mc, const BatchItem *items, size_t n,
+                        const char *client, NDArray **out, int out_loc);
+
+#endif
