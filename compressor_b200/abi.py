@@ -312,6 +312,8 @@ class Codec:
     def __init__(self, lib_path: str, client: str = "Client1", **cfg):
         self.lib = ctypes.CDLL(os.path.abspath(lib_path))
         _bind(self.lib)
+        if hasattr(self.lib, "falcom_set_residual_codec"):
+            bind_extensions(self.lib)
         c = self.lib.momentum_compressor_default_config()
         for k, v in cfg.items():
             if isinstance(v, str):
@@ -423,3 +425,78 @@ class Codec:
                    for i in range(s.num_clients)]
         self.lib.detailed_stats_free(p)
         return clients
+
+
+class PreparedBatch:
+    """Reusable C-side batch for a fixed list of tensors: one BatchItem and one
+    NDArray per tensor, built once; each round only the data pointers change.
+    compress -> decompress -> release run without per-item Python work."""
+
+    def __init__(self, lib: ctypes.CDLL, names: Sequence[str], shapes: Sequence[Sequence[int]],
+                 dtype=np.float32):
+        self.lib = lib
+        self.n = len(names)
+        self._names = [nm.encode() for nm in names]
+        self._shapes = [(ctypes.c_size_t * len(s))(*s) for s in shapes]
+        self.arrays = (NDArrayC * self.n)()
+        self.items = (BatchItemC * self.n)()
+        self.outs = (ctypes.POINTER(NDArrayC) * self.n)()
+        code = NP_TO_DTYPE[np.dtype(dtype)]
+        for i, s in enumerate(shapes):
+            a = self.arrays[i]
+            a.shape = self._shapes[i]
+            a.ndim = len(s)
+            a.total_size = int(np.prod(s))
+            a.dtype = code
+            self.items[i].layer_name = self._names[i]
+            self.items[i].gradient = ctypes.pointer(a)
+        lib.falcom_free_batch.argtypes = [ctypes.POINTER(BatchItemC), ctypes.c_size_t,
+                                          ctypes.POINTER(ctypes.POINTER(NDArrayC))]
+        lib.falcom_free_batch.restype = None
+
+    def set_pointers(self, base: int, offsets_bytes: Sequence[int]) -> None:
+        for i, o in enumerate(offsets_bytes):
+            self.arrays[i].data = base + o
+
+    def compress(self, handle, client: bytes) -> int:
+        return self.lib.momentum_compressor_compress_batch(handle, self.items, self.n, client)
+
+    def decompress(self, handle, client: bytes) -> int:
+        return self.lib.momentum_compressor_decompress_batch(handle, self.items, self.n, client, self.outs)
+
+    def payload_bytes(self) -> int:
+        tot = 0
+        for it in self.items:
+            if it.compressed:
+                c = it.compressed.contents
+                tot += c.data_size + c.bitmap_size + c.dominant_signs_size
+        return tot
+
+    def release(self) -> None:
+        self.lib.falcom_free_batch(self.items, self.n, self.outs)
+
+
+def bind_extensions(lib: ctypes.CDLL) -> None:
+    c_vp = ctypes.c_void_p
+    lib.falcom_set_residual_codec.argtypes = [c_vp, ctypes.c_char_p]
+    lib.falcom_set_frame_mode.argtypes = [c_vp, ctypes.c_char_p]
+    lib.falcom_set_payload_location.argtypes = [c_vp, ctypes.c_int]
+    lib.falcom_set_output_location.argtypes = [c_vp, ctypes.c_int]
+    lib.falcom_set_stream.argtypes = [c_vp, c_vp]
+    lib.falcom_last_error.argtypes = [c_vp]
+    lib.falcom_last_error.restype = ctypes.c_char_p
+    lib.falcom_last_launches.argtypes = [c_vp]
+    lib.falcom_total_launches.argtypes = [c_vp]
+    lib.falcom_total_launches.restype = ctypes.c_longlong
+    lib.falcom_set_kernel_timing.argtypes = [c_vp, ctypes.c_int]
+    lib.falcom_kernel_times.argtypes = [c_vp, ctypes.POINTER(ctypes.c_double),
+                                        ctypes.POINTER(ctypes.c_longlong), ctypes.c_int]
+    lib.falcom_kernel_name.argtypes = [ctypes.c_int]
+    lib.falcom_kernel_name.restype = ctypes.c_char_p
+
+
+def kernel_times(lib: ctypes.CDLL, handle) -> dict:
+    ms = (ctypes.c_double * 16)()
+    cnt = (ctypes.c_longlong * 16)()
+    k = lib.falcom_kernel_times(handle, ms, cnt, 16)
+    return {lib.falcom_kernel_name(i).decode(): (ms[i], cnt[i]) for i in range(k)}

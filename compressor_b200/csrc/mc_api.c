@@ -173,6 +173,8 @@ MC_EXPORT void momentum_compressor_destroy(MomentumCompressor *mc) {
     map_free(mc->mem_clients, NULL);
     scratch_free(&mc->scratch);
     if (mc->own_stream) cudaStreamDestroy(mc->own_stream);
+    for (int i = 0; i < 2 * MC_KTRACE_MAX; i++)
+        if (mc->ktrace.ev[i]) cudaEventDestroy((cudaEvent_t)mc->ktrace.ev[i]);
     free(mc->stats.prediction_ratios);
     free(mc->stats.sign_mismatch_ratios);
     int lvl = mc->log_level;
@@ -951,4 +953,70 @@ MC_EXPORT long long falcom_total_launches(const MomentumCompressor *mc) { return
 MC_EXPORT int falcom_is_device_pointer(const void *ptr) {
     int d = -1;
     return mc_ptr_is_device(ptr, &d);
+}
+
+/* ----------------------------------------------------------- kernel timing */
+static const char *k_names[MC_NKERN] = {"enc_pass1_stats_sign", "enc_pass2_variance", "enc_pass3_predict",
+                                        "enc_pass4_quantize_pack", "frames_write", "frames_expand",
+                                        "dec_prefix", "dec_reconstruct"};
+
+mc_ktrace *mc_trace_begin(MomentumCompressor *mc) {
+    if (!mc->ktiming) return NULL;
+    if (!mc->ktrace.ev[0]) {
+        for (int i = 0; i < 2 * MC_KTRACE_MAX; i++) {
+            cudaEvent_t e;
+            if (cudaEventCreate(&e) != cudaSuccess) return NULL;
+            mc->ktrace.ev[i] = (void *)e;
+        }
+    }
+    mc->ktrace.n = 0;
+    return &mc->ktrace;
+}
+
+void mc_trace_end(MomentumCompressor *mc) {
+    if (!mc->ktiming || !mc->ktrace.ev[0]) return;
+    for (int i = 0; i < mc->ktrace.n; i++) {
+        float ms = 0.0f;
+        if (cudaEventElapsedTime(&ms, (cudaEvent_t)mc->ktrace.ev[2 * i], (cudaEvent_t)mc->ktrace.ev[2 * i + 1]) ==
+            cudaSuccess) {
+            mc->ktime_ms[mc->ktrace.kid[i]] += ms;
+            mc->kcount[mc->ktrace.kid[i]] += 1;
+        }
+    }
+    (void)cudaGetLastError();
+    mc->ktrace.n = 0;
+}
+
+MC_EXPORT int falcom_set_kernel_timing(MomentumCompressor *mc, int on) {
+    if (!mc) return ERROR_INVALID_PARAM;
+    mc->ktiming = on ? 1 : 0;
+    memset(mc->ktime_ms, 0, sizeof(mc->ktime_ms));
+    memset(mc->kcount, 0, sizeof(mc->kcount));
+    return ERROR_NONE;
+}
+
+MC_EXPORT int falcom_kernel_times(const MomentumCompressor *mc, double *ms, long long *counts, int n) {
+    if (!mc) return 0;
+    for (int i = 0; i < n && i < MC_NKERN; i++) {
+        if (ms) ms[i] = mc->ktime_ms[i];
+        if (counts) counts[i] = mc->kcount[i];
+    }
+    return MC_NKERN;
+}
+
+MC_EXPORT const char *falcom_kernel_name(int id) {
+    return (id >= 0 && id < MC_NKERN) ? k_names[id] : "";
+}
+
+MC_EXPORT void falcom_free_batch(BatchItem *items, size_t n, NDArray **outs) {
+    for (size_t i = 0; i < n; i++) {
+        if (items && items[i].compressed) {
+            compressed_layer_data_free(items[i].compressed);
+            items[i].compressed = NULL;
+        }
+        if (outs && outs[i]) {
+            ndarray_destroy(outs[i]);
+            outs[i] = NULL;
+        }
+    }
 }

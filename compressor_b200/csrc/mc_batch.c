@@ -43,6 +43,47 @@ enum {
 };
 enum { SH_TABLES = 0, SH_RESULTS, SH_STAGE };
 
+/* Call-local string -> int table (keys are borrowed, not copied). */
+typedef struct {
+    const char **keys;
+    int *vals;
+    size_t cap;
+} strtab;
+
+static uint64_t st_hash(const char *s) {
+    uint64_t h = 1469598103934665603ull;
+    while (*s) {
+        h ^= (unsigned char)*s++;
+        h *= 1099511628211ull;
+    }
+    return h;
+}
+
+static int strtab_init(strtab *t, size_t n) {
+    t->cap = 16;
+    while (t->cap < 4 * n) t->cap <<= 1;
+    t->keys = (const char **)calloc(t->cap, sizeof(char *));
+    t->vals = (int *)calloc(t->cap, sizeof(int));
+    return t->keys && t->vals ? 0 : -1;
+}
+
+static void strtab_free(strtab *t) {
+    free(t->keys);
+    free(t->vals);
+}
+
+/* Returns the value slot of `key`, inserting it with value `init` if absent. */
+static int *strtab_slot(strtab *t, const char *key, int init) {
+    size_t i = (size_t)st_hash(key) & (t->cap - 1);
+    while (t->keys[i]) {
+        if (strcmp(t->keys[i], key) == 0) return &t->vals[i];
+        i = (i + 1) & (t->cap - 1);
+    }
+    t->keys[i] = key;
+    t->vals[i] = init;
+    return &t->vals[i];
+}
+
 /* ================================================================ compress */
 typedef struct {
     char hkey[MAX_KEY_LENGTH];
@@ -76,6 +117,7 @@ typedef struct {
     mc_tensor *mem_committed;
     mc_tensor *mem_new;
     int n_mom;
+    int last;   /* last item of the group in batch order, -1 before the first */
 } cgroup;
 
 static int layout_equal(const NDArray *a, DataType dt, size_t ndim, const size_t *shape, size_t n) {
@@ -194,65 +236,67 @@ int mc_compress_grouped(MomentumCompressor *mc, BatchItem *items, size_t n, cons
     }
 
     /* --------------------------------------------- group keys (:2627-2645) */
-    for (size_t i = 0; i < n; i++) {
-        size_t same = 0;
-        for (size_t j = 0; j < n; j++) same += strcmp(P[i].hkey, P[j].hkey) == 0;
-        const mc_tensor *h0 = (const mc_tensor *)map_get(mc->history, P[i].hkey);
-        char gk[MAX_KEY_LENGTH];
-        if (P[i].candidate && (h0 != NULL || same > 1)) snprintf(gk, sizeof(gk), "%s", P[i].lkey);
-        else if (same > 1) snprintf(gk, sizeof(gk), "%s", P[i].hkey);
-        else snprintf(gk, sizeof(gk), "item:%zu", i);
-        size_t g;
-        for (g = 0; g < ng; g++)
-            if (strcmp(G[g].key, gk) == 0) break;
-        if (g == ng) {
-            snprintf(G[g].key, sizeof(G[g].key), "%s", gk);
-            char mk[2 * MAX_KEY_LENGTH];
-            mc_memory_key(mk, sizeof(mk), client, gk);
-            G[g].mem_committed = (mc_tensor *)map_get(mc->memory, mk);
-            ng++;
+    {
+        strtab hcount, gidx;
+        if (strtab_init(&hcount, n) || strtab_init(&gidx, n)) {
+            strtab_free(&hcount);
+            strtab_free(&gidx);
+            rc = ERROR_ALLOCATION;
+            goto out;
         }
-        P[i].group = (int)g;
+        for (size_t i = 0; i < n; i++) (*strtab_slot(&hcount, P[i].hkey, 0))++;
+        for (size_t i = 0; i < n; i++) {
+            int same = *strtab_slot(&hcount, P[i].hkey, 0);
+            P[i].prev_t = (mc_tensor *)map_get(mc->history, P[i].hkey);
+            char gk[MAX_KEY_LENGTH];
+            if (P[i].candidate && (P[i].prev_t != NULL || same > 1)) snprintf(gk, sizeof(gk), "%s", P[i].lkey);
+            else if (same > 1) snprintf(gk, sizeof(gk), "%s", P[i].hkey);
+            else snprintf(gk, sizeof(gk), "item:%zu", i);
+            snprintf(G[ng].key, sizeof(G[ng].key), "%s", gk);
+            int *slot = strtab_slot(&gidx, G[ng].key, (int)ng);
+            if (*slot == (int)ng) {
+                char mk[2 * MAX_KEY_LENGTH];
+                mc_memory_key(mk, sizeof(mk), client, gk);
+                G[ng].mem_committed = (mc_tensor *)map_get(mc->memory, mk);
+                G[ng].last = -1;
+                ng++;
+            }
+            P[i].group = *slot;
+        }
+        strtab_free(&hcount);
+        strtab_free(&gidx);
     }
 
-    /* ------------------------ per-group step chains (:2710-2814, in order) */
-    for (size_t g = 0; g < ng; g++) {
-        for (size_t i = 0; i < n; i++) {
-            if (P[i].group != (int)g) continue;
-            /* state of this history key inside the group: last earlier item */
-            int last = -1;
-            for (size_t j = 0; j < i; j++)
-                if (P[j].group == (int)g && strcmp(P[j].hkey, P[i].hkey) == 0) last = (int)j;
-            int step0;
-            if (last >= 0) {
-                step0 = P[last].local_step;
-            } else {
-                step0 = (int)(intptr_t)map_get(mc->steps, P[i].hkey);
-            }
-            P[i].local_step = step0 + 1;
-            const NDArray *g_i = P[i].g;
-            int has_prev = 0, prev_match = 0;
-            if (last >= 0) {
-                has_prev = 1;
-                const NDArray *pg = P[last].g;
-                prev_match = layout_equal(g_i, pg->dtype, pg->ndim, pg->shape, pg->total_size);
-                P[i].prev_item = last;
-            } else {
-                mc_tensor *h = (mc_tensor *)map_get(mc->history, P[i].hkey);
-                if (h) {
-                    has_prev = 1;
-                    prev_match = layout_equal(g_i, h->dtype, h->ndim, h->shape, h->n);
-                    P[i].prev_t = h;
-                }
-            }
-            if (P[i].local_step == 1) P[i].mode = MODE_DIRECT;
-            else if (has_prev && prev_match && P[i].candidate) P[i].mode = MODE_MOMENTUM;
-            else P[i].mode = MODE_GENERIC;
-            if (P[i].mode == MODE_MOMENTUM) {
-                P[i].wave = G[g].n_mom;
-                G[g].n_mom++;
-            }
+    /* ------------------------ per-group step chains (:2710-2814, in order)
+     * Every item of a group has the same history key (the group key is the
+     * layer key, which contains the layer name, or the history key itself),
+     * so the group's chain state is its last processed item. */
+    for (size_t i = 0; i < n; i++) {
+        cgroup *grp = &G[P[i].group];
+        const int last = grp->last;
+        int step0 = last >= 0 ? P[last].local_step : (int)(intptr_t)map_get(mc->steps, P[i].hkey);
+        P[i].local_step = step0 + 1;
+        const NDArray *g_i = P[i].g;
+        int has_prev = 0, prev_match = 0;
+        if (last >= 0) {
+            has_prev = 1;
+            const NDArray *pg = P[last].g;
+            prev_match = layout_equal(g_i, pg->dtype, pg->ndim, pg->shape, pg->total_size);
+            P[i].prev_item = last;
+            P[i].prev_t = NULL;
+        } else if (P[i].prev_t) {
+            mc_tensor *h = P[i].prev_t;
+            has_prev = 1;
+            prev_match = layout_equal(g_i, h->dtype, h->ndim, h->shape, h->n);
         }
+        if (P[i].local_step == 1) P[i].mode = MODE_DIRECT;
+        else if (has_prev && prev_match && P[i].candidate) P[i].mode = MODE_MOMENTUM;
+        else P[i].mode = MODE_GENERIC;
+        if (P[i].mode == MODE_MOMENTUM) {
+            P[i].wave = grp->n_mom;
+            grp->n_mom++;
+        }
+        grp->last = (int)i;
     }
 
     /* --------------------------------------------- kinds, codecs, tiling */
@@ -353,16 +397,12 @@ int mc_compress_grouped(MomentumCompressor *mc, BatchItem *items, size_t n, cons
             goto fail;
         }
     }
-    for (size_t g = 0; g < ng; g++) {
-        if (G[g].n_mom == 0) continue;
+    for (size_t i = 0; i < n; i++) {
+        cgroup *grp = &G[P[i].group];
+        if (P[i].mode != MODE_MOMENTUM || grp->mem_new) continue;
         /* every momentum item of a group has the group's shape */
-        for (size_t i = 0; i < n; i++) {
-            if (P[i].group == (int)g && P[i].mode == MODE_MOMENTUM) {
-                G[g].mem_new = tensor_new(DTYPE_FLOAT32, 4, P[i].g->shape, dev);
-                break;
-            }
-        }
-        if (!G[g].mem_new) {
+        grp->mem_new = tensor_new(DTYPE_FLOAT32, 4, P[i].g->shape, dev);
+        if (!grp->mem_new) {
             rc = ERROR_ALLOCATION;
             mc_set_error(mc, "Batch compress: device allocation failed for prediction memory");
             goto fail;
@@ -373,9 +413,11 @@ int mc_compress_grouped(MomentumCompressor *mc, BatchItem *items, size_t n, cons
     {
         size_t stage_bytes = 0;
         int any_host = 0;
+        mc_ptrcache pc;
+        pc.n = 0;
         for (size_t i = 0; i < n; i++) {
             int d = -1;
-            P[i].src_dev = mc_ptr_is_device(P[i].g->data, &d);
+            P[i].src_dev = mc_classify(&pc, P[i].g->data, &d);
             if (P[i].src_dev && d != dev) P[i].src_dev = 0;   /* another GPU: copy */
             if (!P[i].src_dev) any_host = 1;
         }
@@ -586,6 +628,7 @@ int mc_compress_grouped(MomentumCompressor *mc, BatchItem *items, size_t n, cons
 
     /* ---------------------------------------------------------- launch */
     mc->last_launches = 0;
+    mc_ktrace *tr = mc_trace_begin(mc);
     for (int w = 0; w < nwaves; w++) {
         uint8_t *dl = dtab + tab_items + tab_tiles + 2 * tab_tiles * (size_t)w;
         mc_enc_launch L;
@@ -602,7 +645,7 @@ int mc_compress_grouped(MomentumCompressor *mc, BatchItem *items, size_t n, cons
         L.tile_poff = poff;
         L.frames = (w == nwaves - 1) ? dfr : NULL;
         L.nframes = (w == nwaves - 1) ? fj : 0;
-        int k = mc_launch_encode(&L, st);
+        int k = mc_launch_encode(&L, st, tr);
         if (k < 0) {
             free(wave_na);
             free(wave_nm);
@@ -626,6 +669,7 @@ int mc_compress_grouped(MomentumCompressor *mc, BatchItem *items, size_t n, cons
     if (host_arena)
         cudaMemcpyAsync(host_arena->ptr, payload_dev, arena_bytes, cudaMemcpyDeviceToHost, st);
     cudaError_t e = cudaStreamSynchronize(st);
+    mc_trace_end(mc);
     if (e != cudaSuccess) {
         rc = ERROR_COMPRESSION;
         mc_set_error(mc, "Batch compress: device execution failed: %s", cudaGetErrorString(e));
@@ -828,9 +872,9 @@ typedef struct {
     const uint8_t **dst;      /* where the device address is written */
 } hrange;
 
-static int is_our_device_arena_ptr(const void *p, int dev) {
+static int on_device(mc_ptrcache *pc, const void *p, int dev) {
     int d = -1;
-    return mc_ptr_is_device(p, &d) && d == dev;
+    return mc_classify(pc, p, &d) && d == dev;
 }
 
 /* Plans one item (reference decompress_layer :3476-3598 validation order). */
@@ -940,6 +984,8 @@ static int dec_segment(MomentumCompressor *mc, const BatchItem *items, size_t n,
     uint8_t **host_dec = (uint8_t **)calloc(3 * n + 1, sizeof(uint8_t *));
     size_t nhd = 0;
     if (!R || !host_dec) { rc = ERROR_ALLOCATION; goto done; }
+    mc_ptrcache pc;
+    pc.n = 0;
     for (size_t i = 0; i < n; i++) {
         dplan *d = &D[i];
         if (!d->ok) continue;
@@ -950,7 +996,7 @@ static int dec_segment(MomentumCompressor *mc, const BatchItem *items, size_t n,
         int is_frame[3] = {d->data_frame, 1, 1};
         for (int k = 0; k < 3; k++) {
             if (!srcs[k] || lens[k] == 0) continue;
-            if (is_our_device_arena_ptr(srcs[k], dev)) {
+            if (on_device(&pc, srcs[k], dev)) {
                 *dsts[k] = srcs[k];
                 continue;
             }
@@ -1191,10 +1237,11 @@ static int dec_segment(MomentumCompressor *mc, const BatchItem *items, size_t n,
 
     /* ------------------------------------------------------- launch */
     mc->last_launches = 0;
+    mc_ktrace *tr = mc_trace_begin(mc);
     if (njobs) {
         /* bitmaps must decode into clean zero-padded words */
         if (content_bytes) cudaMemsetAsync(content, 0, content_bytes, st);
-        int k = mc_launch_unframe((const mc_unframe_job *)(dt + t_items + 3 * t_tiles), njobs, st);
+        int k = mc_launch_unframe((const mc_unframe_job *)(dt + t_items + 3 * t_tiles), njobs, st, tr);
         if (k < 0) { rc = ERROR_DECOMPRESSION; goto fail_arena; }
         mc->last_launches += k;
     }
@@ -1211,7 +1258,7 @@ static int dec_segment(MomentumCompressor *mc, const BatchItem *items, size_t n,
         L.nmom_tiles = nm;
         L.tile_count = d_count;
         L.tile_poff = d_poff;
-        int k = mc_launch_decode(&L, st);
+        int k = mc_launch_decode(&L, st, tr);
         if (k < 0) { rc = ERROR_DECOMPRESSION; goto fail_arena; }
         mc->last_launches += k;
     }
@@ -1225,6 +1272,7 @@ static int dec_segment(MomentumCompressor *mc, const BatchItem *items, size_t n,
     if (out_loc != FALCOM_LOC_DEVICE && out_bytes)
         cudaMemcpyAsync(oarena->ptr, dout, out_bytes, cudaMemcpyDeviceToHost, st);
     cudaError_t e = cudaStreamSynchronize(st);
+    mc_trace_end(mc);
     if (e != cudaSuccess) {
         mc_set_error(mc, "Batch decompress: device execution failed: %s", cudaGetErrorString(e));
         rc = ERROR_DECOMPRESSION;
@@ -1303,17 +1351,18 @@ int mc_decompress_items(MomentumCompressor *mc, const BatchItem *items, size_t n
     size_t ok = 0;
     size_t a = 0;
     int rc = ERROR_NONE;
+    strtab seen;
+    if (strtab_init(&seen, n)) return ERROR_ALLOCATION;
     while (a < n) {
-        size_t b = a + 1;
+        size_t b = a;
+        /* a segment ends before the first repeated layer name */
         for (; b < n; b++) {
-            int clash = 0;
-            for (size_t j = a; j < b && !clash; j++) {
-                if (items[j].layer_name && items[b].layer_name &&
-                    strcmp(items[j].layer_name, items[b].layer_name) == 0)
-                    clash = 1;
-            }
-            if (clash) break;
+            const char *nm = items[b].layer_name ? items[b].layer_name : "";
+            int *s = strtab_slot(&seen, nm, (int)a - 1);
+            if (*s == (int)a) break;   /* already in this segment */
+            *s = (int)a;
         }
+        if (b == a) b = a + 1;
         int r = dec_segment(mc, items + a, b - a, client, out + a, out_loc, &ok);
         if (r != ERROR_NONE) {
             rc = r;
@@ -1323,6 +1372,7 @@ int mc_decompress_items(MomentumCompressor *mc, const BatchItem *items, size_t n
         }
         a = b;
     }
+    strtab_free(&seen);
     (void)rc;
     if (ok == 0) return ERROR_DECOMPRESSION;
     if (ok < n) return -((int)n - (int)ok);

@@ -170,11 +170,23 @@ typedef struct {
     int64_t *tile_poff;         /* scratch */
 } mc_dec_launch;
 
+/* Optional per-kernel event trace (events created by the host). */
+enum {
+    MC_KT_ENC_PASS1 = 0, MC_KT_ENC_PASS2, MC_KT_ENC_PASS3, MC_KT_ENC_PASS4, MC_KT_FRAMES,
+    MC_KT_UNFRAME, MC_KT_DEC_PREFIX, MC_KT_DEC_RECON, MC_NKERN
+};
+#define MC_KTRACE_MAX 64
+typedef struct {
+    void *ev[2 * MC_KTRACE_MAX];   /* cudaEvent_t pairs */
+    int kid[MC_KTRACE_MAX];
+    int n;
+} mc_ktrace;
+
 /* Launchers: return the number of kernels launched, or a negative value
- * when a launch failed. */
-int mc_launch_encode(const mc_enc_launch *L, void *stream);
-int mc_launch_decode(const mc_dec_launch *L, void *stream);
-int mc_launch_unframe(const mc_unframe_job *jobs, int njobs, void *stream);
+ * when a launch failed.  `tr` may be NULL. */
+int mc_launch_encode(const mc_enc_launch *L, void *stream, mc_ktrace *tr);
+int mc_launch_decode(const mc_dec_launch *L, void *stream, mc_ktrace *tr);
+int mc_launch_unframe(const mc_unframe_job *jobs, int njobs, void *stream, mc_ktrace *tr);
 
 /* Reusable device / pinned scratch owned by one compressor instance. */
 typedef struct {

@@ -103,7 +103,18 @@ struct MomentumCompressor {
 
     /* reusable scratch (grown on demand) */
     mc_scratch scratch;
+
+    /* per-kernel device time (falcom_set_kernel_timing) */
+    int ktiming;
+    mc_ktrace ktrace;
+    double ktime_ms[MC_NKERN];
+    long long kcount[MC_NKERN];
 };
+
+/* kernel timing: start a trace for one call / fold it into the totals after
+ * the call's stream synchronisation */
+mc_ktrace *mc_trace_begin(MomentumCompressor *mc);
+void mc_trace_end(MomentumCompressor *mc);
 
 enum { MC_CODEC_Q8 = 0, MC_CODEC_INT4, MC_CODEC_RAW, MC_CODEC_Q8_RAW, MC_CODEC_INT4_RAW };
 enum { MC_FRAME_GPU = 0, MC_FRAME_LIBZSTD = 1 };
@@ -121,6 +132,15 @@ int mc_env_flag(const char *name);
 void mc_set_error(MomentumCompressor *mc, const char *fmt, ...);
 void mc_log(const MomentumCompressor *mc, int level, const char *fmt, ...);
 int mc_ptr_is_device(const void *p, int *device);
+#define MC_PTRCACHE 32
+typedef struct {
+    struct {
+        uintptr_t lo, hi;
+        int device;
+    } r[MC_PTRCACHE];
+    int n;
+} mc_ptrcache;
+int mc_classify(mc_ptrcache *pc, const void *p, int *device);
 void mc_record_stats(MomentumCompressor *mc, const CompressedLayerData *c);
 
 /* zstd frames (mc_wire.c) */

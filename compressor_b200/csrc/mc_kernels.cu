@@ -855,48 +855,78 @@ __global__ void __launch_bounds__(TPB) k_dec_recon(mc_dec_launch L) {
 }  // namespace
 
 // ---------------------------------------------------------------- launchers
-extern "C" int mc_launch_encode(const mc_enc_launch *L, void *stream) {
+static inline void tr_begin(mc_ktrace *tr, int kid, cudaStream_t s) {
+    if (tr && tr->n < MC_KTRACE_MAX) {
+        cudaEventRecord((cudaEvent_t)tr->ev[2 * tr->n], s);
+        tr->kid[tr->n] = kid;
+    }
+}
+static inline void tr_end(mc_ktrace *tr, cudaStream_t s) {
+    if (tr && tr->n < MC_KTRACE_MAX) {
+        cudaEventRecord((cudaEvent_t)tr->ev[2 * tr->n + 1], s);
+        tr->n++;
+    }
+}
+
+extern "C" int mc_launch_encode(const mc_enc_launch *L, void *stream, mc_ktrace *tr) {
     cudaStream_t s = (cudaStream_t)stream;
     int n = 0;
     if (L->nall_tiles > 0) {
+        tr_begin(tr, MC_KT_ENC_PASS1, s);
         k_enc_pass1<<<L->nall_tiles, TPB, 0, s>>>(*L);
+        tr_end(tr, s);
         n++;
     }
     if (L->nmom_tiles > 0) {
+        tr_begin(tr, MC_KT_ENC_PASS2, s);
         k_enc_pass2<<<L->nmom_tiles, TPB, 0, s>>>(*L);
+        tr_end(tr, s);
+        tr_begin(tr, MC_KT_ENC_PASS3, s);
         k_enc_pass3<<<L->nmom_tiles, TPB, 0, s>>>(*L);
+        tr_end(tr, s);
         n += 2;
     }
     if (L->nall_tiles > 0) {
+        tr_begin(tr, MC_KT_ENC_PASS4, s);
         k_enc_pass4<<<L->nall_tiles, TPB, 0, s>>>(*L);
+        tr_end(tr, s);
         n++;
     }
     if (L->nframes > 0) {
+        tr_begin(tr, MC_KT_FRAMES, s);
         k_frames<<<L->nframes, TPB, 0, s>>>(L->frames);
+        tr_end(tr, s);
         n++;
     }
     if (cudaGetLastError() != cudaSuccess) return -1;
     return n;
 }
 
-extern "C" int mc_launch_decode(const mc_dec_launch *L, void *stream) {
+extern "C" int mc_launch_decode(const mc_dec_launch *L, void *stream, mc_ktrace *tr) {
     cudaStream_t s = (cudaStream_t)stream;
     int n = 0;
     if (L->nmom_tiles > 0) {
+        tr_begin(tr, MC_KT_DEC_PREFIX, s);
         k_dec_prefix<<<L->nmom_tiles, TPB, 0, s>>>(*L);
+        tr_end(tr, s);
         n++;
     }
     if (L->nall_tiles > 0) {
+        tr_begin(tr, MC_KT_DEC_RECON, s);
         k_dec_recon<<<L->nall_tiles, TPB, 0, s>>>(*L);
+        tr_end(tr, s);
         n++;
     }
     if (cudaGetLastError() != cudaSuccess) return -1;
     return n;
 }
 
-extern "C" int mc_launch_unframe(const mc_unframe_job *jobs, int njobs, void *stream) {
+extern "C" int mc_launch_unframe(const mc_unframe_job *jobs, int njobs, void *stream, mc_ktrace *tr) {
     if (njobs <= 0) return 0;
-    k_unframe<<<njobs, TPB, 0, (cudaStream_t)stream>>>(jobs);
+    cudaStream_t s = (cudaStream_t)stream;
+    tr_begin(tr, MC_KT_UNFRAME, s);
+    k_unframe<<<njobs, TPB, 0, s>>>(jobs);
+    tr_end(tr, s);
     if (cudaGetLastError() != cudaSuccess) return -1;
     return 1;
 }

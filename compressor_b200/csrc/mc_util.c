@@ -139,14 +139,20 @@ typedef struct pool_ent {
 } pool_ent;
 
 static pthread_mutex_t g_pool_mu = PTHREAD_MUTEX_INITIALIZER;
-static pool_ent *g_dpool = NULL;      /* free device buffers */
-static pool_ent *g_hpool = NULL;      /* free pinned / device arenas */
+#define DPOOL_BUCKETS 1024
+static pool_ent *g_dpool[DPOOL_BUCKETS];   /* free device buffers, by exact size */
+static pool_ent *g_hpool = NULL;           /* free pinned / device arenas */
+
+static size_t dpool_bucket(int device, size_t bytes) {
+    uint64_t x = (uint64_t)bytes * 0x9E3779B97F4A7C15ull ^ (uint64_t)(device + 7);
+    return (size_t)(x >> 54) & (DPOOL_BUCKETS - 1);
+}
 
 void *dbuf_get(int device, size_t bytes) {
     if (bytes == 0) bytes = 16;
+    size_t b = dpool_bucket(device, bytes);
     pthread_mutex_lock(&g_pool_mu);
-    pool_ent **pp = &g_dpool;
-    while (*pp) {
+    for (pool_ent **pp = &g_dpool[b]; *pp; pp = &(*pp)->next) {
         if ((*pp)->device == device && (*pp)->bytes == bytes) {
             pool_ent *e = *pp;
             *pp = e->next;
@@ -155,26 +161,27 @@ void *dbuf_get(int device, size_t bytes) {
             free(e);
             return p;
         }
-        pp = &(*pp)->next;
     }
     pthread_mutex_unlock(&g_pool_mu);
     void *p = NULL;
     if (cudaMalloc(&p, bytes) != cudaSuccess) {
         /* release cached buffers of this device and retry once */
+        (void)cudaGetLastError();
         pthread_mutex_lock(&g_pool_mu);
-        pool_ent **q = &g_dpool;
-        while (*q) {
-            if ((*q)->device == device) {
-                pool_ent *e = *q;
-                *q = e->next;
-                cudaFree(e->ptr);
-                free(e);
-            } else {
-                q = &(*q)->next;
+        for (size_t k = 0; k < DPOOL_BUCKETS; k++) {
+            pool_ent **q = &g_dpool[k];
+            while (*q) {
+                if ((*q)->device == device) {
+                    pool_ent *e = *q;
+                    *q = e->next;
+                    cudaFree(e->ptr);
+                    free(e);
+                } else {
+                    q = &(*q)->next;
+                }
             }
         }
         pthread_mutex_unlock(&g_pool_mu);
-        (void)cudaGetLastError();
         if (cudaMalloc(&p, bytes) != cudaSuccess) {
             (void)cudaGetLastError();
             return NULL;
@@ -194,13 +201,57 @@ void dbuf_put(int device, void *ptr, size_t bytes) {
     e->ptr = ptr;
     e->bytes = bytes;
     e->device = device;
+    size_t b = dpool_bucket(device, bytes);
     pthread_mutex_lock(&g_pool_mu);
-    e->next = g_dpool;
-    g_dpool = e;
+    e->next = g_dpool[b];
+    g_dpool[b] = e;
     pthread_mutex_unlock(&g_pool_mu);
 }
 
 /* ================================================================ arenas */
+/* Every arena allocation ever made (arenas are pooled, never freed), so that
+ * pointers into library-owned memory are classified without a driver query. */
+typedef struct {
+    uintptr_t lo, hi;
+    int device;
+} arena_range;
+static arena_range *g_arena_ranges = NULL;
+static size_t g_arena_nranges = 0, g_arena_cap = 0;
+
+static void arena_note_range(void *p, size_t bytes, int device) {
+    pthread_mutex_lock(&g_pool_mu);
+    if (g_arena_nranges == g_arena_cap) {
+        size_t nc = g_arena_cap ? 2 * g_arena_cap : 64;
+        arena_range *n = (arena_range *)realloc(g_arena_ranges, nc * sizeof(arena_range));
+        if (!n) {
+            pthread_mutex_unlock(&g_pool_mu);
+            return;
+        }
+        g_arena_ranges = n;
+        g_arena_cap = nc;
+    }
+    g_arena_ranges[g_arena_nranges].lo = (uintptr_t)p;
+    g_arena_ranges[g_arena_nranges].hi = (uintptr_t)p + bytes;
+    g_arena_ranges[g_arena_nranges].device = device;
+    g_arena_nranges++;
+    pthread_mutex_unlock(&g_pool_mu);
+}
+
+static int arena_lookup(uintptr_t a, uintptr_t *lo, uintptr_t *hi, int *device) {
+    int found = 0;
+    pthread_mutex_lock(&g_pool_mu);
+    for (size_t i = 0; i < g_arena_nranges; i++) {
+        if (a >= g_arena_ranges[i].lo && a < g_arena_ranges[i].hi) {
+            *lo = g_arena_ranges[i].lo;
+            *hi = g_arena_ranges[i].hi;
+            *device = g_arena_ranges[i].device;
+            found = 1;
+            break;
+        }
+    }
+    pthread_mutex_unlock(&g_pool_mu);
+    return found;
+}
 mc_arena *arena_acquire(size_t bytes, int device) {
     if (bytes == 0) bytes = 64;
     mc_arena *a = (mc_arena *)calloc(1, sizeof(mc_arena));
@@ -233,6 +284,7 @@ mc_arena *arena_acquire(size_t bytes, int device) {
         }
         a->ptr = p;
         a->bytes = bytes;
+        arena_note_range(p, bytes, device);
     }
     a->device = device;
     a->refs = 1;
@@ -508,17 +560,75 @@ void mc_log(const MomentumCompressor *mc, int level, const char *fmt, ...) {
 }
 
 int mc_ptr_is_device(const void *p, int *device) {
+    mc_ptrcache pc;
+    pc.n = 0;
+    return mc_classify(&pc, p, device);
+}
+
+typedef int (*fn_getrange)(unsigned long long *, size_t *, unsigned long long);
+static fn_getrange p_getrange = NULL;
+static int g_getrange_state = 0;
+
+static int driver_range(const void *p, uintptr_t *lo, uintptr_t *hi) {
+    if (g_getrange_state == 0) {
+        void *fp = NULL;
+        enum cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &fp, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess && fp) {
+            p_getrange = (fn_getrange)fp;
+            g_getrange_state = 1;
+        } else {
+            (void)cudaGetLastError();
+            g_getrange_state = -1;
+        }
+    }
+    if (g_getrange_state != 1) return 0;
+    unsigned long long base = 0;
+    size_t size = 0;
+    if (p_getrange(&base, &size, (unsigned long long)(uintptr_t)p) != 0 || size == 0) return 0;
+    *lo = (uintptr_t)base;
+    *hi = (uintptr_t)base + size;
+    return 1;
+}
+
+/* Classifies a pointer as device memory (1, *device set) or host memory (0).
+ * Ranges seen during one call are remembered in `pc`, so a batch whose
+ * tensors live in one allocation costs one driver query. */
+int mc_classify(mc_ptrcache *pc, const void *p, int *device) {
     if (!p) return 0;
-    struct cudaPointerAttributes a;
-    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+    uintptr_t a = (uintptr_t)p;
+    for (int i = 0; i < pc->n; i++) {
+        if (a >= pc->r[i].lo && a < pc->r[i].hi) {
+            if (device) *device = pc->r[i].device;
+            return pc->r[i].device >= 0;
+        }
+    }
+    uintptr_t lo, hi;
+    int d;
+    if (arena_lookup(a, &lo, &hi, &d)) {
+        if (pc->n < MC_PTRCACHE) {
+            pc->r[pc->n].lo = lo;
+            pc->r[pc->n].hi = hi;
+            pc->r[pc->n].device = d;
+            pc->n++;
+        }
+        if (device) *device = d;
+        return d >= 0;
+    }
+    struct cudaPointerAttributes at;
+    if (cudaPointerGetAttributes(&at, p) != cudaSuccess) {
         (void)cudaGetLastError();
         return 0;
     }
-    if (a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged) {
-        if (device) *device = a.device;
-        return 1;
+    int is_dev = at.type == cudaMemoryTypeDevice || at.type == cudaMemoryTypeManaged;
+    if (at.type != cudaMemoryTypeUnregistered && pc->n < MC_PTRCACHE && driver_range(p, &lo, &hi)) {
+        pc->r[pc->n].lo = lo;
+        pc->r[pc->n].hi = hi;
+        pc->r[pc->n].device = is_dev ? at.device : -1;
+        pc->n++;
     }
-    return 0;
+    if (is_dev && device) *device = at.device;
+    return is_dev;
 }
 
 /* reference :2844-2867 */

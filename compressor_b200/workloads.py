@@ -11,8 +11,8 @@ architecture):
 * ``gpt2-medium``: Student-t (nu = 3) scaled by 1e-4, rho = 0.8.
 * multi-client federations add a shared N(0, (1e-3)^2) component per round.
 
-Draws are float64 from numpy PCG64 with fixed seeds, cast to float32; the
-same host bytes feed the GPU codec and the CPU checker.
+Draws are float32 from numpy PCG64 with fixed seeds; the same host bytes feed
+the GPU codec and the CPU checker.
 """
 from __future__ import annotations
 
@@ -101,12 +101,12 @@ class UpdateStream:
         else:
             self.rho = 0.9 if rho is None else rho
             self.dist = dist or "normal"
-        self.sigma = np.zeros(self.layout.total, np.float64)
+        self.sigma = np.zeros(self.layout.total, np.float32)
+        self.mask = np.zeros(self.layout.total, bool)
         for o, s in zip(self.layout.offsets, self.layout.shapes):
             n = int(np.prod(s))
-            if model == "microbench":
-                self.sigma[o:o + n] = 1e-4
-            elif self.dist == "student_t3":
+            self.mask[o:o + n] = True
+            if model == "microbench" or self.dist == "student_t3":
                 self.sigma[o:o + n] = 1e-4
             else:
                 self.sigma[o:o + n] = 1e-3 / np.sqrt(fan_in(s))
@@ -114,23 +114,18 @@ class UpdateStream:
 
     def _noise(self) -> np.ndarray:
         if self.dist == "student_t3":
-            return self.rng.standard_t(3, self.layout.total) * self.sigma
-        return self.rng.standard_normal(self.layout.total) * self.sigma
+            return (self.rng.standard_t(3, self.layout.total).astype(np.float32) * self.sigma)
+        return self.rng.standard_normal(self.layout.total, dtype=np.float32) * self.sigma
 
     def next(self) -> np.ndarray:
         if self.state is None:
             self.state = self._noise()
         else:
-            self.state = self.rho * self.state + self._noise()
+            self.state = np.float32(self.rho) * self.state + self._noise()
         out = self.state
         if self.common is not None:
-            out = out + self.common.standard_normal(self.layout.total) * self.common_std
-        flat = out.astype(np.float32)
-        # padding between tensors stays zero
-        mask = np.zeros(self.layout.total, bool)
-        for o, s in zip(self.layout.offsets, self.layout.shapes):
-            mask[o:o + int(np.prod(s))] = True
-        flat[~mask] = 0.0
+            out = out + self.common.standard_normal(self.layout.total, dtype=np.float32) * np.float32(self.common_std)
+        flat = np.where(self.mask, out, np.float32(0.0)).astype(np.float32)
         return flat
 
 

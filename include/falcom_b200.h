@@ -67,6 +67,21 @@ long long falcom_total_launches(const MomentumCompressor *mc);
 /* 1 when this pointer is device memory that the library can read directly. */
 int falcom_is_device_pointer(const void *ptr);
 
+/* Per-kernel device time.  When enabled, every kernel launch of the instance
+ * is bracketed by CUDA events on the instance's stream; after each call the
+ * elapsed times are added to per-kernel totals.  falcom_kernel_times fills
+ * up to n totals (milliseconds) and launch counts, indexed by kernel id, and
+ * returns the number of kernel ids; falcom_kernel_name names an id.
+ * Enabling resets the totals. */
+int falcom_set_kernel_timing(MomentumCompressor *mc, int on);
+
+/* Releases, in one call, every CompressedLayerData held by items[0..n) and
+ * every array in outs[0..n) (either pointer may be NULL); entries are reset
+ * to NULL. */
+void falcom_free_batch(BatchItem *items, size_t n, NDArray **outs);
+int falcom_kernel_times(const MomentumCompressor *mc, double *ms, long long *counts, int n);
+const char *falcom_kernel_name(int id);
+
 #ifdef __cplusplus
 }
 #endif
