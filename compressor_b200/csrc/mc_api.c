@@ -129,8 +129,7 @@ MC_EXPORT MomentumCompressor *momentum_compressor_create(const CompressorConfig 
     memcpy(&mc->config, config, sizeof(CompressorConfig));
     mc->device = dev;
     mc->log_level = log_level_parse(getenv("FALCOM_LOG_LEVEL"), LOG_LEVEL_WARNING);
-    mc->steps = map_new();
-    mc->history = map_new();
+    mc->layers = map_new();
     mc->memory = map_new();
     mc->mem_clients = map_new();
     int codec = codec_parse(getenv("FALCOM_RESIDUAL_CODEC"));
@@ -138,11 +137,10 @@ MC_EXPORT MomentumCompressor *momentum_compressor_create(const CompressorConfig 
     const char *fm = getenv("FALCOM_FRAME_MODE");
     mc->frame_mode = (fm && !strcmp(fm, "libzstd")) ? MC_FRAME_LIBZSTD : MC_FRAME_GPU;
     if (cudaStreamCreateWithFlags(&mc->own_stream, cudaStreamNonBlocking) != cudaSuccess ||
-        !mc->steps || !mc->history || !mc->memory || !mc->mem_clients) {
+        !mc->layers || !mc->memory || !mc->mem_clients) {
         (void)cudaGetLastError();
         fprintf(stderr, "[ERROR] momentum_compressor_create: initialisation failed\n");
-        map_free(mc->steps, NULL);
-        map_free(mc->history, NULL);
+        map_free(mc->layers, NULL);
         map_free(mc->memory, NULL);
         map_free(mc->mem_clients, NULL);
         free(mc);
@@ -167,10 +165,11 @@ MC_EXPORT void momentum_compressor_destroy(MomentumCompressor *mc) {
     if (!mc) return;
     int prev = dev_enter(mc);
     cudaStreamSynchronize(mc->stream);
-    map_free(mc->history, tensor_drop);
-    map_free(mc->memory, tensor_drop);
-    map_free(mc->steps, NULL);
+    map_free(mc->layers, layer_rec_drop);
+    map_free(mc->memory, mem_rec_drop);
     map_free(mc->mem_clients, NULL);
+    keycache_free(&mc->enc_kc);
+    keycache_free(&mc->dec_kc);
     scratch_free(&mc->scratch);
     if (mc->own_stream) cudaStreamDestroy(mc->own_stream);
     for (int i = 0; i < 2 * MC_KTRACE_MAX; i++)
@@ -403,21 +402,9 @@ MC_EXPORT int momentum_compressor_decompress_batch(MomentumCompressor *mc, const
 }
 
 /* ---------------------------------------------------------------- resets */
-static void drop_prefixed(mc_map *m, const char *prefix, size_t plen, char sep, void (*drop)(void *),
-                          int *count) {
-    for (size_t i = 0; i < m->cap; i++) {
-        if (!MAP_LIVE(m, i)) continue;
-        if (strncmp(m->keys[i], prefix, plen) == 0 && m->keys[i][plen] == sep) {
-            char *k = strdup(m->keys[i]);
-            void *v = map_del(m, k);
-            free(k);
-            if (drop) drop(v);
-            (*count)++;
-        }
-    }
-}
 
-/* reference :3941-4000 */
+/* reference :3941-4000: histories and step counts of "client:*", and the
+ * client's prediction-memory table */
 MC_EXPORT void momentum_compressor_reset_client(MomentumCompressor *mc, const char *client_id) {
     if (!mc || !client_id) return;
     if (mc->log_level <= LOG_LEVEL_INFO) printf("[INFO] Resetting state for client: %s\n", client_id);
@@ -425,11 +412,28 @@ MC_EXPORT void momentum_compressor_reset_client(MomentumCompressor *mc, const ch
     cudaStreamSynchronize(mc->stream);
     size_t len = strlen(client_id);
     int count = 0;
-    drop_prefixed(mc->history, client_id, len, ':', tensor_drop, &count);
-    int mem_count = 0;
-    drop_prefixed(mc->memory, client_id, len, '\x1f', tensor_drop, &mem_count);
+    for (size_t i = 0; i < mc->layers->cap; i++) {
+        if (!MAP_LIVE(mc->layers, i)) continue;
+        const char *k = mc->layers->keys[i];
+        if (strncmp(k, client_id, len) == 0 && k[len] == ':') {
+            mc_layer_rec *r = (mc_layer_rec *)mc->layers->vals[i];
+            count += (r->hist != NULL) + (r->step > 0);
+            char *key = strdup(k);
+            layer_rec_drop(map_del(mc->layers, key));
+            free(key);
+        }
+    }
+    for (size_t i = 0; i < mc->memory->cap; i++) {
+        if (!MAP_LIVE(mc->memory, i)) continue;
+        const char *k = mc->memory->keys[i];
+        if (strncmp(k, client_id, len) == 0 && k[len] == '\x1f') {
+            char *key = strdup(k);
+            mem_rec_drop(map_del(mc->memory, key));
+            free(key);
+        }
+    }
     if (map_del(mc->mem_clients, client_id)) count++;
-    drop_prefixed(mc->steps, client_id, len, ':', NULL, &count);
+    mc->state_gen++;
     dev_leave(mc, prev);
     if (mc->log_level <= LOG_LEVEL_INFO) printf("PASS Deleted %d entries for client %s\n", count, client_id);
 }
@@ -439,14 +443,13 @@ MC_EXPORT void momentum_compressor_reset_all(MomentumCompressor *mc) {
     if (!mc) return;
     int prev = dev_enter(mc);
     cudaStreamSynchronize(mc->stream);
-    map_free(mc->history, tensor_drop);
-    map_free(mc->memory, tensor_drop);
-    map_free(mc->steps, NULL);
+    map_free(mc->layers, layer_rec_drop);
+    map_free(mc->memory, mem_rec_drop);
     map_free(mc->mem_clients, NULL);
-    mc->history = map_new();
+    mc->layers = map_new();
     mc->memory = map_new();
-    mc->steps = map_new();
     mc->mem_clients = map_new();
+    mc->state_gen++;
     dev_leave(mc, prev);
     if (mc->log_level <= LOG_LEVEL_INFO) printf("PASS All states reset\n");
 }
@@ -459,9 +462,16 @@ MC_EXPORT void momentum_compressor_print_stats(const MomentumCompressor *mc) {
     printf("| Compression Statistics                                       |\n");
     printf("+--------------------------------------------------------------+\n");
     printf("| Total compressions: %-41zu|\n", mc->stats.total_compressions);
-    printf("| History entries: %-44zu|\n", mc->history->len);
+    size_t nh = 0, ns = 0;
+    for (size_t i = 0; i < mc->layers->cap; i++) {
+        if (!MAP_LIVE(mc->layers, i)) continue;
+        const mc_layer_rec *r = (const mc_layer_rec *)mc->layers->vals[i];
+        nh += r->hist != NULL;
+        ns += r->step > 0;
+    }
+    printf("| History entries: %-44zu|\n", nh);
     printf("| Prediction memories: %-40zu|\n", mc->mem_clients->len);
-    printf("| Step counters: %-46zu|\n", mc->steps->len);
+    printf("| Step counters: %-46zu|\n", ns);
     if (mc->stats.pr_count > 0) {
         float s = 0.0f;
         for (size_t i = 0; i < mc->stats.pr_count; i++) s += mc->stats.prediction_ratios[i];
@@ -519,12 +529,13 @@ MC_EXPORT DetailedStats *momentum_compressor_get_detailed_stats(const MomentumCo
     }
     d->compression = *cs;
     free(cs);
-    /* unique client ids from the step counters ("client:layer"), first-seen order */
+    /* unique client ids from the step counters ("client:layer") */
     char(*ids)[256] = (char(*)[256])calloc(256, 256);
     size_t nu = 0;
-    for (size_t i = 0; ids && i < mc->steps->cap; i++) {
-        if (!MAP_LIVE(mc->steps, i)) continue;
-        const char *k = mc->steps->keys[i];
+    for (size_t i = 0; ids && i < mc->layers->cap; i++) {
+        if (!MAP_LIVE(mc->layers, i)) continue;
+        if (((const mc_layer_rec *)mc->layers->vals[i])->step <= 0) continue;
+        const char *k = mc->layers->keys[i];
         const char *colon = strchr(k, ':');
         if (!colon) continue;
         size_t len = (size_t)(colon - k);
@@ -550,23 +561,20 @@ MC_EXPORT DetailedStats *momentum_compressor_get_detailed_stats(const MomentumCo
         ClientStats *s = &d->clients[c];
         size_t len = strlen(ids[c]);
         memcpy(s->client_id, ids[c], len + 1);
-        for (size_t i = 0; i < mc->steps->cap; i++) {
-            if (!MAP_LIVE(mc->steps, i)) continue;
-            const char *k = mc->steps->keys[i];
-            if (strncmp(k, ids[c], len) == 0 && k[len] == ':') {
-                int st = (int)(intptr_t)mc->steps->vals[i];
-                if (st > s->step_count) s->step_count = st;
-            }
-        }
-        for (size_t i = 0; i < mc->history->cap; i++) {
-            if (!MAP_LIVE(mc->history, i)) continue;
-            const char *k = mc->history->keys[i];
-            if (strncmp(k, ids[c], len) == 0 && k[len] == ':') s->history_length++;
+        for (size_t i = 0; i < mc->layers->cap; i++) {
+            if (!MAP_LIVE(mc->layers, i)) continue;
+            const char *k = mc->layers->keys[i];
+            if (strncmp(k, ids[c], len) != 0 || k[len] != ':') continue;
+            const mc_layer_rec *r = (const mc_layer_rec *)mc->layers->vals[i];
+            if (r->step > s->step_count) s->step_count = r->step;
+            s->history_length += r->hist != NULL;
         }
         for (size_t i = 0; i < mc->memory->cap; i++) {
             if (!MAP_LIVE(mc->memory, i)) continue;
             const char *k = mc->memory->keys[i];
-            if (strncmp(k, ids[c], len) == 0 && k[len] == '\x1f') s->num_memory_layers++;
+            if (strncmp(k, ids[c], len) == 0 && k[len] == '\x1f' &&
+                ((const mc_mem_rec *)mc->memory->vals[i])->t)
+                s->num_memory_layers++;
         }
     }
     free(ids);

@@ -22,6 +22,32 @@
 #include "mc_internal.h"
 
 #define ALIGN_UP(x, a) (((x) + ((a)-1)) & ~((size_t)(a)-1))
+
+/* Host phase profile, printed to stderr when FALCOM_PROFILE is set. */
+#include <time.h>
+static double prof_now(void) {
+    struct timespec ts;
+    clock_gettime(CLOCK_MONOTONIC, &ts);
+    return (double)ts.tv_sec * 1e6 + (double)ts.tv_nsec * 1e-3;
+}
+typedef struct {
+    int on;
+    int n;
+    double t[24];
+    const char *what[24];
+} prof_t;
+static void prof_mark(prof_t *p, const char *what) {
+    if (!p->on || p->n >= 24) return;
+    p->t[p->n] = prof_now();
+    p->what[p->n] = what;
+    p->n++;
+}
+static void prof_print(prof_t *p, const char *tag) {
+    if (!p->on || p->n < 2) return;
+    fprintf(stderr, "[falcom-profile] %s total %.1f us:", tag, p->t[p->n - 1] - p->t[0]);
+    for (int i = 1; i < p->n; i++) fprintf(stderr, " %s=%.1f", p->what[i], p->t[i] - p->t[i - 1]);
+    fprintf(stderr, "\n");
+}
 #define SLOT_ALIGN 256
 #define TILE_ELEMS 8192
 
@@ -86,8 +112,8 @@ static int *strtab_slot(strtab *t, const char *key, int init) {
 
 /* ================================================================ compress */
 typedef struct {
-    char hkey[MAX_KEY_LENGTH];
-    char lkey[MAX_KEY_LENGTH];
+    mc_layer_rec *lrec;
+    mc_mem_rec *mrec;
     int group;
     int mode;
     int local_step;
@@ -113,7 +139,7 @@ typedef struct {
 } cplan;
 
 typedef struct {
-    char key[MAX_KEY_LENGTH];
+    mc_mem_rec *mrec;          /* memory record of a layer-key group */
     mc_tensor *mem_committed;
     mc_tensor *mem_new;
     int n_mom;
@@ -161,13 +187,20 @@ static int tile_kernels_for(size_t ks) {
     return (int)tk;
 }
 
+/* Returns the batch's new tensors to their records' spare slots (or the pool). */
 static void free_plan_tensors(MomentumCompressor *mc, cplan *P, size_t n, cgroup *G, size_t ng) {
     for (size_t i = 0; i < n; i++) {
-        if (P[i].hist) tensor_drop(P[i].hist);
+        if (P[i].hist) {
+            if (P[i].lrec && !P[i].lrec->spare) P[i].lrec->spare = P[i].hist;
+            else tensor_drop(P[i].hist);
+        }
         P[i].hist = NULL;
     }
     for (size_t g = 0; g < ng; g++) {
-        if (G[g].mem_new) tensor_drop(G[g].mem_new);
+        if (G[g].mem_new) {
+            if (G[g].mrec && !G[g].mrec->spare) G[g].mrec->spare = G[g].mem_new;
+            else tensor_drop(G[g].mem_new);
+        }
         G[g].mem_new = NULL;
     }
     (void)mc;
@@ -184,12 +217,22 @@ int mc_compress_grouped(MomentumCompressor *mc, BatchItem *items, size_t n, cons
         return ERROR_ALLOCATION;
     }
     size_t ng = 0;
-    const size_t thr = mc->config.param_count_threshold;
+    prof_t prof = {0};
+    prof.on = mc_env_flag("FALCOM_PROFILE");
+    prof_mark(&prof, "start");
 
     /* ---------------------------------------------------- validation / meta */
     for (size_t i = 0; i < n; i++) {
         items[i].compressed = NULL;
         items[i].error = ERROR_NONE;
+    }
+    mc_keyreq *req = (mc_keyreq *)malloc(n * sizeof(mc_keyreq));
+    int *gid = (int *)malloc(3 * n * sizeof(int));
+    if (!req || !gid) {
+        free(req);
+        free(gid);
+        rc = ERROR_ALLOCATION;
+        goto out;
     }
     for (size_t i = 0; i < n; i++) {
         const NDArray *g = items[i].gradient;
@@ -197,7 +240,7 @@ int mc_compress_grouped(MomentumCompressor *mc, BatchItem *items, size_t n, cons
             items[i].error = ERROR_INVALID_PARAM;
             mc_set_error(mc, "Batch compress: item[%zu] has NULL gradient or layer_name", i);
             rc = ERROR_INVALID_PARAM;
-            goto out;
+            break;
         }
         size_t elem = mc_dtype_size(g->dtype);
         size_t prod = 1;
@@ -208,19 +251,32 @@ int mc_compress_grouped(MomentumCompressor *mc, BatchItem *items, size_t n, cons
             mc_set_error(mc, "Batch compress: item[%zu] '%s' has an invalid array descriptor", i,
                          items[i].layer_name);
             rc = ERROR_INVALID_PARAM;
-            goto out;
+            break;
         }
         cplan *p = &P[i];
         p->g = g;
         p->dt = g->dtype;
         p->n = g->total_size;
         p->bytes = p->n * elem;
-        mc_history_key(p->hkey, client, items[i].layer_name);
-        mc_layer_key(p->lkey, sizeof(p->lkey), items[i].layer_name, g->shape, g->ndim, g->dtype);
-        p->use_lossy = mc_should_lossy(items[i].layer_name, p->n, p->dt, thr);
-        p->candidate = g->ndim == 4 && g->dtype == DTYPE_FLOAT32 && p->use_lossy;
         p->prev_item = -1;
         p->fs_bm = p->fs_sg = p->fs_data = (size_t)-1;
+        req[i].name = items[i].layer_name;
+        req[i].dt = g->dtype;
+        req[i].ndim = g->ndim;
+        req[i].shape = g->shape;
+    }
+    if (rc == ERROR_NONE) rc = keycache_resolve(mc, &mc->enc_kc, client, req, n);
+    free(req);
+    if (rc != ERROR_NONE) {
+        free(gid);
+        goto out;
+    }
+    const mc_keycache *kc = &mc->enc_kc;
+    for (size_t i = 0; i < n; i++) {
+        P[i].lrec = kc->lrec[i];
+        P[i].mrec = kc->mrec[i];
+        P[i].use_lossy = kc->lossy[i];
+        P[i].candidate = P[i].g->ndim == 4 && P[i].dt == DTYPE_FLOAT32 && P[i].use_lossy;
     }
 
     /* ------------------------------------------------ fault injection hook */
@@ -231,41 +287,33 @@ int mc_compress_grouped(MomentumCompressor *mc, BatchItem *items, size_t n, cons
                          (size_t)strtoull(fault, NULL, 10));
             for (size_t i = 0; i < n; i++) items[i].error = ERROR_COMPRESSION;
             rc = ERROR_COMPRESSION;
+            free(gid);
             goto out;
         }
     }
 
-    /* --------------------------------------------- group keys (:2627-2645) */
-    {
-        strtab hcount, gidx;
-        if (strtab_init(&hcount, n) || strtab_init(&gidx, n)) {
-            strtab_free(&hcount);
-            strtab_free(&gidx);
-            rc = ERROR_ALLOCATION;
-            goto out;
+    prof_mark(&prof, "validate");
+    /* --------------------------------------------- group keys (:2627-2645)
+     * layer-key groups are identified by the first item with that layer
+     * key, history-key groups by the first item with that history key. */
+    for (size_t i = 0; i < 3 * n; i++) gid[i] = -1;
+    for (size_t i = 0; i < n; i++) {
+        const int same = kc->same[i];
+        P[i].prev_t = P[i].lrec->hist;
+        int slot;
+        if (P[i].candidate && (P[i].prev_t != NULL || same > 1)) slot = kc->first_l[i];
+        else if (same > 1) slot = (int)n + kc->first_h[i];
+        else slot = 2 * (int)n + (int)i;
+        if (gid[slot] < 0) {
+            gid[slot] = (int)ng;
+            G[ng].mrec = slot < (int)n ? P[i].mrec : NULL;
+            G[ng].mem_committed = G[ng].mrec ? G[ng].mrec->t : NULL;
+            G[ng].last = -1;
+            ng++;
         }
-        for (size_t i = 0; i < n; i++) (*strtab_slot(&hcount, P[i].hkey, 0))++;
-        for (size_t i = 0; i < n; i++) {
-            int same = *strtab_slot(&hcount, P[i].hkey, 0);
-            P[i].prev_t = (mc_tensor *)map_get(mc->history, P[i].hkey);
-            char gk[MAX_KEY_LENGTH];
-            if (P[i].candidate && (P[i].prev_t != NULL || same > 1)) snprintf(gk, sizeof(gk), "%s", P[i].lkey);
-            else if (same > 1) snprintf(gk, sizeof(gk), "%s", P[i].hkey);
-            else snprintf(gk, sizeof(gk), "item:%zu", i);
-            snprintf(G[ng].key, sizeof(G[ng].key), "%s", gk);
-            int *slot = strtab_slot(&gidx, G[ng].key, (int)ng);
-            if (*slot == (int)ng) {
-                char mk[2 * MAX_KEY_LENGTH];
-                mc_memory_key(mk, sizeof(mk), client, gk);
-                G[ng].mem_committed = (mc_tensor *)map_get(mc->memory, mk);
-                G[ng].last = -1;
-                ng++;
-            }
-            P[i].group = *slot;
-        }
-        strtab_free(&hcount);
-        strtab_free(&gidx);
+        P[i].group = gid[slot];
     }
+    free(gid);
 
     /* ------------------------ per-group step chains (:2710-2814, in order)
      * Every item of a group has the same history key (the group key is the
@@ -274,7 +322,7 @@ int mc_compress_grouped(MomentumCompressor *mc, BatchItem *items, size_t n, cons
     for (size_t i = 0; i < n; i++) {
         cgroup *grp = &G[P[i].group];
         const int last = grp->last;
-        int step0 = last >= 0 ? P[last].local_step : (int)(intptr_t)map_get(mc->steps, P[i].hkey);
+        int step0 = last >= 0 ? P[last].local_step : P[i].lrec->step;
         P[i].local_step = step0 + 1;
         const NDArray *g_i = P[i].g;
         int has_prev = 0, prev_match = 0;
@@ -299,6 +347,7 @@ int mc_compress_grouped(MomentumCompressor *mc, BatchItem *items, size_t n, cons
         grp->last = (int)i;
     }
 
+    prof_mark(&prof, "plan");
     /* --------------------------------------------- kinds, codecs, tiling */
     const int dcodec = dcodec_of(mc->residual_codec);
     int nwaves = 1;
@@ -388,9 +437,13 @@ int mc_compress_grouped(MomentumCompressor *mc, BatchItem *items, size_t n, cons
         goto fail;
     }
 
+    prof_mark(&prof, "layout");
     /* history tensors, group memories */
     for (size_t i = 0; i < n; i++) {
-        P[i].hist = tensor_new(P[i].dt, P[i].g->ndim, P[i].g->shape, dev);
+        /* an item that is not the last of its history key in this batch
+         * never becomes the committed head: take a pooled buffer for it */
+        int last_of_key = G[P[i].group].last == (int)i;
+        P[i].hist = rec_take(last_of_key ? &P[i].lrec->spare : NULL, P[i].dt, P[i].g->ndim, P[i].g->shape, dev);
         if (!P[i].hist) {
             rc = ERROR_ALLOCATION;
             mc_set_error(mc, "Batch compress: device allocation failed for history");
@@ -401,7 +454,7 @@ int mc_compress_grouped(MomentumCompressor *mc, BatchItem *items, size_t n, cons
         cgroup *grp = &G[P[i].group];
         if (P[i].mode != MODE_MOMENTUM || grp->mem_new) continue;
         /* every momentum item of a group has the group's shape */
-        grp->mem_new = tensor_new(DTYPE_FLOAT32, 4, P[i].g->shape, dev);
+        grp->mem_new = rec_take(grp->mrec ? &grp->mrec->spare : NULL, DTYPE_FLOAT32, 4, P[i].g->shape, dev);
         if (!grp->mem_new) {
             rc = ERROR_ALLOCATION;
             mc_set_error(mc, "Batch compress: device allocation failed for prediction memory");
@@ -409,6 +462,7 @@ int mc_compress_grouped(MomentumCompressor *mc, BatchItem *items, size_t n, cons
         }
     }
 
+    prof_mark(&prof, "alloc");
     /* ----------------------------------------------- stage host inputs */
     {
         size_t stage_bytes = 0;
@@ -488,6 +542,7 @@ int mc_compress_grouped(MomentumCompressor *mc, BatchItem *items, size_t n, cons
             if (P[i].src_dev) P[i].dev_in = P[i].g->data;
     }
 
+    prof_mark(&prof, "stage");
     /* ------------------------------------------------------ scratch sizes */
     uint32_t *words = NULL;
     if (words_total) {
@@ -545,6 +600,7 @@ int mc_compress_grouped(MomentumCompressor *mc, BatchItem *items, size_t n, cons
         I->tile_base = p->tile_base;
         I->elem_bytes = (int32_t)mc_dtype_size(p->dt);
         I->step = p->local_step;
+        I->vec = (((uintptr_t)I->cur | (uintptr_t)I->hist_out | (uintptr_t)I->data_out) & 15) == 0;
         I->lr = mc->config.momentum_lr;
         I->thr = mc->config.consistency_threshold;
         for (int t = 0; t < p->ntiles; t++) h_tile_item[p->tile_base + t] = (int32_t)i;
@@ -558,6 +614,7 @@ int mc_compress_grouped(MomentumCompressor *mc, BatchItem *items, size_t n, cons
                                                            : NULL)
                                      : (const float *)grp->mem_new->dev;
             I->mem_out = (float *)grp->mem_new->dev;
+            I->vec = I->vec && (((uintptr_t)I->prev | (uintptr_t)I->mem_in | (uintptr_t)I->mem_out) & 15) == 0;
             I->K = (int64_t)p->K;
             I->ks = (int32_t)p->ks;
             I->ksdiv = mc_fastdiv_make((uint32_t)p->ks);
@@ -626,6 +683,7 @@ int mc_compress_grouped(MomentumCompressor *mc, BatchItem *items, size_t n, cons
         goto fail;
     }
 
+    prof_mark(&prof, "tables");
     /* ---------------------------------------------------------- launch */
     mc->last_launches = 0;
     mc_ktrace *tr = mc_trace_begin(mc);
@@ -668,7 +726,9 @@ int mc_compress_grouped(MomentumCompressor *mc, BatchItem *items, size_t n, cons
     if (fj) cudaMemcpyAsync(hfs, fsize, (size_t)fj * 8, cudaMemcpyDeviceToHost, st);
     if (host_arena)
         cudaMemcpyAsync(host_arena->ptr, payload_dev, arena_bytes, cudaMemcpyDeviceToHost, st);
+    prof_mark(&prof, "launch");
     cudaError_t e = cudaStreamSynchronize(st);
+    prof_mark(&prof, "sync");
     mc_trace_end(mc);
     if (e != cudaSuccess) {
         rc = ERROR_COMPRESSION;
@@ -794,30 +854,27 @@ int mc_compress_grouped(MomentumCompressor *mc, BatchItem *items, size_t n, cons
         /* ------------------------------------------------------- commit */
         for (size_t g = 0; g < ng; g++) {
             if (!G[g].mem_new) continue;
-            char mk[2 * MAX_KEY_LENGTH];
-            mc_memory_key(mk, sizeof(mk), client, G[g].key);
-            mc_tensor *old = (mc_tensor *)map_get(mc->memory, mk);
-            map_put(mc->memory, mk, G[g].mem_new);
+            rec_commit(&G[g].mrec->t, &G[g].mrec->spare, G[g].mem_new);
             G[g].mem_new = NULL;
-            if (old) tensor_drop(old);
             map_put(mc->mem_clients, client, (void *)1);
         }
         for (size_t i = 0; i < n; i++) {
-            intptr_t s = (intptr_t)map_get(mc->steps, P[i].hkey);
-            map_put(mc->steps, P[i].hkey, (void *)(s + 1));
-            mc_tensor *old = (mc_tensor *)map_get(mc->history, P[i].hkey);
-            map_put(mc->history, P[i].hkey, P[i].hist);
+            mc_layer_rec *r = P[i].lrec;
+            r->step++;
+            /* the last item of a history key becomes the head (ref :2902) */
+            rec_commit(&r->hist, &r->spare, P[i].hist);
             P[i].hist = NULL;
-            if (old) tensor_drop(old);
             mc_record_stats(mc, outs[i]);
             items[i].compressed = outs[i];
             items[i].error = ERROR_NONE;
-            registry_add(outs[i], arena);
         }
+        registry_add_many((const void **)outs, n, arena);
         arena_retain(arena, (int)n - 1);
         free(outs);
         if (n == 0) arena_release(arena);
     }
+    prof_mark(&prof, "commit");
+    prof_print(&prof, "compress");
     rc = ERROR_NONE;
     goto out;
 
@@ -842,8 +899,8 @@ typedef struct {
     int dcodec;
     DataType dt;
     size_t ndim, shape[MAX_NDIM], n, bytes, K, ks;
-    char hkey[MAX_KEY_LENGTH];
-    char mkey[2 * MAX_KEY_LENGTH];
+    mc_layer_rec *lrec;       /* "client:layer" record (history) */
+    mc_mem_rec *mrec;         /* decoder prediction memory record */
     mc_tensor *prev;          /* decoder history head (MOMENTUM) */
     mc_tensor *mem_in;
     mc_tensor *mem_new;
@@ -863,6 +920,9 @@ typedef struct {
     int j_data, j_bm, j_sg;   /* unframe job indices, -1 when none */
     size_t out_off;
     int tile_base, ntiles, tile_param;
+    int bm_mode, sg_mode;     /* MC_BM_* */
+    int data_mode;            /* lossless frame: MC_BM_* */
+    int foreign;              /* a frame lives in device memory the library does not own */
     const char *why;
 } dplan;
 
@@ -878,7 +938,8 @@ static int on_device(mc_ptrcache *pc, const void *p, int dev) {
 }
 
 /* Plans one item (reference decompress_layer :3476-3598 validation order). */
-static void dplan_item(MomentumCompressor *mc, dplan *d, const BatchItem *it, const char *client) {
+static void dplan_item(MomentumCompressor *mc, dplan *d, const BatchItem *it, const mc_keycache *kc,
+                       size_t idx) {
     const CompressedLayerData *c = it->compressed;
     d->ok = 0;
     d->j_data = d->j_bm = d->j_sg = -1;
@@ -895,7 +956,8 @@ static void dplan_item(MomentumCompressor *mc, dplan *d, const BatchItem *it, co
     }
     if (d->n == 0) { d->why = "empty shape"; return; }
     d->bytes = d->n * mc_dtype_size(d->dt);
-    mc_history_key(d->hkey, client, it->layer_name);
+    d->lrec = kc->lrec[idx];
+    d->mrec = kc->mrec[idx];
     d->data = c->data;
     d->data_size = c->data_size;
     const char *codec = c->codec;
@@ -944,16 +1006,13 @@ static void dplan_item(MomentumCompressor *mc, dplan *d, const BatchItem *it, co
         d->bm_size = c->bitmap ? c->bitmap_size : 0;
         d->sg = c->dominant_signs;
         d->sg_size = c->dominant_signs ? c->dominant_signs_size : 0;
-        mc_tensor *h = (mc_tensor *)map_get(mc->history, d->hkey);
+        mc_tensor *h = d->lrec->hist;
         int hist_ok = h && h->dtype == DTYPE_FLOAT32 && h->ndim == 4 && h->n == d->n;
         for (size_t i = 0; hist_ok && i < 4; i++) hist_ok = h->shape[i] == d->shape[i];
         if (d->bm_size > 0 && hist_ok) {
             d->kind = MC_D_MOMENTUM;
             d->prev = h;
-            char lk[MAX_KEY_LENGTH];
-            mc_layer_key(lk, sizeof(lk), it->layer_name, d->shape, d->ndim, d->dt);
-            mc_memory_key(d->mkey, sizeof(d->mkey), client, lk);
-            d->mem_in = (mc_tensor *)map_get(mc->memory, d->mkey);
+            d->mem_in = d->mrec->t;
         }
     } else if (d->kind == MC_D_QUANT) {
         /* direct tensor through the quantiser */
@@ -961,21 +1020,45 @@ static void dplan_item(MomentumCompressor *mc, dplan *d, const BatchItem *it, co
     d->ok = 1;
 }
 
+#define DEC_RETRY_EXPAND 1
 static int dec_segment(MomentumCompressor *mc, const BatchItem *items, size_t n, const char *client,
-                       NDArray **out, int out_loc, size_t *n_ok) {
+                       NDArray **out, int out_loc, size_t *n_ok, int force_expand) {
     cudaStream_t st = mc->stream;
     const int dev = mc->device;
     dplan *D = (dplan *)calloc(n, sizeof(dplan));
     if (!D) return ERROR_ALLOCATION;
     int rc = ERROR_NONE;
+    prof_t prof = {0};
+    prof.on = mc_env_flag("FALCOM_PROFILE");
+    prof_mark(&prof, "start");
+    /* keys and state records of every item (cached across rounds) */
+    {
+        mc_keyreq *req = (mc_keyreq *)malloc(n * sizeof(mc_keyreq));
+        static const size_t one = 1;
+        if (!req) { free(D); return ERROR_ALLOCATION; }
+        for (size_t i = 0; i < n; i++) {
+            const CompressedLayerData *c = items[i].compressed;
+            DataType dt = DTYPE_FLOAT32;
+            if (c) mc_dtype_parse(c->original_dtype, &dt);
+            int ok = c && items[i].layer_name && c->ndim >= MIN_NDIM && c->ndim <= MAX_NDIM;
+            req[i].name = items[i].layer_name ? items[i].layer_name : "";
+            req[i].dt = dt;
+            req[i].ndim = ok ? c->ndim : 1;
+            req[i].shape = ok ? c->shape : &one;
+        }
+        rc = keycache_resolve(mc, &mc->dec_kc, client, req, n);
+        free(req);
+        if (rc != ERROR_NONE) { free(D); return rc; }
+    }
     for (size_t i = 0; i < n; i++) {
         out[i] = NULL;
-        dplan_item(mc, &D[i], &items[i], client);
+        dplan_item(mc, &D[i], &items[i], &mc->dec_kc, i);
         if (!D[i].ok)
             fprintf(stderr, "[ERROR] Batch decompress: item '%s': %s\n",
                     items[i].layer_name ? items[i].layer_name : "(null)", D[i].why);
     }
 
+    prof_mark(&prof, "plan");
     /* ---------------------------------------------- payload residency */
     /* host payload ranges are copied to the device (adjacent ranges merged);
      * frames with compressed blocks are decoded on the host first */
@@ -998,6 +1081,7 @@ static int dec_segment(MomentumCompressor *mc, const BatchItem *items, size_t n,
             if (!srcs[k] || lens[k] == 0) continue;
             if (on_device(&pc, srcs[k], dev)) {
                 *dsts[k] = srcs[k];
+                if (!mc_is_arena_ptr(srcs[k])) d->foreign = 1;
                 continue;
             }
             const uint8_t *src = srcs[k];
@@ -1083,6 +1167,7 @@ static int dec_segment(MomentumCompressor *mc, const BatchItem *items, size_t n,
         }
     }
 
+    prof_mark(&prof, "stage");
     /* ------------------------------------------ tiles, contents, outputs */
     int ntiles = 0, nmom_tiles = 0, njobs = 0;
     size_t content_bytes = 0, out_bytes = 0;
@@ -1094,21 +1179,45 @@ static int dec_segment(MomentumCompressor *mc, const BatchItem *items, size_t n,
             d->ntiles = (int)((d->K + (size_t)d->tile_param - 1) / (size_t)d->tile_param);
             nmom_tiles += d->ntiles;
             size_t wb = ALIGN_UP(((d->K + 31) / 32 + 1) * 4 + 4096, 256);
-            d->c_bm_off = content_bytes;
-            content_bytes += wb;
-            d->j_bm = njobs++;
-            if (d->d_sg) {
-                d->c_sg_off = content_bytes;
+            /* Frames of one Raw / RLE block are read in place (the kernel
+             * checks the header it relies on; a mismatch re-runs the segment
+             * with expansion).  Everything else is expanded first. */
+            const size_t c = (d->K + 7) / 8;
+            d->bm_mode = MC_BM_WORDS;
+            /* in place only inside library-owned or staged memory: a word read
+             * may touch up to 3 bytes past the frame, inside the slot padding */
+            const int inplace = !force_expand && !d->foreign;
+            if (inplace && c >= 2 && d->bm_size == 12 + c && ((uintptr_t)d->d_bm & 3) == 0)
+                d->bm_mode = MC_BM_RAW1;
+            else if (inplace && c >= 2 && d->bm_size == 13)
+                d->bm_mode = MC_BM_RLE1;
+            if (d->bm_mode == MC_BM_WORDS) {
+                d->c_bm_off = content_bytes;
                 content_bytes += wb;
-                d->j_sg = njobs++;
+                d->j_bm = njobs++;
+            }
+            d->sg_mode = MC_BM_WORDS;
+            if (d->d_sg) {
+                if (inplace && d->sg_size > 13) d->sg_mode = MC_BM_RAW1;
+                if (d->sg_mode == MC_BM_WORDS) {
+                    d->c_sg_off = content_bytes;
+                    content_bytes += wb;
+                    d->j_sg = njobs++;
+                }
             }
         } else if (d->kind == MC_D_COPY) {
             d->tile_param = TILE_ELEMS * 4;
             d->ntiles = (int)((d->bytes + (size_t)d->tile_param - 1) / (size_t)d->tile_param);
+            d->data_mode = MC_BM_WORDS;
             if (d->data_frame) {
-                d->c_data_off = content_bytes;
-                content_bytes += ALIGN_UP(d->bytes + 16, 256);
-                d->j_data = njobs++;
+                const int inplace = !force_expand && !d->foreign;
+                if (inplace && d->data_size == 12 + d->bytes) d->data_mode = MC_BM_RAW1;
+                else if (inplace && d->bytes >= 2 && d->data_size == 13) d->data_mode = MC_BM_RLE1;
+                if (d->data_mode == MC_BM_WORDS) {
+                    d->c_data_off = content_bytes;
+                    content_bytes += ALIGN_UP(d->bytes + 16, 256);
+                    d->j_data = njobs++;
+                }
             }
         } else {
             d->tile_param = TILE_ELEMS;
@@ -1133,14 +1242,15 @@ static int dec_segment(MomentumCompressor *mc, const BatchItem *items, size_t n,
     for (size_t i = 0; i < n; i++) {
         dplan *d = &D[i];
         if (!d->ok) continue;
-        d->hist = tensor_new(d->dt, d->ndim, d->shape, dev);
+        d->hist = rec_take(&d->lrec->spare, d->dt, d->ndim, d->shape, dev);
         if (!d->hist) { rc = ERROR_ALLOCATION; goto fail_arena; }
         if (d->kind == MC_D_MOMENTUM) {
-            d->mem_new = tensor_new(DTYPE_FLOAT32, 4, d->shape, dev);
+            d->mem_new = rec_take(&d->mrec->spare, DTYPE_FLOAT32, 4, d->shape, dev);
             if (!d->mem_new) { rc = ERROR_ALLOCATION; goto fail_arena; }
         }
     }
 
+    prof_mark(&prof, "alloc");
     /* ------------------------------------------------------- tables */
     size_t t_items = ALIGN_UP(n * sizeof(mc_dec_item), 256);
     size_t t_tiles = ALIGN_UP((size_t)(ntiles + 1) * 4, 256);
@@ -1185,6 +1295,11 @@ static int dec_segment(MomentumCompressor *mc, const BatchItem *items, size_t n,
         } else {
             I->data = d->d_data;
         }
+        if (d->data_frame && d->data_mode != MC_BM_WORDS) {
+            I->data_mode = d->data_mode;
+            I->data_frame = d->d_data;
+            I->data = d->d_data + 12;
+        }
         if (d->j_data >= 0) {
             mc_unframe_job *J = &h_jobs[d->j_data];
             J->frame = d->d_data;
@@ -1207,16 +1322,24 @@ static int dec_segment(MomentumCompressor *mc, const BatchItem *items, size_t n,
             I->pm = c->prev_mean;
             I->ps = c->prev_std;
             I->lr = mc->config.momentum_lr;
-            mc_unframe_job *J = &h_jobs[d->j_bm];
-            J->frame = d->d_bm;
-            J->frame_size = (int64_t)d->bm_size;
-            J->dst = content + d->c_bm_off;
-            J->cap = (int64_t)(((d->K + 31) / 32 + 1) * 4 + 4096);
-            J->content_out = d_lens + d->j_bm;
-            I->bm_words = (const uint32_t *)(content + d->c_bm_off);
-            I->bm_len_ptr = d_lens + d->j_bm;
+            I->bm_mode = d->bm_mode;
+            I->sg_mode = d->sg_mode;
+            I->bm_bits = (int64_t)d->K;
+            if (d->bm_mode == MC_BM_WORDS) {
+                mc_unframe_job *J = &h_jobs[d->j_bm];
+                J->frame = d->d_bm;
+                J->frame_size = (int64_t)d->bm_size;
+                J->dst = content + d->c_bm_off;
+                J->cap = (int64_t)(((d->K + 31) / 32 + 1) * 4 + 4096);
+                J->content_out = d_lens + d->j_bm;
+                I->bm_words = (const uint32_t *)(content + d->c_bm_off);
+                I->bm_len_ptr = d_lens + d->j_bm;
+            } else {
+                I->bm_frame = d->d_bm;
+                I->bm_words = (const uint32_t *)(d->d_bm + 12);
+            }
             if (d->j_sg >= 0) {
-                J = &h_jobs[d->j_sg];
+                mc_unframe_job *J = &h_jobs[d->j_sg];
                 J->frame = d->d_sg;
                 J->frame_size = (int64_t)d->sg_size;
                 J->dst = content + d->c_sg_off;
@@ -1224,7 +1347,18 @@ static int dec_segment(MomentumCompressor *mc, const BatchItem *items, size_t n,
                 J->content_out = d_lens + d->j_sg;
                 I->sg_bytes = content + d->c_sg_off;
                 I->sg_len_ptr = d_lens + d->j_sg;
+            } else if (d->sg_mode == MC_BM_RAW1) {
+                I->sg_frame = d->d_sg;
+                I->sg_bytes = d->d_sg + 12;
+                I->sg_len = (int64_t)d->sg_size - 12;
             }
+        }
+        {
+            uintptr_t need = (d->kind == MC_D_COPY || I->codec == MC_DC_RAW || I->codec == MC_DC_Q8_RAW ||
+                              I->codec == MC_DC_INT4_RAW) ? 15 : (I->codec == MC_DC_Q8 ? 3 : 1);
+            uintptr_t al = (uintptr_t)I->hist_out | (uintptr_t)I->out | (uintptr_t)I->mem_in |
+                           (uintptr_t)I->mem_out | (uintptr_t)I->prev;
+            I->vec = ((al & 15) == 0) && (((uintptr_t)I->data & need) == 0);
         }
         for (int t = 0; t < d->ntiles; t++) {
             h_ti[d->tile_base + t] = (int32_t)i;
@@ -1235,6 +1369,7 @@ static int dec_segment(MomentumCompressor *mc, const BatchItem *items, size_t n,
     if (cudaMemcpyAsync(dt, ht, tab, cudaMemcpyHostToDevice, st) != cudaSuccess ||
         cudaMemsetAsync(d_res, 0, t_res, st) != cudaSuccess) { rc = ERROR_DECOMPRESSION; goto fail_arena; }
 
+    prof_mark(&prof, "tables");
     /* ------------------------------------------------------- launch */
     mc->last_launches = 0;
     mc_ktrace *tr = mc_trace_begin(mc);
@@ -1271,12 +1406,27 @@ static int dec_segment(MomentumCompressor *mc, const BatchItem *items, size_t n,
     cudaMemcpyAsync(h_res, d_res, n * sizeof(mc_dec_result), cudaMemcpyDeviceToHost, st);
     if (out_loc != FALCOM_LOC_DEVICE && out_bytes)
         cudaMemcpyAsync(oarena->ptr, dout, out_bytes, cudaMemcpyDeviceToHost, st);
+    prof_mark(&prof, "launch");
     cudaError_t e = cudaStreamSynchronize(st);
+    prof_mark(&prof, "sync");
     mc_trace_end(mc);
     if (e != cudaSuccess) {
         mc_set_error(mc, "Batch decompress: device execution failed: %s", cudaGetErrorString(e));
         rc = ERROR_DECOMPRESSION;
         goto fail_arena;
+    }
+
+    /* an in-place frame that was not what its size suggested: redo the
+     * segment with every frame expanded (nothing is committed yet) */
+    for (size_t i = 0; i < n; i++) {
+        if (D[i].ok && h_res[i].err) {
+            if (prof.on)
+                fprintf(stderr, "[falcom-profile] decompress: in-place frame check failed for item %zu "
+                                "(kind %d bm %d sg %d data %d, sizes %zu/%zu/%zu); expanding\n", i, D[i].kind,
+                        D[i].bm_mode, D[i].sg_mode, D[i].data_mode, D[i].data_size, D[i].bm_size, D[i].sg_size);
+            rc = DEC_RETRY_EXPAND;
+            goto fail_arena;
+        }
     }
 
     /* ------------------------------------------------------- commit */
@@ -1300,7 +1450,6 @@ static int dec_segment(MomentumCompressor *mc, const BatchItem *items, size_t n,
         a->total_size = d->n;
         a->dtype = d->dt;
         out[i] = a;
-        registry_add(a, oarena);
         handed++;
         (*n_ok)++;
         int commit_hist = 1;
@@ -1309,31 +1458,62 @@ static int dec_segment(MomentumCompressor *mc, const BatchItem *items, size_t n,
              * neither memory nor history touched */
             if (h_res[i].P == 0) commit_hist = 0;
             else {
-                mc_tensor *old = (mc_tensor *)map_get(mc->memory, d->mkey);
-                map_put(mc->memory, d->mkey, d->mem_new);
+                rec_commit(&d->mrec->t, &d->mrec->spare, d->mem_new);
                 d->mem_new = NULL;
-                if (old) tensor_drop(old);
                 map_put(mc->mem_clients, client, (void *)1);
             }
         } else if (d->kind == MC_D_RESIDUAL) {
             commit_hist = 0;
         }
         if (commit_hist) {
-            mc_tensor *old = (mc_tensor *)map_get(mc->history, d->hkey);
-            map_put(mc->history, d->hkey, d->hist);
+            rec_commit(&d->lrec->hist, &d->lrec->spare, d->hist);
             d->hist = NULL;
-            if (old) tensor_drop(old);
         }
+    }
+    {
+        const void **objs = (const void **)malloc(n * sizeof(void *));
+        size_t no = 0;
+        for (size_t i = 0; objs && i < n; i++)
+            if (out[i]) objs[no++] = out[i];
+        if (objs) registry_add_many(objs, no, oarena);
+        else
+            for (size_t i = 0; i < n; i++)
+                if (out[i]) registry_add(out[i], oarena);
+        free(objs);
     }
     if (handed > 0) arena_retain(oarena, handed - 1);
     else arena_release(oarena);
     oarena = NULL;
+    prof_mark(&prof, "commit");
+    prof_print(&prof, "decompress");
+    if (prof.on) {
+        int nb[3] = {0, 0, 0}, ns[3] = {0, 0, 0}, nd[3] = {0, 0, 0};
+        for (size_t i = 0; i < n; i++) {
+            if (!D[i].ok) continue;
+            if (D[i].kind == MC_D_MOMENTUM) {
+                nb[D[i].bm_mode]++;
+                if (D[i].d_sg) ns[D[i].sg_mode]++;
+            }
+            if (D[i].data_frame) nd[D[i].data_mode]++;
+        }
+        int nf = 0;
+        for (size_t i = 0; i < n; i++) nf += D[i].foreign;
+        fprintf(stderr, "[falcom-profile] decompress frames: force_expand=%d foreign=%d jobs=%d bitmap "
+                        "words/raw/rle=%d/%d/%d signs=%d/%d/%d data=%d/%d/%d\n", force_expand, nf, njobs,
+                nb[0], nb[1], nb[2], ns[0], ns[1], ns[2], nd[0], nd[1], nd[2]);
+    }
 
 fail_arena:
     if (oarena) arena_release(oarena);
     for (size_t i = 0; i < n; i++) {
-        if (D[i].hist) tensor_drop(D[i].hist);
-        if (D[i].mem_new) tensor_drop(D[i].mem_new);
+        if (D[i].hist) {
+            if (D[i].lrec && !D[i].lrec->spare) D[i].lrec->spare = D[i].hist;
+            else tensor_drop(D[i].hist);
+        }
+        if (D[i].mem_new) {
+            if (D[i].mrec && !D[i].mrec->spare) D[i].mrec->spare = D[i].mem_new;
+            else tensor_drop(D[i].mem_new);
+        }
     }
 done:
     for (size_t i = 0; i < nhd; i++) free(host_dec[i]);
@@ -1363,7 +1543,8 @@ int mc_decompress_items(MomentumCompressor *mc, const BatchItem *items, size_t n
             *s = (int)a;
         }
         if (b == a) b = a + 1;
-        int r = dec_segment(mc, items + a, b - a, client, out + a, out_loc, &ok);
+        int r = dec_segment(mc, items + a, b - a, client, out + a, out_loc, &ok, 0);
+        if (r == DEC_RETRY_EXPAND) r = dec_segment(mc, items + a, b - a, client, out + a, out_loc, &ok, 1);
         if (r != ERROR_NONE) {
             rc = r;
             for (size_t j = a; j < b; j++) {

@@ -56,6 +56,7 @@ typedef struct {
     int32_t tile_base;      /* index of the first tile in the batch tile list */
     int32_t elem_bytes;     /* bytes per element of the input */
     int32_t step;
+    int32_t vec;            /* 1: every fp32 pointer of the item is 16-byte aligned */
     mc_fastdiv ksdiv;
     float lr;
     float thr;
@@ -114,10 +115,19 @@ enum {
     MC_D_COPY = 3           /* direct, bytes copied (raw floats or lossless content) */
 };
 
+/* How the decoder reads a bitmap / sign payload. */
+enum {
+    MC_BM_WORDS = 0,        /* contiguous content (expanded, or staged content) */
+    MC_BM_RAW1 = 1,         /* zstd frame, one Raw block, content read in place at +12 */
+    MC_BM_RLE1 = 2          /* zstd frame, one RLE block, the repeated byte at +12 */
+};
+
 typedef struct {
     const uint8_t *data;        /* codes (after the scale header), raw floats or content bytes */
-    const uint32_t *bm_words;   /* MOMENTUM: bitmap content (zero padded words) */
-    const uint8_t *sg_bytes;    /* MOMENTUM: sign content, NULL when absent */
+    const uint32_t *bm_words;   /* MOMENTUM: bitmap content words (WORDS / RAW1) */
+    const uint8_t *bm_frame;    /* MOMENTUM: the bitmap frame (RAW1 / RLE1) */
+    const uint8_t *sg_bytes;    /* MOMENTUM: sign content (WORDS / RAW1), NULL when absent */
+    const uint8_t *sg_frame;    /* MOMENTUM: the sign frame (RAW1 / RLE1) */
     int64_t sg_len;             /* sign content bytes (when sg_len_ptr is NULL) */
     const int64_t *sg_len_ptr;  /* device-expanded sign content length, -1 = failed */
     const int64_t *bm_len_ptr;  /* device-expanded bitmap content length, -1 = failed */
@@ -128,7 +138,7 @@ typedef struct {
     void *out;                  /* optional second copy (device output), NULL */
     int64_t n;
     int64_t K;
-    int64_t bm_bits;            /* min(bitmap bytes*8, K) */
+    int64_t bm_bits;            /* min(bitmap content bytes*8, K) */
     int32_t ks;
     int32_t kind;
     int32_t codec;              /* MC_DC_* for the residual / QUANT data */
@@ -136,8 +146,13 @@ typedef struct {
     int32_t ntiles;
     int32_t tile_base;
     int32_t elem_bytes;
-    int32_t pad;
-    const float *scale_ptr;     /* device pointer to the f32 scale header */
+    int32_t vec;                /* 1: float4 / packed-code access is aligned */
+    int32_t bm_mode;            /* MC_BM_* */
+    int32_t sg_mode;            /* MC_BM_* */
+    int32_t data_mode;          /* COPY from a frame: MC_BM_WORDS (content), RAW1 or RLE1 */
+    int32_t pad2;
+    const uint8_t *data_frame;  /* COPY: the lossless zstd frame read in place */
+    const float *scale_ptr;     /* device pointer to the f32 scale header (any alignment) */
     mc_fastdiv ksdiv;
     float cm, cs, pm, ps, lr;
 } mc_dec_item;

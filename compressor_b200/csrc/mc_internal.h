@@ -53,6 +53,7 @@ void arena_retain(mc_arena *a, int n);
 
 /* Ownership registry of returned objects. */
 void registry_add(const void *obj, mc_arena *a);
+void registry_add_many(const void **objs, size_t n, mc_arena *a);
 mc_arena *registry_take(const void *obj, int *found);
 
 /* Device buffers held by state entries (pooled per device by byte size). */
@@ -66,11 +67,51 @@ typedef struct {
     size_t shape[MAX_NDIM];
     size_t n;          /* elements */
     size_t bytes;
+    int device;
     void *dev;         /* device copy */
 } mc_tensor;
 
 mc_tensor *tensor_new(DataType dt, size_t ndim, const size_t *shape, int device);
-void tensor_drop(void *t);   /* for map_free */
+void tensor_drop(void *t);   /* for map_free; NULL is ignored */
+
+/* Step count and latest history tensor of one "client:layer". */
+typedef struct {
+    int step;
+    mc_tensor *hist;     /* committed history head, NULL when none */
+    mc_tensor *spare;    /* previous head, reused by the next round */
+} mc_layer_rec;
+
+/* One prediction memory ("client" + "layer|dtype|conv_(shape)"). */
+typedef struct {
+    mc_tensor *t;        /* committed memory, NULL when none */
+    mc_tensor *spare;
+} mc_mem_rec;
+
+/* Keys and records of every item of the last batch an engine saw. */
+typedef struct {
+    int valid;
+    unsigned gen;
+    char client[256];
+    size_t n;
+    char **names;
+    DataType *dt;
+    size_t *ndim;
+    size_t *shape;                  /* n x MAX_NDIM */
+    char (*hkey)[MAX_KEY_LENGTH];   /* "client:layer" */
+    char (*lkey)[MAX_KEY_LENGTH];   /* "layer|dtype|conv_(...)" */
+    mc_layer_rec **lrec;
+    mc_mem_rec **mrec;              /* memory record of (client, lkey) */
+    int *same;                      /* items sharing the history key */
+    int *first_l, *first_h;         /* first item with the same layer / history key */
+    int *lossy;                     /* reference :399-415 routing */
+} mc_keycache;
+
+typedef struct {
+    const char *name;
+    DataType dt;
+    size_t ndim;
+    const size_t *shape;
+} mc_keyreq;
 
 struct MomentumCompressor {
     CompressorConfig config;
@@ -84,10 +125,11 @@ struct MomentumCompressor {
     int payload_loc;
     int output_loc;
 
-    mc_map *steps;           /* "client:layer" -> (intptr_t) step */
-    mc_map *history;         /* "client:layer" -> mc_tensor* (latest gradient) */
-    mc_map *memory;          /* "client\x1f<layer|dtype|conv_(...)>" -> mc_tensor* */
+    mc_map *layers;          /* "client:layer" -> mc_layer_rec* */
+    mc_map *memory;          /* "client\x1f<layer|dtype|conv_(...)>" -> mc_mem_rec* */
     mc_map *mem_clients;     /* clients that own a prediction-memory table */
+    unsigned state_gen;      /* bumped when records are deleted (resets) */
+    mc_keycache enc_kc, dec_kc;
 
     struct {
         size_t total_compressions;
@@ -141,6 +183,7 @@ typedef struct {
     int n;
 } mc_ptrcache;
 int mc_classify(mc_ptrcache *pc, const void *p, int *device);
+int mc_is_arena_ptr(const void *p);   /* inside memory the library allocated for outputs */
 void mc_record_stats(MomentumCompressor *mc, const CompressedLayerData *c);
 
 /* zstd frames (mc_wire.c) */
@@ -151,6 +194,17 @@ int zf_decode_host(const uint8_t *frame, size_t n, uint8_t *dst, size_t cap, siz
 int zf_is_simple(const uint8_t *frame, size_t n);   /* raw/RLE blocks only */
 int zf_libzstd_available(void);
 size_t zf_libzstd_compress(uint8_t *dst, size_t cap, const uint8_t *src, size_t n, int level);
+
+/* state records and key cache (mc_state.c) */
+mc_layer_rec *state_layer(MomentumCompressor *mc, const char *hkey, int create);
+mc_mem_rec *state_mem(MomentumCompressor *mc, const char *mkey, int create);
+void layer_rec_drop(void *r);
+void mem_rec_drop(void *r);
+mc_tensor *rec_take(mc_tensor **spare, DataType dt, size_t ndim, const size_t *shape, int device);
+void rec_commit(mc_tensor **slot, mc_tensor **spare, mc_tensor *t);
+void keycache_free(mc_keycache *kc);
+int keycache_resolve(MomentumCompressor *mc, mc_keycache *kc, const char *client, const mc_keyreq *req,
+                     size_t n);
 
 /* batch engines (mc_batch.c) */
 int mc_compress_grouped(MomentumCompressor *mc, BatchItem *items, size_t n, const char *client,

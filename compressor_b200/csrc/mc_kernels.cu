@@ -174,24 +174,91 @@ __device__ __forceinline__ TileRange mom_range(const mc_enc_item &I, int t) {
     return r;
 }
 
-// Residual of one element of a momentum layer, recomputed from the updated
-// memory (pass 4).  Same operation order as pass 3.
+// Residual of one element of a momentum layer from its updated memory, in the
+// reference's operation order (ref :2122-2158).
 struct MomParams {
     float cm, cs, gmin, gmax;
     bool use_cs;
 };
+__device__ __forceinline__ float mom_pred_abs(float nm, const MomParams &p) {
+    return fabsf(p.use_cs ? __fmaf_rn(nm, p.cs, p.cm) : __fadd_rn(nm, p.cm));
+}
 __device__ __forceinline__ float mom_residual(float c, float nm, bool pos, const MomParams &p) {
-    float ap = p.use_cs ? __fmaf_rn(nm, p.cs, p.cm) : __fadd_rn(nm, p.cm);
-    ap = fabsf(ap);
-    float pred = pos ? ap : -ap;
-    float r = __fsub_rn(c, pred);
+    const float ap = mom_pred_abs(nm, p);
+    const float pred = pos ? ap : -ap;
+    const float r = __fsub_rn(c, pred);
     return x86min(x86max(r, p.gmin), p.gmax);
+}
+
+// ---- quads: 4 consecutive elements, vector access when aligned and whole
+__device__ __forceinline__ void ld4(const float *p, int64_t g, int64_t e1, bool vec, float (&o)[4]) {
+    if (vec && g + 4 <= e1) {
+        const float4 t = *(const float4 *)(p + g);
+        o[0] = t.x; o[1] = t.y; o[2] = t.z; o[3] = t.w;
+    } else {
+#pragma unroll
+        for (int j = 0; j < 4; j++) o[j] = (g + j < e1) ? p[g + j] : 0.0f;
+    }
+}
+__device__ __forceinline__ void st4(float *p, int64_t g, int64_t e1, bool vec, const float (&v)[4]) {
+    if (vec && g + 4 <= e1) {
+        *(float4 *)(p + g) = make_float4(v[0], v[1], v[2], v[3]);
+    } else {
+#pragma unroll
+        for (int j = 0; j < 4; j++)
+            if (g + j < e1) p[g + j] = v[j];
+    }
+}
+
+// Kernel index of element g (first of a quad) and the predicted / dominant
+// bits of the quad's 4 elements from bitmap and sign words.
+struct QuadBits {
+    uint32_t f, pos;   // bit j: element j predicted / dominant sign positive
+};
+__device__ __forceinline__ QuadBits quad_bits(const uint32_t *bm, const uint32_t *dom, uint32_t wbase,
+                                              uint32_t k0, int64_t g, int64_t e0, int64_t e1, int ks,
+                                              mc_fastdiv ksdiv) {
+    const uint32_t off = (uint32_t)(g - e0);
+    const uint32_t q = fdiv32(off, ksdiv);
+    uint32_t r = off - q * (uint32_t)ks;
+    uint32_t k = k0 + q;
+    QuadBits b = {0u, 0u};
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        if (g + j < e1) {
+            const uint32_t sh = k & 31, w = (k >> 5) - wbase;
+            b.f |= ((bm[w] >> sh) & 1u) << j;
+            if (dom) b.pos |= ((dom[w] >> sh) & 1u) << j;
+        }
+        if (++r == (uint32_t)ks) {
+            r = 0;
+            k++;
+        }
+    }
+    return b;
+}
+
+// Exclusive prefix of the per-tile predicted counts of one item, written to
+// out[base .. base+nt); returns the total.  Whole block participates.
+__device__ int64_t scan_tile_counts(const int32_t *cnt, int stride_words, int base, int nt,
+                                    int64_t *out, int *sh) {
+    int64_t carry = 0;
+    for (int b0 = 0; b0 < nt; b0 += TPB) {
+        const int i = b0 + threadIdx.x;
+        const int v = i < nt ? __ldcg(cnt + (size_t)(base + i) * stride_words) : 0;
+        int tot;
+        const int ex = block_excl_scan(v, sh, &tot);
+        if (i < nt) out[base + i] = carry + ex;
+        carry += tot;
+    }
+    return carry;
 }
 
 // ------------------------------------------------------------------ pass 1
 __global__ void __launch_bounds__(TPB) k_enc_pass1(mc_enc_launch L) {
     __shared__ Red red;
     __shared__ int s_flag;
+    __shared__ int scan_sh[NWARP + 1];
     const int gt = L.all_tiles[blockIdx.x];
     const int ii = L.tile_item[gt];
     const mc_enc_item I = L.items[ii];
@@ -206,14 +273,20 @@ __global__ void __launch_bounds__(TPB) k_enc_pass1(mc_enc_launch L) {
         const float *cur = (const float *)I.cur;
         const float *prev = I.prev;
         float *hist = (float *)I.hist_out;
-        for (int64_t e = tr.e0 + threadIdx.x; e < tr.e1; e += TPB) {
-            const float c = cur[e];
-            const float p = prev[e];
-            d[0] += (double)fabsf(c);
-            d[1] += (double)fabsf(p);
-            mn = c < mn ? c : mn;
-            mx = c > mx ? c : mx;
-            if (hist) hist[e] = c;
+        for (int64_t g = tr.e0 + 4 * (int64_t)threadIdx.x; g < tr.e1; g += 4 * TPB) {
+            float c[4], p[4];
+            ld4(cur, g, tr.e1, I.vec, c);
+            ld4(prev, g, tr.e1, I.vec, p);
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                if (g + j < tr.e1) {
+                    d[0] += (double)fabsf(c[j]);
+                    d[1] += (double)fabsf(p[j]);
+                    mn = c[j] < mn ? c[j] : mn;
+                    mx = c[j] > mx ? c[j] : mx;
+                }
+            }
+            if (hist) st4(hist, g, tr.e1, I.vec, c);
         }
         // per-kernel sign consistency: one lane per kernel, 32 kernels per ballot word
         const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -223,10 +296,10 @@ __global__ void __launch_bounds__(TPB) k_enc_pass1(mc_enc_launch L) {
             const int64_t k = kb + lane;
             bool flag = false, dom = false;
             if (k < tr.k1) {
-                const float *p = cur + k * I.ks;
+                const float *pk = cur + k * I.ks;
                 int pos = 0, neg = 0;
                 for (int j = 0; j < I.ks; j++) {
-                    const float v = p[j];
+                    const float v = pk[j];
                     pos += v > 0.0f;
                     neg += v < 0.0f;
                 }
@@ -268,68 +341,71 @@ __global__ void __launch_bounds__(TPB) k_enc_pass1(mc_enc_launch L) {
                 tmx = tx > tmx ? tx : tmx;
             }
             block_reduce(red, a, 2, tmn, tmx, t2, z, 0);
+            const int64_t total = scan_tile_counts(&L.tiles[0].P, (int)(sizeof(mc_enc_tile) / 4),
+                                                   I.tile_base, I.ntiles, L.tile_poff, scan_sh);
             if (threadIdx.x == 0) {
                 const double dn = (double)I.n;
                 R->cm = __double2float_rn(__ddiv_rn(a[0], dn));
                 R->pm = __double2float_rn(__ddiv_rn(a[1], dn));
                 R->gmin = tmn;
                 R->gmax = tmx;
-                long long off = 0;
-                for (int i = 0; i < I.ntiles; i++) {
-                    L.tile_poff[I.tile_base + i] = off;
-                    off += __ldcg(&L.tiles[I.tile_base + i].P);
-                }
-                R->P = off;
+                R->P = total;
             }
         }
         return;
     }
 
-    // direct items: element tiles
+    // direct items: element tiles (byte tiles for COPY / FRAME)
     const int64_t e0 = (int64_t)t * I.tile_kernels;
     const int64_t e1 = min(e0 + (int64_t)I.tile_kernels, I.n);
-    if (I.kind == MC_K_COPY) {
-        // raw payload ("sz3_memcpy") and history copy; tiles count bytes
+    if (I.kind == MC_K_COPY || I.kind == MC_K_FRAME) {
+        // raw payload ("sz3_memcpy") and/or history copy of the input bytes
         const uint8_t *src = (const uint8_t *)I.cur;
         uint8_t *hist = (uint8_t *)I.hist_out;
-        uint8_t *raw = I.data_out;
-        for (int64_t e = e0 + threadIdx.x; e < e1; e += TPB) {
-            const uint8_t v = src[e];
-            raw[e] = v;
-            if (hist) hist[e] = v;
-        }
-        return;
-    }
-    if (I.kind == MC_K_QUANT) {
-        const float *cur = (const float *)I.cur;
-        float *hist = (float *)I.hist_out;
-        for (int64_t e = e0 + threadIdx.x; e < e1; e += TPB) {
-            const float c = cur[e];
-            mx2 = fmaxf(mx2, fabsf(c));
-            if (hist) hist[e] = c;
-        }
-        block_reduce(red, d, 0, mn, mx, mx2, l, 0);
-        if (threadIdx.x == 0) L.tiles[gt].maxr = mx2;
-        if (last_cta(&R->ticket[0], I.ntiles, &s_flag)) {
-            float m = 0.0f, u0 = FLT_MAX, u1 = -FLT_MAX;
-            for (int i = threadIdx.x; i < I.ntiles; i += TPB)
-                m = fmaxf(m, __ldcg(&L.tiles[I.tile_base + i].maxr));
-            block_reduce(red, d, 0, u0, u1, m, l, 0);
-            if (threadIdx.x == 0) {
-                R->maxr = m;
-                R->scale = (m == 0.0f) ? 1.0f : __fdiv_rn(m, (float)qmax_of(I.codec));
-                if (I.codec == MC_DC_Q8 || I.codec == MC_DC_INT4) {
-                    *(float *)I.data_out = R->scale;
-                }
+        uint8_t *raw = I.kind == MC_K_COPY ? I.data_out : nullptr;
+        if (I.vec) {   // 16-byte aligned base pointers; tiles are multiples of 16 bytes
+            const int64_t v0 = e0 >> 4, v1 = e1 >> 4;
+            for (int64_t v = v0 + threadIdx.x; v < v1; v += TPB) {
+                const uint4 x = ((const uint4 *)src)[v];
+                if (raw) ((uint4 *)raw)[v] = x;
+                if (hist) ((uint4 *)hist)[v] = x;
+            }
+            for (int64_t e = (v1 << 4) + threadIdx.x; e < e1; e += TPB) {
+                const uint8_t x = src[e];
+                if (raw) raw[e] = x;
+                if (hist) hist[e] = x;
+            }
+        } else {
+            for (int64_t e = e0 + threadIdx.x; e < e1; e += TPB) {
+                const uint8_t x = src[e];
+                if (raw) raw[e] = x;
+                if (hist) hist[e] = x;
             }
         }
         return;
     }
-    if (I.kind == MC_K_FRAME && I.hist_out) {
-        // element tiles in bytes for lossless payloads
-        const uint8_t *src = (const uint8_t *)I.cur;
-        uint8_t *dst = (uint8_t *)I.hist_out;
-        for (int64_t e = e0 + threadIdx.x; e < e1; e += TPB) dst[e] = src[e];
+    // MC_K_QUANT: max |x| for the scale, history copy
+    const float *cur = (const float *)I.cur;
+    float *hist = (float *)I.hist_out;
+    for (int64_t g = e0 + 4 * (int64_t)threadIdx.x; g < e1; g += 4 * TPB) {
+        float c[4];
+        ld4(cur, g, e1, I.vec, c);
+#pragma unroll
+        for (int j = 0; j < 4; j++)
+            if (g + j < e1) mx2 = fmaxf(mx2, fabsf(c[j]));
+        if (hist) st4(hist, g, e1, I.vec, c);
+    }
+    block_reduce(red, d, 0, mn, mx, mx2, l, 0);
+    if (threadIdx.x == 0) L.tiles[gt].maxr = mx2;
+    if (last_cta(&R->ticket[0], I.ntiles, &s_flag)) {
+        float m = 0.0f, u0 = FLT_MAX, u1 = -FLT_MAX;
+        for (int i = threadIdx.x; i < I.ntiles; i += TPB) m = fmaxf(m, __ldcg(&L.tiles[I.tile_base + i].maxr));
+        block_reduce(red, d, 0, u0, u1, m, l, 0);
+        if (threadIdx.x == 0) {
+            R->maxr = m;
+            R->scale = (m == 0.0f) ? 1.0f : __fdiv_rn(m, (float)qmax_of(I.codec));
+            if (I.codec == MC_DC_Q8 || I.codec == MC_DC_INT4) *(float *)I.data_out = R->scale;
+        }
     }
 }
 
@@ -349,11 +425,19 @@ __global__ void __launch_bounds__(TPB) k_enc_pass2(mc_enc_launch L) {
     double d[4] = {0.0, 0.0, 0.0, 0.0};
     long long l[2] = {0, 0};
     float mn = FLT_MAX, mx = -FLT_MAX, mx2 = 0.0f;
-    for (int64_t e = tr.e0 + threadIdx.x; e < tr.e1; e += TPB) {
-        const double dc = (double)__fsub_rn(fabsf(cur[e]), cm);
-        const double dp = (double)__fsub_rn(fabsf(prev[e]), pm);
-        d[0] = __fma_rn(dc, dc, d[0]);
-        d[1] = __fma_rn(dp, dp, d[1]);
+    for (int64_t g = tr.e0 + 4 * (int64_t)threadIdx.x; g < tr.e1; g += 4 * TPB) {
+        float c[4], p[4];
+        ld4(cur, g, tr.e1, I.vec, c);
+        ld4(prev, g, tr.e1, I.vec, p);
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            if (g + j < tr.e1) {
+                const double dc = (double)__fsub_rn(fabsf(c[j]), cm);
+                const double dp = (double)__fsub_rn(fabsf(p[j]), pm);
+                d[0] = __fma_rn(dc, dc, d[0]);
+                d[1] = __fma_rn(dp, dp, d[1]);
+            }
+        }
     }
     block_reduce(red, d, 2, mn, mx, mx2, l, 0);
     if (threadIdx.x == 0) {
@@ -394,33 +478,34 @@ __global__ void __launch_bounds__(TPB) k_enc_pass3(mc_enc_launch L) {
     const float lr = I.lr;
     const float oml = __fsub_rn(1.0f, lr);
     const float *cur = (const float *)I.cur;
-    const float *prev = I.prev;
-    const float *mem_in = I.mem_in;
-    float *mem_out = I.mem_out;
     long long mism = 0;
     float maxr = 0.0f;
     const uint32_t k0 = (uint32_t)tr.k0;
-    for (int64_t e = tr.e0 + threadIdx.x; e < tr.e1; e += TPB) {
-        const uint32_t k = k0 + fdiv32((uint32_t)(e - tr.e0), I.ksdiv);
-        const bool f = (I.bm_words[k >> 5] >> (k & 31)) & 1u;
-        const float c = cur[e];
-        const float m0 = mem_in ? mem_in[e] : 0.0f;
-        float r;
-        if (f) {
-            const bool pos = (I.dom_words[k >> 5] >> (k & 31)) & 1u;
-            const float pv = __fsub_rn(fabsf(prev[e]), pm);
-            const float pn = use_ps ? __fmul_rn(pv, inv_ps) : pv;
-            const float nm = __fmaf_rn(oml, m0, __fmul_rn(lr, pn));
-            mem_out[e] = nm;
-            r = mom_residual(c, nm, pos, mp);
-            const float ap = fabsf(mp.use_cs ? __fmaf_rn(nm, cs, cm) : __fadd_rn(nm, cm));
-            const float pred = pos ? ap : -ap;
-            mism += (pred > 0.0f) != (c > 0.0f);
-        } else {
-            mem_out[e] = m0;
-            r = c;
+    for (int64_t g = tr.e0 + 4 * (int64_t)threadIdx.x; g < tr.e1; g += 4 * TPB) {
+        const QuadBits qb = quad_bits(I.bm_words, I.dom_words, 0u, k0, g, tr.e0, tr.e1, I.ks, I.ksdiv);
+        float c[4], m0[4], p[4], mo[4];
+        ld4(cur, g, tr.e1, I.vec, c);
+        if (I.mem_in) ld4(I.mem_in, g, tr.e1, I.vec, m0);
+        else m0[0] = m0[1] = m0[2] = m0[3] = 0.0f;
+        if (qb.f) ld4(I.prev, g, tr.e1, I.vec, p);
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            float r = c[j];
+            mo[j] = m0[j];
+            if ((qb.f >> j) & 1u) {
+                const float pv = __fsub_rn(fabsf(p[j]), pm);
+                const float pn = use_ps ? __fmul_rn(pv, inv_ps) : pv;
+                const float nm = __fmaf_rn(oml, m0[j], __fmul_rn(lr, pn));
+                mo[j] = nm;
+                const bool pos = (qb.pos >> j) & 1u;
+                const float ap = mom_pred_abs(nm, mp);
+                const float pred = pos ? ap : -ap;
+                mism += (pred > 0.0f) != (c[j] > 0.0f);
+                r = x86min(x86max(__fsub_rn(c[j], pred), mp.gmin), mp.gmax);
+            }
+            if (g + j < tr.e1) maxr = fmaxf(maxr, fabsf(r));
         }
-        maxr = fmaxf(maxr, fabsf(r));
+        st4(I.mem_out, g, tr.e1, I.vec, mo);
     }
     double d[4];
     long long l[2] = {mism, 0};
@@ -461,6 +546,39 @@ __device__ __forceinline__ uint32_t pext32(uint32_t v, uint32_t m) {
     return out;
 }
 
+// Writes the residual codes of one quad (4 consecutive elements at g).
+__device__ __forceinline__ void put_codes(uint8_t *data_out, int codec, int64_t g, int64_t e1, bool vec,
+                                          const float (&r)[4], float scale, float qm) {
+    if (codec == MC_DC_RAW) {
+        st4((float *)data_out, g, e1, vec, r);
+    } else if (codec == MC_DC_Q8) {
+        uint8_t *codes = data_out + 4;   // 4-byte aligned; g is a multiple of 4
+        uint32_t word = 0;
+#pragma unroll
+        for (int j = 0; j < 4; j++)
+            if (g + j < e1) word |= ((uint32_t)(uint8_t)(int8_t)quant1(r[j], scale, qm)) << (8 * j);
+        if (g + 4 <= e1) *(uint32_t *)(codes + g) = word;
+        else
+            for (int j = 0; g + j < e1; j++) codes[g + j] = (uint8_t)(word >> (8 * j));
+    } else if (codec == MC_DC_INT4) {
+        uint8_t *packed = data_out + 4;  // byte g/2, 2-byte aligned
+        uint32_t nib[4];
+#pragma unroll
+        for (int j = 0; j < 4; j++) nib[j] = (g + j < e1) ? (uint32_t)((quant1(r[j], scale, qm) + 8) & 15) : 0u;
+        const uint32_t b0 = nib[0] | (nib[1] << 4), b1 = nib[2] | (nib[3] << 4);
+        if (g + 4 <= e1) *(uint16_t *)(packed + (g >> 1)) = (uint16_t)(b0 | (b1 << 8));
+        else {
+            packed[g >> 1] = (uint8_t)b0;
+            if (g + 2 < e1) packed[(g >> 1) + 1] = (uint8_t)b1;
+        }
+    } else {   // Q8_RAW / INT4_RAW: dequantised floats
+        float v[4];
+#pragma unroll
+        for (int j = 0; j < 4; j++) v[j] = __fmul_rn((float)quant1(r[j], scale, qm), scale);
+        st4((float *)data_out, g, e1, vec, v);
+    }
+}
+
 // ------------------------------------------------------------------ pass 4
 __global__ void __launch_bounds__(TPB) k_enc_pass4(mc_enc_launch L) {
     __shared__ int scan_sh[NWARP + 1];
@@ -475,61 +593,30 @@ __global__ void __launch_bounds__(TPB) k_enc_pass4(mc_enc_launch L) {
         const float scale = R->scale;
         const float qm = (float)qmax_of(I.codec);
         const float *cur = (const float *)I.cur;
-        const float *mem = I.mem_out;
         const uint32_t k0 = (uint32_t)tr.k0;
-        auto resid = [&](int64_t e) -> float {
-            const uint32_t k = k0 + fdiv32((uint32_t)(e - tr.e0), I.ksdiv);
-            const uint32_t bw = I.bm_words[k >> 5];
-            const float c = cur[e];
-            if (!((bw >> (k & 31)) & 1u)) return c;
-            const bool pos = (I.dom_words[k >> 5] >> (k & 31)) & 1u;
-            return mom_residual(c, mem[e], pos, mp);
-        };
-        if (I.codec == MC_DC_RAW) {
-            float *out = (float *)I.data_out;
-            for (int64_t e = tr.e0 + threadIdx.x; e < tr.e1; e += TPB) out[e] = resid(e);
-        } else if (I.codec == MC_DC_Q8) {
-            // four codes per 32-bit store; tiles start at multiples of 4 elements
-            uint8_t *codes = I.data_out + 4;
-            for (int64_t g = tr.e0 + 4 * (int64_t)threadIdx.x; g < tr.e1; g += 4 * TPB) {
-                uint32_t word = 0;
-                for (int j = 0; j < 4; j++) {
-                    if (g + j < tr.e1) {
-                        const int q = quant1(resid(g + j), scale, qm);
-                        word |= ((uint32_t)(uint8_t)(int8_t)q) << (8 * j);
-                    }
-                }
-                if (g + 3 < tr.e1) {
-                    *(uint32_t *)(codes + g) = word;
-                } else {
-                    for (int j = 0; g + j < tr.e1; j++) codes[g + j] = (uint8_t)(word >> (8 * j));
-                }
-            }
-        } else if (I.codec == MC_DC_INT4) {
-            uint8_t *packed = I.data_out + 4;
-            for (int64_t p = (tr.e0 >> 1) + threadIdx.x; 2 * p < tr.e1; p += TPB) {
-                const int lo = quant1(resid(2 * p), scale, qm) + 8;
-                const int hi = (2 * p + 1 < tr.e1) ? quant1(resid(2 * p + 1), scale, qm) + 8 : 0;
-                packed[p] = (uint8_t)((lo & 15) | ((hi & 15) << 4));
-            }
-        } else {  // Q8_RAW / INT4_RAW: dequantised floats
-            float *out = (float *)I.data_out;
-            for (int64_t e = tr.e0 + threadIdx.x; e < tr.e1; e += TPB)
-                out[e] = __fmul_rn((float)quant1(resid(e), scale, qm), scale);
+        for (int64_t g = tr.e0 + 4 * (int64_t)threadIdx.x; g < tr.e1; g += 4 * TPB) {
+            const QuadBits qb = quad_bits(I.bm_words, I.dom_words, 0u, k0, g, tr.e0, tr.e1, I.ks, I.ksdiv);
+            float c[4], m[4], r[4];
+            ld4(cur, g, tr.e1, I.vec, c);
+            if (qb.f) ld4(I.mem_out, g, tr.e1, I.vec, m);
+#pragma unroll
+            for (int j = 0; j < 4; j++)
+                r[j] = ((qb.f >> j) & 1u) ? mom_residual(c[j], m[j], (qb.pos >> j) & 1u, mp) : c[j];
+            put_codes(I.data_out, I.codec, g, tr.e1, I.vec, r, scale, qm);
         }
         // dense dominant signs of predicted kernels (ref :2258-2283)
         const int64_t wb = tr.k0 >> 5, we = (tr.k1 + 31) >> 5;
         const int i = threadIdx.x;
-        uint32_t m = 0, dv = 0;
+        uint32_t mw = 0, dv = 0;
         if (wb + i < we) {
-            m = I.bm_words[wb + i];
+            mw = I.bm_words[wb + i];
             dv = I.dom_words[wb + i];
         }
-        const int pc = __popc(m);
+        const int pc = __popc(mw);
         const int off_l = block_excl_scan(pc, scan_sh, nullptr);
         if (pc) {
             const int64_t off = L.tile_poff[gt] + off_l;
-            const uint32_t bits = pext32(dv, m);
+            const uint32_t bits = pext32(dv, mw);
             const int64_t w0 = off >> 5;
             const int sh = (int)(off & 31);
             atomicOr(&I.sign_words[w0], bits << sh);
@@ -540,28 +627,28 @@ __global__ void __launch_bounds__(TPB) k_enc_pass4(mc_enc_launch L) {
     if (I.kind == MC_K_QUANT) {
         const int64_t e0 = (int64_t)t * I.tile_kernels;
         const int64_t e1 = min(e0 + (int64_t)I.tile_kernels, I.n);
-        const float *cur = (const float *)I.cur;
         const float scale = R->scale;
         const float qm = (float)qmax_of(I.codec);
-        if (I.codec == MC_DC_Q8) {
-            int8_t *codes = (int8_t *)(I.data_out + 4);
-            for (int64_t e = e0 + threadIdx.x; e < e1; e += TPB) codes[e] = (int8_t)quant1(cur[e], scale, qm);
-        } else if (I.codec == MC_DC_INT4) {
-            uint8_t *packed = I.data_out + 4;
-            for (int64_t p = (e0 >> 1) + threadIdx.x; 2 * p < e1; p += TPB) {
-                const int lo = quant1(cur[2 * p], scale, qm) + 8;
-                const int hi = (2 * p + 1 < e1) ? quant1(cur[2 * p + 1], scale, qm) + 8 : 0;
-                packed[p] = (uint8_t)((lo & 15) | ((hi & 15) << 4));
-            }
-        } else {
-            float *out = (float *)I.data_out;
-            for (int64_t e = e0 + threadIdx.x; e < e1; e += TPB)
-                out[e] = __fmul_rn((float)quant1(cur[e], scale, qm), scale);
+        for (int64_t g = e0 + 4 * (int64_t)threadIdx.x; g < e1; g += 4 * TPB) {
+            float c[4];
+            ld4((const float *)I.cur, g, e1, I.vec, c);
+            put_codes(I.data_out, I.codec, g, e1, I.vec, c, scale, qm);
         }
     }
 }
 
 // ------------------------------------------------------------------ frames
+// Copies n bytes; 4-byte words when both ends are 4-byte aligned.
+__device__ __forceinline__ void copy_bytes(uint8_t *dst, const uint8_t *src, int64_t n) {
+    if ((((uintptr_t)dst | (uintptr_t)src) & 3) == 0) {
+        const int64_t nw = n >> 2;
+        for (int64_t i = threadIdx.x; i < nw; i += TPB) ((uint32_t *)dst)[i] = ((const uint32_t *)src)[i];
+        for (int64_t i = (nw << 2) + threadIdx.x; i < n; i += TPB) dst[i] = src[i];
+    } else {
+        for (int64_t i = threadIdx.x; i < n; i += TPB) dst[i] = src[i];
+    }
+}
+
 // zstd frame (RFC 8878) with a single-segment header, 4- or 8-byte content
 // size, and Raw / RLE blocks of at most 128 KiB.
 __global__ void __launch_bounds__(TPB) k_frames(const mc_frame_job *jobs) {
@@ -591,7 +678,14 @@ __global__ void __launch_bounds__(TPB) k_frames(const mc_frame_job *jobs) {
         int eq = 1;
         if (bs > 1) {
             const uint8_t first = src[0];
-            for (int64_t i = threadIdx.x; i < bs; i += TPB) eq &= (src[i] == first);
+            if (((uintptr_t)src & 3) == 0) {
+                const uint32_t w4 = first * 0x01010101u;
+                const int64_t nw = bs >> 2;
+                for (int64_t i = threadIdx.x; i < nw; i += TPB) eq &= ((const uint32_t *)src)[i] == w4;
+                for (int64_t i = (nw << 2) + threadIdx.x; i < bs; i += TPB) eq &= src[i] == first;
+            } else {
+                for (int64_t i = threadIdx.x; i < bs; i += TPB) eq &= (src[i] == first);
+            }
         }
         const int rle = (bs > 1) && __syncthreads_and(eq);
         const uint32_t last = (b == nblk - 1) ? 1u : 0u;
@@ -603,8 +697,7 @@ __global__ void __launch_bounds__(TPB) k_frames(const mc_frame_job *jobs) {
             if (rle) dst[pos + 3] = src[0];
         }
         if (!rle) {
-            uint8_t *o = dst + pos + 3;
-            for (int64_t i = threadIdx.x; i < bs; i += TPB) o[i] = src[i];
+            copy_bytes(dst + pos + 3, src, bs);
             pos += 3 + bs;
         } else {
             pos += 4;
@@ -680,7 +773,7 @@ __global__ void __launch_bounds__(TPB) k_unframe(const mc_unframe_job *jobs) {
         uint8_t *o = J.dst + s_dst[s];
         const uint8_t *src = J.frame + s_src[s];
         if (s_type[s] == 0) {
-            for (int64_t i = threadIdx.x; i < s_len[s]; i += TPB) o[i] = src[i];
+            copy_bytes(o, src, s_len[s]);
         } else {
             const uint8_t v = src[0];
             for (int64_t i = threadIdx.x; i < s_len[s]; i += TPB) o[i] = v;
@@ -720,19 +813,50 @@ __device__ __forceinline__ int64_t dec_bm_bits(const mc_dec_item &I) {
     return min(len * 8, I.K);
 }
 
+// Bitmap word w (unmasked).
+__device__ __forceinline__ uint32_t dec_bm_word(const mc_dec_item &I, int64_t w) {
+    if (I.bm_mode == MC_BM_RLE1) return (uint32_t)I.bm_frame[12] * 0x01010101u;
+    return I.bm_words[w];
+}
+
+__device__ __forceinline__ uint32_t le32(const uint8_t *p) {
+    return (uint32_t)p[0] | ((uint32_t)p[1] << 8) | ((uint32_t)p[2] << 16) | ((uint32_t)p[3] << 24);
+}
+
+// Checks that an in-place frame is what the host assumed: single-segment
+// header with a 4-byte content size, then one last block of the given type
+// whose size equals the content size.  Returns the content size or -1.
+__device__ int64_t check_frame1(const uint8_t *f, int type, int64_t want) {
+    if (f[0] != 0x28 || f[1] != 0xB5 || f[2] != 0x2F || f[3] != 0xFD || f[4] != 0xA0) return -1;
+    const int64_t cs = le32(f + 5);
+    const uint32_t h = f[9] | ((uint32_t)f[10] << 8) | ((uint32_t)f[11] << 16);
+    if ((h & 1u) != 1u || (int)((h >> 1) & 3u) != type || (int64_t)(h >> 3) != cs) return -1;
+    if (want >= 0 && cs != want) return -1;
+    return cs;
+}
+
 __global__ void __launch_bounds__(TPB) k_dec_prefix(mc_dec_launch L) {
     __shared__ long long sh[NWARP];
     __shared__ int s_flag;
+    __shared__ int scan_sh[NWARP + 1];
     const int gt = L.mom_tiles[blockIdx.x];
     const int ii = L.tile_item[gt];
     const mc_dec_item I = L.items[ii];
     const int t = gt - I.tile_base;
     mc_dec_result *R = L.results + ii;
+    if (t == 0 && threadIdx.x == 0) {
+        int bad = 0;
+        if (I.bm_mode == MC_BM_RAW1) bad |= check_frame1(I.bm_frame, 0, (I.bm_bits + 7) >> 3) < 0;
+        if (I.bm_mode == MC_BM_RLE1) bad |= check_frame1(I.bm_frame, 1, (I.bm_bits + 7) >> 3) < 0;
+        if (I.sg_mode == MC_BM_RAW1) bad |= check_frame1(I.sg_frame, 0, I.sg_len) < 0;
+        if (I.sg_mode == MC_BM_RLE1) bad |= check_frame1(I.sg_frame, 1, -1) < 0;
+        if (bad) R->err = 1;
+    }
     const DecTile tr = dec_range(I, t);
     const int64_t wb = tr.k0 >> 5, we = (tr.k1 + 31) >> 5;
     const int64_t bm_bits = dec_bm_bits(I);
     int c = 0;
-    for (int64_t w = wb + threadIdx.x; w < we; w += TPB) c += __popc(I.bm_words[w] & word_mask(w, bm_bits));
+    for (int64_t w = wb + threadIdx.x; w < we; w += TPB) c += __popc(dec_bm_word(I, w) & word_mask(w, bm_bits));
     long long v = warp_sum_ll(c);
     if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = v;
     __syncthreads();
@@ -741,24 +865,39 @@ __global__ void __launch_bounds__(TPB) k_dec_prefix(mc_dec_launch L) {
         for (int j = 0; j < NWARP; j++) s += sh[j];
         L.tile_count[gt] = (int32_t)s;
     }
-    if (last_cta(&R->ticket, I.ntiles, &s_flag) && threadIdx.x == 0) {
-        long long off = 0;
-        for (int i = 0; i < I.ntiles; i++) {
-            L.tile_poff[I.tile_base + i] = off;
-            off += __ldcg(&L.tile_count[I.tile_base + i]);
-        }
-        R->P = off;
+    if (last_cta(&R->ticket, I.ntiles, &s_flag)) {
+        const int64_t total = scan_tile_counts(L.tile_count, 1, I.tile_base, I.ntiles, L.tile_poff, scan_sh);
+        if (threadIdx.x == 0) R->P = total;
     }
 }
 
-__device__ __forceinline__ float dec_resid(const mc_dec_item &I, int64_t e, float scale) {
-    if (I.codec == MC_DC_Q8) return __fmul_rn((float)(int8_t)I.data[e], scale);
-    if (I.codec == MC_DC_INT4) {
-        const uint8_t b = I.data[e >> 1];
-        const int q = (int)((e & 1) ? (b >> 4) : (b & 15)) - 8;
-        return __fmul_rn((float)q, scale);
+// Residual values of one quad from the payload (codes * scale or raw floats).
+__device__ __forceinline__ void dec_resid4(const mc_dec_item &I, int64_t g, int64_t e1, float scale,
+                                           float (&r)[4]) {
+    if (I.codec == MC_DC_Q8) {
+        uint32_t w;
+        if (I.vec && g + 4 <= e1) {
+            w = *(const uint32_t *)(I.data + g);
+        } else {
+            w = 0;
+            for (int j = 0; j < 4; j++)
+                if (g + j < e1) w |= (uint32_t)I.data[g + j] << (8 * j);
+        }
+#pragma unroll
+        for (int j = 0; j < 4; j++) r[j] = __fmul_rn((float)(int8_t)(uint8_t)(w >> (8 * j)), scale);
+    } else if (I.codec == MC_DC_INT4) {
+        uint32_t w;
+        if (I.vec && g + 4 <= e1) {
+            w = *(const uint16_t *)(I.data + (g >> 1));
+        } else {
+            w = I.data[g >> 1];
+            if (g + 2 < e1) w |= (uint32_t)I.data[(g >> 1) + 1] << 8;
+        }
+#pragma unroll
+        for (int j = 0; j < 4; j++) r[j] = __fmul_rn((float)((int)((w >> (4 * j)) & 15u) - 8), scale);
+    } else {
+        ld4((const float *)I.data, g, e1, I.vec, r);
     }
-    return ((const float *)I.data)[e];
 }
 
 __global__ void __launch_bounds__(TPB) k_dec_recon(mc_dec_launch L) {
@@ -768,7 +907,9 @@ __global__ void __launch_bounds__(TPB) k_dec_recon(mc_dec_launch L) {
     const int ii = L.tile_item[gt];
     const mc_dec_item I = L.items[ii];
     const int t = gt - I.tile_base;
-    const float scale = (I.codec == MC_DC_Q8 || I.codec == MC_DC_INT4) ? *I.scale_ptr : 1.0f;
+    // the scale header may sit at any byte address (payloads from the caller)
+    const float scale = (I.codec == MC_DC_Q8 || I.codec == MC_DC_INT4)
+                            ? __uint_as_float(le32((const uint8_t *)I.scale_ptr)) : 1.0f;
     float *hist = (float *)I.hist_out;
     float *out = (float *)I.out;
     if (I.kind == MC_D_MOMENTUM) {
@@ -776,14 +917,21 @@ __global__ void __launch_bounds__(TPB) k_dec_recon(mc_dec_launch L) {
         const int64_t wb = tr.k0 >> 5, we = (tr.k1 + 31) >> 5;
         const int i = threadIdx.x;
         const int64_t bm_bits = dec_bm_bits(I);
+        // sign source: content bytes, or the repeated byte of an RLE frame
         const uint8_t *sg = I.sg_bytes;
         int64_t sg_len = I.sg_len;
+        int sg_rle = -1;
         if (I.sg_len_ptr) {
             sg_len = *I.sg_len_ptr;
             if (sg_len < 0) sg = nullptr;
         }
+        if (I.sg_mode == MC_BM_RLE1) {
+            sg_rle = I.sg_frame[12];
+            sg_len = le32(I.sg_frame + 5);
+            sg = nullptr;
+        }
         uint32_t m = 0;
-        if (wb + i < we) m = I.bm_words[wb + i] & word_mask(wb + i, bm_bits);
+        if (wb + i < we) m = dec_bm_word(I, wb + i) & word_mask(wb + i, bm_bits);
         const int pc = __popc(m);
         const int off_l = block_excl_scan(pc, scan_sh, nullptr);
         uint32_t dm = 0;
@@ -792,8 +940,11 @@ __global__ void __launch_bounds__(TPB) k_dec_recon(mc_dec_launch L) {
             uint32_t mm = m;
             while (mm) {
                 const int b = __ffs(mm) - 1;
-                int bit = 1;
-                if (sg && (idx >> 3) < sg_len) bit = (sg[idx >> 3] >> (idx & 7)) & 1;
+                int bit = 1;   // missing signs default to +1 (ref :3296-3302)
+                if ((idx >> 3) < sg_len) {
+                    if (sg) bit = (sg[idx >> 3] >> (idx & 7)) & 1;
+                    else if (sg_rle >= 0) bit = (sg_rle >> (idx & 7)) & 1;
+                }
                 dm |= (uint32_t)bit << b;
                 idx++;
                 mm &= mm - 1;
@@ -802,53 +953,98 @@ __global__ void __launch_bounds__(TPB) k_dec_recon(mc_dec_launch L) {
         s_m[i] = m;
         s_d[i] = dm;
         __syncthreads();
-        const float cm = I.cm, cs = I.cs, pm = I.pm, lr = I.lr;
-        const bool use_cs = cs > 1e-8f, use_ps = I.ps > 1e-8f;
+        const MomParams mp = {I.cm, I.cs, 0.0f, 0.0f, I.cs > 1e-8f};
+        const float pm = I.pm, lr = I.lr;
+        const bool use_ps = I.ps > 1e-8f;
         const float inv_ps = use_ps ? __fdiv_rn(1.0f, I.ps) : 1.0f;
         const float oml = __fsub_rn(1.0f, lr);
         const uint32_t k0 = (uint32_t)tr.k0;
-        for (int64_t e = tr.e0 + threadIdx.x; e < tr.e1; e += TPB) {
-            const uint32_t k = k0 + fdiv32((uint32_t)(e - tr.e0), I.ksdiv);
-            const uint32_t lw = (k >> 5) - (uint32_t)wb;
-            const bool f = (s_m[lw] >> (k & 31)) & 1u;
-            const float r = dec_resid(I, e, scale);
-            const float m0 = I.mem_in ? I.mem_in[e] : 0.0f;
-            float rec;
-            if (f) {
-                const bool pos = (s_d[lw] >> (k & 31)) & 1u;
-                const float pv = __fsub_rn(fabsf(I.prev[e]), pm);
-                const float pn = use_ps ? __fmul_rn(pv, inv_ps) : pv;
-                const float nm = __fmaf_rn(oml, m0, __fmul_rn(lr, pn));
-                I.mem_out[e] = nm;
-                float ap = use_cs ? __fmaf_rn(nm, cs, cm) : __fadd_rn(nm, cm);
-                ap = fabsf(ap);
-                rec = __fadd_rn(r, pos ? ap : -ap);
-            } else {
-                I.mem_out[e] = m0;
-                rec = r;
+        // bitmap / sign words of the tile are in shared memory from word wb on
+        for (int64_t g = tr.e0 + 4 * (int64_t)threadIdx.x; g < tr.e1; g += 4 * TPB) {
+            const QuadBits qb = quad_bits(s_m, s_d, (uint32_t)wb, k0, g, tr.e0, tr.e1, I.ks, I.ksdiv);
+            float r[4], m0[4], p[4], mo[4], rec[4];
+            dec_resid4(I, g, tr.e1, scale, r);
+            if (I.mem_in) ld4(I.mem_in, g, tr.e1, I.vec, m0);
+            else m0[0] = m0[1] = m0[2] = m0[3] = 0.0f;
+            if (qb.f) ld4(I.prev, g, tr.e1, I.vec, p);
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                rec[j] = r[j];
+                mo[j] = m0[j];
+                if ((qb.f >> j) & 1u) {
+                    const float pv = __fsub_rn(fabsf(p[j]), pm);
+                    const float pn = use_ps ? __fmul_rn(pv, inv_ps) : pv;
+                    const float nm = __fmaf_rn(oml, m0[j], __fmul_rn(lr, pn));
+                    mo[j] = nm;
+                    const float ap = mom_pred_abs(nm, mp);
+                    rec[j] = __fadd_rn(r[j], ((qb.pos >> j) & 1u) ? ap : -ap);
+                }
             }
-            hist[e] = rec;
-            if (out) out[e] = rec;
+            st4(I.mem_out, g, tr.e1, I.vec, mo);
+            st4(hist, g, tr.e1, I.vec, rec);
+            if (out) st4(out, g, tr.e1, I.vec, rec);
         }
         return;
     }
     const int64_t e0 = (int64_t)t * I.tile_kernels;
     const int64_t e1 = min(e0 + (int64_t)I.tile_kernels, I.n);
     if (I.kind == MC_D_RESIDUAL || I.kind == MC_D_QUANT) {
-        for (int64_t e = e0 + threadIdx.x; e < e1; e += TPB) {
-            const float r = dec_resid(I, e, scale);
-            hist[e] = r;
-            if (out) out[e] = r;
+        for (int64_t g = e0 + 4 * (int64_t)threadIdx.x; g < e1; g += 4 * TPB) {
+            float r[4];
+            dec_resid4(I, g, e1, scale, r);
+            st4(hist, g, e1, I.vec, r);
+            if (out) st4(out, g, e1, I.vec, r);
         }
         return;
     }
     // MC_D_COPY: bytes (tile in bytes)
     const uint8_t *src = I.data;
     uint8_t *h8 = (uint8_t *)I.hist_out, *o8 = (uint8_t *)I.out;
-    for (int64_t e = e0 + threadIdx.x; e < e1; e += TPB) {
-        const uint8_t v = src[e];
-        h8[e] = v;
-        if (o8) o8[e] = v;
+    if (I.data_mode != MC_BM_WORDS) {
+        // lossless frame read in place: check the header the host assumed
+        if (t == 0 && threadIdx.x == 0 &&
+            check_frame1(I.data_frame, I.data_mode == MC_BM_RAW1 ? 0 : 1, I.n) < 0)
+            L.results[ii].err = 1;
+        if (I.data_mode == MC_BM_RLE1) {
+            const uint8_t v = I.data_frame[12];
+            for (int64_t e = e0 + threadIdx.x; e < e1; e += TPB) {
+                h8[e] = v;
+                if (o8) o8[e] = v;
+            }
+            return;
+        }
+    }
+    if (!I.vec && ((((uintptr_t)src | (uintptr_t)h8 | (uintptr_t)o8) & 3) == 0)) {
+        // 4-byte words (tiles are multiples of 16 bytes)
+        const int64_t w0 = e0 >> 2, w1 = e1 >> 2;
+        for (int64_t w = w0 + threadIdx.x; w < w1; w += TPB) {
+            const uint32_t x = ((const uint32_t *)src)[w];
+            ((uint32_t *)h8)[w] = x;
+            if (o8) ((uint32_t *)o8)[w] = x;
+        }
+        for (int64_t e = (w1 << 2) + threadIdx.x; e < e1; e += TPB) {
+            h8[e] = src[e];
+            if (o8) o8[e] = src[e];
+        }
+        return;
+    }
+    if (I.vec) {
+        const int64_t v0 = e0 >> 4, v1 = e1 >> 4;
+        for (int64_t v = v0 + threadIdx.x; v < v1; v += TPB) {
+            const uint4 x = ((const uint4 *)src)[v];
+            ((uint4 *)h8)[v] = x;
+            if (o8) ((uint4 *)o8)[v] = x;
+        }
+        for (int64_t e = (v1 << 4) + threadIdx.x; e < e1; e += TPB) {
+            h8[e] = src[e];
+            if (o8) o8[e] = src[e];
+        }
+    } else {
+        for (int64_t e = e0 + threadIdx.x; e < e1; e += TPB) {
+            const uint8_t v = src[e];
+            h8[e] = v;
+            if (o8) o8[e] = v;
+        }
     }
 }
 

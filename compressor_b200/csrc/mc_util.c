@@ -369,6 +369,19 @@ void registry_add(const void *obj, mc_arena *a) {
     pthread_mutex_unlock(&g_reg_mu);
 }
 
+void registry_add_many(const void **objs, size_t n, mc_arena *a) {
+    pthread_mutex_lock(&g_reg_mu);
+    for (size_t k = 0; k < n; k++) {
+        if ((g_reg_len + 1) * 2 >= g_reg_cap && reg_grow() != 0) break;
+        size_t j = reg_hash(objs[k], g_reg_cap);
+        while (g_reg[j].obj && g_reg[j].obj != REG_TOMB) j = (j + 1) & (g_reg_cap - 1);
+        g_reg[j].obj = objs[k];
+        g_reg[j].arena = a;
+        g_reg_len++;
+    }
+    pthread_mutex_unlock(&g_reg_mu);
+}
+
 mc_arena *registry_take(const void *obj, int *found) {
     *found = 0;
     pthread_mutex_lock(&g_reg_mu);
@@ -452,6 +465,7 @@ mc_tensor *tensor_new(DataType dt, size_t ndim, const size_t *shape, int device)
         t->n *= shape[i];
     }
     t->bytes = t->n * mc_dtype_size(dt);
+    t->device = device;
     t->dev = dbuf_get(device, t->bytes);
     if (!t->dev) {
         free(t);
@@ -460,13 +474,11 @@ mc_tensor *tensor_new(DataType dt, size_t ndim, const size_t *shape, int device)
     return t;
 }
 
-/* Releases a tensor entry; the device of the buffer is the current device. */
+/* Returns a tensor's buffer to the pool of its device. */
 void tensor_drop(void *p) {
     mc_tensor *t = (mc_tensor *)p;
     if (!t) return;
-    int dev = 0;
-    cudaGetDevice(&dev);
-    dbuf_put(dev, t->dev, t->bytes);
+    dbuf_put(t->device, t->dev, t->bytes);
     free(t);
 }
 
@@ -557,6 +569,12 @@ void mc_log(const MomentumCompressor *mc, int level, const char *fmt, ...) {
     va_start(ap, fmt);
     vfprintf(level >= LOG_LEVEL_WARNING ? stderr : stdout, fmt, ap);
     va_end(ap);
+}
+
+int mc_is_arena_ptr(const void *p) {
+    uintptr_t lo, hi;
+    int d;
+    return arena_lookup((uintptr_t)p, &lo, &hi, &d);
 }
 
 int mc_ptr_is_device(const void *p, int *device) {
