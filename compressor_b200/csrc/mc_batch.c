@@ -135,7 +135,8 @@ typedef struct {
     size_t words_off;    /* in SD_WORDS, units of uint32 */
     size_t kwords;
     int tile_base, ntiles, tile_param;
-    size_t fs_bm, fs_sg, fs_data;   /* indices into the frame-size array, or (size_t)-1 */
+    size_t nblk;                     /* MOMENTUM: bitmap frame blocks */
+    size_t fs_bm, fs_sg, fs_data;    /* frame sizes in libzstd frame mode */
 } cplan;
 
 typedef struct {
@@ -179,12 +180,17 @@ static const char *codec_tag_of(int dcodec) {
     }
 }
 
+/* Kernels per momentum tile: the largest power of two with at most 8192
+ * elements per tile, at least 32 (one ballot word).  Powers of two make every
+ * 2^20-kernel block of the bitmap frame a union of whole tiles. */
 static int tile_kernels_for(size_t ks) {
-    size_t tk = TILE_ELEMS / (ks ? ks : 1);
-    tk = tk / 32 * 32;
-    if (tk < 32) tk = 32;
-    if (tk > 8192) tk = 8192;
+    size_t tk = 8192;
+    while (tk > 32 && tk * (ks ? ks : 1) > TILE_ELEMS) tk >>= 1;
     return (int)tk;
+}
+
+static size_t frame_blocks(size_t content) {
+    return content == 0 ? 1 : (content + MC_ZBLOCK - 1) / MC_ZBLOCK;
 }
 
 /* Returns the batch's new tensors to their records' spare slots (or the pool). */
@@ -259,7 +265,7 @@ int mc_compress_grouped(MomentumCompressor *mc, BatchItem *items, size_t n, cons
         p->n = g->total_size;
         p->bytes = p->n * elem;
         p->prev_item = -1;
-        p->fs_bm = p->fs_sg = p->fs_data = (size_t)-1;
+        p->fs_bm = p->fs_sg = p->fs_data = 0;
         req[i].name = items[i].layer_name;
         req[i].dt = g->dtype;
         req[i].ndim = g->ndim;
@@ -351,7 +357,7 @@ int mc_compress_grouped(MomentumCompressor *mc, BatchItem *items, size_t n, cons
     /* --------------------------------------------- kinds, codecs, tiling */
     const int dcodec = dcodec_of(mc->residual_codec);
     int nwaves = 1;
-    int ntiles_total = 0, nframes = 0, nmom = 0;
+    int ntiles_total = 0, nmom = 0;
     size_t words_total = 0;
     for (size_t i = 0; i < n; i++) {
         cplan *p = &P[i];
@@ -364,10 +370,10 @@ int mc_compress_grouped(MomentumCompressor *mc, BatchItem *items, size_t n, cons
             p->tile_param = tile_kernels_for(p->ks);
             p->ntiles = (int)((p->K + (size_t)p->tile_param - 1) / (size_t)p->tile_param);
             p->kwords = (p->K + 31) / 32 + 1;
+            p->nblk = frame_blocks((p->K + 7) / 8);
             p->words_off = words_total;
-            words_total += 3 * ALIGN_UP(p->kwords, 64);
+            words_total += 2 * ALIGN_UP(p->kwords, 64) + ALIGN_UP(p->nblk, 64);
             if (p->wave + 1 > nwaves) nwaves = p->wave + 1;
-            nframes += 2;
             nmom++;
         } else if (p->use_lossy && p->dt == DTYPE_FLOAT32 && dcodec != MC_DC_RAW) {
             p->dcodec = dcodec;
@@ -388,7 +394,6 @@ int mc_compress_grouped(MomentumCompressor *mc, BatchItem *items, size_t n, cons
             p->codec_tag = "zstd";
             p->tile_param = TILE_ELEMS * 4;
             p->ntiles = (int)((p->bytes + (size_t)p->tile_param - 1) / (size_t)p->tile_param);
-            nframes += 1;
         }
         p->tile_base = ntiles_total;
         ntiles_total += p->ntiles;
@@ -402,14 +407,13 @@ int mc_compress_grouped(MomentumCompressor *mc, BatchItem *items, size_t n, cons
         size_t cap;
         if (p->kind == MC_K_MOMENTUM || p->kind == MC_K_QUANT) cap = residual_bytes(p->dcodec, p->n);
         else if (p->kind == MC_K_COPY) cap = p->bytes;
-        else cap = mc->frame_mode == MC_FRAME_LIBZSTD ? p->bytes + p->bytes / 64 + 1024
-                                                      : zf_max_frame_size(p->bytes);
+        else cap = zf_max_frame_size(p->bytes) + (mc->frame_mode == MC_FRAME_LIBZSTD ? p->bytes / 64 + 1024 : 0);
         p->off_data = arena_bytes;
         p->cap_data = cap;
         arena_bytes = ALIGN_UP(arena_bytes + cap, SLOT_ALIGN);
         if (p->kind == MC_K_MOMENTUM) {
             size_t c = (p->K + 7) / 8;
-            size_t fc = mc->frame_mode == MC_FRAME_LIBZSTD ? c + c / 64 + 1024 : zf_max_frame_size(c);
+            size_t fc = ALIGN_UP(zf_max_frame_size(c) + (mc->frame_mode == MC_FRAME_LIBZSTD ? c / 64 + 1024 : 0), 16);
             p->off_bm = arena_bytes;
             p->cap_bm = fc;
             arena_bytes = ALIGN_UP(arena_bytes + fc, SLOT_ALIGN);
@@ -551,26 +555,23 @@ int mc_compress_grouped(MomentumCompressor *mc, BatchItem *items, size_t n, cons
             rc = ERROR_ALLOCATION;
             goto fail;
         }
-        cudaMemsetAsync(words, 0, words_total * 4, st);
     }
     mc_enc_result *results = (mc_enc_result *)scratch_dev(&mc->scratch, SD_RESULTS,
                                                           n * sizeof(mc_enc_result));
     mc_enc_tile *tiles = (mc_enc_tile *)scratch_dev(&mc->scratch, SD_TILES,
                                                     (size_t)(ntiles_total + 1) * sizeof(mc_enc_tile));
     int64_t *poff = (int64_t *)scratch_dev(&mc->scratch, SD_POFF, (size_t)(ntiles_total + 1) * 8);
-    int64_t *fsize = (int64_t *)scratch_dev(&mc->scratch, SD_FSIZE, (size_t)(nframes + 1) * 8);
-    if (!results || !tiles || !poff || !fsize) {
+    if (!results || !tiles || !poff) {
         rc = ERROR_ALLOCATION;
         goto fail;
     }
 
     /* ------------------------------------------------ build device tables */
-    /* layout: [items][tile_item by tile id][per wave: all-tile list, momentum-tile list][frames] */
+    /* layout: [items][tile_item by tile id][per wave: all-tile list, momentum-tile list] */
     size_t tab_items = ALIGN_UP(n * sizeof(mc_enc_item), 256);
     size_t tab_tiles = ALIGN_UP((size_t)(ntiles_total + 1) * 4, 256);
     size_t tab_lists = 2 * tab_tiles * (size_t)nwaves;
-    size_t tab_frames = ALIGN_UP((size_t)(nframes + 1) * sizeof(mc_frame_job), 256);
-    size_t tab_total = tab_items + tab_tiles + tab_lists + tab_frames;
+    size_t tab_total = tab_items + tab_tiles + tab_lists;
     uint8_t *htab = (uint8_t *)scratch_host(&mc->scratch, SH_TABLES, tab_total);
     uint8_t *dtab = (uint8_t *)scratch_dev(&mc->scratch, SD_TABLES, tab_total);
     if (!htab || !dtab) {
@@ -583,9 +584,6 @@ int mc_compress_grouped(MomentumCompressor *mc, BatchItem *items, size_t n, cons
     memset(htab, 0, tab_total);
     mc_enc_item *hit = (mc_enc_item *)htab;
     int32_t *h_tile_item = (int32_t *)(htab + tab_items);
-    mc_frame_job *hfr = (mc_frame_job *)(htab + tab_items + tab_tiles + tab_lists);
-    mc_frame_job *dfr = (mc_frame_job *)(dtab + tab_items + tab_tiles + tab_lists);
-    int fj = 0;
     for (size_t i = 0; i < n; i++) {
         cplan *p = &P[i];
         mc_enc_item *I = &hit[i];
@@ -621,32 +619,13 @@ int mc_compress_grouped(MomentumCompressor *mc, BatchItem *items, size_t n, cons
             size_t stride = ALIGN_UP(p->kwords, 64);
             I->bm_words = words + p->words_off;
             I->dom_words = words + p->words_off + stride;
-            I->sign_words = words + p->words_off + 2 * stride;
-            if (mc->frame_mode == MC_FRAME_GPU) {
-                mc_frame_job *J = &hfr[fj];
-                J->src = (const uint8_t *)I->bm_words;
-                J->size = (int64_t)((p->K + 7) / 8);
-                J->dst = payload_dev + p->off_bm;
-                J->size_out = fsize + fj;
-                p->fs_bm = (size_t)fj++;
-                J = &hfr[fj];
-                J->src = (const uint8_t *)I->sign_words;
-                J->size = -1;
-                J->P_src = &results[i].P;
-                J->dst = payload_dev + p->off_sg;
-                J->size_out = fsize + fj;
-                p->fs_sg = (size_t)fj++;
-            }
+            I->blk_pos = words + p->words_off + 2 * stride;
+            I->max_blocks = (int32_t)p->nblk;
+            I->bm_frame = payload_dev + p->off_bm;
+            I->sg_frame = payload_dev + p->off_sg;
+            I->sg_cap = (int64_t)p->cap_sg;
         } else if (p->kind == MC_K_FRAME || p->kind == MC_K_COPY) {
             I->n = (int64_t)p->bytes;   /* byte tiles */
-            if (p->kind == MC_K_FRAME && mc->frame_mode == MC_FRAME_GPU) {
-                mc_frame_job *J = &hfr[fj];
-                J->src = (const uint8_t *)p->dev_in;
-                J->size = (int64_t)p->bytes;
-                J->dst = payload_dev + p->off_data;
-                J->size_out = fsize + fj;
-                p->fs_data = (size_t)fj++;
-            }
         }
     }
     /* per-wave tile lists: direct items run in wave 0, momentum items in the
@@ -701,8 +680,6 @@ int mc_compress_grouped(MomentumCompressor *mc, BatchItem *items, size_t n, cons
         L.nmom_tiles = wave_nm[w];
         L.tiles = tiles;
         L.tile_poff = poff;
-        L.frames = (w == nwaves - 1) ? dfr : NULL;
-        L.nframes = (w == nwaves - 1) ? fj : 0;
         int k = mc_launch_encode(&L, st, tr);
         if (k < 0) {
             free(wave_na);
@@ -719,11 +696,8 @@ int mc_compress_grouped(MomentumCompressor *mc, BatchItem *items, size_t n, cons
     mc->total_launches += mc->last_launches;
 
     /* ------------------------------------------------- results to host */
-    mc_enc_result *hres = (mc_enc_result *)scratch_host(&mc->scratch, SH_RESULTS,
-                                                        n * sizeof(mc_enc_result) + (size_t)(fj + 1) * 8);
-    int64_t *hfs = (int64_t *)((uint8_t *)hres + n * sizeof(mc_enc_result));
+    mc_enc_result *hres = (mc_enc_result *)scratch_host(&mc->scratch, SH_RESULTS, n * sizeof(mc_enc_result));
     cudaMemcpyAsync(hres, results, n * sizeof(mc_enc_result), cudaMemcpyDeviceToHost, st);
-    if (fj) cudaMemcpyAsync(hfs, fsize, (size_t)fj * 8, cudaMemcpyDeviceToHost, st);
     if (host_arena)
         cudaMemcpyAsync(host_arena->ptr, payload_dev, arena_bytes, cudaMemcpyDeviceToHost, st);
     prof_mark(&prof, "launch");
@@ -736,64 +710,52 @@ int mc_compress_grouped(MomentumCompressor *mc, BatchItem *items, size_t n, cons
         goto fail;
     }
 
-    /* libzstd frame mode: frames written on the host from device contents */
+    /* libzstd frame mode: the GPU frames (now in the host arena) are
+     * decoded and written again by libzstd level 10, byte-identical to the
+     * reference's frames */
     if (mc->frame_mode == MC_FRAME_LIBZSTD) {
         if (!zf_libzstd_available()) {
             rc = ERROR_COMPRESSION;
             mc_set_error(mc, "Batch compress: libzstd frame mode requested but libzstd.so.1 is missing");
             goto fail;
         }
-        size_t need = 0;
+        uint8_t *ha = (uint8_t *)host_arena->ptr;
+        size_t tmp_cap = 0;
         for (size_t i = 0; i < n; i++) {
-            if (P[i].kind == MC_K_MOMENTUM) need += 2 * ((P[i].K + 7) / 8) + 8;
-            else if (P[i].kind == MC_K_FRAME) need += P[i].bytes + 8;
+            size_t need = P[i].kind == MC_K_MOMENTUM ? (P[i].K + 7) / 8 : (P[i].kind == MC_K_FRAME ? P[i].bytes : 0);
+            if (need > tmp_cap) tmp_cap = need;
         }
-        uint8_t *hb = (uint8_t *)malloc(need ? need : 1);
-        if (!hb) {
+        uint8_t *tmp = (uint8_t *)malloc(tmp_cap + 16);
+        if (!tmp) {
             rc = ERROR_ALLOCATION;
             goto fail;
         }
-        size_t o = 0;
-        for (size_t i = 0; i < n; i++) {
-            if (P[i].kind == MC_K_MOMENTUM) {
-                size_t c = (P[i].K + 7) / 8;
-                cudaMemcpy(hb + o, hit[i].bm_words, c, cudaMemcpyDeviceToHost);
-                cudaMemcpy(hb + o + c, hit[i].sign_words, c, cudaMemcpyDeviceToHost);
-                o += 2 * c + 8;
-            } else if (P[i].kind == MC_K_FRAME) {
-                cudaMemcpy(hb + o, P[i].dev_in, P[i].bytes, cudaMemcpyDeviceToHost);
-                o += P[i].bytes + 8;
-            }
-        }
-        o = 0;
-        uint8_t *ha = (uint8_t *)host_arena->ptr;
-        for (size_t i = 0; i < n; i++) {
+        int bad = 0;
+        for (size_t i = 0; i < n && !bad; i++) {
             cplan *p = &P[i];
+            size_t got = 0;
             if (p->kind == MC_K_MOMENTUM) {
-                size_t c = (p->K + 7) / 8;
-                size_t sb = (size_t)(hres[i].P + 7) / 8;
-                size_t a = zf_libzstd_compress(ha + p->off_bm, p->cap_bm, hb + o, c, 10);
-                size_t b = hres[i].P ? zf_libzstd_compress(ha + p->off_sg, p->cap_sg, hb + o + c, sb, 10) : 0;
-                if (!a || (hres[i].P && !b)) {
-                    free(hb);
-                    rc = ERROR_COMPRESSION;
-                    goto fail;
+                bad |= zf_decode_host(ha + p->off_bm, (size_t)hres[i].bm_size, tmp, tmp_cap + 16, &got) != 0;
+                p->fs_bm = bad ? 0 : zf_libzstd_compress(ha + p->off_bm, p->cap_bm, tmp, got, 10);
+                bad |= p->fs_bm == 0;
+                if (!bad && hres[i].sg_size) {
+                    bad |= zf_decode_host(ha + p->off_sg, (size_t)hres[i].sg_size, tmp, tmp_cap + 16, &got) != 0;
+                    p->fs_sg = bad ? 0 : zf_libzstd_compress(ha + p->off_sg, p->cap_sg, tmp, got, 10);
+                    bad |= p->fs_sg == 0;
                 }
-                p->fs_bm = a;   /* reuse as sizes */
-                p->fs_sg = b;
-                o += 2 * c + 8;
             } else if (p->kind == MC_K_FRAME) {
-                size_t a = zf_libzstd_compress(ha + p->off_data, p->cap_data, hb + o, p->bytes, 10);
-                if (!a) {
-                    free(hb);
-                    rc = ERROR_COMPRESSION;
-                    goto fail;
-                }
-                p->fs_data = a;
-                o += p->bytes + 8;
+                size_t fsz = MC_ZHDR + 3 * frame_blocks(p->bytes) + p->bytes;
+                bad |= zf_decode_host(ha + p->off_data, fsz, tmp, tmp_cap + 16, &got) != 0;
+                p->fs_data = bad ? 0 : zf_libzstd_compress(ha + p->off_data, p->cap_data, tmp, got, 10);
+                bad |= p->fs_data == 0;
             }
         }
-        free(hb);
+        free(tmp);
+        if (bad) {
+            rc = ERROR_COMPRESSION;
+            mc_set_error(mc, "Batch compress: libzstd framing failed");
+            goto fail;
+        }
     }
 
     /* -------------------------------------------- CompressedLayerData out */
@@ -832,11 +794,11 @@ int mc_compress_grouped(MomentumCompressor *mc, BatchItem *items, size_t n, cons
             c->data = base + p->off_data;
             if (p->kind == MC_K_MOMENTUM || p->kind == MC_K_QUANT) c->data_size = residual_bytes(p->dcodec, p->n);
             else if (p->kind == MC_K_COPY) c->data_size = p->bytes;
-            else c->data_size = libz ? p->fs_data : (size_t)hfs[p->fs_data];
+            else c->data_size = libz ? p->fs_data : MC_ZHDR + 3 * frame_blocks(p->bytes) + p->bytes;
             if (p->kind == MC_K_MOMENTUM) {
                 c->bitmap = base + p->off_bm;
-                c->bitmap_size = libz ? p->fs_bm : (size_t)hfs[p->fs_bm];
-                size_t sgs = libz ? p->fs_sg : (size_t)hfs[p->fs_sg];
+                c->bitmap_size = libz ? p->fs_bm : (size_t)r->bm_size;
+                size_t sgs = libz ? p->fs_sg : (size_t)r->sg_size;
                 c->dominant_signs = sgs ? base + p->off_sg : NULL;
                 c->dominant_signs_size = sgs;
                 c->num_predicted_kernels = (int)r->P;
@@ -922,6 +884,7 @@ typedef struct {
     int tile_base, ntiles, tile_param;
     int bm_mode, sg_mode;     /* MC_BM_* */
     int data_mode;            /* lossless frame: MC_BM_* */
+    size_t sg_len;            /* sign content bytes of a Raw-block sign frame */
     int foreign;              /* a frame lives in device memory the library does not own */
     const char *why;
 } dplan;
@@ -1018,6 +981,26 @@ static void dplan_item(MomentumCompressor *mc, dplan *d, const BatchItem *it, co
         /* direct tensor through the quantiser */
     }
     d->ok = 1;
+}
+
+/* In-place reading mode of a frame of `size` bytes whose content is known to
+ * be `content` bytes: all Raw blocks, all RLE blocks, or neither. */
+static int frame_mode_for(size_t size, size_t content, int inplace) {
+    if (!inplace) return MC_BM_WORDS;
+    const size_t nb = frame_blocks(content);
+    if (size == MC_ZHDR + 3 * nb + content) return MC_BM_RAW;
+    if (content >= 2 && size == MC_ZHDR + 4 * nb) return MC_BM_RLE;
+    return MC_BM_WORDS;
+}
+
+/* Content bytes of an all-Raw frame of `size` bytes, or 0 when no content
+ * length fits that size. */
+static size_t sign_content_len(size_t size) {
+    if (size <= MC_ZHDR + 3) return 0;
+    const size_t nb = (size - MC_ZHDR + MC_ZBLOCK + 2) / (MC_ZBLOCK + 3);
+    if (nb == 0 || size < MC_ZHDR + 3 * nb) return 0;
+    const size_t s = size - MC_ZHDR - 3 * nb;
+    return (s > 0 && frame_blocks(s) == nb) ? s : 0;
 }
 
 #define DEC_RETRY_EXPAND 1
@@ -1179,18 +1162,14 @@ static int dec_segment(MomentumCompressor *mc, const BatchItem *items, size_t n,
             d->ntiles = (int)((d->K + (size_t)d->tile_param - 1) / (size_t)d->tile_param);
             nmom_tiles += d->ntiles;
             size_t wb = ALIGN_UP(((d->K + 31) / 32 + 1) * 4 + 4096, 256);
-            /* Frames of one Raw / RLE block are read in place (the kernel
-             * checks the header it relies on; a mismatch re-runs the segment
-             * with expansion).  Everything else is expanded first. */
+            /* Frames made only of Raw blocks, or only of RLE blocks, are read
+             * in place (the kernel checks every header it relies on; a
+             * mismatch re-runs the segment with expansion); anything else is
+             * expanded first.  In place only inside library-owned or staged
+             * memory: a word read may touch up to 3 bytes past the frame. */
             const size_t c = (d->K + 7) / 8;
-            d->bm_mode = MC_BM_WORDS;
-            /* in place only inside library-owned or staged memory: a word read
-             * may touch up to 3 bytes past the frame, inside the slot padding */
             const int inplace = !force_expand && !d->foreign;
-            if (inplace && c >= 2 && d->bm_size == 12 + c && ((uintptr_t)d->d_bm & 3) == 0)
-                d->bm_mode = MC_BM_RAW1;
-            else if (inplace && c >= 2 && d->bm_size == 13)
-                d->bm_mode = MC_BM_RLE1;
+            d->bm_mode = frame_mode_for(d->bm_size, c, inplace);
             if (d->bm_mode == MC_BM_WORDS) {
                 d->c_bm_off = content_bytes;
                 content_bytes += wb;
@@ -1198,7 +1177,8 @@ static int dec_segment(MomentumCompressor *mc, const BatchItem *items, size_t n,
             }
             d->sg_mode = MC_BM_WORDS;
             if (d->d_sg) {
-                if (inplace && d->sg_size > 13) d->sg_mode = MC_BM_RAW1;
+                d->sg_len = sign_content_len(d->sg_size);
+                if (inplace && d->sg_len > 0) d->sg_mode = MC_BM_RAW;
                 if (d->sg_mode == MC_BM_WORDS) {
                     d->c_sg_off = content_bytes;
                     content_bytes += wb;
@@ -1210,9 +1190,7 @@ static int dec_segment(MomentumCompressor *mc, const BatchItem *items, size_t n,
             d->ntiles = (int)((d->bytes + (size_t)d->tile_param - 1) / (size_t)d->tile_param);
             d->data_mode = MC_BM_WORDS;
             if (d->data_frame) {
-                const int inplace = !force_expand && !d->foreign;
-                if (inplace && d->data_size == 12 + d->bytes) d->data_mode = MC_BM_RAW1;
-                else if (inplace && d->bytes >= 2 && d->data_size == 13) d->data_mode = MC_BM_RLE1;
+                d->data_mode = frame_mode_for(d->data_size, d->bytes, !force_expand && !d->foreign);
                 if (d->data_mode == MC_BM_WORDS) {
                     d->c_data_off = content_bytes;
                     content_bytes += ALIGN_UP(d->bytes + 16, 256);
@@ -1298,7 +1276,7 @@ static int dec_segment(MomentumCompressor *mc, const BatchItem *items, size_t n,
         if (d->data_frame && d->data_mode != MC_BM_WORDS) {
             I->data_mode = d->data_mode;
             I->data_frame = d->d_data;
-            I->data = d->d_data + 12;
+            I->data = d->d_data + MC_ZHDR + 3;
         }
         if (d->j_data >= 0) {
             mc_unframe_job *J = &h_jobs[d->j_data];
@@ -1336,7 +1314,6 @@ static int dec_segment(MomentumCompressor *mc, const BatchItem *items, size_t n,
                 I->bm_len_ptr = d_lens + d->j_bm;
             } else {
                 I->bm_frame = d->d_bm;
-                I->bm_words = (const uint32_t *)(d->d_bm + 12);
             }
             if (d->j_sg >= 0) {
                 mc_unframe_job *J = &h_jobs[d->j_sg];
@@ -1347,10 +1324,9 @@ static int dec_segment(MomentumCompressor *mc, const BatchItem *items, size_t n,
                 J->content_out = d_lens + d->j_sg;
                 I->sg_bytes = content + d->c_sg_off;
                 I->sg_len_ptr = d_lens + d->j_sg;
-            } else if (d->sg_mode == MC_BM_RAW1) {
+            } else if (d->sg_mode == MC_BM_RAW) {
                 I->sg_frame = d->d_sg;
-                I->sg_bytes = d->d_sg + 12;
-                I->sg_len = (int64_t)d->sg_size - 12;
+                I->sg_len = (int64_t)d->sg_len;
             }
         }
         {

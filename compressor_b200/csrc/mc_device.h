@@ -42,10 +42,15 @@ typedef struct {
     const float *mem_in;    /* MOMENTUM: committed prediction memory, NULL = zeros */
     float *mem_out;         /* MOMENTUM: new prediction memory */
     void *hist_out;         /* copy of the input for the new history head, or NULL */
-    uint8_t *data_out;      /* payload data slot */
+    uint8_t *data_out;      /* payload data slot (FRAME: the zstd frame) */
+    uint8_t *bm_frame;      /* MOMENTUM: bitmap zstd frame slot */
+    uint8_t *sg_frame;      /* MOMENTUM: dominant-sign zstd frame slot */
+    int64_t sg_cap;         /* bytes of the sign frame slot */
     uint32_t *bm_words;     /* MOMENTUM: bitmap content, ceil(K/32) words */
     uint32_t *dom_words;    /* MOMENTUM: dominant sign per kernel, ceil(K/32) words */
-    uint32_t *sign_words;   /* MOMENTUM: dense sign content, zeroed, ceil(K/32) words */
+    uint32_t *blk_pos;      /* MOMENTUM: frame offset of each bitmap block's content (~0 = RLE) */
+    int32_t max_blocks;     /* MOMENTUM: capacity of blk_pos */
+    int32_t pad_e;
     int64_t n;              /* elements */
     int64_t K;              /* kernels (MOMENTUM) */
     int32_t ks;             /* kernel size h*w (MOMENTUM) */
@@ -78,19 +83,13 @@ typedef struct {
     float pad0;
     int64_t P;              /* predicted kernels */
     int64_t mism;           /* sign mismatches over predicted elements */
+    int64_t bm_size;        /* bitmap frame bytes */
+    int64_t sg_size;        /* sign frame bytes (0 when no kernel is predicted) */
     uint32_t ticket[4];     /* last-CTA election per pass; zeroed before launch */
     int32_t err;
     int32_t pad1;
 } mc_enc_result;
 
-/* One zstd frame to write from device content. */
-typedef struct {
-    const uint8_t *src;
-    int64_t size;               /* content bytes, or -1: ceil(P/8) of *P_src */
-    const int64_t *P_src;
-    uint8_t *dst;
-    int64_t *size_out;          /* frame bytes written */
-} mc_frame_job;
 
 typedef struct {
     const mc_enc_item *items;   /* device */
@@ -103,8 +102,6 @@ typedef struct {
     int32_t nmom_tiles;
     mc_enc_tile *tiles;         /* device scratch, one per tile id */
     int64_t *tile_poff;         /* device scratch, ntiles */
-    const mc_frame_job *frames; /* device */
-    int32_t nframes;
 } mc_enc_launch;
 
 /* ---------------------------------------------------------------- decode */
@@ -115,11 +112,18 @@ enum {
     MC_D_COPY = 3           /* direct, bytes copied (raw floats or lossless content) */
 };
 
-/* How the decoder reads a bitmap / sign payload. */
+/* zstd framing shared by encoder and decoder: single-segment frame header
+ * (magic, descriptor 0xA0 and a 4-byte content size: 9 bytes), then blocks of
+ * at most 2^17 content bytes, each behind a 3-byte block header. */
+#define MC_ZBLOCK_LOG2 17
+#define MC_ZBLOCK (1 << MC_ZBLOCK_LOG2)
+#define MC_ZHDR 9
+
+/* How the decoder reads a bitmap / sign / lossless payload. */
 enum {
     MC_BM_WORDS = 0,        /* contiguous content (expanded, or staged content) */
-    MC_BM_RAW1 = 1,         /* zstd frame, one Raw block, content read in place at +12 */
-    MC_BM_RLE1 = 2          /* zstd frame, one RLE block, the repeated byte at +12 */
+    MC_BM_RAW = 1,          /* zstd frame of Raw blocks, read in place */
+    MC_BM_RLE = 2           /* zstd frame of RLE blocks, read in place */
 };
 
 typedef struct {

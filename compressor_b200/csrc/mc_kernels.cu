@@ -254,11 +254,100 @@ __device__ int64_t scan_tile_counts(const int32_t *cnt, int stride_words, int ba
     return carry;
 }
 
+// ------------------------------------------------------------------ frames
+// zstd frames are written in place by the passes: header (magic, descriptor
+// 0xA0 = single segment + 4-byte content size), then blocks of at most 2^17
+// content bytes behind 3-byte headers (bit 0 last, bits 1-2 type: 0 Raw,
+// 1 RLE, bits 3.. size).  Content byte b of an all-Raw frame sits at
+// frame + MC_ZHDR + 3 + b + 3 * (b >> 17).
+#define MAX_RLE_BLOCKS 64
+
+__device__ __forceinline__ int64_t fpos_raw(int64_t b) {
+    return MC_ZHDR + 3 + b + 3 * (b >> MC_ZBLOCK_LOG2);
+}
+__device__ __forceinline__ int64_t fpos_rle(int64_t b) { return MC_ZHDR + 3 + 4 * (b >> MC_ZBLOCK_LOG2); }
+__device__ __forceinline__ int64_t nblocks_of(int64_t c) {
+    return c == 0 ? 1 : (c + MC_ZBLOCK - 1) >> MC_ZBLOCK_LOG2;
+}
+
+__device__ __forceinline__ void put_frame_header(uint8_t *f, int64_t content) {
+    f[0] = 0x28; f[1] = 0xB5; f[2] = 0x2F; f[3] = 0xFD;
+    f[4] = 0xA0;
+    for (int i = 0; i < 4; i++) f[5 + i] = (uint8_t)((uint64_t)content >> (8 * i));
+}
+__device__ __forceinline__ void put_block_header(uint8_t *p, bool last, int type, int64_t size) {
+    const uint32_t h = (last ? 1u : 0u) | ((uint32_t)type << 1) | ((uint32_t)size << 3);
+    p[0] = (uint8_t)h;
+    p[1] = (uint8_t)(h >> 8);
+    p[2] = (uint8_t)(h >> 16);
+}
+
+// Headers of the bitmap frame (one block per 2^20 kernels; a block whose
+// kernels are all predicted or all not predicted becomes an RLE block of
+// 0xFF / 0x00, decided from the per-tile predicted counts) and of the
+// dominant-sign frame (Raw blocks; none when no kernel is predicted).
+// Whole block participates; runs in the last CTA of pass 1.
+__device__ void write_frame_headers(const mc_enc_item &I, const mc_enc_launch &L, mc_enc_result *R, int64_t P,
+                                    int *s_blk) {
+    const int64_t c = (I.K + 7) >> 3;
+    const int64_t nb = nblocks_of(c);
+    const bool plan_rle = nb <= MAX_RLE_BLOCKS;
+    if (plan_rle) {
+        for (int j = threadIdx.x; j < MAX_RLE_BLOCKS; j += TPB) s_blk[j] = 0;
+        __syncthreads();
+        for (int i = threadIdx.x; i < I.ntiles; i += TPB) {
+            const int64_t k0 = (int64_t)i * I.tile_kernels;
+            atomicAdd(&s_blk[k0 >> (MC_ZBLOCK_LOG2 + 3)], __ldcg(&L.tiles[I.tile_base + i].P));
+        }
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) {
+        uint8_t *f = I.bm_frame;
+        put_frame_header(f, c);
+        int64_t pos = MC_ZHDR;
+        for (int64_t j = 0; j < nb; j++) {
+            const int64_t b0 = j << MC_ZBLOCK_LOG2;
+            const int64_t bytes = c == 0 ? 0 : min((int64_t)MC_ZBLOCK, c - b0);
+            const int64_t kern = min(I.K, (b0 + bytes) * 8) - b0 * 8;
+            int rle = -1;
+            if (plan_rle && bytes > 1) {
+                const int pj = s_blk[j];
+                if (pj == kern && (kern & 7) == 0) rle = 0xFF;
+                else if (pj == 0) rle = 0;
+            }
+            put_block_header(f + pos, j == nb - 1, rle >= 0 ? 1 : 0, bytes);
+            if (rle >= 0) {
+                f[pos + 3] = (uint8_t)rle;
+                if (j < I.max_blocks) I.blk_pos[j] = 0xFFFFFFFFu;
+                pos += 4;
+            } else {
+                if (j < I.max_blocks) I.blk_pos[j] = (uint32_t)(pos + 3);
+                pos += 3 + bytes;
+            }
+        }
+        R->bm_size = pos;
+        if (P == 0) {
+            R->sg_size = 0;
+        } else {
+            const int64_t s = (P + 7) >> 3;
+            const int64_t ns = nblocks_of(s);
+            uint8_t *g = I.sg_frame;
+            put_frame_header(g, s);
+            for (int64_t j = 0; j < ns; j++) {
+                const int64_t bytes = min((int64_t)MC_ZBLOCK, s - (j << MC_ZBLOCK_LOG2));
+                put_block_header(g + MC_ZHDR + j * (MC_ZBLOCK + 3), j == ns - 1, 0, bytes);
+            }
+            R->sg_size = MC_ZHDR + 3 * ns + s;
+        }
+    }
+}
+
 // ------------------------------------------------------------------ pass 1
 __global__ void __launch_bounds__(TPB) k_enc_pass1(mc_enc_launch L) {
     __shared__ Red red;
     __shared__ int s_flag;
     __shared__ int scan_sh[NWARP + 1];
+    __shared__ int s_blk[MAX_RLE_BLOCKS + 1];
     const int gt = L.all_tiles[blockIdx.x];
     const int ii = L.tile_item[gt];
     const mc_enc_item I = L.items[ii];
@@ -287,6 +376,13 @@ __global__ void __launch_bounds__(TPB) k_enc_pass1(mc_enc_launch L) {
                 }
             }
             if (hist) st4(hist, g, tr.e1, I.vec, c);
+        }
+        {   // this tile's share of zeroing the sign frame slot (pass 4 ORs bits into it)
+            const int64_t nq = I.sg_cap >> 4;
+            const int64_t per = (nq + I.ntiles - 1) / I.ntiles;
+            const int64_t q1 = min(nq, (int64_t)(t + 1) * per);
+            for (int64_t q = (int64_t)t * per + threadIdx.x; q < q1; q += TPB)
+                ((uint4 *)I.sg_frame)[q] = make_uint4(0u, 0u, 0u, 0u);
         }
         // per-kernel sign consistency: one lane per kernel, 32 kernels per ballot word
         const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -343,6 +439,7 @@ __global__ void __launch_bounds__(TPB) k_enc_pass1(mc_enc_launch L) {
             block_reduce(red, a, 2, tmn, tmx, t2, z, 0);
             const int64_t total = scan_tile_counts(&L.tiles[0].P, (int)(sizeof(mc_enc_tile) / 4),
                                                    I.tile_base, I.ntiles, L.tile_poff, scan_sh);
+            write_frame_headers(I, L, R, total, s_blk);
             if (threadIdx.x == 0) {
                 const double dn = (double)I.n;
                 R->cm = __double2float_rn(__ddiv_rn(a[0], dn));
@@ -358,11 +455,45 @@ __global__ void __launch_bounds__(TPB) k_enc_pass1(mc_enc_launch L) {
     // direct items: element tiles (byte tiles for COPY / FRAME)
     const int64_t e0 = (int64_t)t * I.tile_kernels;
     const int64_t e1 = min(e0 + (int64_t)I.tile_kernels, I.n);
-    if (I.kind == MC_K_COPY || I.kind == MC_K_FRAME) {
-        // raw payload ("sz3_memcpy") and/or history copy of the input bytes
+    if (I.kind == MC_K_FRAME) {
+        // lossless payload: history copy plus an all-Raw zstd frame of the
+        // input bytes (tiles of 2^15 bytes never straddle a 2^17-byte block)
         const uint8_t *src = (const uint8_t *)I.cur;
         uint8_t *hist = (uint8_t *)I.hist_out;
-        uint8_t *raw = I.kind == MC_K_COPY ? I.data_out : nullptr;
+        uint8_t *fr = I.data_out;
+        if (t == 0 && threadIdx.x == 0) {
+            const int64_t nb = nblocks_of(I.n);
+            put_frame_header(fr, I.n);
+            for (int64_t j = 0; j < nb; j++)
+                put_block_header(fr + MC_ZHDR + j * (MC_ZBLOCK + 3), j == nb - 1, 0,
+                                 I.n == 0 ? 0 : min((int64_t)MC_ZBLOCK, I.n - (j << MC_ZBLOCK_LOG2)));
+        }
+        uint8_t *dst = fr + fpos_raw(e0) - e0;   // frame position of byte e of this tile: dst + e
+        if (((((uintptr_t)src | (uintptr_t)hist) & 3) == 0) && (((uintptr_t)(dst + e0)) & 3) == 0) {
+            for (int64_t w = (e0 >> 2) + threadIdx.x; w < (e1 >> 2); w += TPB) {
+                const uint32_t x = ((const uint32_t *)src)[w];
+                if (hist) ((uint32_t *)hist)[w] = x;
+                *(uint32_t *)(dst + 4 * w) = x;
+            }
+            for (int64_t e = (e1 & ~(int64_t)3) + threadIdx.x; e < e1; e += TPB) {
+                const uint8_t x = src[e];
+                if (hist) hist[e] = x;
+                dst[e] = x;
+            }
+        } else {
+            for (int64_t e = e0 + threadIdx.x; e < e1; e += TPB) {
+                const uint8_t x = src[e];
+                if (hist) hist[e] = x;
+                dst[e] = x;
+            }
+        }
+        return;
+    }
+    if (I.kind == MC_K_COPY) {
+        // raw payload ("sz3_memcpy") and history copy of the input bytes
+        const uint8_t *src = (const uint8_t *)I.cur;
+        uint8_t *hist = (uint8_t *)I.hist_out;
+        uint8_t *raw = I.data_out;
         if (I.vec) {   // 16-byte aligned base pointers; tiles are multiples of 16 bytes
             const int64_t v0 = e0 >> 4, v1 = e1 >> 4;
             for (int64_t v = v0 + threadIdx.x; v < v1; v += TPB) {
@@ -582,6 +713,7 @@ __device__ __forceinline__ void put_codes(uint8_t *data_out, int codec, int64_t 
 // ------------------------------------------------------------------ pass 4
 __global__ void __launch_bounds__(TPB) k_enc_pass4(mc_enc_launch L) {
     __shared__ int scan_sh[NWARP + 1];
+    __shared__ uint32_t s_sg[TPB + 2];
     const int gt = L.all_tiles[blockIdx.x];
     const int ii = L.tile_item[gt];
     const mc_enc_item I = L.items[ii];
@@ -604,23 +736,62 @@ __global__ void __launch_bounds__(TPB) k_enc_pass4(mc_enc_launch L) {
                 r[j] = ((qb.f >> j) & 1u) ? mom_residual(c[j], m[j], (qb.pos >> j) & 1u, mp) : c[j];
             put_codes(I.data_out, I.codec, g, tr.e1, I.vec, r, scale, qm);
         }
-        // dense dominant signs of predicted kernels (ref :2258-2283)
+        // bitmap content of this tile into its block of the bitmap frame
+        // (ref :2222-2253; RLE blocks were written whole by pass 1)
+        {
+            const int64_t c = (I.K + 7) >> 3;
+            const int64_t cb0 = tr.k0 >> 3, cb1 = min((tr.k1 + 7) >> 3, c);
+            const uint32_t pos = I.blk_pos[tr.k0 >> (MC_ZBLOCK_LOG2 + 3)];
+            if (pos != 0xFFFFFFFFu) {
+                uint8_t *dst = I.bm_frame + pos - ((cb0 >> MC_ZBLOCK_LOG2) << MC_ZBLOCK_LOG2);  // + cb
+                const uint8_t *srcb = (const uint8_t *)I.bm_words;
+                if ((((uintptr_t)(dst + cb0)) & 3) == 0) {
+                    for (int64_t w = (cb0 >> 2) + threadIdx.x; 4 * w < cb1; w += TPB) {
+                        if (4 * w + 4 <= cb1) *(uint32_t *)(dst + 4 * w) = I.bm_words[w];
+                        else
+                            for (int64_t b = 4 * w; b < cb1; b++) dst[b] = srcb[b];
+                    }
+                } else {
+                    for (int64_t b = cb0 + threadIdx.x; b < cb1; b += TPB) dst[b] = srcb[b];
+                }
+            }
+        }
+        // dense dominant signs of predicted kernels (ref :2258-2283): the
+        // tile's bits are assembled in shared memory, then written into the
+        // sign frame; the two edge bytes shared with neighbour tiles are ORed
         const int64_t wb = tr.k0 >> 5, we = (tr.k1 + 31) >> 5;
         const int i = threadIdx.x;
+        s_sg[i] = 0u;
+        if (i < 2) s_sg[TPB + i] = 0u;
         uint32_t mw = 0, dv = 0;
         if (wb + i < we) {
             mw = I.bm_words[wb + i];
             dv = I.dom_words[wb + i];
         }
         const int pc = __popc(mw);
-        const int off_l = block_excl_scan(pc, scan_sh, nullptr);
+        int tot;
+        const int off_l = block_excl_scan(pc, scan_sh, &tot);   // also orders the zeroing above
+        const int64_t poff = L.tile_poff[gt];
         if (pc) {
-            const int64_t off = L.tile_poff[gt] + off_l;
             const uint32_t bits = pext32(dv, mw);
-            const int64_t w0 = off >> 5;
-            const int sh = (int)(off & 31);
-            atomicOr(&I.sign_words[w0], bits << sh);
-            if (sh + pc > 32) atomicOr(&I.sign_words[w0 + 1], bits >> (32 - sh));
+            const int lb = (int)(poff & 7) + off_l;
+            const int sh = lb & 31;
+            atomicOr(&s_sg[lb >> 5], bits << sh);
+            if (sh + pc > 32) atomicOr(&s_sg[(lb >> 5) + 1], bits >> (32 - sh));
+        }
+        __syncthreads();
+        if (tot > 0) {
+            const int64_t cb0 = poff >> 3;
+            const int64_t nbytes = ((poff + tot - 1) >> 3) - cb0 + 1;
+            for (int64_t j = threadIdx.x; j < nbytes; j += TPB) {
+                const uint32_t v = (s_sg[j >> 2] >> (8 * (j & 3))) & 0xFFu;
+                const int64_t fb = fpos_raw(cb0 + j);
+                if (j == 0 || j == nbytes - 1) {
+                    if (v) atomicOr((uint32_t *)(I.sg_frame + (fb & ~(int64_t)3)), v << (8 * (fb & 3)));
+                } else {
+                    I.sg_frame[fb] = (uint8_t)v;
+                }
+            }
         }
         return;
     }
@@ -647,63 +818,6 @@ __device__ __forceinline__ void copy_bytes(uint8_t *dst, const uint8_t *src, int
     } else {
         for (int64_t i = threadIdx.x; i < n; i += TPB) dst[i] = src[i];
     }
-}
-
-// zstd frame (RFC 8878) with a single-segment header, 4- or 8-byte content
-// size, and Raw / RLE blocks of at most 128 KiB.
-__global__ void __launch_bounds__(TPB) k_frames(const mc_frame_job *jobs) {
-    const mc_frame_job &J = jobs[blockIdx.x];
-    int64_t size = J.size;
-    if (size < 0) {
-        const int64_t P = *J.P_src;
-        if (P == 0) {
-            if (threadIdx.x == 0) *J.size_out = 0;
-            return;
-        }
-        size = (P + 7) >> 3;
-    }
-    uint8_t *dst = J.dst;
-    const bool big = size >= (int64_t)0xFFFFFFFFll;
-    int64_t pos = big ? 13 : 9;
-    if (threadIdx.x == 0) {
-        dst[0] = 0x28; dst[1] = 0xB5; dst[2] = 0x2F; dst[3] = 0xFD;
-        dst[4] = big ? 0xE0 : 0xA0;   // FCS flag 3/2, single segment
-        const int nb = big ? 8 : 4;
-        for (int i = 0; i < nb; i++) dst[5 + i] = (uint8_t)((uint64_t)size >> (8 * i));
-    }
-    const int64_t nblk = size == 0 ? 1 : (size + ZBLOCK - 1) / ZBLOCK;
-    for (int64_t b = 0; b < nblk; b++) {
-        const int64_t bs = min((int64_t)ZBLOCK, size - b * ZBLOCK);
-        const uint8_t *src = J.src + b * ZBLOCK;
-        int eq = 1;
-        if (bs > 1) {
-            const uint8_t first = src[0];
-            if (((uintptr_t)src & 3) == 0) {
-                const uint32_t w4 = first * 0x01010101u;
-                const int64_t nw = bs >> 2;
-                for (int64_t i = threadIdx.x; i < nw; i += TPB) eq &= ((const uint32_t *)src)[i] == w4;
-                for (int64_t i = (nw << 2) + threadIdx.x; i < bs; i += TPB) eq &= src[i] == first;
-            } else {
-                for (int64_t i = threadIdx.x; i < bs; i += TPB) eq &= (src[i] == first);
-            }
-        }
-        const int rle = (bs > 1) && __syncthreads_and(eq);
-        const uint32_t last = (b == nblk - 1) ? 1u : 0u;
-        const uint32_t hdr = last | ((uint32_t)(rle ? 1 : 0) << 1) | ((uint32_t)bs << 3);
-        if (threadIdx.x == 0) {
-            dst[pos] = (uint8_t)hdr;
-            dst[pos + 1] = (uint8_t)(hdr >> 8);
-            dst[pos + 2] = (uint8_t)(hdr >> 16);
-            if (rle) dst[pos + 3] = src[0];
-        }
-        if (!rle) {
-            copy_bytes(dst + pos + 3, src, bs);
-            pos += 3 + bs;
-        } else {
-            pos += 4;
-        }
-    }
-    if (threadIdx.x == 0) *J.size_out = pos;
 }
 
 // ------------------------------------------------------------------ unframe
@@ -813,9 +927,22 @@ __device__ __forceinline__ int64_t dec_bm_bits(const mc_dec_item &I) {
     return min(len * 8, I.K);
 }
 
-// Bitmap word w (unmasked).
+// Content byte b of a payload read in place (Raw / RLE frames) or from
+// contiguous content.
+__device__ __forceinline__ uint32_t src_byte(const uint8_t *p, int mode, int64_t b) {
+    if (mode == MC_BM_RAW) return p[fpos_raw(b)];
+    if (mode == MC_BM_RLE) return p[fpos_rle(b)];
+    return p[b];
+}
+
+// Bitmap word w (unmasked).  The 4 bytes of a word never straddle a block.
 __device__ __forceinline__ uint32_t dec_bm_word(const mc_dec_item &I, int64_t w) {
-    if (I.bm_mode == MC_BM_RLE1) return (uint32_t)I.bm_frame[12] * 0x01010101u;
+    if (I.bm_mode == MC_BM_RLE) return src_byte(I.bm_frame, MC_BM_RLE, 4 * w) * 0x01010101u;
+    if (I.bm_mode == MC_BM_RAW) {
+        const uint8_t *q = I.bm_frame + fpos_raw(4 * w);
+        if ((((uintptr_t)q) & 3) == 0) return *(const uint32_t *)q;
+        return (uint32_t)q[0] | ((uint32_t)q[1] << 8) | ((uint32_t)q[2] << 16) | ((uint32_t)q[3] << 24);
+    }
     return I.bm_words[w];
 }
 
@@ -823,15 +950,23 @@ __device__ __forceinline__ uint32_t le32(const uint8_t *p) {
     return (uint32_t)p[0] | ((uint32_t)p[1] << 8) | ((uint32_t)p[2] << 16) | ((uint32_t)p[3] << 24);
 }
 
-// Checks that an in-place frame is what the host assumed: single-segment
-// header with a 4-byte content size, then one last block of the given type
-// whose size equals the content size.  Returns the content size or -1.
-__device__ int64_t check_frame1(const uint8_t *f, int type, int64_t want) {
+// Checks that a frame read in place is what the host assumed: descriptor
+// 0xA0 with a 4-byte content size (equal to `want` when want >= 0), then
+// blocks of 2^17 bytes (the last one shorter), all of one type, the last
+// one flagged.  Returns the content size or -1.  One thread.
+__device__ int64_t check_frame(const uint8_t *f, int mode, int64_t want) {
     if (f[0] != 0x28 || f[1] != 0xB5 || f[2] != 0x2F || f[3] != 0xFD || f[4] != 0xA0) return -1;
     const int64_t cs = le32(f + 5);
-    const uint32_t h = f[9] | ((uint32_t)f[10] << 8) | ((uint32_t)f[11] << 16);
-    if ((h & 1u) != 1u || (int)((h >> 1) & 3u) != type || (int64_t)(h >> 3) != cs) return -1;
     if (want >= 0 && cs != want) return -1;
+    const int64_t nb = nblocks_of(cs);
+    const int type = mode == MC_BM_RAW ? 0 : 1;
+    for (int64_t j = 0; j < nb; j++) {
+        const uint8_t *p = f + MC_ZHDR + j * (mode == MC_BM_RAW ? (int64_t)MC_ZBLOCK + 3 : 4);
+        const uint32_t h = p[0] | ((uint32_t)p[1] << 8) | ((uint32_t)p[2] << 16);
+        const int64_t bytes = cs == 0 ? 0 : min((int64_t)MC_ZBLOCK, cs - (j << MC_ZBLOCK_LOG2));
+        if ((int)(h & 1u) != (j == nb - 1) || (int)((h >> 1) & 3u) != type || (int64_t)(h >> 3) != bytes)
+            return -1;
+    }
     return cs;
 }
 
@@ -846,10 +981,8 @@ __global__ void __launch_bounds__(TPB) k_dec_prefix(mc_dec_launch L) {
     mc_dec_result *R = L.results + ii;
     if (t == 0 && threadIdx.x == 0) {
         int bad = 0;
-        if (I.bm_mode == MC_BM_RAW1) bad |= check_frame1(I.bm_frame, 0, (I.bm_bits + 7) >> 3) < 0;
-        if (I.bm_mode == MC_BM_RLE1) bad |= check_frame1(I.bm_frame, 1, (I.bm_bits + 7) >> 3) < 0;
-        if (I.sg_mode == MC_BM_RAW1) bad |= check_frame1(I.sg_frame, 0, I.sg_len) < 0;
-        if (I.sg_mode == MC_BM_RLE1) bad |= check_frame1(I.sg_frame, 1, -1) < 0;
+        if (I.bm_mode != MC_BM_WORDS) bad |= check_frame(I.bm_frame, I.bm_mode, (I.bm_bits + 7) >> 3) < 0;
+        if (I.sg_mode != MC_BM_WORDS && I.sg_frame) bad |= check_frame(I.sg_frame, I.sg_mode, I.sg_len) < 0;
         if (bad) R->err = 1;
     }
     const DecTile tr = dec_range(I, t);
@@ -917,18 +1050,12 @@ __global__ void __launch_bounds__(TPB) k_dec_recon(mc_dec_launch L) {
         const int64_t wb = tr.k0 >> 5, we = (tr.k1 + 31) >> 5;
         const int i = threadIdx.x;
         const int64_t bm_bits = dec_bm_bits(I);
-        // sign source: content bytes, or the repeated byte of an RLE frame
-        const uint8_t *sg = I.sg_bytes;
+        // sign source: expanded content, or a frame read in place
+        const uint8_t *sg = I.sg_mode == MC_BM_WORDS ? I.sg_bytes : I.sg_frame;
         int64_t sg_len = I.sg_len;
-        int sg_rle = -1;
         if (I.sg_len_ptr) {
             sg_len = *I.sg_len_ptr;
             if (sg_len < 0) sg = nullptr;
-        }
-        if (I.sg_mode == MC_BM_RLE1) {
-            sg_rle = I.sg_frame[12];
-            sg_len = le32(I.sg_frame + 5);
-            sg = nullptr;
         }
         uint32_t m = 0;
         if (wb + i < we) m = dec_bm_word(I, wb + i) & word_mask(wb + i, bm_bits);
@@ -941,10 +1068,7 @@ __global__ void __launch_bounds__(TPB) k_dec_recon(mc_dec_launch L) {
             while (mm) {
                 const int b = __ffs(mm) - 1;
                 int bit = 1;   // missing signs default to +1 (ref :3296-3302)
-                if ((idx >> 3) < sg_len) {
-                    if (sg) bit = (sg[idx >> 3] >> (idx & 7)) & 1;
-                    else if (sg_rle >= 0) bit = (sg_rle >> (idx & 7)) & 1;
-                }
+                if (sg && (idx >> 3) < sg_len) bit = (src_byte(sg, I.sg_mode, idx >> 3) >> (idx & 7)) & 1;
                 dm |= (uint32_t)bit << b;
                 idx++;
                 mm &= mm - 1;
@@ -1001,18 +1125,19 @@ __global__ void __launch_bounds__(TPB) k_dec_recon(mc_dec_launch L) {
     const uint8_t *src = I.data;
     uint8_t *h8 = (uint8_t *)I.hist_out, *o8 = (uint8_t *)I.out;
     if (I.data_mode != MC_BM_WORDS) {
-        // lossless frame read in place: check the header the host assumed
-        if (t == 0 && threadIdx.x == 0 &&
-            check_frame1(I.data_frame, I.data_mode == MC_BM_RAW1 ? 0 : 1, I.n) < 0)
+        // lossless frame read in place: check the header the host assumed;
+        // a tile (2^15 bytes) lies inside one block of the frame
+        if (t == 0 && threadIdx.x == 0 && check_frame(I.data_frame, I.data_mode, I.n) < 0)
             L.results[ii].err = 1;
-        if (I.data_mode == MC_BM_RLE1) {
-            const uint8_t v = I.data_frame[12];
+        if (I.data_mode == MC_BM_RLE) {
+            const uint8_t v = (uint8_t)src_byte(I.data_frame, MC_BM_RLE, e0);
             for (int64_t e = e0 + threadIdx.x; e < e1; e += TPB) {
                 h8[e] = v;
                 if (o8) o8[e] = v;
             }
             return;
         }
+        src = I.data_frame + fpos_raw(e0) - e0;   // byte e of this tile at src[e]
     }
     if (!I.vec && ((((uintptr_t)src | (uintptr_t)h8 | (uintptr_t)o8) & 3) == 0)) {
         // 4-byte words (tiles are multiples of 16 bytes)
@@ -1085,12 +1210,6 @@ extern "C" int mc_launch_encode(const mc_enc_launch *L, void *stream, mc_ktrace 
     if (L->nall_tiles > 0) {
         tr_begin(tr, MC_KT_ENC_PASS4, s);
         k_enc_pass4<<<L->nall_tiles, TPB, 0, s>>>(*L);
-        tr_end(tr, s);
-        n++;
-    }
-    if (L->nframes > 0) {
-        tr_begin(tr, MC_KT_FRAMES, s);
-        k_frames<<<L->nframes, TPB, 0, s>>>(L->frames);
         tr_end(tr, s);
         n++;
     }
