@@ -581,7 +581,7 @@ int mc_compress_grouped(MomentumCompressor *mc, BatchItem *items, size_t n, cons
     /* the pinned table buffer is reused by every call: wait for the previous
      * upload from it to finish before rewriting it */
     cudaStreamSynchronize(st);
-    memset(htab, 0, tab_total);
+    memset(htab, 0, n * sizeof(mc_enc_item));
     mc_enc_item *hit = (mc_enc_item *)htab;
     int32_t *h_tile_item = (int32_t *)(htab + tab_items);
     for (size_t i = 0; i < n; i++) {
@@ -781,15 +781,15 @@ int mc_compress_grouped(MomentumCompressor *mc, BatchItem *items, size_t n, cons
             cplan *p = &P[i];
             CompressedLayerData *c = outs[i];
             const mc_enc_result *r = &hres[i];
-            snprintf(c->type, sizeof(c->type), "%s",
-                     p->mode == MODE_DIRECT ? "direct"
-                                            : (p->mode == MODE_MOMENTUM ? "momentum_predicted"
-                                                                        : "direct_generic"));
-            snprintf(c->codec, sizeof(c->codec), "%s", p->codec_tag);
+            /* fixed strings, all shorter than their fields */
+            strcpy(c->type, p->mode == MODE_DIRECT ? "direct"
+                                                   : (p->mode == MODE_MOMENTUM ? "momentum_predicted"
+                                                                               : "direct_generic"));
+            strcpy(c->codec, p->codec_tag);
             c->ndim = p->g->ndim;
             memcpy(c->shape, p->g->shape, p->g->ndim * sizeof(size_t));
-            snprintf(c->original_dtype, sizeof(c->original_dtype), "%s", mc_dtype_name(p->dt));
-            snprintf(c->stored_dtype, sizeof(c->stored_dtype), "%s", mc_dtype_name(p->dt));
+            strcpy(c->original_dtype, mc_dtype_name(p->dt));
+            strcpy(c->stored_dtype, c->original_dtype);
             c->step = p->local_step;
             c->data = base + p->off_data;
             if (p->kind == MC_K_MOMENTUM || p->kind == MC_K_QUANT) c->data_size = residual_bytes(p->dcodec, p->n);
