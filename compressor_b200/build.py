@@ -20,7 +20,7 @@ CC = "/usr/bin/gcc"
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 C_SOURCES = ["mc_util.c", "mc_wire.c", "mc_state.c", "mc_batch.c", "mc_api.c"]
-CU_SOURCES = ["mc_kernels.cu"]
+CU_SOURCES = ["mc_kernels.cu", "mc_noalloc.cu"]
 
 
 def _run(cmd):

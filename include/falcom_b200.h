@@ -82,6 +82,43 @@ void falcom_free_batch(BatchItem *items, size_t n, NDArray **outs);
 int falcom_kernel_times(const MomentumCompressor *mc, double *ms, long long *counts, int n);
 const char *falcom_kernel_name(int id);
 
+/* Residual quantiser that allocates no memory.  No counterpart in the
+ * reference interface.
+ *
+ * Writes the quantised payload of a float32 residual -- the same bytes the
+ * codec stores in CompressedLayerData.data under codec tag "q8" (bits = 8:
+ * [f32 scale][int8 code x n], 4 + n bytes) or "int4" (bits = 4: [f32 scale]
+ * [(q + 8) nibbles, element 2i low], 4 + (n + 1) / 2 bytes) -- with
+ * scale = max|r| / qmax (1 when max|r| == 0) and q = clamp(rint(r / scale)).
+ * `residual` and `out` are device memory of the current CUDA device; the
+ * work is queued on `stream` (cudaStream_t, NULL = the legacy default
+ * stream) and the function returns without waiting for it.
+ *
+ * Who needs it: callers that cannot allocate device memory -- a training
+ * step whose GPU memory belongs to another allocator (e.g. a framework's
+ * caching allocator, which must account for every byte), and
+ * latency-critical paths, where cudaMalloc / cudaFree would stall the GPU
+ * (cudaFree synchronises the device).  The batch entry points above grow
+ * device pools of their own on demand; this one only launches two kernels.
+ *
+ * Scratch is a fixed 65,792-byte __device__ array inside the library, one per
+ * device, which bounds n at FALCOM_NOALLOC_MAX_ELEMS (8192-element tiles x
+ * 16384 tiles).  Its arrival counter must be zero when a call starts: it is
+ * zero when the library is loaded and every completed call leaves it at
+ * zero.  The first call on each device does a one-time set-up (looks up the
+ * scratch address with cudaGetSymbolAddress); make that call before any
+ * stream capture begins -- n = 0 does the set-up only.
+ *
+ * Calls share the scratch of their device, so calls on one device must not
+ * overlap: issue them on one stream, or order them with events.  Two calls
+ * running at once on different streams race and give wrong results.
+ *
+ * Returns 0; ERROR_INVALID_PARAM (message on stderr) when bits is not 8 or
+ * 4, n > FALCOM_NOALLOC_MAX_ELEMS, or a pointer is NULL with n > 0;
+ * ERROR_COMPRESSION when set-up or the launch fails. */
+#define FALCOM_NOALLOC_MAX_ELEMS 134217728LL
+int falcom_quantize_residual_noalloc(const float *residual, size_t n, int bits, void *out, void *stream);
+
 #ifdef __cplusplus
 }
 #endif
