@@ -91,6 +91,9 @@ class ClockSampler:
                  "-lms", "20"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
+            t0 = time.time()   # sampling is running once the first line is in
+            while not self.lines and time.time() - t0 < 3.0:
+                time.sleep(0.005)
         except Exception:
             self.proc = None
         return self
@@ -101,6 +104,11 @@ class ClockSampler:
 
     def __exit__(self, *exc):
         if self.proc:
+            # a short timed region can end before the first sample: wait for
+            # one more sample (taken as the region ends) before stopping
+            n0, t0 = len(self.lines), time.time()
+            while len(self.lines) <= n0 and time.time() - t0 < 1.0:
+                time.sleep(0.005)
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
@@ -457,10 +465,198 @@ def run_ours(args):
     return 0
 
 
+# --------------------------------------------------------------- federated
+def run_federated(args):
+    """Federated round per step: every rank compresses its clients' updates
+    (one encoder instance per client), decodes them on one server decoder
+    instance whose weighted aggregate is fused into the decode, then one sum
+    all-reduce of the flat aggregate over NCCL."""
+    import torch
+    import torch.distributed as dist
+    from compressor_b200 import build as B
+    from compressor_b200 import federated as F
+    from compressor_b200 import workloads as W
+    from compressor_b200.abi import Codec, PreparedBatch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    if not os.path.exists(B.OUT):
+        B.build()
+    os.environ.setdefault("FALCOM_LOG_LEVEL", "ERROR")
+    model = args.model
+    K, Wm = args.steps, args.warmup
+    lay = W.Layout.of(model)
+    n_clients = args.clients_per_gpu * world
+    mine = list(F.shard(n_clients, world, rank))
+    weights = F.uniform_weights(n_clients)
+    upd = lay.numel * 4
+    offs_b = [4 * o for o in lay.offsets]
+    c_offs = (ctypes.c_size_t * len(lay.offsets))(*lay.offsets)
+    stream = torch.cuda.current_stream()
+
+    # per-client AR(1) rho 0.9 (own seed) plus a common N(0, 1e-3^2) component
+    # drawn once per round with the same seed on every rank
+    sigma = torch.zeros(lay.total, device=dev)
+    for o, sh in zip(lay.offsets, lay.shapes):
+        sigma[o:o + int(np.prod(sh))] = 1e-3 / float(np.sqrt(W.fan_in(sh)))
+    gens = []
+    for c in mine:
+        g = torch.Generator(device=dev)
+        g.manual_seed(50_000 + c)
+        gens.append(g)
+    gcom = torch.Generator(device=dev)
+    gcom.manual_seed(49_999)
+    states = [None] * len(mine)
+    xs = [torch.empty(lay.total, device=dev) for _ in mine]
+
+    def next_round():
+        common = torch.randn(lay.total, device=dev, generator=gcom) * 1e-3
+        for j in range(len(mine)):
+            noise = torch.randn(lay.total, device=dev, generator=gens[j]) * sigma
+            states[j] = noise if states[j] is None else states[j].mul_(0.9).add_(noise)
+            torch.add(states[j], common, out=xs[j])
+
+    def new_instances():
+        encs = [Codec(B.OUT, client=f"Client{c + 1}") for c in mine]
+        dec = Codec(B.OUT, client="server")
+        for c in encs + [dec]:
+            assert c.lib.falcom_set_residual_codec(c.h, args.codec.encode()) == 0
+            c.lib.falcom_set_stream(c.h, ctypes.c_void_p(stream.cuda_stream))
+        return encs, dec
+
+    agg = torch.zeros(lay.total, dtype=torch.float32, device=dev)
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+    cids = [f"Client{c + 1}".encode() for c in mine]
+
+    def fed_step(encs, dec, pb, ptrs, count, e0=None, ear=None, e1=None):
+        if e0 is not None:
+            e0.record(stream)
+        agg.zero_()
+        payload = 0
+        for j, c in enumerate(mine):
+            pb.set_pointers(ptrs[j], offs_b)
+            r1 = pb.compress(encs[j].h, cids[j])
+            F.set_client_weight(dec.lib, dec.h, agg.data_ptr(), c_offs, len(c_offs), weights[c])
+            r2 = pb.decompress(dec.h, cids[j])
+            if r1 != 0 or r2 != 0:
+                raise RuntimeError(f"codec failed on rank {rank} client {c}: {r1} {r2}")
+            payload += pb.payload_bytes()
+            count[0] += encs[j].lib.falcom_last_launches(encs[j].h) + dec.lib.falcom_last_launches(dec.h)
+            pb.release()
+        if ear is not None:
+            ear.record(stream)
+        F.allreduce_aggregate(agg, dist)
+        if e1 is not None:
+            e1.record(stream)
+        return payload
+
+    # ------------------------------------------------ device-resident value
+    encs, dec = new_instances()
+    pb = PreparedBatch(encs[0].lib, lay.names, lay.shapes)
+    for _ in range(1 + Wm):
+        next_round()
+        fed_step(encs, dec, pb, [x.data_ptr() for x in xs], [0])
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    step_ms, ar_ms, cnt, payload = [], [], [0], 0
+    with ClockSampler(local) as clk:
+        for _ in range(K):
+            next_round()
+            flush.zero_()
+            e0, ear, e1 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+            payload = fed_step(encs, dec, pb, [x.data_ptr() for x in xs], cnt, e0, ear, e1)
+            e1.synchronize()
+            step_ms.append(e0.elapsed_time(e1))
+            ar_ms.append(ear.elapsed_time(e1))
+    torch.cuda.synchronize()
+    tot = torch.tensor([sum(step_ms)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(tot, op=dist.ReduceOp.MAX)
+    ms_per_step = float(tot.item()) / K
+    value = n_clients * upd / (ms_per_step * 1e-3) / 1e9
+    for c in encs + [dec]:
+        c.close()
+
+    # ------------------------------------------------------------ e2e (host)
+    encs, dec = new_instances()
+    pb = PreparedBatch(encs[0].lib, lay.names, lay.shapes)
+    hosts = [torch.empty(lay.total, dtype=torch.float32, pin_memory=True) for _ in mine]
+    agg_host = torch.empty(lay.total, dtype=torch.float32, pin_memory=True)
+    e2e_ms, h2d, d2h = [], 0, 0
+    for it in range(1 + Wm + K):
+        next_round()
+        for h, x in zip(hosts, xs):
+            h.copy_(x)
+        torch.cuda.synchronize()
+        flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        pbytes = fed_step(encs, dec, pb, [h.data_ptr() for h in hosts], [0], e0)
+        agg_host.copy_(agg, non_blocking=True)
+        e1.record(stream)
+        e1.synchronize()
+        if it >= 1 + Wm:
+            e2e_ms.append(e0.elapsed_time(e1))
+            h2d = len(mine) * upd + pbytes       # inputs up, payloads up for the decoder
+            d2h = pbytes + len(mine) * upd + 4 * lay.total   # payloads and decoded outputs down, aggregate
+    for c in encs + [dec]:
+        c.close()
+    e2e_t = torch.tensor([sum(e2e_ms)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(e2e_t, op=dist.ReduceOp.MAX)
+    e2e_step = float(e2e_t.item()) / K
+    e2e_val = n_clients * upd / (e2e_step * 1e-3) / 1e9
+
+    if rank == 0:
+        peak, peak_kind = measured_peak()
+        ab = W.algorithmic_bytes(model, args.codec)
+        # per client: the closed loop's bytes plus the fused aggregate (read
+        # the decoded tensor, read and write the aggregate: 12 B / element)
+        alg = len(mine) * (ab["bytes_per_round"] + 12 * lay.numel)
+        out = {
+            "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world, "steps": K,
+            "warmup": Wm, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (per-client seeded AR(1) Gaussian updates rho=0.9, sigma=1e-3/sqrt(fan_in), "
+                    "plus a shared N(0, 1e-3^2) component per round; ResNet-50 state-dict shapes)",
+            "config": {"workload": f"federated round of {n_clients} {model} clients, {args.clients_per_gpu} per "
+                                   f"GPU: compress_batch per client, decompress_batch on one server decoder "
+                                   f"per GPU with the weighted aggregate fused in, NCCL sum all-reduce of "
+                                   f"the {lay.numel}-element aggregate; residual codec {args.codec}",
+                       "clients": n_clients, "clients_per_gpu": args.clients_per_gpu,
+                       "elements_per_client": lay.numel, "update_bytes_per_client": upd, "codec": args.codec,
+                       "l2": "flushed between steps (256 MiB write, outside the timed events)",
+                       "parallelism": f"clients sharded over {world} GPU(s), NCCL all-reduce of the aggregate"},
+            "gpu_launches": cnt[0],
+            "payload_bytes_per_step_rank0": payload,
+            "allreduce_ms_rank0": round(statistics.mean(ar_ms), 4),
+            "roofline": {"bound": "hbm", "kernel": "federated step (all codec kernels + aggregate)",
+                         "achieved": round(alg / (ms_per_step * 1e-3) / 1e9, 1), "peak": peak,
+                         "peak_kind": peak_kind, "unit": "GB/s",
+                         "frac": round(alg / (ms_per_step * 1e-3) / 1e9 / peak, 4), "traffic": None,
+                         "algorithmic_bytes_per_step_per_gpu": int(alg)},
+            "e2e": {"value": round(e2e_val, 3), "unit": "GB/s", "ms_per_step": round(e2e_step, 4),
+                    "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h)},
+            "clocks": clk.summary(),
+            "cpu_baseline": None,
+        }
+        print(json.dumps(out))
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--model", default="resnet50")
@@ -469,10 +665,16 @@ def main():
     ap.add_argument("--cpu-budget-s", type=float, default=20.0)
     ap.add_argument("--mode", default="full", choices=["full", "value"],
                     help="value: only the device-resident timed loop (for profiler runs)")
+    ap.add_argument("--federated", action="store_true",
+                    help="federated round (decode + weighted aggregate + all-reduce) also on one GPU")
+    ap.add_argument("--clients-per-gpu", type=int, default=1,
+                    help="federated round: clients per GPU (64 / N for the 64-client round)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3) if args.impl == "ours" else args.warmup
     if args.impl == "reference":
         return run_reference(args)
+    if int(os.environ.get("WORLD_SIZE", "1")) > 1 or args.federated:
+        return run_federated(args)
     return run_ours(args)
 
 

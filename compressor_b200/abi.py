@@ -493,6 +493,9 @@ def bind_extensions(lib: ctypes.CDLL) -> None:
                                         ctypes.POINTER(ctypes.c_longlong), ctypes.c_int]
     lib.falcom_kernel_name.argtypes = [ctypes.c_int]
     lib.falcom_kernel_name.restype = ctypes.c_char_p
+    lib.falcom_set_aggregate.argtypes = [c_vp, c_vp, ctypes.POINTER(ctypes.c_size_t), ctypes.c_size_t,
+                                         ctypes.c_float]
+    lib.falcom_set_aggregate.restype = ctypes.c_int
 
 
 def kernel_times(lib: ctypes.CDLL, handle) -> dict:

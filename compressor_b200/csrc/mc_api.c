@@ -168,14 +168,17 @@ MC_EXPORT void momentum_compressor_destroy(MomentumCompressor *mc) {
     map_free(mc->layers, layer_rec_drop);
     map_free(mc->memory, mem_rec_drop);
     map_free(mc->mem_clients, NULL);
-    keycache_free(&mc->enc_kc);
-    keycache_free(&mc->dec_kc);
+    for (int i = 0; i < MC_KC_SLOTS; i++) {
+        keycache_free(&mc->enc_kc[i]);
+        keycache_free(&mc->dec_kc[i]);
+    }
     scratch_free(&mc->scratch);
     if (mc->own_stream) cudaStreamDestroy(mc->own_stream);
     for (int i = 0; i < 2 * MC_KTRACE_MAX; i++)
         if (mc->ktrace.ev[i]) cudaEventDestroy((cudaEvent_t)mc->ktrace.ev[i]);
     free(mc->stats.prediction_ratios);
     free(mc->stats.sign_mismatch_ratios);
+    free(mc->agg_off);
     int lvl = mc->log_level;
     dev_leave(mc, prev);
     free(mc);
@@ -963,9 +966,37 @@ MC_EXPORT int falcom_is_device_pointer(const void *ptr) {
     return mc_ptr_is_device(ptr, &d);
 }
 
+/* ----------------------------------------------------------- aggregate */
+MC_EXPORT int falcom_set_aggregate(MomentumCompressor *mc, float *aggregate, const size_t *offsets, size_t n,
+                                   float weight) {
+    if (!mc) return ERROR_INVALID_PARAM;
+    if (!aggregate) {
+        free(mc->agg_off);
+        mc->agg_off = NULL;
+        mc->agg = NULL;
+        mc->agg_n = 0;
+        return ERROR_NONE;
+    }
+    int d = -1;
+    if (!offsets || n == 0 || !mc_ptr_is_device(aggregate, &d) || d != mc->device) {
+        mc_set_error(mc, "falcom_set_aggregate: aggregate must be device memory of device %d, with offsets",
+                     mc->device);
+        return ERROR_INVALID_PARAM;
+    }
+    size_t *o = (size_t *)malloc(n * sizeof(size_t));
+    if (!o) return ERROR_ALLOCATION;
+    memcpy(o, offsets, n * sizeof(size_t));
+    free(mc->agg_off);
+    mc->agg_off = o;
+    mc->agg = aggregate;
+    mc->agg_n = n;
+    mc->agg_w = weight;
+    return ERROR_NONE;
+}
+
 /* ----------------------------------------------------------- kernel timing */
 static const char *k_names[MC_NKERN] = {"enc_pass1_stats_sign", "enc_pass2_variance", "enc_pass3_predict",
-                                        "enc_pass4_quantize_pack", "frames_write", "frames_expand",
+                                        "enc_pass4_quantize_pack", "dec_accumulate", "frames_expand",
                                         "dec_prefix", "dec_reconstruct"};
 
 mc_ktrace *mc_trace_begin(MomentumCompressor *mc) {

@@ -66,8 +66,9 @@ enum {
     SD_DSTAGE,       /* decoder: staged payload bytes */
     SD_DOUT,         /* decoder: contiguous decoded output before the host copy */
     SD_DCONTENT,     /* decoder: frame contents expanded on the device */
+    SD_ACC,          /* decoder: aggregate accumulation tables */
 };
-enum { SH_TABLES = 0, SH_RESULTS, SH_STAGE };
+enum { SH_TABLES = 0, SH_RESULTS, SH_STAGE, SH_ACC };
 
 /* Call-local string -> int table (keys are borrowed, not copied). */
 typedef struct {
@@ -271,13 +272,13 @@ int mc_compress_grouped(MomentumCompressor *mc, BatchItem *items, size_t n, cons
         req[i].ndim = g->ndim;
         req[i].shape = g->shape;
     }
-    if (rc == ERROR_NONE) rc = keycache_resolve(mc, &mc->enc_kc, client, req, n);
+    const mc_keycache *kc = NULL;
+    if (rc == ERROR_NONE) kc = keycache_get(mc, mc->enc_kc, client, req, n, &rc);
     free(req);
     if (rc != ERROR_NONE) {
         free(gid);
         goto out;
     }
-    const mc_keycache *kc = &mc->enc_kc;
     for (size_t i = 0; i < n; i++) {
         P[i].lrec = kc->lrec[i];
         P[i].mrec = kc->mrec[i];
@@ -1003,9 +1004,60 @@ static size_t sign_content_len(size_t size) {
     return (s > 0 && frame_blocks(s) == nb) ? s : 0;
 }
 
+/* Adds agg_w * (decoded item) into the instance's aggregate for every
+ * decoded float32 item of a segment whose batch index has an offset.  The
+ * source is the device copy of the decoded tensor; queued on the instance's
+ * stream after the segment's commit, so only successful items contribute. */
+static int dec_accumulate(MomentumCompressor *mc, const dplan *D, size_t n, NDArray **out, size_t base,
+                          const uint8_t *dout) {
+    size_t m = 0;
+    int ntiles = 0;
+    for (size_t i = 0; i < n; i++) {
+        if (!out[i] || D[i].dt != DTYPE_FLOAT32 || base + i >= mc->agg_n) continue;
+        m++;
+        ntiles += (int)((D[i].n + TILE_ELEMS - 1) / TILE_ELEMS);
+    }
+    if (m == 0 || ntiles == 0) return ERROR_NONE;
+    size_t t_items = ALIGN_UP(m * sizeof(mc_acc_item), 256);
+    size_t t_ti = ALIGN_UP((size_t)ntiles * 4, 256);
+    uint8_t *ht = (uint8_t *)scratch_host(&mc->scratch, SH_ACC, t_items + t_ti);
+    uint8_t *dt = (uint8_t *)scratch_dev(&mc->scratch, SD_ACC, t_items + t_ti);
+    if (!ht || !dt) return ERROR_ALLOCATION;
+    mc_acc_item *hi = (mc_acc_item *)ht;
+    int32_t *h_ti = (int32_t *)(ht + t_items);
+    size_t j = 0;
+    int tb = 0;
+    for (size_t i = 0; i < n; i++) {
+        if (!out[i] || D[i].dt != DTYPE_FLOAT32 || base + i >= mc->agg_n) continue;
+        mc_acc_item *A = &hi[j];
+        A->src = (const float *)(dout + D[i].out_off);
+        A->dst = mc->agg + mc->agg_off[base + i];
+        A->n = (int64_t)D[i].n;
+        A->w = mc->agg_w;
+        A->tile_base = tb;
+        A->vec = ((((uintptr_t)A->src) | ((uintptr_t)A->dst)) & 15) == 0;
+        const int nt = (int)((D[i].n + TILE_ELEMS - 1) / TILE_ELEMS);
+        for (int t = 0; t < nt; t++) h_ti[tb + t] = (int32_t)j;
+        tb += nt;
+        j++;
+    }
+    if (cudaMemcpyAsync(dt, ht, t_items + t_ti, cudaMemcpyHostToDevice, mc->stream) != cudaSuccess)
+        return ERROR_DECOMPRESSION;
+    mc_ktrace *tr = mc_trace_begin(mc);
+    int k = mc_launch_accumulate((const mc_acc_item *)dt, (const int32_t *)(dt + t_items), ntiles, mc->stream, tr);
+    if (k < 0) return ERROR_DECOMPRESSION;
+    if (tr) {
+        cudaStreamSynchronize(mc->stream);
+        mc_trace_end(mc);
+    }
+    mc->last_launches += k;
+    mc->total_launches += k;
+    return ERROR_NONE;
+}
+
 #define DEC_RETRY_EXPAND 1
 static int dec_segment(MomentumCompressor *mc, const BatchItem *items, size_t n, const char *client,
-                       NDArray **out, int out_loc, size_t *n_ok, int force_expand) {
+                       NDArray **out, int out_loc, size_t *n_ok, int force_expand, size_t base) {
     cudaStream_t st = mc->stream;
     const int dev = mc->device;
     dplan *D = (dplan *)calloc(n, sizeof(dplan));
@@ -1015,6 +1067,7 @@ static int dec_segment(MomentumCompressor *mc, const BatchItem *items, size_t n,
     prof.on = mc_env_flag("FALCOM_PROFILE");
     prof_mark(&prof, "start");
     /* keys and state records of every item (cached across rounds) */
+    const mc_keycache *dkc = NULL;
     {
         mc_keyreq *req = (mc_keyreq *)malloc(n * sizeof(mc_keyreq));
         static const size_t one = 1;
@@ -1029,13 +1082,13 @@ static int dec_segment(MomentumCompressor *mc, const BatchItem *items, size_t n,
             req[i].ndim = ok ? c->ndim : 1;
             req[i].shape = ok ? c->shape : &one;
         }
-        rc = keycache_resolve(mc, &mc->dec_kc, client, req, n);
+        dkc = keycache_get(mc, mc->dec_kc, client, req, n, &rc);
         free(req);
         if (rc != ERROR_NONE) { free(D); return rc; }
     }
     for (size_t i = 0; i < n; i++) {
         out[i] = NULL;
-        dplan_item(mc, &D[i], &items[i], &mc->dec_kc, i);
+        dplan_item(mc, &D[i], &items[i], dkc, i);
         if (!D[i].ok)
             fprintf(stderr, "[ERROR] Batch decompress: item '%s': %s\n",
                     items[i].layer_name ? items[i].layer_name : "(null)", D[i].why);
@@ -1460,6 +1513,11 @@ static int dec_segment(MomentumCompressor *mc, const BatchItem *items, size_t n,
     if (handed > 0) arena_retain(oarena, handed - 1);
     else arena_release(oarena);
     oarena = NULL;
+    if (mc->agg && dec_accumulate(mc, D, n, out, base, dout) != ERROR_NONE) {
+        /* outputs and state stand; the call reports the failed aggregate */
+        mc_set_error(mc, "Batch decompress: aggregate update failed");
+        mc->agg_failed = 1;
+    }
     prof_mark(&prof, "commit");
     prof_print(&prof, "decompress");
     if (prof.on) {
@@ -1519,8 +1577,8 @@ int mc_decompress_items(MomentumCompressor *mc, const BatchItem *items, size_t n
             *s = (int)a;
         }
         if (b == a) b = a + 1;
-        int r = dec_segment(mc, items + a, b - a, client, out + a, out_loc, &ok, 0);
-        if (r == DEC_RETRY_EXPAND) r = dec_segment(mc, items + a, b - a, client, out + a, out_loc, &ok, 1);
+        int r = dec_segment(mc, items + a, b - a, client, out + a, out_loc, &ok, 0, a);
+        if (r == DEC_RETRY_EXPAND) r = dec_segment(mc, items + a, b - a, client, out + a, out_loc, &ok, 1, a);
         if (r != ERROR_NONE) {
             rc = r;
             for (size_t j = a; j < b; j++) {
@@ -1531,6 +1589,10 @@ int mc_decompress_items(MomentumCompressor *mc, const BatchItem *items, size_t n
     }
     strtab_free(&seen);
     (void)rc;
+    if (mc->agg_failed) {
+        mc->agg_failed = 0;
+        return ERROR_DECOMPRESSION;
+    }
     if (ok == 0) return ERROR_DECOMPRESSION;
     if (ok < n) return -((int)n - (int)ok);
     return ERROR_NONE;

@@ -189,9 +189,21 @@ typedef struct {
     int64_t *tile_poff;         /* scratch */
 } mc_dec_launch;
 
+/* Weighted accumulation of decoded tensors into an aggregate:
+ * dst[e] = fma(w, src[e], dst[e]) for e < n; 8192-element tiles. */
+typedef struct {
+    const float *src;
+    float *dst;
+    int64_t n;
+    float w;
+    int32_t tile_base;
+    int32_t vec;                /* 1: src and dst 16-byte aligned */
+    int32_t pad;
+} mc_acc_item;
+
 /* Optional per-kernel event trace (events created by the host). */
 enum {
-    MC_KT_ENC_PASS1 = 0, MC_KT_ENC_PASS2, MC_KT_ENC_PASS3, MC_KT_ENC_PASS4, MC_KT_FRAMES,
+    MC_KT_ENC_PASS1 = 0, MC_KT_ENC_PASS2, MC_KT_ENC_PASS3, MC_KT_ENC_PASS4, MC_KT_ACCUM,
     MC_KT_UNFRAME, MC_KT_DEC_PREFIX, MC_KT_DEC_RECON, MC_NKERN
 };
 #define MC_KTRACE_MAX 64
@@ -206,6 +218,8 @@ typedef struct {
 int mc_launch_encode(const mc_enc_launch *L, void *stream, mc_ktrace *tr);
 int mc_launch_decode(const mc_dec_launch *L, void *stream, mc_ktrace *tr);
 int mc_launch_unframe(const mc_unframe_job *jobs, int njobs, void *stream, mc_ktrace *tr);
+int mc_launch_accumulate(const mc_acc_item *items, const int32_t *tile_item, int ntiles, void *stream,
+                         mc_ktrace *tr);
 
 /* Reusable device / pinned scratch owned by one compressor instance. */
 typedef struct {

@@ -87,10 +87,14 @@ typedef struct {
     mc_tensor *spare;
 } mc_mem_rec;
 
-/* Keys and records of every item of the last batch an engine saw. */
+/* Keys and records of every item of one batch an engine saw.  An engine
+ * keeps MC_KC_SLOTS of them (one per recent client, least recently used
+ * replaced), so a server decoding many clients in turn hits as well. */
+#define MC_KC_SLOTS 64
 typedef struct {
     int valid;
     unsigned gen;
+    unsigned long long used;        /* tick of the last hit */
     char client[256];
     size_t n;
     char **names;
@@ -129,7 +133,8 @@ struct MomentumCompressor {
     mc_map *memory;          /* "client\x1f<layer|dtype|conv_(...)>" -> mc_mem_rec* */
     mc_map *mem_clients;     /* clients that own a prediction-memory table */
     unsigned state_gen;      /* bumped when records are deleted (resets) */
-    mc_keycache enc_kc, dec_kc;
+    mc_keycache enc_kc[MC_KC_SLOTS], dec_kc[MC_KC_SLOTS];
+    unsigned long long kc_tick;
 
     struct {
         size_t total_compressions;
@@ -145,6 +150,14 @@ struct MomentumCompressor {
 
     /* reusable scratch (grown on demand) */
     mc_scratch scratch;
+
+    /* server-side aggregate (falcom_set_aggregate): decoded float32 item i
+     * of every batch decompress is added, times agg_w, at agg + agg_off[i] */
+    float *agg;
+    size_t *agg_off;
+    size_t agg_n;
+    float agg_w;
+    int agg_failed;
 
     /* per-kernel device time (falcom_set_kernel_timing) */
     int ktiming;
@@ -203,8 +216,8 @@ void mem_rec_drop(void *r);
 mc_tensor *rec_take(mc_tensor **spare, DataType dt, size_t ndim, const size_t *shape, int device);
 void rec_commit(mc_tensor **slot, mc_tensor **spare, mc_tensor *t);
 void keycache_free(mc_keycache *kc);
-int keycache_resolve(MomentumCompressor *mc, mc_keycache *kc, const char *client, const mc_keyreq *req,
-                     size_t n);
+mc_keycache *keycache_get(MomentumCompressor *mc, mc_keycache *set, const char *client, const mc_keyreq *req,
+                          size_t n, int *rc);
 
 /* batch engines (mc_batch.c) */
 int mc_compress_grouped(MomentumCompressor *mc, BatchItem *items, size_t n, const char *client,

@@ -1173,6 +1173,22 @@ __global__ void __launch_bounds__(TPB) k_dec_recon(mc_dec_launch L) {
     }
 }
 
+// ------------------------------------------------------------- aggregate
+__global__ void __launch_bounds__(TPB) k_accumulate(const mc_acc_item *items, const int32_t *tile_item) {
+    const int gt = blockIdx.x;
+    const mc_acc_item I = items[tile_item[gt]];
+    const int64_t e0 = (int64_t)(gt - I.tile_base) * 8192;
+    const int64_t e1 = min(e0 + 8192, I.n);
+    for (int64_t g = e0 + 4 * (int64_t)threadIdx.x; g < e1; g += 4 * TPB) {
+        float x[4], a[4];
+        ld4(I.src, g, e1, I.vec, x);
+        ld4(I.dst, g, e1, I.vec, a);
+#pragma unroll
+        for (int j = 0; j < 4; j++) a[j] = __fmaf_rn(I.w, x[j], a[j]);
+        st4(I.dst, g, e1, I.vec, a);
+    }
+}
+
 }  // namespace
 
 // ---------------------------------------------------------------- launchers
@@ -1241,6 +1257,17 @@ extern "C" int mc_launch_unframe(const mc_unframe_job *jobs, int njobs, void *st
     cudaStream_t s = (cudaStream_t)stream;
     tr_begin(tr, MC_KT_UNFRAME, s);
     k_unframe<<<njobs, TPB, 0, s>>>(jobs);
+    tr_end(tr, s);
+    if (cudaGetLastError() != cudaSuccess) return -1;
+    return 1;
+}
+
+extern "C" int mc_launch_accumulate(const mc_acc_item *items, const int32_t *tile_item, int ntiles, void *stream,
+                                    mc_ktrace *tr) {
+    if (ntiles <= 0) return 0;
+    cudaStream_t s = (cudaStream_t)stream;
+    tr_begin(tr, MC_KT_ACCUM, s);
+    k_accumulate<<<ntiles, TPB, 0, s>>>(items, tile_item);
     tr_end(tr, s);
     if (cudaGetLastError() != cudaSuccess) return -1;
     return 1;

@@ -132,9 +132,8 @@ static int keycache_hit(const MomentumCompressor *mc, const mc_keycache *kc, con
     return 1;
 }
 
-int keycache_resolve(MomentumCompressor *mc, mc_keycache *kc, const char *client, const mc_keyreq *req,
-                     size_t n) {
-    if (keycache_hit(mc, kc, client, req, n)) return 0;
+static int keycache_resolve(MomentumCompressor *mc, mc_keycache *kc, const char *client, const mc_keyreq *req,
+                            size_t n) {
     keycache_free(kc);
     kc->names = (char **)calloc(n, sizeof(char *));
     kc->dt = (DataType *)calloc(n, sizeof(DataType));
@@ -203,4 +202,28 @@ int keycache_resolve(MomentumCompressor *mc, mc_keycache *kc, const char *client
     kc->gen = mc->state_gen;
     kc->valid = 1;
     return ERROR_NONE;
+}
+
+/* The cache of this batch: a slot that matches it, else the least recently
+ * used slot rebuilt.  NULL with *rc set when rebuilding fails. */
+mc_keycache *keycache_get(MomentumCompressor *mc, mc_keycache *set, const char *client, const mc_keyreq *req,
+                          size_t n, int *rc) {
+    mc_keycache *victim = &set[0];
+    for (int i = 0; i < MC_KC_SLOTS; i++) {
+        mc_keycache *kc = &set[i];
+        if (keycache_hit(mc, kc, client, req, n)) {
+            kc->used = ++mc->kc_tick;
+            *rc = ERROR_NONE;
+            return kc;
+        }
+        if (!kc->valid) {
+            if (victim->valid) victim = kc;
+        } else if (victim->valid && kc->used < victim->used) {
+            victim = kc;
+        }
+    }
+    *rc = keycache_resolve(mc, victim, client, req, n);
+    if (*rc != ERROR_NONE) return NULL;
+    victim->used = ++mc->kc_tick;
+    return victim;
 }

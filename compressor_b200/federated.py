@@ -1,0 +1,74 @@
+"""Federated round over several GPUs: host-side plan of the server step.
+
+Clients are independent units (the codec keys all encoder and decoder state
+by client id, reference momentum_compressor_openmp_simd_final.c:452-471), so
+they are block-distributed over the ranks, one process per GPU.  Each rank
+compresses its clients' updates, decodes them on its server-side decoder
+instance with the weighted aggregate fused into the decode
+(``falcom_set_aggregate``), and one sum all-reduce of the flat aggregate over
+NCCL finishes the global update.
+
+Everything here is plain host logic (which clients a rank owns, their
+weights, the aggregate layout and the collective); it runs the same under the
+``gloo`` backend on CPU tensors.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+from typing import List, Sequence
+
+import numpy as np
+
+
+def shard(n_clients: int, world: int, rank: int) -> range:
+    """Block distribution of client indices 0..n_clients-1 over `world`
+    ranks: the first n_clients % world ranks get one extra client."""
+    if world <= 0 or not 0 <= rank < world or n_clients < 0:
+        raise ValueError(f"bad shard request: {n_clients} clients, rank {rank} of {world}")
+    base, extra = divmod(n_clients, world)
+    start = rank * base + min(rank, extra)
+    return range(start, start + base + (1 if rank < extra else 0))
+
+
+def uniform_weights(n_clients: int) -> List[float]:
+    """FedAvg weights of equally weighted clients."""
+    if n_clients <= 0:
+        raise ValueError("no clients")
+    return [1.0 / n_clients] * n_clients
+
+
+@dataclass
+class AggregateLayout:
+    """Flat float32 layout of one model update: element offset of every
+    tensor, in state-dict order."""
+    names: List[str]
+    shapes: List[tuple]
+    offsets: List[int]
+    total: int
+
+    @staticmethod
+    def of(names: Sequence[str], shapes: Sequence[Sequence[int]], align: int = 1) -> "AggregateLayout":
+        offs, o = [], 0
+        for s in shapes:
+            o = (o + align - 1) // align * align
+            offs.append(o)
+            o += int(np.prod(s))
+        return AggregateLayout(list(names), [tuple(s) for s in shapes], offs, o)
+
+    def c_offsets(self):
+        return (ctypes.c_size_t * len(self.offsets))(*self.offsets)
+
+
+def set_client_weight(lib, decoder_handle, aggregate_ptr: int, c_offsets, n: int, weight: float) -> None:
+    """Points the decoder's fused aggregate at `aggregate_ptr` with the weight
+    of the client whose batch it decodes next."""
+    rc = lib.falcom_set_aggregate(decoder_handle, ctypes.c_void_p(aggregate_ptr), c_offsets, n, float(weight))
+    if rc != 0:
+        raise RuntimeError(f"falcom_set_aggregate failed ({rc}): {lib.falcom_last_error(decoder_handle)}")
+
+
+def allreduce_aggregate(aggregate, dist=None, group=None) -> None:
+    """Sum of the per-rank aggregates on every rank (no-op on one rank)."""
+    if dist is not None and dist.is_initialized() and dist.get_world_size(group) > 1:
+        dist.all_reduce(aggregate, op=dist.ReduceOp.SUM, group=group)

@@ -82,6 +82,23 @@ void falcom_free_batch(BatchItem *items, size_t n, NDArray **outs);
 int falcom_kernel_times(const MomentumCompressor *mc, double *ms, long long *counts, int n);
 const char *falcom_kernel_name(int id);
 
+/* Server-side weighted aggregate.  No counterpart in the reference
+ * interface (the federated server sums the decoded client updates itself).
+ *
+ * While set, every momentum_compressor_decompress_batch call on `mc` also
+ * adds weight * (decoded item i) into aggregate[offsets[i] ...
+ * offsets[i] + numel_i) for every item i < n that decodes successfully and is
+ * float32 (other dtypes are not added).  `aggregate` is float32 device memory
+ * of the instance's device, `offsets` element offsets (copied); items must
+ * not overlap in the aggregate.  The addition (one fma per element) is queued
+ * on the instance's stream after the call's own work and may still run when
+ * the call returns: synchronise that stream, or order later work on it,
+ * before reading the aggregate.  Set it again to change the weight (one call
+ * per client); aggregate = NULL stops it.  Returns 0, or ERROR_INVALID_PARAM
+ * when aggregate is not device memory of the instance's device. */
+int falcom_set_aggregate(MomentumCompressor *mc, float *aggregate, const size_t *offsets, size_t n,
+                         float weight);
+
 /* Residual quantiser that allocates no memory.  No counterpart in the
  * reference interface.
  *
