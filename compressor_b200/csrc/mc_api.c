@@ -172,6 +172,8 @@ MC_EXPORT void momentum_compressor_destroy(MomentumCompressor *mc) {
         keycache_free(&mc->enc_kc[i]);
         keycache_free(&mc->dec_kc[i]);
     }
+    listcache_free(mc, mc->enc_lists);
+    listcache_free(mc, mc->dec_lists);
     scratch_free(&mc->scratch);
     if (mc->own_stream) cudaStreamDestroy(mc->own_stream);
     for (int i = 0; i < 2 * MC_KTRACE_MAX; i++)
@@ -997,7 +999,7 @@ MC_EXPORT int falcom_set_aggregate(MomentumCompressor *mc, float *aggregate, con
 /* ----------------------------------------------------------- kernel timing */
 static const char *k_names[MC_NKERN] = {"enc_pass1_stats_sign", "enc_pass2_variance", "enc_pass3_predict",
                                         "enc_pass4_quantize_pack", "dec_accumulate", "frames_expand",
-                                        "dec_prefix", "dec_reconstruct"};
+                                        "dec_prefix", "dec_reconstruct", "enc_finalize"};
 
 mc_ktrace *mc_trace_begin(MomentumCompressor *mc) {
     if (!mc->ktiming) return NULL;

@@ -49,7 +49,7 @@ static void prof_print(prof_t *p, const char *tag) {
     fprintf(stderr, "\n");
 }
 #define SLOT_ALIGN 256
-#define TILE_ELEMS 8192
+#define TILE_ELEMS 4096
 
 enum { MODE_DIRECT = 0, MODE_MOMENTUM = 1, MODE_GENERIC = 2 };
 
@@ -69,6 +69,55 @@ enum {
     SD_ACC,          /* decoder: aggregate accumulation tables */
 };
 enum { SH_TABLES = 0, SH_RESULTS, SH_STAGE, SH_ACC };
+
+/* ------------------------------------------------------------ list cache */
+static uint64_t sig_mix(uint64_t h, uint64_t v) {
+    h ^= v + 0x9E3779B97F4A7C15ull + (h << 6) + (h >> 2);
+    return h * 1099511628211ull;
+}
+
+void listcache_free(MomentumCompressor *mc, mc_listcache *set) {
+    for (int i = 0; i < MC_LIST_CACHE; i++) {
+        if (set[i].dev) dbuf_put(mc->device, set[i].dev, set[i].bytes);
+        free(set[i].counts);
+        memset(&set[i], 0, sizeof(set[i]));
+    }
+}
+
+/* The cached lists of signature `sig` (*hit = 1), or a slot prepared for
+ * them: `bytes` of device memory and `nlists` counts (*hit = 0).  NULL when
+ * memory is short. */
+static mc_listcache *lists_get(MomentumCompressor *mc, mc_listcache *set, uint64_t sig, int nlists, size_t bytes,
+                               int *hit) {
+    mc_listcache *v = &set[0];
+    for (int i = 0; i < MC_LIST_CACHE; i++) {
+        if (set[i].sig == sig && set[i].nlists == nlists && set[i].bytes == bytes && set[i].dev) {
+            set[i].used = ++mc->lc_tick;
+            *hit = 1;
+            return &set[i];
+        }
+        if (set[i].used < v->used) v = &set[i];
+    }
+    *hit = 0;
+    if (v->dev && v->bytes != bytes) {
+        dbuf_put(mc->device, v->dev, v->bytes);
+        v->dev = NULL;
+    }
+    if (!v->dev) v->dev = dbuf_get(mc->device, bytes);
+    int *c = (int *)realloc(v->counts, (size_t)nlists * sizeof(int));
+    if (!v->dev || !c) {
+        if (c) v->counts = c;
+        v->sig = 0;
+        return NULL;
+    }
+    v->counts = c;
+    v->bytes = bytes;
+    v->nlists = nlists;
+    v->sig = 0;   /* set by the caller once the lists are uploaded */
+    v->used = ++mc->lc_tick;
+    return v;
+}
+
 
 /* Call-local string -> int table (keys are borrowed, not copied). */
 typedef struct {
@@ -185,7 +234,7 @@ static const char *codec_tag_of(int dcodec) {
  * elements per tile, at least 32 (one ballot word).  Powers of two make every
  * 2^20-kernel block of the bitmap frame a union of whole tiles. */
 static int tile_kernels_for(size_t ks) {
-    size_t tk = 8192;
+    size_t tk = TILE_ELEMS;
     while (tk > 32 && tk * (ks ? ks : 1) > TILE_ELEMS) tk >>= 1;
     return (int)tk;
 }
@@ -568,26 +617,34 @@ int mc_compress_grouped(MomentumCompressor *mc, BatchItem *items, size_t n, cons
     }
 
     /* ------------------------------------------------ build device tables */
-    /* layout: [items][tile_item by tile id][per wave: all-tile list, momentum-tile list] */
+    /* the item table is uploaded every call; the per-wave tile lists (all
+     * tiles, momentum tiles) come from the list cache when this batch has the
+     * structure of a recent one */
     size_t tab_items = ALIGN_UP(n * sizeof(mc_enc_item), 256);
-    size_t tab_tiles = ALIGN_UP((size_t)(ntiles_total + 1) * 4, 256);
-    size_t tab_lists = 2 * tab_tiles * (size_t)nwaves;
-    size_t tab_total = tab_items + tab_tiles + tab_lists;
+    size_t tab_list = ALIGN_UP((size_t)(ntiles_total + 1) * sizeof(mc_tile_ref), 256);
+    uint64_t sig = sig_mix(0x6A09E667F3BCC908ull, (uint64_t)n);
+    sig = sig_mix(sig, (uint64_t)nwaves);
+    for (size_t i = 0; i < n; i++)
+        sig = sig_mix(sig, ((uint64_t)P[i].kind << 56) ^ ((uint64_t)(uint32_t)P[i].wave << 32) ^
+                               (uint64_t)(uint32_t)P[i].ntiles);
+    int lhit = 0;
+    mc_listcache *lc = lists_get(mc, mc->enc_lists, sig, 2 * nwaves, 2 * tab_list * (size_t)nwaves, &lhit);
+    size_t tab_total = tab_items + (lhit ? 0 : 2 * tab_list * (size_t)nwaves);
     uint8_t *htab = (uint8_t *)scratch_host(&mc->scratch, SH_TABLES, tab_total);
-    uint8_t *dtab = (uint8_t *)scratch_dev(&mc->scratch, SD_TABLES, tab_total);
-    if (!htab || !dtab) {
+    uint8_t *dtab = (uint8_t *)scratch_dev(&mc->scratch, SD_TABLES, tab_items);
+    if (!htab || !dtab || !lc) {
         rc = ERROR_ALLOCATION;
         goto fail;
     }
     /* the pinned table buffer is reused by every call: wait for the previous
      * upload from it to finish before rewriting it */
     cudaStreamSynchronize(st);
-    memset(htab, 0, n * sizeof(mc_enc_item));
+    prof_mark(&prof, "t_sync");
     mc_enc_item *hit = (mc_enc_item *)htab;
-    int32_t *h_tile_item = (int32_t *)(htab + tab_items);
     for (size_t i = 0; i < n; i++) {
         cplan *p = &P[i];
         mc_enc_item *I = &hit[i];
+        memset(I, 0, sizeof(*I));
         I->cur = p->dev_in;
         I->hist_out = p->hist->dev;
         I->data_out = payload_dev + p->off_data;
@@ -599,10 +656,10 @@ int mc_compress_grouped(MomentumCompressor *mc, BatchItem *items, size_t n, cons
         I->tile_base = p->tile_base;
         I->elem_bytes = (int32_t)mc_dtype_size(p->dt);
         I->step = p->local_step;
+        I->wave = p->kind == MC_K_MOMENTUM ? p->wave : 0;
         I->vec = (((uintptr_t)I->cur | (uintptr_t)I->hist_out | (uintptr_t)I->data_out) & 15) == 0;
         I->lr = mc->config.momentum_lr;
         I->thr = mc->config.consistency_threshold;
-        for (int t = 0; t < p->ntiles; t++) h_tile_item[p->tile_base + t] = (int32_t)i;
         if (p->kind == MC_K_MOMENTUM) {
             cgroup *grp = &G[p->group];
             if (p->prev_item >= 0) I->prev = (const float *)P[p->prev_item].dev_in;
@@ -629,36 +686,40 @@ int mc_compress_grouped(MomentumCompressor *mc, BatchItem *items, size_t n, cons
             I->n = (int64_t)p->bytes;   /* byte tiles */
         }
     }
-    /* per-wave tile lists: direct items run in wave 0, momentum items in the
-     * wave of their position in the group's memory chain */
-    int *wave_na = (int *)calloc((size_t)nwaves, sizeof(int));
-    int *wave_nm = (int *)calloc((size_t)nwaves, sizeof(int));
-    if (!wave_na || !wave_nm) {
-        free(wave_na);
-        free(wave_nm);
-        rc = ERROR_ALLOCATION;
-        goto fail;
-    }
-    for (int w = 0; w < nwaves; w++) {
-        int32_t *la = (int32_t *)(htab + tab_items + tab_tiles + 2 * tab_tiles * (size_t)w);
-        int32_t *lm = la + tab_tiles / 4;
-        int na = 0, nm = 0;
-        for (size_t i = 0; i < n; i++) {
-            cplan *p = &P[i];
-            int in_wave = p->kind == MC_K_MOMENTUM ? p->wave == w : w == 0;
-            if (!in_wave) continue;
-            for (int t = 0; t < p->ntiles; t++) {
-                la[na++] = p->tile_base + t;
-                if (p->kind == MC_K_MOMENTUM) lm[nm++] = p->tile_base + t;
+    prof_mark(&prof, "t_items");
+    if (!lhit) {
+        /* per-wave tile lists: direct items run in wave 0, momentum items in
+         * the wave of their position in the group's memory chain */
+        for (int w = 0; w < nwaves; w++) {
+            mc_tile_ref *la = (mc_tile_ref *)(htab + tab_items + 2 * tab_list * (size_t)w);
+            mc_tile_ref *lm = (mc_tile_ref *)((uint8_t *)la + tab_list);
+            int na = 0, nm = 0;
+            for (size_t i = 0; i < n; i++) {
+                cplan *p = &P[i];
+                int in_wave = p->kind == MC_K_MOMENTUM ? p->wave == w : w == 0;
+                if (!in_wave) continue;
+                for (int t = 0; t < p->ntiles; t++) {
+                    la[na].tile = p->tile_base + t;
+                    la[na++].item = (int32_t)i;
+                    if (p->kind == MC_K_MOMENTUM) {
+                        lm[nm].tile = p->tile_base + t;
+                        lm[nm++].item = (int32_t)i;
+                    }
+                }
             }
+            lc->counts[2 * w] = na;
+            lc->counts[2 * w + 1] = nm;
         }
-        wave_na[w] = na;
-        wave_nm[w] = nm;
+        if (cudaMemcpyAsync(lc->dev, htab + tab_items, 2 * tab_list * (size_t)nwaves, cudaMemcpyHostToDevice,
+                            st) != cudaSuccess) {
+            rc = ERROR_COMPRESSION;
+            goto fail;
+        }
+        lc->sig = sig;
     }
-    if (cudaMemcpyAsync(dtab, htab, tab_total, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+    prof_mark(&prof, "t_lists");
+    if (cudaMemcpyAsync(dtab, htab, tab_items, cudaMemcpyHostToDevice, st) != cudaSuccess ||
         cudaMemsetAsync(results, 0, n * sizeof(mc_enc_result), st) != cudaSuccess) {
-        free(wave_na);
-        free(wave_nm);
         rc = ERROR_COMPRESSION;
         goto fail;
     }
@@ -667,24 +728,24 @@ int mc_compress_grouped(MomentumCompressor *mc, BatchItem *items, size_t n, cons
     /* ---------------------------------------------------------- launch */
     mc->last_launches = 0;
     mc_ktrace *tr = mc_trace_begin(mc);
+    const int staged = !mc_env_off("FALCOM_STAGE");
     for (int w = 0; w < nwaves; w++) {
-        uint8_t *dl = dtab + tab_items + tab_tiles + 2 * tab_tiles * (size_t)w;
+        uint8_t *dl = (uint8_t *)lc->dev + 2 * tab_list * (size_t)w;
         mc_enc_launch L;
         memset(&L, 0, sizeof(L));
         L.items = (const mc_enc_item *)dtab;
         L.results = results;
         L.nitems = (int32_t)n;
-        L.tile_item = (const int32_t *)(dtab + tab_items);
-        L.all_tiles = (const int32_t *)dl;
-        L.nall_tiles = wave_na[w];
-        L.mom_tiles = (const int32_t *)(dl + tab_tiles);
-        L.nmom_tiles = wave_nm[w];
+        L.all_tiles = dl;
+        L.nall_tiles = lc->counts[2 * w];
+        L.mom_tiles = dl + tab_list;
+        L.nmom_tiles = lc->counts[2 * w + 1];
         L.tiles = tiles;
         L.tile_poff = poff;
+        L.staged = staged;
+        L.wave = w;
         int k = mc_launch_encode(&L, st, tr);
         if (k < 0) {
-            free(wave_na);
-            free(wave_nm);
             rc = ERROR_COMPRESSION;
             mc_set_error(mc, "Batch compress: kernel launch failed: %s",
                          cudaGetErrorString(cudaGetLastError()));
@@ -692,8 +753,6 @@ int mc_compress_grouped(MomentumCompressor *mc, BatchItem *items, size_t n, cons
         }
         mc->last_launches += k;
     }
-    free(wave_na);
-    free(wave_nm);
     mc->total_launches += mc->last_launches;
 
     /* ------------------------------------------------- results to host */
@@ -709,6 +768,13 @@ int mc_compress_grouped(MomentumCompressor *mc, BatchItem *items, size_t n, cons
         rc = ERROR_COMPRESSION;
         mc_set_error(mc, "Batch compress: device execution failed: %s", cudaGetErrorString(e));
         goto fail;
+    }
+    for (size_t i = 0; i < n; i++) {
+        if (hres[i].err) {   /* a tile's bulk copies did not complete in time */
+            rc = ERROR_COMPRESSION;
+            mc_set_error(mc, "Batch compress: device tile staging timed out (item %zu)", i);
+            goto fail;
+        }
     }
 
     /* libzstd frame mode: the GPU frames (now in the host arena) are
@@ -1004,6 +1070,7 @@ static size_t sign_content_len(size_t size) {
     return (s > 0 && frame_blocks(s) == nb) ? s : 0;
 }
 
+
 /* Adds agg_w * (decoded item) into the instance's aggregate for every
  * decoded float32 item of a segment whose batch index has an offset.  The
  * source is the device copy of the decoded tensor; queued on the instance's
@@ -1283,25 +1350,34 @@ static int dec_segment(MomentumCompressor *mc, const BatchItem *items, size_t n,
 
     prof_mark(&prof, "alloc");
     /* ------------------------------------------------------- tables */
+    /* host upload: [items][frame jobs]; device: the same, then job lengths,
+     * results, per-tile counts and offsets; the tile lists (all tiles,
+     * momentum tiles) come from the list cache for a recent structure */
     size_t t_items = ALIGN_UP(n * sizeof(mc_dec_item), 256);
-    size_t t_tiles = ALIGN_UP((size_t)(ntiles + 1) * 4, 256);
+    size_t t_tiles = ALIGN_UP((size_t)(ntiles + 1) * sizeof(mc_tile_ref), 256);
     size_t t_jobs = ALIGN_UP((size_t)(njobs + 1) * sizeof(mc_unframe_job), 256);
     size_t t_lens = ALIGN_UP((size_t)(njobs + 1) * 8, 256);
     size_t t_res = ALIGN_UP(n * sizeof(mc_dec_result), 256);
     size_t t_count = ALIGN_UP((size_t)(ntiles + 1) * 4, 256);
     size_t t_poff = ALIGN_UP((size_t)(ntiles + 1) * 8, 256);
-    size_t tab = t_items + 3 * t_tiles + t_jobs;
+    size_t tab = t_items + t_jobs;
     size_t dyn = t_lens + t_res + t_count + t_poff;
-    uint8_t *ht = (uint8_t *)scratch_host(&mc->scratch, SH_TABLES, tab + t_lens + t_res);
+    uint64_t sig = sig_mix(0xBB67AE8584CAA73Bull, (uint64_t)n);
+    for (size_t i = 0; i < n; i++)
+        sig = sig_mix(sig, D[i].ok ? (((uint64_t)D[i].kind << 40) ^ (uint64_t)(uint32_t)D[i].ntiles) : ~0ull);
+    int lhit = 0;
+    mc_listcache *lc = lists_get(mc, mc->dec_lists, sig, 2, 2 * t_tiles, &lhit);
+    uint8_t *ht = (uint8_t *)scratch_host(&mc->scratch, SH_TABLES, tab + t_lens + t_res + (lhit ? 0 : 2 * t_tiles));
     uint8_t *dt = (uint8_t *)scratch_dev(&mc->scratch, SD_TABLES, tab + dyn);
-    if (!ht || !dt) { rc = ERROR_ALLOCATION; goto fail_arena; }
+    if (!ht || !dt || !lc) { rc = ERROR_ALLOCATION; goto fail_arena; }
+    prof_mark(&prof, "t_scratch");
     cudaStreamSynchronize(st);
-    memset(ht, 0, tab);
+    prof_mark(&prof, "t_sync");
+    if (njobs) memset(ht + t_items, 0, t_jobs);
     mc_dec_item *hi = (mc_dec_item *)ht;
-    int32_t *h_ti = (int32_t *)(ht + t_items);
-    int32_t *h_all = (int32_t *)(ht + t_items + t_tiles);
-    int32_t *h_mom = (int32_t *)(ht + t_items + 2 * t_tiles);
-    mc_unframe_job *h_jobs = (mc_unframe_job *)(ht + t_items + 3 * t_tiles);
+    mc_unframe_job *h_jobs = (mc_unframe_job *)(ht + t_items);
+    mc_tile_ref *h_all = (mc_tile_ref *)(ht + tab + t_lens + t_res);
+    mc_tile_ref *h_mom = (mc_tile_ref *)(ht + tab + t_lens + t_res + t_tiles);
     int64_t *d_lens = (int64_t *)(dt + tab);
     mc_dec_result *d_res = (mc_dec_result *)(dt + tab + t_lens);
     int32_t *d_count = (int32_t *)(dt + tab + t_lens + t_res);
@@ -1309,8 +1385,9 @@ static int dec_segment(MomentumCompressor *mc, const BatchItem *items, size_t n,
     int na = 0, nm = 0;
     for (size_t i = 0; i < n; i++) {
         dplan *d = &D[i];
-        if (!d->ok) continue;
         mc_dec_item *I = &hi[i];
+        memset(I, 0, sizeof(*I));
+        if (!d->ok) continue;
         I->kind = d->kind;
         I->codec = d->dcodec;
         I->n = (int64_t)(d->kind == MC_D_COPY ? d->bytes : d->n);
@@ -1389,11 +1466,24 @@ static int dec_segment(MomentumCompressor *mc, const BatchItem *items, size_t n,
                            (uintptr_t)I->mem_out | (uintptr_t)I->prev;
             I->vec = ((al & 15) == 0) && (((uintptr_t)I->data & need) == 0);
         }
-        for (int t = 0; t < d->ntiles; t++) {
-            h_ti[d->tile_base + t] = (int32_t)i;
-            h_all[na++] = d->tile_base + t;
-            if (d->kind == MC_D_MOMENTUM) h_mom[nm++] = d->tile_base + t;
+        if (!lhit) {
+            for (int t = 0; t < d->ntiles; t++) {
+                h_all[na].tile = d->tile_base + t;
+                h_all[na++].item = (int32_t)i;
+                if (d->kind == MC_D_MOMENTUM) {
+                    h_mom[nm].tile = d->tile_base + t;
+                    h_mom[nm++].item = (int32_t)i;
+                }
+            }
         }
+    }
+    prof_mark(&prof, "t_fill");
+    if (!lhit) {
+        lc->counts[0] = na;
+        lc->counts[1] = nm;
+        if (cudaMemcpyAsync(lc->dev, ht + tab + t_lens + t_res, 2 * t_tiles, cudaMemcpyHostToDevice, st) !=
+            cudaSuccess) { rc = ERROR_DECOMPRESSION; goto fail_arena; }
+        lc->sig = sig;
     }
     if (cudaMemcpyAsync(dt, ht, tab, cudaMemcpyHostToDevice, st) != cudaSuccess ||
         cudaMemsetAsync(d_res, 0, t_res, st) != cudaSuccess) { rc = ERROR_DECOMPRESSION; goto fail_arena; }
@@ -1405,7 +1495,7 @@ static int dec_segment(MomentumCompressor *mc, const BatchItem *items, size_t n,
     if (njobs) {
         /* bitmaps must decode into clean zero-padded words */
         if (content_bytes) cudaMemsetAsync(content, 0, content_bytes, st);
-        int k = mc_launch_unframe((const mc_unframe_job *)(dt + t_items + 3 * t_tiles), njobs, st, tr);
+        int k = mc_launch_unframe((const mc_unframe_job *)(dt + t_items), njobs, st, tr);
         if (k < 0) { rc = ERROR_DECOMPRESSION; goto fail_arena; }
         mc->last_launches += k;
     }
@@ -1415,13 +1505,13 @@ static int dec_segment(MomentumCompressor *mc, const BatchItem *items, size_t n,
         L.items = (const mc_dec_item *)dt;
         L.results = d_res;
         L.nitems = (int32_t)n;
-        L.tile_item = (const int32_t *)(dt + t_items);
-        L.all_tiles = (const int32_t *)(dt + t_items + t_tiles);
-        L.nall_tiles = na;
-        L.mom_tiles = (const int32_t *)(dt + t_items + 2 * t_tiles);
-        L.nmom_tiles = nm;
+        L.all_tiles = lc->dev;
+        L.nall_tiles = lc->counts[0];
+        L.mom_tiles = (uint8_t *)lc->dev + t_tiles;
+        L.nmom_tiles = lc->counts[1];
         L.tile_count = d_count;
         L.tile_poff = d_poff;
+        L.staged = !mc_env_off("FALCOM_STAGE");
         int k = mc_launch_decode(&L, st, tr);
         if (k < 0) { rc = ERROR_DECOMPRESSION; goto fail_arena; }
         mc->last_launches += k;
@@ -1447,6 +1537,13 @@ static int dec_segment(MomentumCompressor *mc, const BatchItem *items, size_t n,
 
     /* an in-place frame that was not what its size suggested: redo the
      * segment with every frame expanded (nothing is committed yet) */
+    for (size_t i = 0; i < n; i++) {
+        if (D[i].ok && h_res[i].err >= 2) {   /* a tile's bulk copies did not complete in time */
+            mc_set_error(mc, "Batch decompress: device tile staging timed out (item %zu)", i);
+            rc = ERROR_DECOMPRESSION;
+            goto fail_arena;
+        }
+    }
     for (size_t i = 0; i < n; i++) {
         if (D[i].ok && h_res[i].err) {
             if (prof.on)

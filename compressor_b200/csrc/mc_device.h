@@ -50,7 +50,7 @@ typedef struct {
     uint32_t *dom_words;    /* MOMENTUM: dominant sign per kernel, ceil(K/32) words */
     uint32_t *blk_pos;      /* MOMENTUM: frame offset of each bitmap block's content (~0 = RLE) */
     int32_t max_blocks;     /* MOMENTUM: capacity of blk_pos */
-    int32_t pad_e;
+    int32_t wave;           /* launch wave the item runs in */
     int64_t n;              /* elements */
     int64_t K;              /* kernels (MOMENTUM) */
     int32_t ks;             /* kernel size h*w (MOMENTUM) */
@@ -95,14 +95,21 @@ typedef struct {
     const mc_enc_item *items;   /* device */
     mc_enc_result *results;     /* device, zeroed by the caller before the first wave */
     int32_t nitems;
-    const int32_t *tile_item;   /* device: item index of every tile id */
-    const int32_t *all_tiles;   /* device: tile ids processed by passes 1 and 4 */
+    const void *all_tiles;      /* device mc_tile_ref[]: tiles processed by passes 1 and 4 */
     int32_t nall_tiles;
-    const int32_t *mom_tiles;   /* device: tile ids of momentum items (passes 2, 3) */
+    const void *mom_tiles;      /* device mc_tile_ref[]: tiles of momentum items (passes 2, 3) */
     int32_t nmom_tiles;
     mc_enc_tile *tiles;         /* device scratch, one per tile id */
     int64_t *tile_poff;         /* device scratch, ntiles */
+    int32_t staged;             /* 1: stage tiles of aligned items in shared memory (bulk copies) */
+    int32_t wave;               /* wave of this launch (finalize kernels skip other items) */
 } mc_enc_launch;
+
+/* One entry of a launch's tile list: tile id and the item it belongs to. */
+typedef struct {
+    int32_t tile;
+    int32_t item;
+} mc_tile_ref;
 
 /* ---------------------------------------------------------------- decode */
 enum {
@@ -180,13 +187,14 @@ typedef struct {
     const mc_dec_item *items;
     mc_dec_result *results;     /* zeroed by the caller */
     int32_t nitems;
-    const int32_t *tile_item;   /* item index of every tile id */
-    const int32_t *all_tiles;   /* tile ids for the reconstruct kernel */
+    const void *all_tiles;      /* mc_tile_ref[] for the reconstruct kernel */
     int32_t nall_tiles;
-    const int32_t *mom_tiles;   /* tile ids of momentum items (prefix kernel) */
+    const void *mom_tiles;      /* mc_tile_ref[] of momentum items (prefix kernel) */
     int32_t nmom_tiles;
     int32_t *tile_count;        /* scratch */
     int64_t *tile_poff;         /* scratch */
+    int32_t staged;             /* 1: stage tiles of aligned items in shared memory (bulk copies) */
+    int32_t pad;
 } mc_dec_launch;
 
 /* Weighted accumulation of decoded tensors into an aggregate:
@@ -204,7 +212,7 @@ typedef struct {
 /* Optional per-kernel event trace (events created by the host). */
 enum {
     MC_KT_ENC_PASS1 = 0, MC_KT_ENC_PASS2, MC_KT_ENC_PASS3, MC_KT_ENC_PASS4, MC_KT_ACCUM,
-    MC_KT_UNFRAME, MC_KT_DEC_PREFIX, MC_KT_DEC_RECON, MC_NKERN
+    MC_KT_UNFRAME, MC_KT_DEC_PREFIX, MC_KT_DEC_RECON, MC_KT_ENC_FINAL, MC_NKERN
 };
 #define MC_KTRACE_MAX 64
 typedef struct {

@@ -117,6 +117,18 @@ typedef struct {
     const size_t *shape;
 } mc_keyreq;
 
+/* Device-resident tile lists of a recent batch structure: a call whose
+ * per-item plan (kinds, tile counts, waves) hashes to `sig` reuses them. */
+#define MC_LIST_CACHE 8
+typedef struct {
+    uint64_t sig;             /* 0: empty */
+    unsigned long long used;
+    void *dev;                /* nlists lists of list_bytes each */
+    size_t bytes;
+    int nlists;
+    int *counts;              /* entries of every list */
+} mc_listcache;
+
 struct MomentumCompressor {
     CompressorConfig config;
     char current_client_id[256];
@@ -135,6 +147,8 @@ struct MomentumCompressor {
     unsigned state_gen;      /* bumped when records are deleted (resets) */
     mc_keycache enc_kc[MC_KC_SLOTS], dec_kc[MC_KC_SLOTS];
     unsigned long long kc_tick;
+    mc_listcache enc_lists[MC_LIST_CACHE], dec_lists[MC_LIST_CACHE];
+    unsigned long long lc_tick;
 
     struct {
         size_t total_compressions;
@@ -184,6 +198,7 @@ void mc_layer_key(char *out, size_t cap, const char *layer, const size_t *shape,
 void mc_memory_key(char *out, size_t cap, const char *client, const char *layer_key);
 int mc_should_lossy(const char *name, size_t n, DataType dt, size_t threshold);
 int mc_env_flag(const char *name);
+int mc_env_off(const char *name);
 void mc_set_error(MomentumCompressor *mc, const char *fmt, ...);
 void mc_log(const MomentumCompressor *mc, int level, const char *fmt, ...);
 int mc_ptr_is_device(const void *p, int *device);
@@ -218,6 +233,9 @@ void rec_commit(mc_tensor **slot, mc_tensor **spare, mc_tensor *t);
 void keycache_free(mc_keycache *kc);
 mc_keycache *keycache_get(MomentumCompressor *mc, mc_keycache *set, const char *client, const mc_keyreq *req,
                           size_t n, int *rc);
+
+/* tile-list cache (mc_batch.c) */
+void listcache_free(MomentumCompressor *mc, mc_listcache *set);
 
 /* batch engines (mc_batch.c) */
 int mc_compress_grouped(MomentumCompressor *mc, BatchItem *items, size_t n, const char *client,

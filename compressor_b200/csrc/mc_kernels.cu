@@ -7,7 +7,8 @@
 // compiled -O3 -ffast-math with FMA contraction), and this file is compiled
 // with -fmad=false so the compiler adds no contraction of its own.
 //
-// Encoder, one launch per pass over the batch tile list (one CTA per tile):
+// Encoder, one streaming launch per pass over the batch tile list
+// (persistent CTAs, tiles staged in shared memory by bulk copies):
 //   pass1  stats sums, min/max, per-kernel sign consistency -> bitmap and
 //          dominant-sign words, history copy          (ref :1322-1431, :2040-2062)
 //   pass2  squared deviations around the float means   (ref :1384-1416)
@@ -15,10 +16,11 @@
 //          (ref :2094-2170)
 //   pass4  residual codec (q8 / int4 / raw) and dense dominant-sign packing
 //          (ref :2196-2214 replaced; :2258-2283)
-//   frames zstd frames with Raw / RLE blocks for bitmap, signs and lossless
-//          payloads (ref :2222-2256 framing via libzstd replaced)
-// The last CTA of an item in each pass (atomic ticket) reduces the per-tile
-// partials in a fixed order, so every result is run-to-run deterministic.
+// zstd frames with Raw / RLE blocks for bitmap, signs and lossless payloads
+// are written in place by passes 1 and 4 (ref :2222-2256 framing via libzstd
+// replaced).  Every pass writes per-tile partials; a finalize kernel after
+// passes 1-3 (one CTA per item) reduces them in tile order, so every result
+// is run-to-run deterministic.
 //
 // Decoder: prefix (predicted-kernel offsets per tile) then reconstruct
 // (ref :3186-3474), plus an optional frame-expansion kernel for
@@ -142,16 +144,6 @@ __device__ int block_excl_scan(int v, int *sh, int *total) {
     return sh[w] + x - v;
 }
 
-// Elect the last CTA of an item for pass `phase` (all threads get the answer).
-__device__ bool last_cta(uint32_t *ticket, int ntiles, int *flag) {
-    __threadfence();
-    __syncthreads();
-    if (threadIdx.x == 0) *flag = (atomicAdd(ticket, 1u) == (uint32_t)(ntiles - 1));
-    __syncthreads();
-    if (*flag) __threadfence();
-    return *flag != 0;
-}
-
 __device__ __forceinline__ int qmax_of(int codec) {
     return (codec == MC_DC_INT4 || codec == MC_DC_INT4_RAW) ? 7 : 127;
 }
@@ -254,6 +246,145 @@ __device__ int64_t scan_tile_counts(const int32_t *cnt, int stride_words, int ba
     return carry;
 }
 
+
+// ------------------------------------------------------------ bulk staging
+// A tile's float inputs are brought into shared memory by one thread with
+// 1-D bulk async copies (cp.async.bulk, TMA engine, no multicast) completing
+// on one mbarrier, so a CTA has its whole tile in flight at once without
+// spending registers on it.  Copies need 16-byte aligned addresses and
+// sizes: the aligned body of the tile is copied in bulk and the remaining
+// (< 4) elements by plain loads.  Every wait on the mbarrier is bounded.
+#define STAGE_ELEMS 4096
+#define MBAR_SPIN_LIMIT (1u << 24)
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"(dst), "l"(src), "r"(bytes), "r"(bar) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile("{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+                 "selp.u32 %0, 1, 0, p;\n\t}" : "=r"(done) : "r"(bar), "r"(parity) : "memory");
+    return done != 0;
+}
+// Bounded wait for phase `parity`; false when the limit ran out.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+    for (uint32_t i = 0; i < MBAR_SPIN_LIMIT; i++)
+        if (mbar_try_wait(bar, parity)) return true;
+    return false;
+}
+
+// ------------------------------------------------------- persistent tiles
+// The streaming passes run persistent CTAs: CTA b walks a contiguous range of
+// the launch's tile list (forwards, or backwards so that a pass starts on the
+// tiles the previous pass touched last, which are still in L2) through a
+// pipeline of NST shared-memory stages: while the CTA computes tile i, the
+// bulk copies of tiles i+1 .. i+NST-1 are in flight.  Thread 0 plans and
+// issues; a staged tile's descriptor travels in shared memory, published by
+// the mbarrier arrive.  A tile only writes its outputs and its partials: the
+// per-item reductions run in separate finalize kernels, so the streaming
+// loop has no fences or atomics.
+#define NSTAGE_ARR 3
+
+struct StageDesc {
+    const float *src[NSTAGE_ARR];   // global source of every staged array (NULL: not staged)
+    int64_t e0, e1;                 // element range of the tile
+    int gt;                         // tile id
+    int ii;                         // item index
+};
+
+struct TileShared {
+    uint64_t bar;
+    StageDesc d;
+};
+
+__device__ __forceinline__ uint32_t stage_body_bytes(const StageDesc &d) {
+    return (uint32_t)(((d.e1 - d.e0) * 4) & ~(int64_t)15);
+}
+
+// Thread 0: start the bulk copies of a tile into a stage buffer of NA
+// arrays; a tile with nothing staged still arrives so that the stage's phase
+// completes.
+template <int NA>
+__device__ void pipe_issue(uint32_t bar, float *buf, const StageDesc &d) {
+    const uint32_t body = stage_body_bytes(d);
+    uint32_t total = 0;
+#pragma unroll
+    for (int k = 0; k < NA; k++)
+        if (d.src[k]) total += body;
+    mbar_expect_tx(bar, total);
+    if (body) {
+#pragma unroll
+        for (int k = 0; k < NA; k++)
+            if (d.src[k]) bulk_g2s(smem_u32(buf + k * STAGE_ELEMS), d.src[k] + d.e0, body, bar);
+    }
+}
+
+// All threads, after the wait: the (< 4) trailing elements of the staged
+// arrays that the bulk copies left out.
+// (visible to the block after the barrier that follows the wait)
+template <int NA>
+__device__ void pipe_tail(float *buf, const StageDesc &d) {
+    const int64_t t0 = d.e0 + stage_body_bytes(d) / 4;
+    if (t0 >= d.e1) return;
+#pragma unroll
+    for (int k = 0; k < NA; k++) {
+        if (!d.src[k]) continue;
+        for (int64_t e = t0 + threadIdx.x; e < d.e1; e += TPB) buf[k * STAGE_ELEMS + (e - d.e0)] = d.src[k][e];
+    }
+}
+
+// Staged copy of array k of a tile as a pointer indexed by element number,
+// or the global array when it is not staged.
+__device__ __forceinline__ const float *staged_or(const StageDesc &d, const float *buf, int k, const float *g) {
+    return d.src[k] ? buf + k * STAGE_ELEMS - d.e0 : g;
+}
+
+// One CTA per tile: list entry blockIdx.x holds the tile id and its item
+// index.  plan(StageDesc&) runs on thread 0 and fills the element range and
+// the arrays to stage (src[k] for k < NA); thread 0 then starts their bulk
+// copies, all threads copy the (< 4) trailing elements the copies leave out
+// and wait (bounded) on the mbarrier, and body(const StageDesc&, const float
+// *buf) runs with the tile in shared memory.  A copy that does not complete
+// within the spin limit sets the item's error flag and skips the tile.
+template <int NA, class Plan, class Body>
+__device__ void run_tile(const int2 *list, float *stage_mem, uint64_t *bar, StageDesc *sd, int32_t *err_of_item,
+                         int err_stride_words, Plan plan, Body body) {
+    const uint32_t b = smem_u32(bar);
+    if (threadIdx.x == 0) {
+        const int2 e = list[blockIdx.x];
+        StageDesc d;
+        d.gt = e.x;
+        d.ii = e.y;
+        plan(d);
+        *sd = d;
+        mbar_init(b, 1);
+        pipe_issue<NA>(b, stage_mem, d);
+    }
+    __syncthreads();
+    const StageDesc d = *sd;
+    pipe_tail<NA>(stage_mem, d);
+    bool ok = mbar_wait(b, 0);
+    if (!ok) ok = mbar_wait(b, 0);   // one more bounded wait for the copies in flight
+    if (!__syncthreads_and(ok)) {
+        if (threadIdx.x == 0) err_of_item[(size_t)d.ii * err_stride_words] = 2;
+        return;
+    }
+    body(d, (const float *)stage_mem);
+}
+
+#define STAGE_BYTES(na) ((size_t)(na) * STAGE_ELEMS * sizeof(float))
+
 // ------------------------------------------------------------------ frames
 // zstd frames are written in place by the passes: header (magic, descriptor
 // 0xA0 = single segment + 4-byte content size), then blocks of at most 2^17
@@ -343,24 +474,18 @@ __device__ void write_frame_headers(const mc_enc_item &I, const mc_enc_launch &L
 }
 
 // ------------------------------------------------------------------ pass 1
-__global__ void __launch_bounds__(TPB) k_enc_pass1(mc_enc_launch L) {
-    __shared__ Red red;
-    __shared__ int s_flag;
-    __shared__ int scan_sh[NWARP + 1];
-    __shared__ int s_blk[MAX_RLE_BLOCKS + 1];
-    const int gt = L.all_tiles[blockIdx.x];
-    const int ii = L.tile_item[gt];
+__device__ void pass1_tile(const mc_enc_launch &L, const StageDesc &d, const float *buf, Red &red) {
+    const int ii = d.ii;
     const mc_enc_item I = L.items[ii];
-    const int t = gt - I.tile_base;
-    mc_enc_result *R = L.results + ii;
-    double d[4] = {0.0, 0.0, 0.0, 0.0};
+    const int t = d.gt - I.tile_base;
+    double dd[4] = {0.0, 0.0, 0.0, 0.0};
     long long l[2] = {0, 0};
     float mn = FLT_MAX, mx = -FLT_MAX, mx2 = 0.0f;
 
     if (I.kind == MC_K_MOMENTUM) {
         const TileRange tr = mom_range(I, t);
-        const float *cur = (const float *)I.cur;
-        const float *prev = I.prev;
+        const float *cur = staged_or(d, buf, 0, (const float *)I.cur);
+        const float *prev = staged_or(d, buf, 1, I.prev);
         float *hist = (float *)I.hist_out;
         for (int64_t g = tr.e0 + 4 * (int64_t)threadIdx.x; g < tr.e1; g += 4 * TPB) {
             float c[4], p[4];
@@ -369,8 +494,8 @@ __global__ void __launch_bounds__(TPB) k_enc_pass1(mc_enc_launch L) {
 #pragma unroll
             for (int j = 0; j < 4; j++) {
                 if (g + j < tr.e1) {
-                    d[0] += (double)fabsf(c[j]);
-                    d[1] += (double)fabsf(p[j]);
+                    dd[0] += (double)fabsf(c[j]);
+                    dd[1] += (double)fabsf(p[j]);
                     mn = c[j] < mn ? c[j] : mn;
                     mx = c[j] > mx ? c[j] : mx;
                 }
@@ -384,7 +509,8 @@ __global__ void __launch_bounds__(TPB) k_enc_pass1(mc_enc_launch L) {
             for (int64_t q = (int64_t)t * per + threadIdx.x; q < q1; q += TPB)
                 ((uint4 *)I.sg_frame)[q] = make_uint4(0u, 0u, 0u, 0u);
         }
-        // per-kernel sign consistency: one lane per kernel, 32 kernels per ballot word
+        // per-kernel sign consistency: one lane per kernel, 32 kernels per
+        // ballot word (reads the staged tile when there is one)
         const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
         const float inv_ks = __fdiv_rn(1.0f, (float)I.ks);
         int P = 0;
@@ -415,39 +541,14 @@ __global__ void __launch_bounds__(TPB) k_enc_pass1(mc_enc_launch L) {
             }
         }
         l[0] = P;
-        block_reduce(red, d, 2, mn, mx, mx2, l, 1);
+        block_reduce(red, dd, 2, mn, mx, mx2, l, 1);
         if (threadIdx.x == 0) {
-            mc_enc_tile &T = L.tiles[gt];
-            T.s_cur = d[0];
-            T.s_prev = d[1];
+            mc_enc_tile &T = L.tiles[d.gt];
+            T.s_cur = dd[0];
+            T.s_prev = dd[1];
             T.mn = mn;
             T.mx = mx;
             T.P = (int32_t)l[0];
-        }
-        if (last_cta(&R->ticket[0], I.ntiles, &s_flag)) {
-            double a[4] = {0.0, 0.0, 0.0, 0.0};
-            long long z[2] = {0, 0};
-            float tmn = FLT_MAX, tmx = -FLT_MAX, t2 = 0.0f;
-            for (int i = threadIdx.x; i < I.ntiles; i += TPB) {
-                const mc_enc_tile *T = L.tiles + I.tile_base + i;
-                a[0] += __ldcg(&T->s_cur);
-                a[1] += __ldcg(&T->s_prev);
-                const float tm = __ldcg(&T->mn), tx = __ldcg(&T->mx);
-                tmn = tm < tmn ? tm : tmn;
-                tmx = tx > tmx ? tx : tmx;
-            }
-            block_reduce(red, a, 2, tmn, tmx, t2, z, 0);
-            const int64_t total = scan_tile_counts(&L.tiles[0].P, (int)(sizeof(mc_enc_tile) / 4),
-                                                   I.tile_base, I.ntiles, L.tile_poff, scan_sh);
-            write_frame_headers(I, L, R, total, s_blk);
-            if (threadIdx.x == 0) {
-                const double dn = (double)I.n;
-                R->cm = __double2float_rn(__ddiv_rn(a[0], dn));
-                R->pm = __double2float_rn(__ddiv_rn(a[1], dn));
-                R->gmin = tmn;
-                R->gmax = tmx;
-                R->P = total;
-            }
         }
         return;
     }
@@ -457,7 +558,7 @@ __global__ void __launch_bounds__(TPB) k_enc_pass1(mc_enc_launch L) {
     const int64_t e1 = min(e0 + (int64_t)I.tile_kernels, I.n);
     if (I.kind == MC_K_FRAME) {
         // lossless payload: history copy plus an all-Raw zstd frame of the
-        // input bytes (tiles of 2^15 bytes never straddle a 2^17-byte block)
+        // input bytes (tiles of at most 2^15 bytes never straddle a 2^17-byte block)
         const uint8_t *src = (const uint8_t *)I.cur;
         uint8_t *hist = (uint8_t *)I.hist_out;
         uint8_t *fr = I.data_out;
@@ -516,7 +617,7 @@ __global__ void __launch_bounds__(TPB) k_enc_pass1(mc_enc_launch L) {
         return;
     }
     // MC_K_QUANT: max |x| for the scale, history copy
-    const float *cur = (const float *)I.cur;
+    const float *cur = staged_or(d, buf, 0, (const float *)I.cur);
     float *hist = (float *)I.hist_out;
     for (int64_t g = e0 + 4 * (int64_t)threadIdx.x; g < e1; g += 4 * TPB) {
         float c[4];
@@ -526,12 +627,84 @@ __global__ void __launch_bounds__(TPB) k_enc_pass1(mc_enc_launch L) {
             if (g + j < e1) mx2 = fmaxf(mx2, fabsf(c[j]));
         if (hist) st4(hist, g, e1, I.vec, c);
     }
-    block_reduce(red, d, 0, mn, mx, mx2, l, 0);
-    if (threadIdx.x == 0) L.tiles[gt].maxr = mx2;
-    if (last_cta(&R->ticket[0], I.ntiles, &s_flag)) {
+    block_reduce(red, dd, 0, mn, mx, mx2, l, 0);
+    if (threadIdx.x == 0) L.tiles[d.gt].maxr = mx2;
+}
+
+// Thread 0: tile range of an encoder tile (nothing staged yet).
+__device__ __forceinline__ const mc_enc_item &enc_plan_range(const mc_enc_launch &L, StageDesc &d) {
+    const mc_enc_item &I = L.items[d.ii];
+    const int t = d.gt - I.tile_base;
+    if (I.kind == MC_K_MOMENTUM) {
+        const TileRange tr = mom_range(I, t);
+        d.e0 = tr.e0;
+        d.e1 = tr.e1;
+    } else {
+        d.e0 = (int64_t)t * I.tile_kernels;
+        d.e1 = min(d.e0 + (int64_t)I.tile_kernels, I.n);
+    }
+    d.src[0] = d.src[1] = d.src[2] = nullptr;
+    return I;
+}
+__device__ __forceinline__ bool stageable(int staged, const mc_enc_item &I, const StageDesc &d) {
+    return staged && I.vec && d.e1 - d.e0 <= STAGE_ELEMS;
+}
+#define ENC_ERR(L) &(L).results[0].err, (int)(sizeof(mc_enc_result) / 4)
+
+__global__ void __launch_bounds__(TPB) k_enc_pass1(mc_enc_launch L) {
+    __shared__ Red red;
+    __shared__ TileShared ts;
+    extern __shared__ __align__(128) float s_stage[];
+    run_tile<2>((const int2 *)L.all_tiles, s_stage, &ts.bar, &ts.d, ENC_ERR(L),
+                [&](StageDesc &d) {
+                    const mc_enc_item &I = enc_plan_range(L, d);
+                    if ((I.kind == MC_K_MOMENTUM || I.kind == MC_K_QUANT) && stageable(L.staged, I, d)) {
+                        d.src[0] = (const float *)I.cur;
+                        if (I.kind == MC_K_MOMENTUM) d.src[1] = I.prev;
+                    }
+                },
+                [&](const StageDesc &d, const float *buf) { pass1_tile(L, d, buf, red); });
+}
+
+// Per-item results of pass 1 (one CTA per item of the wave): means and raw
+// min / max of a momentum layer, the exclusive scan of its per-tile predicted
+// counts, the bitmap / sign frame headers; the scale of a direct quantised
+// tensor.  Reductions run over the tiles in order (deterministic).
+__global__ void __launch_bounds__(TPB) k_enc_final1(mc_enc_launch L) {
+    __shared__ Red red;
+    __shared__ int scan_sh[NWARP + 1];
+    __shared__ int s_blk[MAX_RLE_BLOCKS + 1];
+    const int ii = blockIdx.x;
+    const mc_enc_item I = L.items[ii];
+    if (I.wave != L.wave) return;
+    mc_enc_result *R = L.results + ii;
+    double a[4] = {0.0, 0.0, 0.0, 0.0};
+    long long z[2] = {0, 0};
+    if (I.kind == MC_K_MOMENTUM) {
+        float tmn = FLT_MAX, tmx = -FLT_MAX, t2 = 0.0f;
+        for (int i = threadIdx.x; i < I.ntiles; i += TPB) {
+            const mc_enc_tile *T = L.tiles + I.tile_base + i;
+            a[0] += T->s_cur;
+            a[1] += T->s_prev;
+            tmn = T->mn < tmn ? T->mn : tmn;
+            tmx = T->mx > tmx ? T->mx : tmx;
+        }
+        block_reduce(red, a, 2, tmn, tmx, t2, z, 0);
+        const int64_t total = scan_tile_counts(&L.tiles[0].P, (int)(sizeof(mc_enc_tile) / 4), I.tile_base,
+                                               I.ntiles, L.tile_poff, scan_sh);
+        write_frame_headers(I, L, R, total, s_blk);
+        if (threadIdx.x == 0) {
+            const double dn = (double)I.n;
+            R->cm = __double2float_rn(__ddiv_rn(a[0], dn));
+            R->pm = __double2float_rn(__ddiv_rn(a[1], dn));
+            R->gmin = tmn;
+            R->gmax = tmx;
+            R->P = total;
+        }
+    } else if (I.kind == MC_K_QUANT) {
         float m = 0.0f, u0 = FLT_MAX, u1 = -FLT_MAX;
-        for (int i = threadIdx.x; i < I.ntiles; i += TPB) m = fmaxf(m, __ldcg(&L.tiles[I.tile_base + i].maxr));
-        block_reduce(red, d, 0, u0, u1, m, l, 0);
+        for (int i = threadIdx.x; i < I.ntiles; i += TPB) m = fmaxf(m, L.tiles[I.tile_base + i].maxr);
+        block_reduce(red, a, 0, u0, u1, m, z, 0);
         if (threadIdx.x == 0) {
             R->maxr = m;
             R->scale = (m == 0.0f) ? 1.0f : __fdiv_rn(m, (float)qmax_of(I.codec));
@@ -543,123 +716,162 @@ __global__ void __launch_bounds__(TPB) k_enc_pass1(mc_enc_launch L) {
 // ------------------------------------------------------------------ pass 2
 __global__ void __launch_bounds__(TPB) k_enc_pass2(mc_enc_launch L) {
     __shared__ Red red;
-    __shared__ int s_flag;
-    const int gt = L.mom_tiles[blockIdx.x];
-    const int ii = L.tile_item[gt];
+    __shared__ TileShared ts;
+    extern __shared__ __align__(128) float s_stage[];
+    run_tile<2>((const int2 *)L.mom_tiles, s_stage, &ts.bar, &ts.d, ENC_ERR(L),
+                    [&](StageDesc &d) {
+                        const mc_enc_item &I = enc_plan_range(L, d);
+                        if (stageable(L.staged, I, d)) {
+                            d.src[0] = (const float *)I.cur;
+                            d.src[1] = I.prev;
+                        }
+                    },
+                    [&](const StageDesc &d, const float *buf) {
+                        const mc_enc_item I = L.items[d.ii];
+                        const mc_enc_result *R = L.results + d.ii;
+                        const float cm = R->cm, pm = R->pm;
+                        const float *cur = staged_or(d, buf, 0, (const float *)I.cur);
+                        const float *prev = staged_or(d, buf, 1, I.prev);
+                        double dd[4] = {0.0, 0.0, 0.0, 0.0};
+                        long long l[2] = {0, 0};
+                        float mn = FLT_MAX, mx = -FLT_MAX, mx2 = 0.0f;
+                        for (int64_t g = d.e0 + 4 * (int64_t)threadIdx.x; g < d.e1; g += 4 * TPB) {
+                            float c[4], p[4];
+                            ld4(cur, g, d.e1, I.vec, c);
+                            ld4(prev, g, d.e1, I.vec, p);
+#pragma unroll
+                            for (int j = 0; j < 4; j++) {
+                                if (g + j < d.e1) {
+                                    const double dc = (double)__fsub_rn(fabsf(c[j]), cm);
+                                    const double dp = (double)__fsub_rn(fabsf(p[j]), pm);
+                                    dd[0] = __fma_rn(dc, dc, dd[0]);
+                                    dd[1] = __fma_rn(dp, dp, dd[1]);
+                                }
+                            }
+                        }
+                        block_reduce(red, dd, 2, mn, mx, mx2, l, 0);
+                        if (threadIdx.x == 0) {
+                            L.tiles[d.gt].v_cur = dd[0];
+                            L.tiles[d.gt].v_prev = dd[1];
+                        }
+                    });
+}
+
+// Per-item results of pass 2: population std of |cur| and |prev|.
+__global__ void __launch_bounds__(TPB) k_enc_final2(mc_enc_launch L) {
+    __shared__ Red red;
+    const int ii = blockIdx.x;
     const mc_enc_item I = L.items[ii];
-    const int t = gt - I.tile_base;
+    if (I.wave != L.wave || I.kind != MC_K_MOMENTUM) return;
     mc_enc_result *R = L.results + ii;
-    const TileRange tr = mom_range(I, t);
-    const float cm = R->cm, pm = R->pm;
-    const float *cur = (const float *)I.cur;
-    const float *prev = I.prev;
-    double d[4] = {0.0, 0.0, 0.0, 0.0};
+    double a[4] = {0.0, 0.0, 0.0, 0.0};
     long long l[2] = {0, 0};
     float mn = FLT_MAX, mx = -FLT_MAX, mx2 = 0.0f;
-    for (int64_t g = tr.e0 + 4 * (int64_t)threadIdx.x; g < tr.e1; g += 4 * TPB) {
-        float c[4], p[4];
-        ld4(cur, g, tr.e1, I.vec, c);
-        ld4(prev, g, tr.e1, I.vec, p);
-#pragma unroll
-        for (int j = 0; j < 4; j++) {
-            if (g + j < tr.e1) {
-                const double dc = (double)__fsub_rn(fabsf(c[j]), cm);
-                const double dp = (double)__fsub_rn(fabsf(p[j]), pm);
-                d[0] = __fma_rn(dc, dc, d[0]);
-                d[1] = __fma_rn(dp, dp, d[1]);
-            }
-        }
+    for (int i = threadIdx.x; i < I.ntiles; i += TPB) {
+        a[0] += L.tiles[I.tile_base + i].v_cur;
+        a[1] += L.tiles[I.tile_base + i].v_prev;
     }
-    block_reduce(red, d, 2, mn, mx, mx2, l, 0);
+    block_reduce(red, a, 2, mn, mx, mx2, l, 0);
     if (threadIdx.x == 0) {
-        L.tiles[gt].v_cur = d[0];
-        L.tiles[gt].v_prev = d[1];
-    }
-    if (last_cta(&R->ticket[1], I.ntiles, &s_flag)) {
-        double a[4] = {0.0, 0.0, 0.0, 0.0};
-        for (int i = threadIdx.x; i < I.ntiles; i += TPB) {
-            a[0] += __ldcg(&L.tiles[I.tile_base + i].v_cur);
-            a[1] += __ldcg(&L.tiles[I.tile_base + i].v_prev);
-        }
-        block_reduce(red, a, 2, mn, mx, mx2, l, 0);
-        if (threadIdx.x == 0) {
-            const double dn = (double)I.n;
-            const float cs = __fsqrt_rn(__double2float_rn(__ddiv_rn(a[0], dn)));
-            const float ps = __fsqrt_rn(__double2float_rn(__ddiv_rn(a[1], dn)));
-            R->cs = cs;
-            R->ps = ps;
-            R->inv_ps = (ps > 1e-8f) ? __fdiv_rn(1.0f, ps) : 1.0f;
-        }
+        const double dn = (double)I.n;
+        const float cs = __fsqrt_rn(__double2float_rn(__ddiv_rn(a[0], dn)));
+        const float ps = __fsqrt_rn(__double2float_rn(__ddiv_rn(a[1], dn)));
+        R->cs = cs;
+        R->ps = ps;
+        R->inv_ps = (ps > 1e-8f) ? __fdiv_rn(1.0f, ps) : 1.0f;
     }
 }
 
 // ------------------------------------------------------------------ pass 3
+// The previous gradient is read only for predicted kernels: it is staged
+// when most kernels of the layer are predicted, else read directly.
 __global__ void __launch_bounds__(TPB) k_enc_pass3(mc_enc_launch L) {
     __shared__ Red red;
-    __shared__ int s_flag;
-    const int gt = L.mom_tiles[blockIdx.x];
-    const int ii = L.tile_item[gt];
-    const mc_enc_item I = L.items[ii];
-    const int t = gt - I.tile_base;
-    mc_enc_result *R = L.results + ii;
-    const TileRange tr = mom_range(I, t);
-    const float cm = R->cm, cs = R->cs, pm = R->pm, inv_ps = R->inv_ps;
-    const bool use_ps = R->ps > 1e-8f;
-    const MomParams mp = {cm, cs, R->gmin, R->gmax, cs > 1e-8f};
-    const float lr = I.lr;
-    const float oml = __fsub_rn(1.0f, lr);
-    const float *cur = (const float *)I.cur;
-    long long mism = 0;
-    float maxr = 0.0f;
-    const uint32_t k0 = (uint32_t)tr.k0;
-    for (int64_t g = tr.e0 + 4 * (int64_t)threadIdx.x; g < tr.e1; g += 4 * TPB) {
-        const QuadBits qb = quad_bits(I.bm_words, I.dom_words, 0u, k0, g, tr.e0, tr.e1, I.ks, I.ksdiv);
-        float c[4], m0[4], p[4], mo[4];
-        ld4(cur, g, tr.e1, I.vec, c);
-        if (I.mem_in) ld4(I.mem_in, g, tr.e1, I.vec, m0);
-        else m0[0] = m0[1] = m0[2] = m0[3] = 0.0f;
-        if (qb.f) ld4(I.prev, g, tr.e1, I.vec, p);
+    __shared__ TileShared ts;
+    extern __shared__ __align__(128) float s_stage[];
+    run_tile<3>((const int2 *)L.mom_tiles, s_stage, &ts.bar, &ts.d, ENC_ERR(L),
+                    [&](StageDesc &d) {
+                        const mc_enc_item &I = enc_plan_range(L, d);
+                        if (stageable(L.staged, I, d)) {
+                            d.src[0] = (const float *)I.cur;
+                            d.src[1] = I.mem_in;
+                            if (2 * L.tiles[d.gt].P >= (int32_t)I.tile_kernels) d.src[2] = I.prev;
+                        }
+                    },
+                    [&](const StageDesc &d, const float *buf) {
+                        const mc_enc_item I = L.items[d.ii];
+                        const mc_enc_result *R = L.results + d.ii;
+                        const TileRange tr = mom_range(I, d.gt - I.tile_base);
+                        const float cm = R->cm, cs = R->cs, pm = R->pm, inv_ps = R->inv_ps;
+                        const bool use_ps = R->ps > 1e-8f;
+                        const MomParams mp = {cm, cs, R->gmin, R->gmax, cs > 1e-8f};
+                        const float lr = I.lr;
+                        const float oml = __fsub_rn(1.0f, lr);
+                        const float *cur = staged_or(d, buf, 0, (const float *)I.cur);
+                        const float *mem_in = staged_or(d, buf, 1, I.mem_in);
+                        const float *prev = staged_or(d, buf, 2, I.prev);
+                        long long mism = 0;
+                        float maxr = 0.0f;
+                        const uint32_t k0 = (uint32_t)tr.k0;
+                        for (int64_t g = tr.e0 + 4 * (int64_t)threadIdx.x; g < tr.e1; g += 4 * TPB) {
+                            const QuadBits qb = quad_bits(I.bm_words, I.dom_words, 0u, k0, g, tr.e0, tr.e1, I.ks,
+                                                          I.ksdiv);
+                            float c[4], m0[4], p[4], mo[4];
+                            ld4(cur, g, tr.e1, I.vec, c);
+                            if (mem_in) ld4(mem_in, g, tr.e1, I.vec, m0);
+                            else m0[0] = m0[1] = m0[2] = m0[3] = 0.0f;
+                            if (qb.f) ld4(prev, g, tr.e1, I.vec, p);
 #pragma unroll
-        for (int j = 0; j < 4; j++) {
-            float r = c[j];
-            mo[j] = m0[j];
-            if ((qb.f >> j) & 1u) {
-                const float pv = __fsub_rn(fabsf(p[j]), pm);
-                const float pn = use_ps ? __fmul_rn(pv, inv_ps) : pv;
-                const float nm = __fmaf_rn(oml, m0[j], __fmul_rn(lr, pn));
-                mo[j] = nm;
-                const bool pos = (qb.pos >> j) & 1u;
-                const float ap = mom_pred_abs(nm, mp);
-                const float pred = pos ? ap : -ap;
-                mism += (pred > 0.0f) != (c[j] > 0.0f);
-                r = x86min(x86max(__fsub_rn(c[j], pred), mp.gmin), mp.gmax);
-            }
-            if (g + j < tr.e1) maxr = fmaxf(maxr, fabsf(r));
-        }
-        st4(I.mem_out, g, tr.e1, I.vec, mo);
+                            for (int j = 0; j < 4; j++) {
+                                float r = c[j];
+                                mo[j] = m0[j];
+                                if ((qb.f >> j) & 1u) {
+                                    const float pv = __fsub_rn(fabsf(p[j]), pm);
+                                    const float pn = use_ps ? __fmul_rn(pv, inv_ps) : pv;
+                                    const float nm = __fmaf_rn(oml, m0[j], __fmul_rn(lr, pn));
+                                    mo[j] = nm;
+                                    const bool pos = (qb.pos >> j) & 1u;
+                                    const float ap = mom_pred_abs(nm, mp);
+                                    const float pred = pos ? ap : -ap;
+                                    mism += (pred > 0.0f) != (c[j] > 0.0f);
+                                    r = x86min(x86max(__fsub_rn(c[j], pred), mp.gmin), mp.gmax);
+                                }
+                                if (g + j < tr.e1) maxr = fmaxf(maxr, fabsf(r));
+                            }
+                            st4(I.mem_out, g, tr.e1, I.vec, mo);
+                        }
+                        double dd[4];
+                        long long l[2] = {mism, 0};
+                        float mn = FLT_MAX, mx = -FLT_MAX;
+                        block_reduce(red, dd, 0, mn, mx, maxr, l, 1);
+                        if (threadIdx.x == 0) {
+                            L.tiles[d.gt].maxr = maxr;
+                            L.tiles[d.gt].mism = l[0];
+                        }
+                    });
+}
+
+// Per-item results of pass 3: max |residual| (the codec scale, written into
+// the payload header) and sign mismatches.
+__global__ void __launch_bounds__(TPB) k_enc_final3(mc_enc_launch L) {
+    __shared__ Red red;
+    const int ii = blockIdx.x;
+    const mc_enc_item I = L.items[ii];
+    if (I.wave != L.wave || I.kind != MC_K_MOMENTUM) return;
+    mc_enc_result *R = L.results + ii;
+    double dd[4];
+    float m = 0.0f, mn = FLT_MAX, mx = -FLT_MAX;
+    long long z[2] = {0, 0};
+    for (int i = threadIdx.x; i < I.ntiles; i += TPB) {
+        m = fmaxf(m, L.tiles[I.tile_base + i].maxr);
+        z[0] += L.tiles[I.tile_base + i].mism;
     }
-    double d[4];
-    long long l[2] = {mism, 0};
-    float mn = FLT_MAX, mx = -FLT_MAX;
-    block_reduce(red, d, 0, mn, mx, maxr, l, 1);
+    block_reduce(red, dd, 0, mn, mx, m, z, 1);
     if (threadIdx.x == 0) {
-        L.tiles[gt].maxr = maxr;
-        L.tiles[gt].mism = l[0];
-    }
-    if (last_cta(&R->ticket[2], I.ntiles, &s_flag)) {
-        float m = 0.0f;
-        long long z[2] = {0, 0};
-        for (int i = threadIdx.x; i < I.ntiles; i += TPB) {
-            m = fmaxf(m, __ldcg(&L.tiles[I.tile_base + i].maxr));
-            z[0] += __ldcg(&L.tiles[I.tile_base + i].mism);
-        }
-        block_reduce(red, d, 0, mn, mx, m, z, 1);
-        if (threadIdx.x == 0) {
-            R->maxr = m;
-            R->mism = z[0];
-            R->scale = (m == 0.0f) ? 1.0f : __fdiv_rn(m, (float)qmax_of(I.codec));
-            if (I.codec == MC_DC_Q8 || I.codec == MC_DC_INT4) *(float *)I.data_out = R->scale;
-        }
+        R->maxr = m;
+        R->mism = z[0];
+        R->scale = (m == 0.0f) ? 1.0f : __fdiv_rn(m, (float)qmax_of(I.codec));
+        if (I.codec == MC_DC_Q8 || I.codec == MC_DC_INT4) *(float *)I.data_out = R->scale;
     }
 }
 
@@ -711,11 +923,10 @@ __device__ __forceinline__ void put_codes(uint8_t *data_out, int codec, int64_t 
 }
 
 // ------------------------------------------------------------------ pass 4
-__global__ void __launch_bounds__(TPB) k_enc_pass4(mc_enc_launch L) {
-    __shared__ int scan_sh[NWARP + 1];
-    __shared__ uint32_t s_sg[TPB + 2];
-    const int gt = L.all_tiles[blockIdx.x];
-    const int ii = L.tile_item[gt];
+__device__ void pass4_tile(const mc_enc_launch &L, const StageDesc &d, const float *buf, int *scan_sh,
+                           uint32_t *s_sg) {
+    const int gt = d.gt;
+    const int ii = d.ii;
     const mc_enc_item I = L.items[ii];
     const int t = gt - I.tile_base;
     const mc_enc_result *R = L.results + ii;
@@ -724,13 +935,14 @@ __global__ void __launch_bounds__(TPB) k_enc_pass4(mc_enc_launch L) {
         const MomParams mp = {R->cm, R->cs, R->gmin, R->gmax, R->cs > 1e-8f};
         const float scale = R->scale;
         const float qm = (float)qmax_of(I.codec);
-        const float *cur = (const float *)I.cur;
+        const float *cur = staged_or(d, buf, 0, (const float *)I.cur);
+        const float *mem = staged_or(d, buf, 1, I.mem_out);
         const uint32_t k0 = (uint32_t)tr.k0;
         for (int64_t g = tr.e0 + 4 * (int64_t)threadIdx.x; g < tr.e1; g += 4 * TPB) {
             const QuadBits qb = quad_bits(I.bm_words, I.dom_words, 0u, k0, g, tr.e0, tr.e1, I.ks, I.ksdiv);
             float c[4], m[4], r[4];
             ld4(cur, g, tr.e1, I.vec, c);
-            if (qb.f) ld4(I.mem_out, g, tr.e1, I.vec, m);
+            if (qb.f) ld4(mem, g, tr.e1, I.vec, m);
 #pragma unroll
             for (int j = 0; j < 4; j++)
                 r[j] = ((qb.f >> j) & 1u) ? mom_residual(c[j], m[j], (qb.pos >> j) & 1u, mp) : c[j];
@@ -800,12 +1012,30 @@ __global__ void __launch_bounds__(TPB) k_enc_pass4(mc_enc_launch L) {
         const int64_t e1 = min(e0 + (int64_t)I.tile_kernels, I.n);
         const float scale = R->scale;
         const float qm = (float)qmax_of(I.codec);
+        const float *cur = staged_or(d, buf, 0, (const float *)I.cur);
         for (int64_t g = e0 + 4 * (int64_t)threadIdx.x; g < e1; g += 4 * TPB) {
             float c[4];
-            ld4((const float *)I.cur, g, e1, I.vec, c);
+            ld4(cur, g, e1, I.vec, c);
             put_codes(I.data_out, I.codec, g, e1, I.vec, c, scale, qm);
         }
     }
+}
+
+__global__ void __launch_bounds__(TPB) k_enc_pass4(mc_enc_launch L) {
+    __shared__ int scan_sh[NWARP + 1];
+    __shared__ uint32_t s_sg[TPB + 2];
+    __shared__ TileShared ts;
+    extern __shared__ __align__(128) float s_stage[];
+    run_tile<2>((const int2 *)L.all_tiles, s_stage, &ts.bar, &ts.d, ENC_ERR(L),
+                    [&](StageDesc &d) {
+                        const mc_enc_item &I = enc_plan_range(L, d);
+                        if ((I.kind == MC_K_MOMENTUM || I.kind == MC_K_QUANT) && stageable(L.staged, I, d)) {
+                            d.src[0] = (const float *)I.cur;
+                            if (I.kind == MC_K_MOMENTUM && 2 * L.tiles[d.gt].P >= (int32_t)I.tile_kernels)
+                                d.src[1] = I.mem_out;
+                        }
+                    },
+                    [&](const StageDesc &d, const float *buf) { pass4_tile(L, d, buf, scan_sh, s_sg); });
 }
 
 // ------------------------------------------------------------------ frames
@@ -970,38 +1200,40 @@ __device__ int64_t check_frame(const uint8_t *f, int mode, int64_t want) {
     return cs;
 }
 
+// Sum of one value per thread over the block (result in every thread).
+__device__ long long block_sum_ll(long long v, long long *sh) {
+    v = warp_sum_ll(v);
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = v;
+    __syncthreads();
+    long long s = 0;
+#pragma unroll
+    for (int j = 0; j < NWARP; j++) s += sh[j];
+    return s;
+}
+
+// Decoder, first launch (one CTA per momentum tile): predicted kernels of the
+// tile from its bitmap words; the first tile of an item also checks the
+// headers of the frames read in place.
 __global__ void __launch_bounds__(TPB) k_dec_prefix(mc_dec_launch L) {
     __shared__ long long sh[NWARP];
-    __shared__ int s_flag;
-    __shared__ int scan_sh[NWARP + 1];
-    const int gt = L.mom_tiles[blockIdx.x];
-    const int ii = L.tile_item[gt];
+    const int2 e = ((const int2 *)L.mom_tiles)[blockIdx.x];
+    const int gt = e.x, ii = e.y;
     const mc_dec_item I = L.items[ii];
     const int t = gt - I.tile_base;
-    mc_dec_result *R = L.results + ii;
     if (t == 0 && threadIdx.x == 0) {
         int bad = 0;
         if (I.bm_mode != MC_BM_WORDS) bad |= check_frame(I.bm_frame, I.bm_mode, (I.bm_bits + 7) >> 3) < 0;
         if (I.sg_mode != MC_BM_WORDS && I.sg_frame) bad |= check_frame(I.sg_frame, I.sg_mode, I.sg_len) < 0;
-        if (bad) R->err = 1;
+        if (bad) L.results[ii].err = 1;
     }
     const DecTile tr = dec_range(I, t);
     const int64_t wb = tr.k0 >> 5, we = (tr.k1 + 31) >> 5;
     const int64_t bm_bits = dec_bm_bits(I);
     int c = 0;
     for (int64_t w = wb + threadIdx.x; w < we; w += TPB) c += __popc(dec_bm_word(I, w) & word_mask(w, bm_bits));
-    long long v = warp_sum_ll(c);
-    if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = v;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        long long s = 0;
-        for (int j = 0; j < NWARP; j++) s += sh[j];
-        L.tile_count[gt] = (int32_t)s;
-    }
-    if (last_cta(&R->ticket, I.ntiles, &s_flag)) {
-        const int64_t total = scan_tile_counts(L.tile_count, 1, I.tile_base, I.ntiles, L.tile_poff, scan_sh);
-        if (threadIdx.x == 0) R->P = total;
-    }
+    const long long tot = block_sum_ll(c, sh);
+    if (threadIdx.x == 0) L.tile_count[gt] = (int32_t)tot;
 }
 
 // Residual values of one quad from the payload (codes * scale or raw floats).
@@ -1033,11 +1265,15 @@ __device__ __forceinline__ void dec_resid4(const mc_dec_item &I, int64_t g, int6
     }
 }
 
-__global__ void __launch_bounds__(TPB) k_dec_recon(mc_dec_launch L) {
-    __shared__ uint32_t s_m[TPB], s_d[TPB];
-    __shared__ int scan_sh[NWARP + 1];
-    const int gt = L.all_tiles[blockIdx.x];
-    const int ii = L.tile_item[gt];
+// Sign bytes a reconstruct tile needs: its predicted kernels' bits start at
+// bit (tile_poff & 7) of the window; up to 8192 kernels per tile, plus the
+// read-ahead of the 5-byte gather.
+#define SIGN_WIN 1040
+
+__device__ void recon_tile(const mc_dec_launch &L, const StageDesc &d, const float *buf, uint32_t *s_m,
+                           uint32_t *s_d, int *scan_sh, uint8_t *s_sb, long long *s_ll) {
+    const int gt = d.gt;
+    const int ii = d.ii;
     const mc_dec_item I = L.items[ii];
     const int t = gt - I.tile_base;
     // the scale header may sit at any byte address (payloads from the caller)
@@ -1060,17 +1296,46 @@ __global__ void __launch_bounds__(TPB) k_dec_recon(mc_dec_launch L) {
         uint32_t m = 0;
         if (wb + i < we) m = dec_bm_word(I, wb + i) & word_mask(wb + i, bm_bits);
         const int pc = __popc(m);
-        const int off_l = block_excl_scan(pc, scan_sh, nullptr);
+        int tot;
+        const int off_l = block_excl_scan(pc, scan_sh, &tot);
+        // offset of the tile's first predicted kernel in the dense signs: the
+        // counts of the item's earlier tiles; the first tile also reports the
+        // item's total
+        long long before = 0, all = 0;
+        for (int k = threadIdx.x; k < I.ntiles; k += TPB) {
+            const long long c = L.tile_count[I.tile_base + k];
+            if (k < t) before += c;
+            all += c;
+        }
+        const int64_t poff = block_sum_ll(before, s_ll);
+        if (t == 0) {
+            const long long P = block_sum_ll(all, s_ll);
+            if (threadIdx.x == 0) L.results[ii].P = P;
+        }
+        // the tile's sign bits, staged as bytes; bytes past the sign content
+        // read as 0xFF: missing signs default to +1 (ref :3296-3302)
+        const int64_t b0 = poff >> 3;
+        const int nb = tot > 0 ? (int)(((poff + tot + 7) >> 3) - b0) : 0;
+        for (int j = threadIdx.x; j < nb + 8; j += TPB) {
+            const int64_t b = b0 + j;
+            uint32_t v = 0xFFu;
+            if (sg && j < nb && b < sg_len) v = src_byte(sg, I.sg_mode, b);
+            s_sb[j] = (uint8_t)v;
+        }
+        __syncthreads();
         uint32_t dm = 0;
         if (pc) {
-            int64_t idx = L.tile_poff[gt] + off_l;
+            const int o = (int)(poff & 7) + off_l;
+            const int ob = o >> 3;
+            uint64_t w = 0;
+#pragma unroll
+            for (int k = 0; k < 5; k++) w |= (uint64_t)s_sb[ob + k] << (8 * k);
+            uint32_t bits = (uint32_t)(w >> (o & 7));
             uint32_t mm = m;
-            while (mm) {
+            while (mm) {   // deposit the pc sign bits at the set bits of m
                 const int b = __ffs(mm) - 1;
-                int bit = 1;   // missing signs default to +1 (ref :3296-3302)
-                if (sg && (idx >> 3) < sg_len) bit = (src_byte(sg, I.sg_mode, idx >> 3) >> (idx & 7)) & 1;
-                dm |= (uint32_t)bit << b;
-                idx++;
+                dm |= (bits & 1u) << b;
+                bits >>= 1;
                 mm &= mm - 1;
             }
         }
@@ -1083,14 +1348,16 @@ __global__ void __launch_bounds__(TPB) k_dec_recon(mc_dec_launch L) {
         const float inv_ps = use_ps ? __fdiv_rn(1.0f, I.ps) : 1.0f;
         const float oml = __fsub_rn(1.0f, lr);
         const uint32_t k0 = (uint32_t)tr.k0;
+        const float *mem_in = staged_or(d, buf, 0, I.mem_in);
+        const float *prev = staged_or(d, buf, 1, I.prev);
         // bitmap / sign words of the tile are in shared memory from word wb on
         for (int64_t g = tr.e0 + 4 * (int64_t)threadIdx.x; g < tr.e1; g += 4 * TPB) {
             const QuadBits qb = quad_bits(s_m, s_d, (uint32_t)wb, k0, g, tr.e0, tr.e1, I.ks, I.ksdiv);
             float r[4], m0[4], p[4], mo[4], rec[4];
             dec_resid4(I, g, tr.e1, scale, r);
-            if (I.mem_in) ld4(I.mem_in, g, tr.e1, I.vec, m0);
+            if (mem_in) ld4(mem_in, g, tr.e1, I.vec, m0);
             else m0[0] = m0[1] = m0[2] = m0[3] = 0.0f;
-            if (qb.f) ld4(I.prev, g, tr.e1, I.vec, p);
+            if (qb.f) ld4(prev, g, tr.e1, I.vec, p);
 #pragma unroll
             for (int j = 0; j < 4; j++) {
                 rec[j] = r[j];
@@ -1126,7 +1393,7 @@ __global__ void __launch_bounds__(TPB) k_dec_recon(mc_dec_launch L) {
     uint8_t *h8 = (uint8_t *)I.hist_out, *o8 = (uint8_t *)I.out;
     if (I.data_mode != MC_BM_WORDS) {
         // lossless frame read in place: check the header the host assumed;
-        // a tile (2^15 bytes) lies inside one block of the frame
+        // a tile (at most 2^15 bytes) lies inside one block of the frame
         if (t == 0 && threadIdx.x == 0 && check_frame(I.data_frame, I.data_mode, I.n) < 0)
             L.results[ii].err = 1;
         if (I.data_mode == MC_BM_RLE) {
@@ -1173,6 +1440,35 @@ __global__ void __launch_bounds__(TPB) k_dec_recon(mc_dec_launch L) {
     }
 }
 
+__global__ void __launch_bounds__(TPB) k_dec_recon(mc_dec_launch L) {
+    __shared__ uint32_t s_m[TPB], s_d[TPB];
+    __shared__ int scan_sh[NWARP + 1];
+    __shared__ uint8_t s_sb[SIGN_WIN];
+    __shared__ long long s_ll[NWARP];
+    __shared__ TileShared ts;
+    extern __shared__ __align__(128) float s_stage[];
+    run_tile<2>((const int2 *)L.all_tiles, s_stage, &ts.bar, &ts.d, &L.results[0].err,
+                (int)(sizeof(mc_dec_result) / 4),
+                    [&](StageDesc &d) {
+                        const mc_dec_item &I = L.items[d.ii];
+                        const int t = d.gt - I.tile_base;
+                        d.src[0] = d.src[1] = d.src[2] = nullptr;
+                        if (I.kind == MC_D_MOMENTUM) {
+                            const DecTile tr = dec_range(I, t);
+                            d.e0 = tr.e0;
+                            d.e1 = tr.e1;
+                            if (L.staged && I.vec && d.e1 - d.e0 <= STAGE_ELEMS) {
+                                d.src[0] = I.mem_in;
+                                if (2 * L.tile_count[d.gt] >= (int32_t)I.tile_kernels) d.src[1] = I.prev;
+                            }
+                        } else {
+                            d.e0 = (int64_t)t * I.tile_kernels;
+                            d.e1 = min(d.e0 + (int64_t)I.tile_kernels, I.n);
+                        }
+                    },
+                    [&](const StageDesc &d, const float *buf) { recon_tile(L, d, buf, s_m, s_d, scan_sh, s_sb, s_ll); });
+}
+
 // ------------------------------------------------------------- aggregate
 __global__ void __launch_bounds__(TPB) k_accumulate(const mc_acc_item *items, const int32_t *tile_item) {
     const int gt = blockIdx.x;
@@ -1205,27 +1501,61 @@ static inline void tr_end(mc_ktrace *tr, cudaStream_t s) {
     }
 }
 
+// Dynamic shared memory of the staged kernels (one stage of NA arrays),
+// opted in above the 48 KiB default once per kernel and device.
+enum { KF_P1 = 0, KF_P2, KF_P3, KF_P4, KF_RECON, KF_N };
+#define MAX_DEVICES 64
+static int g_smem_set[KF_N][MAX_DEVICES];
+
+static void smem_opt_in(int kf, const void *fn, size_t smem) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= MAX_DEVICES) dev = 0;
+    if (!g_smem_set[kf][dev]) {
+        cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        g_smem_set[kf][dev] = 1;
+    }
+}
+
+#define P1_SMEM STAGE_BYTES(2)
+#define P2_SMEM STAGE_BYTES(2)
+#define P3_SMEM STAGE_BYTES(3)
+#define P4_SMEM STAGE_BYTES(2)
+#define RECON_SMEM STAGE_BYTES(2)
+
 extern "C" int mc_launch_encode(const mc_enc_launch *L, void *stream, mc_ktrace *tr) {
     cudaStream_t s = (cudaStream_t)stream;
     int n = 0;
     if (L->nall_tiles > 0) {
+        smem_opt_in(KF_P1, (const void *)k_enc_pass1, P1_SMEM);
         tr_begin(tr, MC_KT_ENC_PASS1, s);
-        k_enc_pass1<<<L->nall_tiles, TPB, 0, s>>>(*L);
+        k_enc_pass1<<<L->nall_tiles, TPB, P1_SMEM, s>>>(*L);
         tr_end(tr, s);
-        n++;
-    }
-    if (L->nmom_tiles > 0) {
-        tr_begin(tr, MC_KT_ENC_PASS2, s);
-        k_enc_pass2<<<L->nmom_tiles, TPB, 0, s>>>(*L);
-        tr_end(tr, s);
-        tr_begin(tr, MC_KT_ENC_PASS3, s);
-        k_enc_pass3<<<L->nmom_tiles, TPB, 0, s>>>(*L);
+        tr_begin(tr, MC_KT_ENC_FINAL, s);
+        k_enc_final1<<<L->nitems, TPB, 0, s>>>(*L);
         tr_end(tr, s);
         n += 2;
     }
+    if (L->nmom_tiles > 0) {
+        smem_opt_in(KF_P2, (const void *)k_enc_pass2, P2_SMEM);
+        tr_begin(tr, MC_KT_ENC_PASS2, s);
+        k_enc_pass2<<<L->nmom_tiles, TPB, P2_SMEM, s>>>(*L);
+        tr_end(tr, s);
+        tr_begin(tr, MC_KT_ENC_FINAL, s);
+        k_enc_final2<<<L->nitems, TPB, 0, s>>>(*L);
+        tr_end(tr, s);
+        smem_opt_in(KF_P3, (const void *)k_enc_pass3, P3_SMEM);
+        tr_begin(tr, MC_KT_ENC_PASS3, s);
+        k_enc_pass3<<<L->nmom_tiles, TPB, P3_SMEM, s>>>(*L);
+        tr_end(tr, s);
+        tr_begin(tr, MC_KT_ENC_FINAL, s);
+        k_enc_final3<<<L->nitems, TPB, 0, s>>>(*L);
+        tr_end(tr, s);
+        n += 4;
+    }
     if (L->nall_tiles > 0) {
+        smem_opt_in(KF_P4, (const void *)k_enc_pass4, P4_SMEM);
         tr_begin(tr, MC_KT_ENC_PASS4, s);
-        k_enc_pass4<<<L->nall_tiles, TPB, 0, s>>>(*L);
+        k_enc_pass4<<<L->nall_tiles, TPB, P4_SMEM, s>>>(*L);
         tr_end(tr, s);
         n++;
     }
@@ -1243,8 +1573,9 @@ extern "C" int mc_launch_decode(const mc_dec_launch *L, void *stream, mc_ktrace 
         n++;
     }
     if (L->nall_tiles > 0) {
+        smem_opt_in(KF_RECON, (const void *)k_dec_recon, RECON_SMEM);
         tr_begin(tr, MC_KT_DEC_RECON, s);
-        k_dec_recon<<<L->nall_tiles, TPB, 0, s>>>(*L);
+        k_dec_recon<<<L->nall_tiles, TPB, RECON_SMEM, s>>>(*L);
         tr_end(tr, s);
         n++;
     }

@@ -327,7 +327,7 @@ typedef struct reg_ent {
     mc_arena *arena;
 } reg_ent;
 static reg_ent *g_reg = NULL;
-static size_t g_reg_cap = 0, g_reg_len = 0;
+static size_t g_reg_cap = 0, g_reg_len = 0, g_reg_tomb = 0;
 static pthread_mutex_t g_reg_mu = PTHREAD_MUTEX_INITIALIZER;
 #define REG_TOMB ((const void *)1)
 
@@ -339,8 +339,11 @@ static size_t reg_hash(const void *p, size_t cap) {
     return (size_t)x & (cap - 1);
 }
 
-static int reg_grow(void) {
-    size_t ncap = g_reg_cap ? g_reg_cap * 2 : 1024;
+/* Rebuilds the table without tombstones, doubling it when it is more than a
+ * quarter full of live entries. */
+static int reg_rehash(void) {
+    size_t ncap = g_reg_cap ? g_reg_cap : 1024;
+    if ((g_reg_len + 1) * 4 >= ncap) ncap *= 2;
     reg_ent *n = (reg_ent *)calloc(ncap, sizeof(reg_ent));
     if (!n) return -1;
     for (size_t i = 0; i < g_reg_cap; i++) {
@@ -352,33 +355,32 @@ static int reg_grow(void) {
     free(g_reg);
     g_reg = n;
     g_reg_cap = ncap;
+    g_reg_tomb = 0;
+    return 0;
+}
+
+/* caller holds g_reg_mu */
+static int reg_insert(const void *obj, mc_arena *a) {
+    if ((g_reg_len + g_reg_tomb + 1) * 2 >= g_reg_cap && reg_rehash() != 0) return -1;
+    size_t j = reg_hash(obj, g_reg_cap);
+    while (g_reg[j].obj && g_reg[j].obj != REG_TOMB) j = (j + 1) & (g_reg_cap - 1);
+    if (g_reg[j].obj == REG_TOMB) g_reg_tomb--;
+    g_reg[j].obj = obj;
+    g_reg[j].arena = a;
+    g_reg_len++;
     return 0;
 }
 
 void registry_add(const void *obj, mc_arena *a) {
     pthread_mutex_lock(&g_reg_mu);
-    if ((g_reg_len + 1) * 2 >= g_reg_cap && reg_grow() != 0) {
-        pthread_mutex_unlock(&g_reg_mu);
-        return;
-    }
-    size_t j = reg_hash(obj, g_reg_cap);
-    while (g_reg[j].obj && g_reg[j].obj != REG_TOMB) j = (j + 1) & (g_reg_cap - 1);
-    g_reg[j].obj = obj;
-    g_reg[j].arena = a;
-    g_reg_len++;
+    reg_insert(obj, a);
     pthread_mutex_unlock(&g_reg_mu);
 }
 
 void registry_add_many(const void **objs, size_t n, mc_arena *a) {
     pthread_mutex_lock(&g_reg_mu);
-    for (size_t k = 0; k < n; k++) {
-        if ((g_reg_len + 1) * 2 >= g_reg_cap && reg_grow() != 0) break;
-        size_t j = reg_hash(objs[k], g_reg_cap);
-        while (g_reg[j].obj && g_reg[j].obj != REG_TOMB) j = (j + 1) & (g_reg_cap - 1);
-        g_reg[j].obj = objs[k];
-        g_reg[j].arena = a;
-        g_reg_len++;
-    }
+    for (size_t k = 0; k < n; k++)
+        if (reg_insert(objs[k], a) != 0) break;
     pthread_mutex_unlock(&g_reg_mu);
 }
 
@@ -396,6 +398,7 @@ mc_arena *registry_take(const void *obj, int *found) {
             g_reg[j].obj = REG_TOMB;
             g_reg[j].arena = NULL;
             g_reg_len--;
+            g_reg_tomb++;
             *found = 1;
             pthread_mutex_unlock(&g_reg_mu);
             return a;
@@ -551,6 +554,12 @@ int mc_env_flag(const char *name) {
     if (!v || !*v) return 0;
     return strcmp(v, "0") != 0 && strcmp(v, "false") != 0 && strcmp(v, "FALSE") != 0 &&
            strcmp(v, "off") != 0 && strcmp(v, "OFF") != 0;
+}
+
+/* 1 when the variable is set to an off value ("0", "false", "off") */
+int mc_env_off(const char *name) {
+    const char *v = getenv(name);
+    return v && *v && !mc_env_flag(name);
 }
 
 void mc_set_error(MomentumCompressor *mc, const char *fmt, ...) {
