@@ -230,6 +230,35 @@ __device__ __forceinline__ QuadBits quad_bits(const uint32_t *bm, const uint32_t
     return b;
 }
 
+// Predicted / dominant bits of the whole quad at tile offset o (the quad's
+// elements all lie inside the tile); kernels of one element read the four
+// bits straight from the words.
+__device__ __forceinline__ QuadBits quad_bits_full(const uint32_t *bm, const uint32_t *dom, uint32_t wbase,
+                                                   uint32_t k0, uint32_t o, int ks, mc_fastdiv ksdiv) {
+    QuadBits b;
+    if (ks == 1) {
+        const uint32_t k = k0 + o, w = (k >> 5) - wbase, sh = k & 31;
+        b.f = (bm[w] >> sh) & 0xFu;
+        b.pos = dom ? (dom[w] >> sh) & 0xFu : 0u;
+        return b;
+    }
+    const uint32_t q = fdiv32(o, ksdiv);
+    uint32_t r = o - q * (uint32_t)ks;
+    uint32_t k = k0 + q;
+    b.f = b.pos = 0u;
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        const uint32_t sh = k & 31, w = (k >> 5) - wbase;
+        b.f |= ((bm[w] >> sh) & 1u) << j;
+        if (dom) b.pos |= ((dom[w] >> sh) & 1u) << j;
+        if (++r == (uint32_t)ks) {
+            r = 0;
+            k++;
+        }
+    }
+    return b;
+}
+
 // Exclusive prefix of the per-tile predicted counts of one item, written to
 // out[base .. base+nt); returns the total.  Whole block participates.
 __device__ int64_t scan_tile_counts(const int32_t *cnt, int stride_words, int base, int nt,
@@ -350,19 +379,21 @@ __device__ __forceinline__ const float *staged_or(const StageDesc &d, const floa
     return d.src[k] ? buf + k * STAGE_ELEMS - d.e0 : g;
 }
 
-// One CTA per tile: list entry blockIdx.x holds the tile id and its item
-// index.  plan(StageDesc&) runs on thread 0 and fills the element range and
+// One CTA per tile: list entry blockIdx.x (counted from the end when
+// REVERSE: CTAs start roughly in index order, so a reversed pass first
+// touches the tiles the previous pass touched last, still in L2) holds the
+// tile id and its item index.  plan(StageDesc&) runs on thread 0 and fills the element range and
 // the arrays to stage (src[k] for k < NA); thread 0 then starts their bulk
 // copies, all threads copy the (< 4) trailing elements the copies leave out
 // and wait (bounded) on the mbarrier, and body(const StageDesc&, const float
 // *buf) runs with the tile in shared memory.  A copy that does not complete
 // within the spin limit sets the item's error flag and skips the tile.
-template <int NA, class Plan, class Body>
+template <int NA, bool REVERSE, class Plan, class Body>
 __device__ void run_tile(const int2 *list, float *stage_mem, uint64_t *bar, StageDesc *sd, int32_t *err_of_item,
                          int err_stride_words, Plan plan, Body body) {
     const uint32_t b = smem_u32(bar);
     if (threadIdx.x == 0) {
-        const int2 e = list[blockIdx.x];
+        const int2 e = list[REVERSE ? gridDim.x - 1 - blockIdx.x : blockIdx.x];
         StageDesc d;
         d.gt = e.x;
         d.ii = e.y;
@@ -487,20 +518,58 @@ __device__ void pass1_tile(const mc_enc_launch &L, const StageDesc &d, const flo
         const float *cur = staged_or(d, buf, 0, (const float *)I.cur);
         const float *prev = staged_or(d, buf, 1, I.prev);
         float *hist = (float *)I.hist_out;
-        for (int64_t g = tr.e0 + 4 * (int64_t)threadIdx.x; g < tr.e1; g += 4 * TPB) {
-            float c[4], p[4];
-            ld4(cur, g, tr.e1, I.vec, c);
-            ld4(prev, g, tr.e1, I.vec, p);
-#pragma unroll
-            for (int j = 0; j < 4; j++) {
-                if (g + j < tr.e1) {
-                    dd[0] += (double)fabsf(c[j]);
-                    dd[1] += (double)fabsf(p[j]);
-                    mn = c[j] < mn ? c[j] : mn;
-                    mx = c[j] > mx ? c[j] : mx;
+        if (I.vec) {
+            // whole quads without range checks (tile-relative 32-bit offsets);
+            // the ragged end goes to the thread that owns that quad
+            const int len = (int)(tr.e1 - tr.e0), nq = len >> 2;
+            const float4 *c4 = (const float4 *)(cur + tr.e0), *p4 = (const float4 *)(prev + tr.e0);
+            float4 *h4 = hist ? (float4 *)(hist + tr.e0) : nullptr;
+            for (int q = threadIdx.x; q < nq; q += TPB) {
+                const float4 c = c4[q], p = p4[q];
+                dd[0] += (double)fabsf(c.x);
+                dd[1] += (double)fabsf(p.x);
+                dd[0] += (double)fabsf(c.y);
+                dd[1] += (double)fabsf(p.y);
+                dd[0] += (double)fabsf(c.z);
+                dd[1] += (double)fabsf(p.z);
+                dd[0] += (double)fabsf(c.w);
+                dd[1] += (double)fabsf(p.w);
+                mn = c.x < mn ? c.x : mn;
+                mx = c.x > mx ? c.x : mx;
+                mn = c.y < mn ? c.y : mn;
+                mx = c.y > mx ? c.y : mx;
+                mn = c.z < mn ? c.z : mn;
+                mx = c.z > mx ? c.z : mx;
+                mn = c.w < mn ? c.w : mn;
+                mx = c.w > mx ? c.w : mx;
+                if (h4) h4[q] = c;
+            }
+            if ((len & 3) && threadIdx.x == (nq % TPB)) {
+                for (int64_t g = tr.e0 + 4 * (int64_t)nq; g < tr.e1; g++) {
+                    const float c = cur[g];
+                    dd[0] += (double)fabsf(c);
+                    dd[1] += (double)fabsf(prev[g]);
+                    mn = c < mn ? c : mn;
+                    mx = c > mx ? c : mx;
+                    if (hist) hist[g] = c;
                 }
             }
-            if (hist) st4(hist, g, tr.e1, I.vec, c);
+        } else {
+            for (int64_t g = tr.e0 + 4 * (int64_t)threadIdx.x; g < tr.e1; g += 4 * TPB) {
+                float c[4], p[4];
+                ld4(cur, g, tr.e1, false, c);
+                ld4(prev, g, tr.e1, false, p);
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    if (g + j < tr.e1) {
+                        dd[0] += (double)fabsf(c[j]);
+                        dd[1] += (double)fabsf(p[j]);
+                        mn = c[j] < mn ? c[j] : mn;
+                        mx = c[j] > mx ? c[j] : mx;
+                    }
+                }
+                if (hist) st4(hist, g, tr.e1, false, c);
+            }
         }
         {   // this tile's share of zeroing the sign frame slot (pass 4 ORs bits into it)
             const int64_t nq = I.sg_cap >> 4;
@@ -514,7 +583,25 @@ __device__ void pass1_tile(const mc_enc_launch &L, const StageDesc &d, const flo
         const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
         const float inv_ks = __fdiv_rn(1.0f, (float)I.ks);
         int P = 0;
-        for (int64_t kb = tr.k0 + warp * 32; kb < tr.k1; kb += TPB) {
+        if (I.ks == 1) {
+            // one element per kernel: maj = 1, so every kernel has the same
+            // consistency ((1 * 1 - 0.5) * 2) and the dominant sign is
+            // "not negative"
+            const float half = __fmaf_rn(1.0f, inv_ks, -0.5f);
+            const bool flag = __fadd_rn(half, half) >= I.thr;
+            for (int64_t kb = tr.k0 + warp * 32; kb < tr.k1; kb += TPB) {
+                const int64_t k = kb + lane;
+                const bool in = k < tr.k1;
+                const uint32_t b = __ballot_sync(FULL, in && flag);
+                const uint32_t dw = __ballot_sync(FULL, in && !(cur[in ? k : kb] < 0.0f));
+                if (lane == 0) {
+                    I.bm_words[kb >> 5] = b;
+                    I.dom_words[kb >> 5] = dw;
+                    P += __popc(b);
+                }
+            }
+        }
+        for (int64_t kb = tr.k0 + warp * 32; I.ks != 1 && kb < tr.k1; kb += TPB) {
             const int64_t k = kb + lane;
             bool flag = false, dom = false;
             if (k < tr.k1) {
@@ -651,11 +738,11 @@ __device__ __forceinline__ bool stageable(int staged, const mc_enc_item &I, cons
 }
 #define ENC_ERR(L) &(L).results[0].err, (int)(sizeof(mc_enc_result) / 4)
 
-__global__ void __launch_bounds__(TPB) k_enc_pass1(mc_enc_launch L) {
+__global__ void __launch_bounds__(TPB, 4) k_enc_pass1(mc_enc_launch L) {
     __shared__ Red red;
     __shared__ TileShared ts;
     extern __shared__ __align__(128) float s_stage[];
-    run_tile<2>((const int2 *)L.all_tiles, s_stage, &ts.bar, &ts.d, ENC_ERR(L),
+    run_tile<2, false>((const int2 *)L.all_tiles, s_stage, &ts.bar, &ts.d, ENC_ERR(L),
                 [&](StageDesc &d) {
                     const mc_enc_item &I = enc_plan_range(L, d);
                     if ((I.kind == MC_K_MOMENTUM || I.kind == MC_K_QUANT) && stageable(L.staged, I, d)) {
@@ -714,11 +801,11 @@ __global__ void __launch_bounds__(TPB) k_enc_final1(mc_enc_launch L) {
 }
 
 // ------------------------------------------------------------------ pass 2
-__global__ void __launch_bounds__(TPB) k_enc_pass2(mc_enc_launch L) {
+__global__ void __launch_bounds__(TPB, 6) k_enc_pass2(mc_enc_launch L) {
     __shared__ Red red;
     __shared__ TileShared ts;
     extern __shared__ __align__(128) float s_stage[];
-    run_tile<2>((const int2 *)L.mom_tiles, s_stage, &ts.bar, &ts.d, ENC_ERR(L),
+    run_tile<2, true>((const int2 *)L.mom_tiles, s_stage, &ts.bar, &ts.d, ENC_ERR(L),
                     [&](StageDesc &d) {
                         const mc_enc_item &I = enc_plan_range(L, d);
                         if (stageable(L.staged, I, d)) {
@@ -735,19 +822,27 @@ __global__ void __launch_bounds__(TPB) k_enc_pass2(mc_enc_launch L) {
                         double dd[4] = {0.0, 0.0, 0.0, 0.0};
                         long long l[2] = {0, 0};
                         float mn = FLT_MAX, mx = -FLT_MAX, mx2 = 0.0f;
-                        for (int64_t g = d.e0 + 4 * (int64_t)threadIdx.x; g < d.e1; g += 4 * TPB) {
-                            float c[4], p[4];
-                            ld4(cur, g, d.e1, I.vec, c);
-                            ld4(prev, g, d.e1, I.vec, p);
-#pragma unroll
-                            for (int j = 0; j < 4; j++) {
-                                if (g + j < d.e1) {
-                                    const double dc = (double)__fsub_rn(fabsf(c[j]), cm);
-                                    const double dp = (double)__fsub_rn(fabsf(p[j]), pm);
-                                    dd[0] = __fma_rn(dc, dc, dd[0]);
-                                    dd[1] = __fma_rn(dp, dp, dd[1]);
-                                }
+                        auto acc = [&](float c, float p) {
+                            const double dc = (double)__fsub_rn(fabsf(c), cm);
+                            const double dp = (double)__fsub_rn(fabsf(p), pm);
+                            dd[0] = __fma_rn(dc, dc, dd[0]);
+                            dd[1] = __fma_rn(dp, dp, dd[1]);
+                        };
+                        const int len = (int)(d.e1 - d.e0), nq = len >> 2;
+                        if (I.vec) {
+                            const float4 *c4 = (const float4 *)(cur + d.e0), *p4 = (const float4 *)(prev + d.e0);
+                            for (int q = threadIdx.x; q < nq; q += TPB) {
+                                const float4 c = c4[q], p = p4[q];
+                                acc(c.x, p.x);
+                                acc(c.y, p.y);
+                                acc(c.z, p.z);
+                                acc(c.w, p.w);
                             }
+                            if ((len & 3) && threadIdx.x == (nq % TPB))
+                                for (int64_t g = d.e0 + 4 * (int64_t)nq; g < d.e1; g++) acc(cur[g], prev[g]);
+                        } else {
+                            for (int64_t g = d.e0 + threadIdx.x * 4; g < d.e1; g += 4 * TPB)
+                                for (int64_t e = g; e < g + 4 && e < d.e1; e++) acc(cur[e], prev[e]);
                         }
                         block_reduce(red, dd, 2, mn, mx, mx2, l, 0);
                         if (threadIdx.x == 0) {
@@ -785,11 +880,11 @@ __global__ void __launch_bounds__(TPB) k_enc_final2(mc_enc_launch L) {
 // ------------------------------------------------------------------ pass 3
 // The previous gradient is read only for predicted kernels: it is staged
 // when most kernels of the layer are predicted, else read directly.
-__global__ void __launch_bounds__(TPB) k_enc_pass3(mc_enc_launch L) {
+__global__ void __launch_bounds__(TPB, 4) k_enc_pass3(mc_enc_launch L) {
     __shared__ Red red;
     __shared__ TileShared ts;
     extern __shared__ __align__(128) float s_stage[];
-    run_tile<3>((const int2 *)L.mom_tiles, s_stage, &ts.bar, &ts.d, ENC_ERR(L),
+    run_tile<3, false>((const int2 *)L.mom_tiles, s_stage, &ts.bar, &ts.d, ENC_ERR(L),
                     [&](StageDesc &d) {
                         const mc_enc_item &I = enc_plan_range(L, d);
                         if (stageable(L.staged, I, d)) {
@@ -813,7 +908,51 @@ __global__ void __launch_bounds__(TPB) k_enc_pass3(mc_enc_launch L) {
                         long long mism = 0;
                         float maxr = 0.0f;
                         const uint32_t k0 = (uint32_t)tr.k0;
-                        for (int64_t g = tr.e0 + 4 * (int64_t)threadIdx.x; g < tr.e1; g += 4 * TPB) {
+                        // one element: memory update and clamped residual of a predicted element
+                        auto elem = [&](float c, float m0, float p, bool pos, float &mo) -> float {
+                            const float pv = __fsub_rn(fabsf(p), pm);
+                            const float pn = use_ps ? __fmul_rn(pv, inv_ps) : pv;
+                            const float nm = __fmaf_rn(oml, m0, __fmul_rn(lr, pn));
+                            mo = nm;
+                            const float ap = mom_pred_abs(nm, mp);
+                            const float pred = pos ? ap : -ap;
+                            mism += (pred > 0.0f) != (c > 0.0f);
+                            return x86min(x86max(__fsub_rn(c, pred), mp.gmin), mp.gmax);
+                        };
+                        auto quad = [&](int64_t g, const QuadBits &qb, const float (&c)[4], const float (&m0)[4],
+                                        const float (&p)[4], float (&mo)[4], int nvalid) {
+#pragma unroll
+                            for (int j = 0; j < 4; j++) {
+                                float r = c[j];
+                                mo[j] = m0[j];
+                                if ((qb.f >> j) & 1u) r = elem(c[j], m0[j], p[j], (qb.pos >> j) & 1u, mo[j]);
+                                if (j < nvalid) maxr = fmaxf(maxr, fabsf(r));
+                            }
+                        };
+                        const int len = (int)(tr.e1 - tr.e0), nq = len >> 2;
+                        if (I.vec) {
+                            const float4 *c4 = (const float4 *)(cur + tr.e0);
+                            const float4 *m4 = mem_in ? (const float4 *)(mem_in + tr.e0) : nullptr;
+                            const float4 *p4 = (const float4 *)(prev + tr.e0);
+                            float4 *o4 = (float4 *)(I.mem_out + tr.e0);
+                            for (int q = threadIdx.x; q < nq; q += TPB) {
+                                const QuadBits qb = quad_bits_full(I.bm_words, I.dom_words, 0u, k0, 4u * q, I.ks,
+                                                                   I.ksdiv);
+                                const float4 cv = c4[q];
+                                const float4 mv = m4 ? m4[q] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                                float4 pv = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                                if (qb.f) pv = p4[q];
+                                const float c[4] = {cv.x, cv.y, cv.z, cv.w}, m0[4] = {mv.x, mv.y, mv.z, mv.w};
+                                const float p[4] = {pv.x, pv.y, pv.z, pv.w};
+                                float mo[4];
+                                quad(tr.e0 + 4 * q, qb, c, m0, p, mo, 4);
+                                o4[q] = make_float4(mo[0], mo[1], mo[2], mo[3]);
+                            }
+                        }
+                        const int64_t gstart = I.vec ? tr.e0 + 4 * (int64_t)nq : tr.e0;
+                        const int owner = I.vec ? nq % TPB : 0;
+                        for (int64_t g = gstart + 4 * (int64_t)((threadIdx.x - owner + TPB) % TPB); g < tr.e1;
+                             g += 4 * TPB) {
                             const QuadBits qb = quad_bits(I.bm_words, I.dom_words, 0u, k0, g, tr.e0, tr.e1, I.ks,
                                                           I.ksdiv);
                             float c[4], m0[4], p[4], mo[4];
@@ -821,23 +960,7 @@ __global__ void __launch_bounds__(TPB) k_enc_pass3(mc_enc_launch L) {
                             if (mem_in) ld4(mem_in, g, tr.e1, I.vec, m0);
                             else m0[0] = m0[1] = m0[2] = m0[3] = 0.0f;
                             if (qb.f) ld4(prev, g, tr.e1, I.vec, p);
-#pragma unroll
-                            for (int j = 0; j < 4; j++) {
-                                float r = c[j];
-                                mo[j] = m0[j];
-                                if ((qb.f >> j) & 1u) {
-                                    const float pv = __fsub_rn(fabsf(p[j]), pm);
-                                    const float pn = use_ps ? __fmul_rn(pv, inv_ps) : pv;
-                                    const float nm = __fmaf_rn(oml, m0[j], __fmul_rn(lr, pn));
-                                    mo[j] = nm;
-                                    const bool pos = (qb.pos >> j) & 1u;
-                                    const float ap = mom_pred_abs(nm, mp);
-                                    const float pred = pos ? ap : -ap;
-                                    mism += (pred > 0.0f) != (c[j] > 0.0f);
-                                    r = x86min(x86max(__fsub_rn(c[j], pred), mp.gmin), mp.gmax);
-                                }
-                                if (g + j < tr.e1) maxr = fmaxf(maxr, fabsf(r));
-                            }
+                            quad(g, qb, c, m0, p, mo, (int)min((int64_t)4, tr.e1 - g));
                             st4(I.mem_out, g, tr.e1, I.vec, mo);
                         }
                         double dd[4];
@@ -938,7 +1061,25 @@ __device__ void pass4_tile(const mc_enc_launch &L, const StageDesc &d, const flo
         const float *cur = staged_or(d, buf, 0, (const float *)I.cur);
         const float *mem = staged_or(d, buf, 1, I.mem_out);
         const uint32_t k0 = (uint32_t)tr.k0;
-        for (int64_t g = tr.e0 + 4 * (int64_t)threadIdx.x; g < tr.e1; g += 4 * TPB) {
+        const int len = (int)(tr.e1 - tr.e0), nq = len >> 2;
+        if (I.vec) {   // whole quads, no range checks
+            const float4 *c4 = (const float4 *)(cur + tr.e0), *m4 = (const float4 *)(mem + tr.e0);
+            for (int q = threadIdx.x; q < nq; q += TPB) {
+                const QuadBits qb = quad_bits_full(I.bm_words, I.dom_words, 0u, k0, 4u * q, I.ks, I.ksdiv);
+                const float4 cv = c4[q];
+                float4 mv = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                if (qb.f) mv = m4[q];
+                const float c[4] = {cv.x, cv.y, cv.z, cv.w}, m[4] = {mv.x, mv.y, mv.z, mv.w};
+                float r[4];
+#pragma unroll
+                for (int j = 0; j < 4; j++)
+                    r[j] = ((qb.f >> j) & 1u) ? mom_residual(c[j], m[j], (qb.pos >> j) & 1u, mp) : c[j];
+                put_codes(I.data_out, I.codec, tr.e0 + 4 * q, tr.e1, true, r, scale, qm);
+            }
+        }
+        const int64_t gstart = I.vec ? tr.e0 + 4 * (int64_t)nq : tr.e0;
+        const int owner = I.vec ? nq % TPB : 0;
+        for (int64_t g = gstart + 4 * (int64_t)((threadIdx.x - owner + TPB) % TPB); g < tr.e1; g += 4 * TPB) {
             const QuadBits qb = quad_bits(I.bm_words, I.dom_words, 0u, k0, g, tr.e0, tr.e1, I.ks, I.ksdiv);
             float c[4], m[4], r[4];
             ld4(cur, g, tr.e1, I.vec, c);
@@ -1021,12 +1162,12 @@ __device__ void pass4_tile(const mc_enc_launch &L, const StageDesc &d, const flo
     }
 }
 
-__global__ void __launch_bounds__(TPB) k_enc_pass4(mc_enc_launch L) {
+__global__ void __launch_bounds__(TPB, 5) k_enc_pass4(mc_enc_launch L) {
     __shared__ int scan_sh[NWARP + 1];
     __shared__ uint32_t s_sg[TPB + 2];
     __shared__ TileShared ts;
     extern __shared__ __align__(128) float s_stage[];
-    run_tile<2>((const int2 *)L.all_tiles, s_stage, &ts.bar, &ts.d, ENC_ERR(L),
+    run_tile<2, true>((const int2 *)L.all_tiles, s_stage, &ts.bar, &ts.d, ENC_ERR(L),
                     [&](StageDesc &d) {
                         const mc_enc_item &I = enc_plan_range(L, d);
                         if ((I.kind == MC_K_MOMENTUM || I.kind == MC_K_QUANT) && stageable(L.staged, I, d)) {
@@ -1350,14 +1491,9 @@ __device__ void recon_tile(const mc_dec_launch &L, const StageDesc &d, const flo
         const uint32_t k0 = (uint32_t)tr.k0;
         const float *mem_in = staged_or(d, buf, 0, I.mem_in);
         const float *prev = staged_or(d, buf, 1, I.prev);
-        // bitmap / sign words of the tile are in shared memory from word wb on
-        for (int64_t g = tr.e0 + 4 * (int64_t)threadIdx.x; g < tr.e1; g += 4 * TPB) {
-            const QuadBits qb = quad_bits(s_m, s_d, (uint32_t)wb, k0, g, tr.e0, tr.e1, I.ks, I.ksdiv);
-            float r[4], m0[4], p[4], mo[4], rec[4];
-            dec_resid4(I, g, tr.e1, scale, r);
-            if (mem_in) ld4(mem_in, g, tr.e1, I.vec, m0);
-            else m0[0] = m0[1] = m0[2] = m0[3] = 0.0f;
-            if (qb.f) ld4(prev, g, tr.e1, I.vec, p);
+        // reconstruction of a quad: memory update and prediction on predicted elements
+        auto quad = [&](const QuadBits &qb, const float (&r)[4], const float (&m0)[4], const float (&p)[4],
+                        float (&mo)[4], float (&rec)[4]) {
 #pragma unroll
             for (int j = 0; j < 4; j++) {
                 rec[j] = r[j];
@@ -1371,6 +1507,40 @@ __device__ void recon_tile(const mc_dec_launch &L, const StageDesc &d, const flo
                     rec[j] = __fadd_rn(r[j], ((qb.pos >> j) & 1u) ? ap : -ap);
                 }
             }
+        };
+        // bitmap / sign words of the tile are in shared memory from word wb on
+        const int len = (int)(tr.e1 - tr.e0), nq = len >> 2;
+        if (I.vec) {   // whole quads, no range checks
+            const float4 *m4 = mem_in ? (const float4 *)(mem_in + tr.e0) : nullptr;
+            const float4 *p4 = (const float4 *)(prev + tr.e0);
+            float4 *mo4 = (float4 *)(I.mem_out + tr.e0), *h4 = (float4 *)(hist + tr.e0);
+            float4 *o4 = out ? (float4 *)(out + tr.e0) : nullptr;
+            for (int q = threadIdx.x; q < nq; q += TPB) {
+                const QuadBits qb = quad_bits_full(s_m, s_d, (uint32_t)wb, k0, 4u * q, I.ks, I.ksdiv);
+                float r[4];
+                dec_resid4(I, tr.e0 + 4 * q, tr.e1, scale, r);
+                const float4 mv = m4 ? m4[q] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                float4 pv = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                if (qb.f) pv = p4[q];
+                const float m0[4] = {mv.x, mv.y, mv.z, mv.w}, p[4] = {pv.x, pv.y, pv.z, pv.w};
+                float mo[4], rec[4];
+                quad(qb, r, m0, p, mo, rec);
+                mo4[q] = make_float4(mo[0], mo[1], mo[2], mo[3]);
+                const float4 rv = make_float4(rec[0], rec[1], rec[2], rec[3]);
+                h4[q] = rv;
+                if (o4) o4[q] = rv;
+            }
+        }
+        const int64_t gstart = I.vec ? tr.e0 + 4 * (int64_t)nq : tr.e0;
+        const int owner = I.vec ? nq % TPB : 0;
+        for (int64_t g = gstart + 4 * (int64_t)((threadIdx.x - owner + TPB) % TPB); g < tr.e1; g += 4 * TPB) {
+            const QuadBits qb = quad_bits(s_m, s_d, (uint32_t)wb, k0, g, tr.e0, tr.e1, I.ks, I.ksdiv);
+            float r[4], m0[4], p[4], mo[4], rec[4];
+            dec_resid4(I, g, tr.e1, scale, r);
+            if (mem_in) ld4(mem_in, g, tr.e1, I.vec, m0);
+            else m0[0] = m0[1] = m0[2] = m0[3] = 0.0f;
+            if (qb.f) ld4(prev, g, tr.e1, I.vec, p);
+            quad(qb, r, m0, p, mo, rec);
             st4(I.mem_out, g, tr.e1, I.vec, mo);
             st4(hist, g, tr.e1, I.vec, rec);
             if (out) st4(out, g, tr.e1, I.vec, rec);
@@ -1440,14 +1610,14 @@ __device__ void recon_tile(const mc_dec_launch &L, const StageDesc &d, const flo
     }
 }
 
-__global__ void __launch_bounds__(TPB) k_dec_recon(mc_dec_launch L) {
+__global__ void __launch_bounds__(TPB, 4) k_dec_recon(mc_dec_launch L) {
     __shared__ uint32_t s_m[TPB], s_d[TPB];
     __shared__ int scan_sh[NWARP + 1];
     __shared__ uint8_t s_sb[SIGN_WIN];
     __shared__ long long s_ll[NWARP];
     __shared__ TileShared ts;
     extern __shared__ __align__(128) float s_stage[];
-    run_tile<2>((const int2 *)L.all_tiles, s_stage, &ts.bar, &ts.d, &L.results[0].err,
+    run_tile<2, false>((const int2 *)L.all_tiles, s_stage, &ts.bar, &ts.d, &L.results[0].err,
                 (int)(sizeof(mc_dec_result) / 4),
                     [&](StageDesc &d) {
                         const mc_dec_item &I = L.items[d.ii];
