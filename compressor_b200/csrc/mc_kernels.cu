@@ -386,11 +386,12 @@ __device__ __forceinline__ const float *staged_or(const StageDesc &d, const floa
 // the arrays to stage (src[k] for k < NA); thread 0 then starts their bulk
 // copies, all threads copy the (< 4) trailing elements the copies leave out
 // and wait (bounded) on the mbarrier, and body(const StageDesc&, const float
-// *buf) runs with the tile in shared memory.  A copy that does not complete
+// *buf) runs with the tile in shared memory; pre(const StageDesc&) runs on
+// all threads between the issue and the wait.  A copy that does not complete
 // within the spin limit sets the item's error flag and skips the tile.
-template <int NA, bool REVERSE, class Plan, class Body>
+template <int NA, bool REVERSE, class Plan, class Pre, class Body>
 __device__ void run_tile(const int2 *list, float *stage_mem, uint64_t *bar, StageDesc *sd, int32_t *err_of_item,
-                         int err_stride_words, Plan plan, Body body) {
+                         int err_stride_words, Plan plan, Pre pre, Body body) {
     const uint32_t b = smem_u32(bar);
     if (threadIdx.x == 0) {
         const int2 e = list[REVERSE ? gridDim.x - 1 - blockIdx.x : blockIdx.x];
@@ -405,6 +406,7 @@ __device__ void run_tile(const int2 *list, float *stage_mem, uint64_t *bar, Stag
     __syncthreads();
     const StageDesc d = *sd;
     pipe_tail<NA>(stage_mem, d);
+    pre(d);   // the tile's own global reads, while its bulk copies are in flight
     bool ok = mbar_wait(b, 0);
     if (!ok) ok = mbar_wait(b, 0);   // one more bounded wait for the copies in flight
     if (!__syncthreads_and(ok)) {
@@ -750,7 +752,21 @@ __global__ void __launch_bounds__(TPB, 4) k_enc_pass1(mc_enc_launch L) {
                         if (I.kind == MC_K_MOMENTUM) d.src[1] = I.prev;
                     }
                 },
+                [](const StageDesc &) {},
                 [&](const StageDesc &d, const float *buf) { pass1_tile(L, d, buf, red); });
+}
+
+// The bitmap and dominant-sign words of a momentum tile, copied to shared
+// memory (word wb = k0 / 32 of the layer at index 0).  Called between the
+// issue of a tile's bulk copies and the wait; read after the wait.
+__device__ __forceinline__ void stage_words(const mc_enc_item &I, int t, uint32_t *s_bw, uint32_t *s_dw) {
+    const int64_t k0 = (int64_t)t * I.tile_kernels;
+    const int64_t k1 = min(k0 + (int64_t)I.tile_kernels, I.K);
+    const int64_t wb = k0 >> 5, we = (k1 + 31) >> 5;
+    if (wb + threadIdx.x < we) {
+        s_bw[threadIdx.x] = I.bm_words[wb + threadIdx.x];
+        s_dw[threadIdx.x] = I.dom_words[wb + threadIdx.x];
+    }
 }
 
 // Per-item results of pass 1 (one CTA per item of the wave): means and raw
@@ -813,6 +829,7 @@ __global__ void __launch_bounds__(TPB, 6) k_enc_pass2(mc_enc_launch L) {
                             d.src[1] = I.prev;
                         }
                     },
+                    [](const StageDesc &) {},
                     [&](const StageDesc &d, const float *buf) {
                         const mc_enc_item I = L.items[d.ii];
                         const mc_enc_result *R = L.results + d.ii;
@@ -883,6 +900,7 @@ __global__ void __launch_bounds__(TPB) k_enc_final2(mc_enc_launch L) {
 __global__ void __launch_bounds__(TPB, 4) k_enc_pass3(mc_enc_launch L) {
     __shared__ Red red;
     __shared__ TileShared ts;
+    __shared__ uint32_t s_bw[TPB], s_dw[TPB];
     extern __shared__ __align__(128) float s_stage[];
     run_tile<3, false>((const int2 *)L.mom_tiles, s_stage, &ts.bar, &ts.d, ENC_ERR(L),
                     [&](StageDesc &d) {
@@ -892,6 +910,10 @@ __global__ void __launch_bounds__(TPB, 4) k_enc_pass3(mc_enc_launch L) {
                             d.src[1] = I.mem_in;
                             if (2 * L.tiles[d.gt].P >= (int32_t)I.tile_kernels) d.src[2] = I.prev;
                         }
+                    },
+                    [&](const StageDesc &d) {
+                        const mc_enc_item &I = L.items[d.ii];
+                        stage_words(I, d.gt - I.tile_base, s_bw, s_dw);
                     },
                     [&](const StageDesc &d, const float *buf) {
                         const mc_enc_item I = L.items[d.ii];
@@ -936,8 +958,7 @@ __global__ void __launch_bounds__(TPB, 4) k_enc_pass3(mc_enc_launch L) {
                             const float4 *p4 = (const float4 *)(prev + tr.e0);
                             float4 *o4 = (float4 *)(I.mem_out + tr.e0);
                             for (int q = threadIdx.x; q < nq; q += TPB) {
-                                const QuadBits qb = quad_bits_full(I.bm_words, I.dom_words, 0u, k0, 4u * q, I.ks,
-                                                                   I.ksdiv);
+                                const QuadBits qb = quad_bits_full(s_bw, s_dw, k0 >> 5, k0, 4u * q, I.ks, I.ksdiv);
                                 const float4 cv = c4[q];
                                 const float4 mv = m4 ? m4[q] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
                                 float4 pv = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
@@ -953,8 +974,7 @@ __global__ void __launch_bounds__(TPB, 4) k_enc_pass3(mc_enc_launch L) {
                         const int owner = I.vec ? nq % TPB : 0;
                         for (int64_t g = gstart + 4 * (int64_t)((threadIdx.x - owner + TPB) % TPB); g < tr.e1;
                              g += 4 * TPB) {
-                            const QuadBits qb = quad_bits(I.bm_words, I.dom_words, 0u, k0, g, tr.e0, tr.e1, I.ks,
-                                                          I.ksdiv);
+                            const QuadBits qb = quad_bits(s_bw, s_dw, k0 >> 5, k0, g, tr.e0, tr.e1, I.ks, I.ksdiv);
                             float c[4], m0[4], p[4], mo[4];
                             ld4(cur, g, tr.e1, I.vec, c);
                             if (mem_in) ld4(mem_in, g, tr.e1, I.vec, m0);
@@ -1047,7 +1067,7 @@ __device__ __forceinline__ void put_codes(uint8_t *data_out, int codec, int64_t 
 
 // ------------------------------------------------------------------ pass 4
 __device__ void pass4_tile(const mc_enc_launch &L, const StageDesc &d, const float *buf, int *scan_sh,
-                           uint32_t *s_sg) {
+                           uint32_t *s_sg, const uint32_t *s_bw, const uint32_t *s_dw) {
     const int gt = d.gt;
     const int ii = d.ii;
     const mc_enc_item I = L.items[ii];
@@ -1065,7 +1085,7 @@ __device__ void pass4_tile(const mc_enc_launch &L, const StageDesc &d, const flo
         if (I.vec) {   // whole quads, no range checks
             const float4 *c4 = (const float4 *)(cur + tr.e0), *m4 = (const float4 *)(mem + tr.e0);
             for (int q = threadIdx.x; q < nq; q += TPB) {
-                const QuadBits qb = quad_bits_full(I.bm_words, I.dom_words, 0u, k0, 4u * q, I.ks, I.ksdiv);
+                const QuadBits qb = quad_bits_full(s_bw, s_dw, k0 >> 5, k0, 4u * q, I.ks, I.ksdiv);
                 const float4 cv = c4[q];
                 float4 mv = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
                 if (qb.f) mv = m4[q];
@@ -1080,7 +1100,7 @@ __device__ void pass4_tile(const mc_enc_launch &L, const StageDesc &d, const flo
         const int64_t gstart = I.vec ? tr.e0 + 4 * (int64_t)nq : tr.e0;
         const int owner = I.vec ? nq % TPB : 0;
         for (int64_t g = gstart + 4 * (int64_t)((threadIdx.x - owner + TPB) % TPB); g < tr.e1; g += 4 * TPB) {
-            const QuadBits qb = quad_bits(I.bm_words, I.dom_words, 0u, k0, g, tr.e0, tr.e1, I.ks, I.ksdiv);
+            const QuadBits qb = quad_bits(s_bw, s_dw, k0 >> 5, k0, g, tr.e0, tr.e1, I.ks, I.ksdiv);
             float c[4], m[4], r[4];
             ld4(cur, g, tr.e1, I.vec, c);
             if (qb.f) ld4(mem, g, tr.e1, I.vec, m);
@@ -1118,8 +1138,8 @@ __device__ void pass4_tile(const mc_enc_launch &L, const StageDesc &d, const flo
         if (i < 2) s_sg[TPB + i] = 0u;
         uint32_t mw = 0, dv = 0;
         if (wb + i < we) {
-            mw = I.bm_words[wb + i];
-            dv = I.dom_words[wb + i];
+            mw = s_bw[i];
+            dv = s_dw[i];
         }
         const int pc = __popc(mw);
         int tot;
@@ -1165,6 +1185,7 @@ __device__ void pass4_tile(const mc_enc_launch &L, const StageDesc &d, const flo
 __global__ void __launch_bounds__(TPB, 5) k_enc_pass4(mc_enc_launch L) {
     __shared__ int scan_sh[NWARP + 1];
     __shared__ uint32_t s_sg[TPB + 2];
+    __shared__ uint32_t s_bw[TPB], s_dw[TPB];
     __shared__ TileShared ts;
     extern __shared__ __align__(128) float s_stage[];
     run_tile<2, true>((const int2 *)L.all_tiles, s_stage, &ts.bar, &ts.d, ENC_ERR(L),
@@ -1176,7 +1197,11 @@ __global__ void __launch_bounds__(TPB, 5) k_enc_pass4(mc_enc_launch L) {
                                 d.src[1] = I.mem_out;
                         }
                     },
-                    [&](const StageDesc &d, const float *buf) { pass4_tile(L, d, buf, scan_sh, s_sg); });
+                    [&](const StageDesc &d) {
+                        const mc_enc_item &I = L.items[d.ii];
+                        if (I.kind == MC_K_MOMENTUM) stage_words(I, d.gt - I.tile_base, s_bw, s_dw);
+                    },
+                    [&](const StageDesc &d, const float *buf) { pass4_tile(L, d, buf, scan_sh, s_sg, s_bw, s_dw); });
 }
 
 // ------------------------------------------------------------------ frames
@@ -1411,17 +1436,16 @@ __device__ __forceinline__ void dec_resid4(const mc_dec_item &I, int64_t g, int6
 // read-ahead of the 5-byte gather.
 #define SIGN_WIN 1040
 
-__device__ void recon_tile(const mc_dec_launch &L, const StageDesc &d, const float *buf, uint32_t *s_m,
-                           uint32_t *s_d, int *scan_sh, uint8_t *s_sb, long long *s_ll) {
-    const int gt = d.gt;
+// Momentum tiles of the decoder, before the wait on the tile's bulk copies:
+// the tile's bitmap words, the offset of its first predicted kernel in the
+// dense signs (counts of the item's earlier tiles; the first tile also
+// reports the item's total) and the deposited dominant-sign words, into
+// shared memory (s_m, s_d; word wb = k0 / 32 at index 0).
+__device__ void recon_pre(const mc_dec_launch &L, const StageDesc &d, uint32_t *s_m, uint32_t *s_d, int *scan_sh,
+                          uint8_t *s_sb, long long *s_ll) {
     const int ii = d.ii;
-    const mc_dec_item I = L.items[ii];
-    const int t = gt - I.tile_base;
-    // the scale header may sit at any byte address (payloads from the caller)
-    const float scale = (I.codec == MC_DC_Q8 || I.codec == MC_DC_INT4)
-                            ? __uint_as_float(le32((const uint8_t *)I.scale_ptr)) : 1.0f;
-    float *hist = (float *)I.hist_out;
-    float *out = (float *)I.out;
+    const mc_dec_item &I = L.items[ii];
+    const int t = d.gt - I.tile_base;
     if (I.kind == MC_D_MOMENTUM) {
         const DecTile tr = dec_range(I, t);
         const int64_t wb = tr.k0 >> 5, we = (tr.k1 + 31) >> 5;
@@ -1482,7 +1506,23 @@ __device__ void recon_tile(const mc_dec_launch &L, const StageDesc &d, const flo
         }
         s_m[i] = m;
         s_d[i] = dm;
-        __syncthreads();
+    }
+}
+
+__device__ void recon_tile(const mc_dec_launch &L, const StageDesc &d, const float *buf, const uint32_t *s_m,
+                           const uint32_t *s_d) {
+    const int gt = d.gt;
+    const int ii = d.ii;
+    const mc_dec_item I = L.items[ii];
+    const int t = gt - I.tile_base;
+    // the scale header may sit at any byte address (payloads from the caller)
+    const float scale = (I.codec == MC_DC_Q8 || I.codec == MC_DC_INT4)
+                            ? __uint_as_float(le32((const uint8_t *)I.scale_ptr)) : 1.0f;
+    float *hist = (float *)I.hist_out;
+    float *out = (float *)I.out;
+    if (I.kind == MC_D_MOMENTUM) {
+        const DecTile tr = dec_range(I, t);
+        const int64_t wb = tr.k0 >> 5;
         const MomParams mp = {I.cm, I.cs, 0.0f, 0.0f, I.cs > 1e-8f};
         const float pm = I.pm, lr = I.lr;
         const bool use_ps = I.ps > 1e-8f;
@@ -1636,7 +1676,8 @@ __global__ void __launch_bounds__(TPB, 4) k_dec_recon(mc_dec_launch L) {
                             d.e1 = min(d.e0 + (int64_t)I.tile_kernels, I.n);
                         }
                     },
-                    [&](const StageDesc &d, const float *buf) { recon_tile(L, d, buf, s_m, s_d, scan_sh, s_sb, s_ll); });
+                    [&](const StageDesc &d) { recon_pre(L, d, s_m, s_d, scan_sh, s_sb, s_ll); },
+                    [&](const StageDesc &d, const float *buf) { recon_tile(L, d, buf, s_m, s_d); });
 }
 
 // ------------------------------------------------------------- aggregate
