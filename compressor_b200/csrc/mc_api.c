@@ -674,11 +674,11 @@ MC_EXPORT void ndarray_destroy(NDArray *a) {
     if (!a) return;
     int found = 0;
     mc_arena *ar = registry_take(a, &found);
-    if (found) {
+    if (found) {   /* the array, its shape and its data belong to the arena */
         arena_release(ar);
-    } else {
-        free(a->data);
+        return;
     }
+    free(a->data);
     free(a->shape);
     free(a);
 }
@@ -717,13 +717,13 @@ MC_EXPORT void compressed_layer_data_free(CompressedLayerData *c) {
     if (!c) return;
     int found = 0;
     mc_arena *a = registry_take(c, &found);
-    if (found) {
+    if (found) {   /* the struct and its payloads belong to the arena */
         arena_release(a);
-    } else {
-        free(c->data);
-        free(c->bitmap);
-        free(c->dominant_signs);
+        return;
     }
+    free(c->data);
+    free(c->bitmap);
+    free(c->dominant_signs);
     free(c);
 }
 
@@ -1050,14 +1050,57 @@ MC_EXPORT const char *falcom_kernel_name(int id) {
 }
 
 MC_EXPORT void falcom_free_batch(BatchItem *items, size_t n, NDArray **outs) {
-    for (size_t i = 0; i < n; i++) {
-        if (items && items[i].compressed) {
-            compressed_layer_data_free(items[i].compressed);
-            items[i].compressed = NULL;
+    /* one registry pass for all objects; arena references dropped per run of
+     * objects that share an arena */
+    const void **objs = (const void **)malloc(2 * n * sizeof(void *));
+    mc_arena **ar = (mc_arena **)malloc(2 * n * sizeof(mc_arena *));
+    if (!objs || !ar) {
+        free(objs);
+        free(ar);
+        for (size_t i = 0; i < n; i++) {
+            if (items && items[i].compressed) compressed_layer_data_free(items[i].compressed);
+            if (items) items[i].compressed = NULL;
+            if (outs && outs[i]) ndarray_destroy(outs[i]);
+            if (outs) outs[i] = NULL;
         }
-        if (outs && outs[i]) {
-            ndarray_destroy(outs[i]);
-            outs[i] = NULL;
-        }
+        return;
     }
+    for (size_t i = 0; i < n; i++) {
+        objs[i] = items ? items[i].compressed : NULL;
+        objs[n + i] = outs ? outs[i] : NULL;
+    }
+    registry_take_many(objs, 2 * n, ar);
+    mc_arena *run = NULL;
+    int cnt = 0;
+    for (size_t k = 0; k < 2 * n; k++) {
+        if (!objs[k]) continue;
+        if (!ar[k]) {   /* not library-owned: free it field by field */
+            if (k < n) {
+                CompressedLayerData *c = (CompressedLayerData *)objs[k];
+                free(c->data);
+                free(c->bitmap);
+                free(c->dominant_signs);
+                free(c);
+            } else {
+                NDArray *a = (NDArray *)objs[k];
+                free(a->data);
+                free(a->shape);
+                free(a);
+            }
+            continue;
+        }
+        if (ar[k] != run) {
+            arena_release_n(run, cnt);
+            run = ar[k];
+            cnt = 0;
+        }
+        cnt++;
+    }
+    arena_release_n(run, cnt);
+    for (size_t i = 0; i < n; i++) {
+        if (items) items[i].compressed = NULL;
+        if (outs) outs[i] = NULL;
+    }
+    free(objs);
+    free(ar);
 }

@@ -829,20 +829,18 @@ int mc_compress_grouped(MomentumCompressor *mc, BatchItem *items, size_t n, cons
     {
         mc_arena *arena = dev_arena ? dev_arena : host_arena;
         uint8_t *base = (uint8_t *)arena->ptr;
-        CompressedLayerData **outs = (CompressedLayerData **)calloc(n, sizeof(*outs));
-        if (!outs) {
+        /* the structs live in one block owned by the payload arena, released
+         * with it once the caller has freed every item */
+        CompressedLayerData **outs = (CompressedLayerData **)malloc(n * sizeof(*outs));
+        CompressedLayerData *blk = (CompressedLayerData *)calloc(n ? n : 1, sizeof(CompressedLayerData));
+        if (!outs || !blk) {
+            free(outs);
+            free(blk);
             rc = ERROR_ALLOCATION;
             goto fail;
         }
-        for (size_t i = 0; i < n; i++) {
-            outs[i] = (CompressedLayerData *)calloc(1, sizeof(CompressedLayerData));
-            if (!outs[i]) {
-                for (size_t j = 0; j < i; j++) free(outs[j]);
-                free(outs);
-                rc = ERROR_ALLOCATION;
-                goto fail;
-            }
-        }
+        for (size_t i = 0; i < n; i++) outs[i] = &blk[i];
+        arena->objs = blk;
         const int libz = mc->frame_mode == MC_FRAME_LIBZSTD;
         for (size_t i = 0; i < n; i++) {
             cplan *p = &P[i];
@@ -961,11 +959,6 @@ typedef struct {
     size_t len;
     const uint8_t **dst;      /* where the device address is written */
 } hrange;
-
-static int on_device(mc_ptrcache *pc, const void *p, int dev) {
-    int d = -1;
-    return mc_classify(pc, p, &d) && d == dev;
-}
 
 /* Plans one item (reference decompress_layer :3476-3598 validation order). */
 static void dplan_item(MomentumCompressor *mc, dplan *d, const BatchItem *it, const mc_keycache *kc,
@@ -1182,9 +1175,10 @@ static int dec_segment(MomentumCompressor *mc, const BatchItem *items, size_t n,
         int is_frame[3] = {d->data_frame, 1, 1};
         for (int k = 0; k < 3; k++) {
             if (!srcs[k] || lens[k] == 0) continue;
-            if (on_device(&pc, srcs[k], dev)) {
+            int pd = -1, in_arena = 0;
+            if (mc_classify2(&pc, srcs[k], &pd, &in_arena) && pd == dev) {
                 *dsts[k] = srcs[k];
-                if (!mc_is_arena_ptr(srcs[k])) d->foreign = 1;
+                if (!in_arena) d->foreign = 1;
                 continue;
             }
             const uint8_t *src = srcs[k];
@@ -1566,9 +1560,12 @@ static int dec_segment(MomentumCompressor *mc, const BatchItem *items, size_t n,
             d->ok = 0;
             continue;
         }
-        NDArray *a = (NDArray *)calloc(1, sizeof(NDArray));
-        size_t *shp = (size_t *)malloc(d->ndim * sizeof(size_t));
-        if (!a || !shp) { free(a); free(shp); d->ok = 0; continue; }
+        if (!oarena->objs) {   /* arrays and shapes: one block owned by the output arena */
+            oarena->objs = calloc(n, sizeof(NDArray) + MAX_NDIM * sizeof(size_t));
+            if (!oarena->objs) { rc = ERROR_ALLOCATION; goto fail_arena; }
+        }
+        NDArray *a = (NDArray *)oarena->objs + i;
+        size_t *shp = (size_t *)((NDArray *)oarena->objs + n) + i * MAX_NDIM;
         memcpy(shp, d->shape, d->ndim * sizeof(size_t));
         a->data = (uint8_t *)oarena->ptr + d->out_off;
         a->shape = shp;

@@ -45,16 +45,19 @@ typedef struct mc_arena {
     size_t bytes;
     int device;      /* -1 for pinned host memory */
     int refs;
+    void *objs;      /* malloc'd block holding the objects themselves, freed with the arena */
 } mc_arena;
 
 mc_arena *arena_acquire(size_t bytes, int device);   /* refs = 1 */
-void arena_release(mc_arena *a);                      /* refs--, pooled at 0 */
+void arena_release(mc_arena *a);
+void arena_release_n(mc_arena *a, int k);                      /* refs--, pooled at 0 */
 void arena_retain(mc_arena *a, int n);
 
 /* Ownership registry of returned objects. */
 void registry_add(const void *obj, mc_arena *a);
 void registry_add_many(const void **objs, size_t n, mc_arena *a);
 mc_arena *registry_take(const void *obj, int *found);
+void registry_take_many(const void *const *objs, size_t n, mc_arena **arenas);
 
 /* Device buffers held by state entries (pooled per device by byte size). */
 void *dbuf_get(int device, size_t bytes);
@@ -207,10 +210,13 @@ typedef struct {
     struct {
         uintptr_t lo, hi;
         int device;
+        int arena;   /* 1: memory the library allocated for outputs */
     } r[MC_PTRCACHE];
     int n;
 } mc_ptrcache;
 int mc_classify(mc_ptrcache *pc, const void *p, int *device);
+/* as mc_classify; *in_arena = 1 when p lies in library-owned output memory */
+int mc_classify2(mc_ptrcache *pc, const void *p, int *device, int *in_arena);
 int mc_is_arena_ptr(const void *p);   /* inside memory the library allocated for outputs */
 void mc_record_stats(MomentumCompressor *mc, const CompressedLayerData *c);
 

@@ -288,6 +288,7 @@ mc_arena *arena_acquire(size_t bytes, int device) {
     }
     a->device = device;
     a->refs = 1;
+    a->objs = NULL;
     return a;
 }
 
@@ -297,10 +298,13 @@ void arena_retain(mc_arena *a, int n) {
     pthread_mutex_unlock(&g_pool_mu);
 }
 
-void arena_release(mc_arena *a) {
-    if (!a) return;
+void arena_release(mc_arena *a) { arena_release_n(a, 1); }
+
+void arena_release_n(mc_arena *a, int k) {
+    if (!a || k <= 0) return;
     pthread_mutex_lock(&g_pool_mu);
-    int left = --a->refs;
+    a->refs -= k;
+    int left = a->refs;
     if (left > 0) {
         pthread_mutex_unlock(&g_pool_mu);
         return;
@@ -318,6 +322,7 @@ void arena_release(mc_arena *a) {
         if (a->device < 0) cudaFreeHost(a->ptr);
         else cudaFree(a->ptr);
     }
+    free(a->objs);
     free(a);
 }
 
@@ -407,6 +412,29 @@ mc_arena *registry_take(const void *obj, int *found) {
     }
     pthread_mutex_unlock(&g_reg_mu);
     return NULL;
+}
+
+/* Takes the registry entries of objs[0..n) under one lock: arenas[i] is the
+ * owning arena, or NULL for an object the registry does not hold. */
+void registry_take_many(const void *const *objs, size_t n, mc_arena **arenas) {
+    pthread_mutex_lock(&g_reg_mu);
+    for (size_t k = 0; k < n; k++) {
+        arenas[k] = NULL;
+        if (!objs[k] || g_reg_cap == 0) continue;
+        size_t j = reg_hash(objs[k], g_reg_cap);
+        while (g_reg[j].obj) {
+            if (g_reg[j].obj == objs[k]) {
+                arenas[k] = g_reg[j].arena;
+                g_reg[j].obj = REG_TOMB;
+                g_reg[j].arena = NULL;
+                g_reg_len--;
+                g_reg_tomb++;
+                break;
+            }
+            j = (j + 1) & (g_reg_cap - 1);
+        }
+    }
+    pthread_mutex_unlock(&g_reg_mu);
 }
 
 /* =============================================================== scratch */
@@ -622,11 +650,18 @@ static int driver_range(const void *p, uintptr_t *lo, uintptr_t *hi) {
  * Ranges seen during one call are remembered in `pc`, so a batch whose
  * tensors live in one allocation costs one driver query. */
 int mc_classify(mc_ptrcache *pc, const void *p, int *device) {
+    int in_arena;
+    return mc_classify2(pc, p, device, &in_arena);
+}
+
+int mc_classify2(mc_ptrcache *pc, const void *p, int *device, int *in_arena) {
+    *in_arena = 0;
     if (!p) return 0;
     uintptr_t a = (uintptr_t)p;
     for (int i = 0; i < pc->n; i++) {
         if (a >= pc->r[i].lo && a < pc->r[i].hi) {
             if (device) *device = pc->r[i].device;
+            *in_arena = pc->r[i].arena;
             return pc->r[i].device >= 0;
         }
     }
@@ -637,9 +672,11 @@ int mc_classify(mc_ptrcache *pc, const void *p, int *device) {
             pc->r[pc->n].lo = lo;
             pc->r[pc->n].hi = hi;
             pc->r[pc->n].device = d;
+            pc->r[pc->n].arena = 1;
             pc->n++;
         }
         if (device) *device = d;
+        *in_arena = 1;
         return d >= 0;
     }
     struct cudaPointerAttributes at;
@@ -652,6 +689,7 @@ int mc_classify(mc_ptrcache *pc, const void *p, int *device) {
         pc->r[pc->n].lo = lo;
         pc->r[pc->n].hi = hi;
         pc->r[pc->n].device = is_dev ? at.device : -1;
+        pc->r[pc->n].arena = 0;
         pc->n++;
     }
     if (is_dev && device) *device = at.device;
