@@ -1,0 +1,122 @@
+"""Full-size parity on the model workloads: ResNet-18 (101 tensors, 5
+rounds) and ResNet-50 (266 tensors, 3 rounds) state-dict shapes with seeded
+AR(1) updates, and the 512x512x3x3 microbenchmark tensor (6 rounds).
+
+Against the reference build (oracle/_ref, the reference's own grouped
+OpenMP/SIMD codec with SZ3 stubbed):
+  * raw residual codec + libzstd frames: every payload byte, every header
+    field, hence the compression ratio, identical;
+  * cross decode: each decoder reads the other's payloads, outputs identical.
+Within this codec, at full size:
+  * q8 / int4 codes equal the oracle's quantisation of the raw residual of
+    the same round (the residual does not depend on the residual codec);
+  * decoding the q8 / int4 stream gives exactly what a decoder fed the same
+    stream with the residual dequantised into raw floats gives.
+The microbenchmark tensor runs through the reference comparison only."""
+import numpy as np
+import pytest
+
+from compressor_b200 import workloads as W
+from compressor_b200.abi import Codec, Layer
+from oracle import binding as ob
+
+pytestmark = pytest.mark.gpu
+
+CASES = [("resnet18", 5), ("resnet50", 3), ("microbench", 6)]
+
+
+def _rounds(model, n):
+    lay = W.Layout.of(model)
+    return lay, [lay.views(f) for f in W.rounds(model, n, seed=2024)]
+
+
+def _same_header(a, b):
+    assert (a.type, a.codec, a.step, a.shape, a.original_dtype, a.stored_dtype) == (
+        b.type, b.codec, b.step, b.shape, b.original_dtype, b.stored_dtype)
+    assert (a.current_mean, a.current_std, a.prev_mean, a.prev_std, a.global_min, a.global_max,
+            a.num_predicted_kernels, a.prediction_ratio, a.sign_mismatch_ratio) == (
+        b.current_mean, b.current_std, b.prev_mean, b.prev_std, b.global_min, b.global_max,
+        b.num_predicted_kernels, b.prediction_ratio, b.sign_mismatch_ratio)
+
+
+@pytest.mark.parametrize("model,n_rounds", CASES)
+def test_model_bytes_identical_to_reference(product_lib, model, n_rounds):
+    if not ob.have_ref():
+        pytest.skip("reference build oracle/_ref not present")
+    lay, rounds = _rounds(model, n_rounds)
+    ours = Codec(product_lib, client="Client1")
+    ours.lib.falcom_set_residual_codec(ours.h, b"raw")
+    assert ours.lib.falcom_set_frame_mode(ours.h, b"libzstd") == 0
+    ref = Codec(ob.REF_SO, client="Client1")
+    ours_d = Codec(product_lib, client="Client1")
+    ref_d = Codec(ob.REF_SO, client="Client1")
+    n_pred = 0
+    for xs in rounds:
+        r1, A, _ = ours.compress_batch(lay.names, xs)
+        r2, B, _ = ref.compress_batch(lay.names, xs)
+        assert r1 == 0 and r2 == 0
+        size_a = size_b = 0
+        for name, a, b in zip(lay.names, A, B):
+            _same_header(a, b)
+            assert a.data == b.data, name
+            assert a.bitmap == b.bitmap, name
+            assert a.dominant_signs == b.dominant_signs, name
+            size_a += len(a.data) + len(a.bitmap) + len(a.dominant_signs)
+            size_b += len(b.data) + len(b.bitmap) + len(b.dominant_signs)
+            n_pred += a.type == "momentum_predicted"
+        assert size_a == size_b
+        ra, YA = ours_d.decompress_batch(lay.names, B)
+        rb, YB = ref_d.decompress_batch(lay.names, A)
+        assert ra == 0 and rb == 0
+        for name, ya, yb in zip(lay.names, YA, YB):
+            assert ya.dtype == yb.dtype and ya.shape == yb.shape, name
+            assert np.array_equal(ya.view(np.uint8), yb.view(np.uint8)), name
+    assert n_pred > 0
+    for c in (ours, ref, ours_d, ref_d):
+        c.close()
+
+
+@pytest.mark.parametrize("codec,qmax", [("q8", 127), ("int4", 7)])
+@pytest.mark.parametrize("model,n_rounds", CASES[:2])
+def test_model_codes_are_quantised_raw_residual(product_lib, model, n_rounds, codec, qmax):
+    lay, rounds = _rounds(model, n_rounds)
+    raw = Codec(product_lib, client="Client1")
+    raw.lib.falcom_set_residual_codec(raw.h, b"raw")
+    q = Codec(product_lib, client="Client1")
+    q.lib.falcom_set_residual_codec(q.h, codec.encode())
+    dq = Codec(product_lib, client="Client1")
+    dz = Codec(product_lib, client="Client1")
+    for xs in rounds:
+        r1, A, _ = raw.compress_batch(lay.names, xs)
+        r2, B, _ = q.compress_batch(lay.names, xs)
+        assert r1 == 0 and r2 == 0
+        dequant = []
+        for name, a, b, x in zip(lay.names, A, B, xs):
+            assert (a.type, a.step, a.bitmap, a.dominant_signs) == (b.type, b.step, b.bitmap, b.dominant_signs)
+            if b.codec in ("q8", "int4"):
+                res = np.frombuffer(a.data, np.float32)
+                es, ec = ob.quantize(res, qmax)
+                scale = np.frombuffer(b.data[:4], np.float32)[0]
+                codes = (np.frombuffer(b.data[4:], np.int8) if codec == "q8"
+                         else ob.unpack_int4(np.frombuffer(b.data[4:], np.uint8), res.size))
+                assert scale == es, name
+                assert np.array_equal(codes, ec), name
+                dequant.append(ob.dequantize(codes, scale))
+            else:
+                assert b.data == a.data, name
+                dequant.append(None)
+        # the q8 / int4 decoder equals the raw decoder fed the dequantised residual
+        ry, Y = dq.decompress_batch(lay.names, B)
+        assert ry == 0
+        fed = []
+        for a, d in zip(A, dequant):
+            if d is None:
+                fed.append(a)
+            else:
+                fed.append(Layer(**{**a.__dict__, "data": d.astype(np.float32).tobytes()}))
+        rz, Z = dz.decompress_batch(lay.names, fed)
+        assert rz == 0
+        for name, y, z in zip(lay.names, Y, Z):
+            assert np.array_equal(y.view(np.uint32), z.view(np.uint32)), name
+    for c in (raw, q, dq, dz):
+        c.close()
