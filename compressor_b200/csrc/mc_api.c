@@ -176,6 +176,12 @@ MC_EXPORT void momentum_compressor_destroy(MomentumCompressor *mc) {
     listcache_free(mc, mc->dec_lists);
     scratch_free(&mc->scratch);
     if (mc->own_stream) cudaStreamDestroy(mc->own_stream);
+    if (mc->copy_in) cudaStreamDestroy(mc->copy_in);
+    if (mc->copy_out) cudaStreamDestroy(mc->copy_out);
+    for (int i = 0; i < MC_MAX_CHUNKS; i++) {
+        if (mc->ev_in[i]) cudaEventDestroy(mc->ev_in[i]);
+        if (mc->ev_done[i]) cudaEventDestroy(mc->ev_done[i]);
+    }
     for (int i = 0; i < 2 * MC_KTRACE_MAX; i++)
         if (mc->ktrace.ev[i]) cudaEventDestroy((cudaEvent_t)mc->ktrace.ev[i]);
     free(mc->stats.prediction_ratios);

@@ -118,6 +118,48 @@ static mc_listcache *lists_get(MomentumCompressor *mc, mc_listcache *set, uint64
     return v;
 }
 
+/* ---------------------------------------------------- chunked pipelines */
+/* A call with host buffers moves every byte over PCIe; splitting its items
+ * into chunks lets the upload of chunk c+1 run under the kernels of chunk c
+ * and the download of chunk c under the kernels of chunk c+1 (two copy
+ * streams, one per direction, ordered against the compute stream by
+ * events). */
+#define CHUNK_MIN_BYTES ((size_t)12 << 20)
+
+int mc_pipeline_init(MomentumCompressor *mc) {
+    if (mc->copy_in && mc->copy_out && mc->ev_done[MC_MAX_CHUNKS - 1]) return 0;
+    if (!mc->copy_in && cudaStreamCreateWithFlags(&mc->copy_in, cudaStreamNonBlocking) != cudaSuccess) return -1;
+    if (!mc->copy_out && cudaStreamCreateWithFlags(&mc->copy_out, cudaStreamNonBlocking) != cudaSuccess) return -1;
+    for (int i = 0; i < MC_MAX_CHUNKS; i++) {
+        if (!mc->ev_in[i] && cudaEventCreateWithFlags(&mc->ev_in[i], cudaEventDisableTiming) != cudaSuccess) return -1;
+        if (!mc->ev_done[i] && cudaEventCreateWithFlags(&mc->ev_done[i], cudaEventDisableTiming) != cudaSuccess)
+            return -1;
+    }
+    return 0;
+}
+
+/* Splits items [0, n) into at most MC_MAX_CHUNKS consecutive ranges of about
+ * equal bytes (bytes[i] per item), each at least CHUNK_MIN_BYTES; starts[c]
+ * is the first item of chunk c, starts[nc] = n.  Returns nc. */
+static int chunk_items(const size_t *bytes, size_t n, size_t *starts) {
+    size_t total = 0;
+    for (size_t i = 0; i < n; i++) total += bytes[i];
+    int nc = (int)(total / CHUNK_MIN_BYTES);
+    if (nc > MC_MAX_CHUNKS) nc = MC_MAX_CHUNKS;
+    if (nc < 1) nc = 1;
+    size_t acc = 0;
+    int c = 0;
+    starts[0] = 0;
+    for (size_t i = 0; i < n && c + 1 < nc; i++) {
+        acc += bytes[i];
+        if (acc * (size_t)nc >= total * (size_t)(c + 1)) starts[++c] = i + 1;
+    }
+    nc = c + 1;
+    starts[nc] = n;
+    return nc;
+}
+
+
 
 /* Call-local string -> int table (keys are borrowed, not copied). */
 typedef struct {
@@ -262,8 +304,21 @@ static void free_plan_tensors(MomentumCompressor *mc, cplan *P, size_t n, cgroup
     (void)mc;
 }
 
+/* one host-to-device copy of adjacent host inputs */
+typedef struct {
+    uintptr_t base, end;
+    size_t off;   /* in the staging buffer */
+    int chunk;
+} in_run;
+
 int mc_compress_grouped(MomentumCompressor *mc, BatchItem *items, size_t n, const char *client,
                         int payload_loc, int allow_fault) {
+    /* chunked pipeline state (declared first: every exit path frees it) */
+    int nchunks = 1;
+    size_t cstart[MC_MAX_CHUNKS + 1];
+    in_run *runs = NULL;
+    size_t nruns = 0;
+    uint8_t *stage = NULL;
     int rc = ERROR_NONE;
     cplan *P = (cplan *)calloc(n, sizeof(cplan));
     cgroup *G = (cgroup *)calloc(n, sizeof(cgroup));
@@ -518,8 +573,14 @@ int mc_compress_grouped(MomentumCompressor *mc, BatchItem *items, size_t n, cons
 
     prof_mark(&prof, "alloc");
     /* ----------------------------------------------- stage host inputs */
+    /* host inputs are copied into one device staging buffer, adjacent
+     * inputs (16-byte aligned) as one copy; with enough host bytes and one
+     * wave the copies are split by item chunk and issued later, interleaved
+     * with the chunk launches (chunked pipeline) */
+    cstart[0] = 0;
+    cstart[1] = n;
     {
-        size_t stage_bytes = 0;
+        size_t stage_bytes = 0, host_bytes = 0;
         int any_host = 0;
         mc_ptrcache pc;
         pc.n = 0;
@@ -527,70 +588,84 @@ int mc_compress_grouped(MomentumCompressor *mc, BatchItem *items, size_t n, cons
             int d = -1;
             P[i].src_dev = mc_classify(&pc, P[i].g->data, &d);
             if (P[i].src_dev && d != dev) P[i].src_dev = 0;   /* another GPU: copy */
-            if (!P[i].src_dev) any_host = 1;
+            if (!P[i].src_dev) {
+                any_host = 1;
+                host_bytes += P[i].bytes;
+            }
+        }
+        if (any_host && nwaves == 1 && host_bytes >= 2 * CHUNK_MIN_BYTES && mc_pipeline_init(mc) == 0) {
+            size_t *hb = (size_t *)malloc(n * sizeof(size_t));
+            if (hb) {
+                for (size_t i = 0; i < n; i++) hb[i] = P[i].src_dev ? 0 : P[i].bytes;
+                nchunks = chunk_items(hb, n, cstart);
+                free(hb);
+            }
         }
         if (any_host) {
-            /* coalesce host inputs that are adjacent in memory (16-byte aligned) */
             size_t *order = (size_t *)malloc(n * sizeof(size_t));
+            int *chunk_of = (int *)malloc(n * sizeof(int));
+            runs = (in_run *)malloc(n * sizeof(in_run));
+            if (!order || !chunk_of || !runs) {
+                free(order);
+                free(chunk_of);
+                rc = ERROR_ALLOCATION;
+                goto fail;
+            }
+            for (int c = 0; c < nchunks; c++)
+                for (size_t i = cstart[c]; i < cstart[c + 1]; i++) chunk_of[i] = c;
             size_t no = 0;
             for (size_t i = 0; i < n; i++)
                 if (!P[i].src_dev) order[no++] = i;
-            for (size_t a = 1; a < no; a++) { /* insertion sort by address */
+            for (size_t a = 1; a < no; a++) { /* insertion sort by (chunk, address) */
                 size_t v = order[a], b = a;
-                while (b > 0 && (uintptr_t)P[order[b - 1]].g->data > (uintptr_t)P[v].g->data) {
+                while (b > 0 && (chunk_of[order[b - 1]] > chunk_of[v] ||
+                                 (chunk_of[order[b - 1]] == chunk_of[v] &&
+                                  (uintptr_t)P[order[b - 1]].g->data > (uintptr_t)P[v].g->data))) {
                     order[b] = order[b - 1];
                     b--;
                 }
                 order[b] = v;
             }
-            size_t *run_off = (size_t *)malloc(n * sizeof(size_t));
             for (size_t a = 0; a < no;) {
                 size_t i0 = order[a];
                 uintptr_t base = (uintptr_t)P[i0].g->data, end = base + P[i0].bytes;
                 size_t b = a + 1;
-                while (b < no) {
-                    uintptr_t s = (uintptr_t)P[order[b]].g->data;
-                    if (s != end || (s & 15) || (base & 15)) break;
-                    end = s + P[order[b]].bytes;
+                while (b < no && chunk_of[order[b]] == chunk_of[i0]) {
+                    uintptr_t s2 = (uintptr_t)P[order[b]].g->data;
+                    if (s2 != end || (s2 & 15) || (base & 15)) break;
+                    end = s2 + P[order[b]].bytes;
                     b++;
                 }
-                size_t start = stage_bytes;
+                runs[nruns].base = base;
+                runs[nruns].end = end;
+                runs[nruns].off = stage_bytes;
+                runs[nruns].chunk = chunk_of[i0];
                 for (size_t c = a; c < b; c++)
-                    run_off[order[c]] = start + ((uintptr_t)P[order[c]].g->data - base);
-                stage_bytes = ALIGN_UP(start + (end - base), SLOT_ALIGN);
+                    P[order[c]].dev_in = (const void *)(stage_bytes + ((uintptr_t)P[order[c]].g->data - base));
+                stage_bytes = ALIGN_UP(stage_bytes + (end - base), SLOT_ALIGN);
+                nruns++;
                 a = b;
             }
-            uint8_t *stage = (uint8_t *)scratch_dev(&mc->scratch, SD_INPUT, stage_bytes);
+            free(order);
+            free(chunk_of);
+            stage = (uint8_t *)scratch_dev(&mc->scratch, SD_INPUT, stage_bytes);
             if (!stage) {
-                free(order);
-                free(run_off);
                 rc = ERROR_ALLOCATION;
                 mc_set_error(mc, "Batch compress: input staging allocation failed");
                 goto fail;
             }
-            for (size_t a = 0; a < no;) {
-                size_t i0 = order[a];
-                uintptr_t base = (uintptr_t)P[i0].g->data, end = base + P[i0].bytes;
-                size_t b = a + 1;
-                while (b < no) {
-                    uintptr_t s = (uintptr_t)P[order[b]].g->data;
-                    if (s != end || (s & 15) || (base & 15)) break;
-                    end = s + P[order[b]].bytes;
-                    b++;
+            for (size_t i = 0; i < n; i++)
+                if (!P[i].src_dev) P[i].dev_in = stage + (uintptr_t)P[i].dev_in;
+            if (nchunks == 1) {   /* one chunk: all copies now, in stream order before the kernels */
+                for (size_t r = 0; r < nruns; r++) {
+                    if (cudaMemcpyAsync(stage + runs[r].off, (const void *)runs[r].base, runs[r].end - runs[r].base,
+                                        cudaMemcpyHostToDevice, st) != cudaSuccess) {
+                        rc = ERROR_COMPRESSION;
+                        mc_set_error(mc, "Batch compress: host-to-device copy failed");
+                        goto fail;
+                    }
                 }
-                if (cudaMemcpyAsync(stage + run_off[i0], (const void *)base, end - base,
-                                    cudaMemcpyHostToDevice, st) != cudaSuccess) {
-                    free(order);
-                    free(run_off);
-                    rc = ERROR_COMPRESSION;
-                    mc_set_error(mc, "Batch compress: host-to-device copy failed");
-                    goto fail;
-                }
-                for (size_t c = a; c < b; c++) P[order[c]].dev_in = stage + run_off[order[c]];
-                a = b;
             }
-            free(order);
-            free(run_off);
         }
         for (size_t i = 0; i < n; i++)
             if (P[i].src_dev) P[i].dev_in = P[i].g->data;
@@ -729,12 +804,75 @@ int mc_compress_grouped(MomentumCompressor *mc, BatchItem *items, size_t n, cons
     mc->last_launches = 0;
     mc_ktrace *tr = mc_trace_begin(mc);
     const int staged = !mc_env_off("FALCOM_STAGE");
-    for (int w = 0; w < nwaves; w++) {
+    if (nchunks > 1) {
+        /* chunked pipeline (one wave): per chunk, its input copies on the
+         * upload stream, its kernels on the compute stream after them, its
+         * payload download on the download stream after the kernels */
+        int all0 = 0, mom0 = 0;
+        for (int c = 0; c < nchunks; c++) {
+            for (size_t r = 0; r < nruns; r++) {
+                if (runs[r].chunk != c) continue;
+                if (cudaMemcpyAsync(stage + runs[r].off, (const void *)runs[r].base, runs[r].end - runs[r].base,
+                                    cudaMemcpyHostToDevice, mc->copy_in) != cudaSuccess) {
+                    rc = ERROR_COMPRESSION;
+                    mc_set_error(mc, "Batch compress: host-to-device copy failed");
+                    goto fail;
+                }
+            }
+            int na = 0, nm = 0;
+            for (size_t i = cstart[c]; i < cstart[c + 1]; i++) {
+                na += P[i].ntiles;
+                if (P[i].kind == MC_K_MOMENTUM) nm += P[i].ntiles;
+            }
+            mc_enc_launch L;
+            memset(&L, 0, sizeof(L));
+            L.items = (const mc_enc_item *)dtab;
+            L.results = results;
+            L.item0 = (int32_t)cstart[c];
+            L.nitems = (int32_t)(cstart[c + 1] - cstart[c]);
+            L.all_tiles = (const uint8_t *)lc->dev + (size_t)all0 * sizeof(mc_tile_ref);
+            L.nall_tiles = na;
+            L.mom_tiles = (const uint8_t *)lc->dev + tab_list + (size_t)mom0 * sizeof(mc_tile_ref);
+            L.nmom_tiles = nm;
+            L.tiles = tiles;
+            L.tile_poff = poff;
+            L.staged = staged;
+            L.wave = 0;
+            all0 += na;
+            mom0 += nm;
+            if (cudaEventRecord(mc->ev_in[c], mc->copy_in) != cudaSuccess ||
+                cudaStreamWaitEvent(st, mc->ev_in[c], 0) != cudaSuccess) {
+                rc = ERROR_COMPRESSION;
+                goto fail;
+            }
+            int k = L.nitems > 0 ? mc_launch_encode(&L, st, tr) : 0;
+            if (k < 0) {
+                rc = ERROR_COMPRESSION;
+                mc_set_error(mc, "Batch compress: kernel launch failed: %s",
+                             cudaGetErrorString(cudaGetLastError()));
+                goto fail;
+            }
+            mc->last_launches += k;
+            if (host_arena) {
+                const size_t o0 = P[cstart[c]].off_data;
+                const size_t o1 = c + 1 < nchunks ? P[cstart[c + 1]].off_data : arena_bytes;
+                if (cudaEventRecord(mc->ev_done[c], st) != cudaSuccess ||
+                    cudaStreamWaitEvent(mc->copy_out, mc->ev_done[c], 0) != cudaSuccess ||
+                    cudaMemcpyAsync((uint8_t *)host_arena->ptr + o0, payload_dev + o0, o1 - o0,
+                                    cudaMemcpyDeviceToHost, mc->copy_out) != cudaSuccess) {
+                    rc = ERROR_COMPRESSION;
+                    goto fail;
+                }
+            }
+        }
+    }
+    for (int w = 0; nchunks == 1 && w < nwaves; w++) {
         uint8_t *dl = (uint8_t *)lc->dev + 2 * tab_list * (size_t)w;
         mc_enc_launch L;
         memset(&L, 0, sizeof(L));
         L.items = (const mc_enc_item *)dtab;
         L.results = results;
+        L.item0 = 0;
         L.nitems = (int32_t)n;
         L.all_tiles = dl;
         L.nall_tiles = lc->counts[2 * w];
@@ -758,10 +896,15 @@ int mc_compress_grouped(MomentumCompressor *mc, BatchItem *items, size_t n, cons
     /* ------------------------------------------------- results to host */
     mc_enc_result *hres = (mc_enc_result *)scratch_host(&mc->scratch, SH_RESULTS, n * sizeof(mc_enc_result));
     cudaMemcpyAsync(hres, results, n * sizeof(mc_enc_result), cudaMemcpyDeviceToHost, st);
-    if (host_arena)
+    if (host_arena && nchunks == 1)
         cudaMemcpyAsync(host_arena->ptr, payload_dev, arena_bytes, cudaMemcpyDeviceToHost, st);
     prof_mark(&prof, "launch");
     cudaError_t e = cudaStreamSynchronize(st);
+    if (nchunks > 1) {
+        const cudaError_t e2 = cudaStreamSynchronize(mc->copy_out);
+        const cudaError_t e3 = cudaStreamSynchronize(mc->copy_in);
+        if (e == cudaSuccess) e = e2 != cudaSuccess ? e2 : e3;
+    }
     prof_mark(&prof, "sync");
     mc_trace_end(mc);
     if (e != cudaSuccess) {
@@ -906,6 +1049,11 @@ int mc_compress_grouped(MomentumCompressor *mc, BatchItem *items, size_t n, cons
     goto out;
 
 fail:
+    /* nothing may still be writing into memory that goes back to the pools */
+    cudaStreamSynchronize(mc->stream);
+    if (mc->copy_in) cudaStreamSynchronize(mc->copy_in);
+    if (mc->copy_out) cudaStreamSynchronize(mc->copy_out);
+    (void)cudaGetLastError();
     free_plan_tensors(mc, P, n, G, ng);
     if (dev_arena) arena_release(dev_arena);
     if (host_arena) arena_release(host_arena);
@@ -914,6 +1062,7 @@ fail:
         if (items[i].error == ERROR_NONE) items[i].error = rc;
     }
 out:
+    free(runs);
     free(P);
     free(G);
     return rc;
@@ -958,7 +1107,16 @@ typedef struct {
     const uint8_t *src;
     size_t len;
     const uint8_t **dst;      /* where the device address is written */
+    int chunk;                /* pipeline chunk of the item */
 } hrange;
+
+/* one host-to-device copy of staged payload bytes */
+typedef struct {
+    uintptr_t base;
+    size_t len;
+    uint8_t *dst;
+    int chunk;
+} dec_run;
 
 /* Plans one item (reference decompress_layer :3476-3598 validation order). */
 static void dplan_item(MomentumCompressor *mc, dplan *d, const BatchItem *it, const mc_keycache *kc,
@@ -1120,6 +1278,12 @@ static int dec_segment(MomentumCompressor *mc, const BatchItem *items, size_t n,
                        NDArray **out, int out_loc, size_t *n_ok, int force_expand, size_t base) {
     cudaStream_t st = mc->stream;
     const int dev = mc->device;
+    int nch = 1;
+    size_t dstart[MC_MAX_CHUNKS + 1];
+    dstart[0] = 0;
+    dstart[1] = n;
+    dec_run *runs = NULL;
+    size_t nruns = 0;
     dplan *D = (dplan *)calloc(n, sizeof(dplan));
     if (!D) return ERROR_ALLOCATION;
     int rc = ERROR_NONE;
@@ -1158,6 +1322,16 @@ static int dec_segment(MomentumCompressor *mc, const BatchItem *items, size_t n,
     /* ---------------------------------------------- payload residency */
     /* host payload ranges are copied to the device (adjacent ranges merged);
      * frames with compressed blocks are decoded on the host first */
+    /* chunked pipeline: items split by decoded bytes when the call moves
+     * payloads or outputs between host and device */
+    if (!force_expand && mc_pipeline_init(mc) == 0) {
+        size_t *ob = (size_t *)malloc(n * sizeof(size_t));
+        if (ob) {
+            for (size_t i = 0; i < n; i++) ob[i] = D[i].ok ? D[i].bytes : 0;
+            nch = chunk_items(ob, n, dstart);
+            free(ob);
+        }
+    }
     size_t nr = 0;
     hrange *R = (hrange *)calloc(3 * n + 1, sizeof(hrange));
     uint8_t **host_dec = (uint8_t **)calloc(3 * n + 1, sizeof(uint8_t *));
@@ -1217,24 +1391,31 @@ static int dec_segment(MomentumCompressor *mc, const BatchItem *items, size_t n,
             R[nr].src = src;
             R[nr].len = len;
             R[nr].dst = dsts[k];
+            R[nr].chunk = 0;
+            while (R[nr].chunk + 1 < nch && i >= dstart[R[nr].chunk + 1]) R[nr].chunk++;
             nr++;
         }
     }
     /* momentum items whose bitmap turned out unusable fall back to residual only */
-    /* stage host ranges */
+    /* stage host ranges: sorted by (chunk, address), ranges with gaps below
+     * 64 KiB merged within a chunk; the copies are recorded and issued at
+     * launch time (per chunk when the call is pipelined) */
     if (nr) {
-        /* sort by address, merge ranges with gaps below 64 KiB */
         for (size_t a = 1; a < nr; a++) {
             hrange v = R[a];
             size_t b = a;
-            while (b > 0 && (uintptr_t)R[b - 1].src > (uintptr_t)v.src) { R[b] = R[b - 1]; b--; }
+            while (b > 0 && (R[b - 1].chunk > v.chunk ||
+                             (R[b - 1].chunk == v.chunk && (uintptr_t)R[b - 1].src > (uintptr_t)v.src))) {
+                R[b] = R[b - 1];
+                b--;
+            }
             R[b] = v;
         }
         size_t total = 0;
         for (size_t a = 0; a < nr;) {
             uintptr_t base = (uintptr_t)R[a].src, end = base + R[a].len;
             size_t b = a + 1;
-            while (b < nr && (uintptr_t)R[b].src <= end + 65536) {
+            while (b < nr && R[b].chunk == R[a].chunk && (uintptr_t)R[b].src <= end + 65536) {
                 uintptr_t e2 = (uintptr_t)R[b].src + R[b].len;
                 if (e2 > end) end = e2;
                 b++;
@@ -1243,12 +1424,13 @@ static int dec_segment(MomentumCompressor *mc, const BatchItem *items, size_t n,
             a = b;
         }
         uint8_t *stage = (uint8_t *)scratch_dev(&mc->scratch, SD_DSTAGE, total + 256);
-        if (!stage) { rc = ERROR_ALLOCATION; goto done; }
+        runs = (dec_run *)malloc(nr * sizeof(dec_run));
+        if (!stage || !runs) { rc = ERROR_ALLOCATION; goto done; }
         size_t off = 0;
         for (size_t a = 0; a < nr;) {
             uintptr_t base = (uintptr_t)R[a].src, end = base + R[a].len;
             size_t b = a + 1;
-            while (b < nr && (uintptr_t)R[b].src <= end + 65536) {
+            while (b < nr && R[b].chunk == R[a].chunk && (uintptr_t)R[b].src <= end + 65536) {
                 uintptr_t e2 = (uintptr_t)R[b].src + R[b].len;
                 if (e2 > end) end = e2;
                 b++;
@@ -1256,8 +1438,11 @@ static int dec_segment(MomentumCompressor *mc, const BatchItem *items, size_t n,
             /* keep the source's 16-byte phase so 4-byte fields stay aligned */
             size_t phase = base & 15;
             uint8_t *dst = stage + off + phase;
-            if (cudaMemcpyAsync(dst, (const void *)base, end - base, cudaMemcpyHostToDevice, st) !=
-                cudaSuccess) { rc = ERROR_DECOMPRESSION; goto done; }
+            runs[nruns].base = base;
+            runs[nruns].len = end - base;
+            runs[nruns].dst = dst;
+            runs[nruns].chunk = R[a].chunk;
+            nruns++;
             for (size_t c = a; c < b; c++) *R[c].dst = dst + ((uintptr_t)R[c].src - base);
             off = ALIGN_UP(off + phase + (end - base), SLOT_ALIGN);
             a = b;
@@ -1486,14 +1671,20 @@ static int dec_segment(MomentumCompressor *mc, const BatchItem *items, size_t n,
     /* ------------------------------------------------------- launch */
     mc->last_launches = 0;
     mc_ktrace *tr = mc_trace_begin(mc);
-    if (njobs) {
-        /* bitmaps must decode into clean zero-padded words */
-        if (content_bytes) cudaMemsetAsync(content, 0, content_bytes, st);
-        int k = mc_launch_unframe((const mc_unframe_job *)(dt + t_items), njobs, st, tr);
-        if (k < 0) { rc = ERROR_DECOMPRESSION; goto fail_arena; }
-        mc->last_launches += k;
-    }
-    {
+    /* pipelined only without frame expansion jobs and with bytes to move */
+    const int pipelined = nch > 1 && njobs == 0 && (nruns > 0 || out_loc != FALCOM_LOC_DEVICE);
+    const int dstaged = !mc_env_off("FALCOM_STAGE");
+    if (!pipelined) {
+        for (size_t r = 0; r < nruns; r++)
+            if (cudaMemcpyAsync(runs[r].dst, (const void *)runs[r].base, runs[r].len, cudaMemcpyHostToDevice, st) !=
+                cudaSuccess) { rc = ERROR_DECOMPRESSION; goto fail_arena; }
+        if (njobs) {
+            /* bitmaps must decode into clean zero-padded words */
+            if (content_bytes) cudaMemsetAsync(content, 0, content_bytes, st);
+            int k = mc_launch_unframe((const mc_unframe_job *)(dt + t_items), njobs, st, tr);
+            if (k < 0) { rc = ERROR_DECOMPRESSION; goto fail_arena; }
+            mc->last_launches += k;
+        }
         mc_dec_launch L;
         memset(&L, 0, sizeof(L));
         L.items = (const mc_dec_item *)dt;
@@ -1505,10 +1696,56 @@ static int dec_segment(MomentumCompressor *mc, const BatchItem *items, size_t n,
         L.nmom_tiles = lc->counts[1];
         L.tile_count = d_count;
         L.tile_poff = d_poff;
-        L.staged = !mc_env_off("FALCOM_STAGE");
+        L.staged = dstaged;
         int k = mc_launch_decode(&L, st, tr);
         if (k < 0) { rc = ERROR_DECOMPRESSION; goto fail_arena; }
         mc->last_launches += k;
+    } else {
+        /* per chunk: its payload copies on the upload stream, its kernels on
+         * the compute stream after them, its decoded outputs downloaded on
+         * the download stream after the kernels */
+        int all0 = 0, mom0 = 0;
+        for (int c = 0; c < nch; c++) {
+            for (size_t r = 0; r < nruns; r++) {
+                if (runs[r].chunk != c) continue;
+                if (cudaMemcpyAsync(runs[r].dst, (const void *)runs[r].base, runs[r].len, cudaMemcpyHostToDevice,
+                                    mc->copy_in) != cudaSuccess) { rc = ERROR_DECOMPRESSION; goto fail_arena; }
+            }
+            int na = 0, nm = 0;
+            size_t o0 = (size_t)-1, o1 = 0;
+            for (size_t i = dstart[c]; i < dstart[c + 1]; i++) {
+                if (!D[i].ok) continue;
+                na += D[i].ntiles;
+                if (D[i].kind == MC_D_MOMENTUM) nm += D[i].ntiles;
+                if (o0 == (size_t)-1) o0 = D[i].out_off;
+                o1 = D[i].out_off + D[i].bytes;
+            }
+            if (cudaEventRecord(mc->ev_in[c], mc->copy_in) != cudaSuccess ||
+                cudaStreamWaitEvent(st, mc->ev_in[c], 0) != cudaSuccess) { rc = ERROR_DECOMPRESSION; goto fail_arena; }
+            mc_dec_launch L;
+            memset(&L, 0, sizeof(L));
+            L.items = (const mc_dec_item *)dt;
+            L.results = d_res;
+            L.nitems = (int32_t)n;
+            L.all_tiles = (const uint8_t *)lc->dev + (size_t)all0 * sizeof(mc_tile_ref);
+            L.nall_tiles = na;
+            L.mom_tiles = (const uint8_t *)lc->dev + t_tiles + (size_t)mom0 * sizeof(mc_tile_ref);
+            L.nmom_tiles = nm;
+            L.tile_count = d_count;
+            L.tile_poff = d_poff;
+            L.staged = dstaged;
+            all0 += na;
+            mom0 += nm;
+            int k = mc_launch_decode(&L, st, tr);
+            if (k < 0) { rc = ERROR_DECOMPRESSION; goto fail_arena; }
+            mc->last_launches += k;
+            if (out_loc != FALCOM_LOC_DEVICE && o0 != (size_t)-1) {
+                if (cudaEventRecord(mc->ev_done[c], st) != cudaSuccess ||
+                    cudaStreamWaitEvent(mc->copy_out, mc->ev_done[c], 0) != cudaSuccess ||
+                    cudaMemcpyAsync((uint8_t *)oarena->ptr + o0, dout + o0, o1 - o0, cudaMemcpyDeviceToHost,
+                                    mc->copy_out) != cudaSuccess) { rc = ERROR_DECOMPRESSION; goto fail_arena; }
+            }
+        }
     }
     mc->total_launches += mc->last_launches;
 
@@ -1517,10 +1754,15 @@ static int dec_segment(MomentumCompressor *mc, const BatchItem *items, size_t n,
     mc_dec_result *h_res = (mc_dec_result *)(ht + tab + t_lens);
     if (njobs) cudaMemcpyAsync(h_lens, d_lens, (size_t)njobs * 8, cudaMemcpyDeviceToHost, st);
     cudaMemcpyAsync(h_res, d_res, n * sizeof(mc_dec_result), cudaMemcpyDeviceToHost, st);
-    if (out_loc != FALCOM_LOC_DEVICE && out_bytes)
+    if (out_loc != FALCOM_LOC_DEVICE && out_bytes && !pipelined)
         cudaMemcpyAsync(oarena->ptr, dout, out_bytes, cudaMemcpyDeviceToHost, st);
     prof_mark(&prof, "launch");
     cudaError_t e = cudaStreamSynchronize(st);
+    if (pipelined) {
+        const cudaError_t e2 = cudaStreamSynchronize(mc->copy_out);
+        const cudaError_t e3 = cudaStreamSynchronize(mc->copy_in);
+        if (e == cudaSuccess) e = e2 != cudaSuccess ? e2 : e3;
+    }
     prof_mark(&prof, "sync");
     mc_trace_end(mc);
     if (e != cudaSuccess) {
@@ -1632,6 +1874,12 @@ static int dec_segment(MomentumCompressor *mc, const BatchItem *items, size_t n,
     }
 
 fail_arena:
+    if (rc != ERROR_NONE) {   /* nothing may still write into memory going back to the pools */
+        cudaStreamSynchronize(st);
+        if (mc->copy_in) cudaStreamSynchronize(mc->copy_in);
+        if (mc->copy_out) cudaStreamSynchronize(mc->copy_out);
+        (void)cudaGetLastError();
+    }
     if (oarena) arena_release(oarena);
     for (size_t i = 0; i < n; i++) {
         if (D[i].hist) {
@@ -1646,6 +1894,7 @@ fail_arena:
 done:
     for (size_t i = 0; i < nhd; i++) free(host_dec[i]);
     free(host_dec);
+    free(runs);
     free(R);
     free(D);
     return rc;

@@ -94,7 +94,7 @@ typedef struct {
 typedef struct {
     const mc_enc_item *items;   /* device */
     mc_enc_result *results;     /* device, zeroed by the caller before the first wave */
-    int32_t nitems;
+    int32_t nitems;             /* items covered by the finalize kernels of this launch */
     const void *all_tiles;      /* device mc_tile_ref[]: tiles processed by passes 1 and 4 */
     int32_t nall_tiles;
     const void *mom_tiles;      /* device mc_tile_ref[]: tiles of momentum items (passes 2, 3) */
@@ -103,6 +103,8 @@ typedef struct {
     int64_t *tile_poff;         /* device scratch, ntiles */
     int32_t staged;             /* 1: stage tiles of aligned items in shared memory (bulk copies) */
     int32_t wave;               /* wave of this launch (finalize kernels skip other items) */
+    int32_t item0;              /* finalize kernels: items item0 .. item0 + nitems - 1 */
+    int32_t pad;
 } mc_enc_launch;
 
 /* One entry of a launch's tile list: tile id and the item it belongs to. */

@@ -139,6 +139,11 @@ struct MomentumCompressor {
     int device;
     cudaStream_t stream;
     cudaStream_t own_stream;
+    /* chunked host<->device pipelines: copy streams and per-chunk events
+     * (created on first use) */
+#define MC_MAX_CHUNKS 8
+    cudaStream_t copy_in, copy_out;
+    cudaEvent_t ev_in[MC_MAX_CHUNKS], ev_done[MC_MAX_CHUNKS];
     int residual_codec;      /* MC_CODEC_* */
     int frame_mode;          /* MC_FRAME_GPU / MC_FRAME_LIBZSTD */
     int payload_loc;
@@ -239,6 +244,9 @@ void rec_commit(mc_tensor **slot, mc_tensor **spare, mc_tensor *t);
 void keycache_free(mc_keycache *kc);
 mc_keycache *keycache_get(MomentumCompressor *mc, mc_keycache *set, const char *client, const mc_keyreq *req,
                           size_t n, int *rc);
+
+/* copy streams and events of the chunked pipelines; 0 on success */
+int mc_pipeline_init(MomentumCompressor *mc);
 
 /* tile-list cache (mc_batch.c) */
 void listcache_free(MomentumCompressor *mc, mc_listcache *set);

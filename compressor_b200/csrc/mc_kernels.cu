@@ -769,7 +769,7 @@ __device__ __forceinline__ void stage_words(const mc_enc_item &I, int t, uint32_
     }
 }
 
-// Per-item results of pass 1 (one CTA per item of the wave): means and raw
+// Per-item results of pass 1 (one CTA per item of the launch, items item0 ..): means and raw
 // min / max of a momentum layer, the exclusive scan of its per-tile predicted
 // counts, the bitmap / sign frame headers; the scale of a direct quantised
 // tensor.  Reductions run over the tiles in order (deterministic).
@@ -777,7 +777,7 @@ __global__ void __launch_bounds__(TPB) k_enc_final1(mc_enc_launch L) {
     __shared__ Red red;
     __shared__ int scan_sh[NWARP + 1];
     __shared__ int s_blk[MAX_RLE_BLOCKS + 1];
-    const int ii = blockIdx.x;
+    const int ii = L.item0 + blockIdx.x;
     const mc_enc_item I = L.items[ii];
     if (I.wave != L.wave) return;
     mc_enc_result *R = L.results + ii;
@@ -872,7 +872,7 @@ __global__ void __launch_bounds__(TPB, 6) k_enc_pass2(mc_enc_launch L) {
 // Per-item results of pass 2: population std of |cur| and |prev|.
 __global__ void __launch_bounds__(TPB) k_enc_final2(mc_enc_launch L) {
     __shared__ Red red;
-    const int ii = blockIdx.x;
+    const int ii = L.item0 + blockIdx.x;
     const mc_enc_item I = L.items[ii];
     if (I.wave != L.wave || I.kind != MC_K_MOMENTUM) return;
     mc_enc_result *R = L.results + ii;
@@ -998,7 +998,7 @@ __global__ void __launch_bounds__(TPB, 4) k_enc_pass3(mc_enc_launch L) {
 // the payload header) and sign mismatches.
 __global__ void __launch_bounds__(TPB) k_enc_final3(mc_enc_launch L) {
     __shared__ Red red;
-    const int ii = blockIdx.x;
+    const int ii = L.item0 + blockIdx.x;
     const mc_enc_item I = L.items[ii];
     if (I.wave != L.wave || I.kind != MC_K_MOMENTUM) return;
     mc_enc_result *R = L.results + ii;
