@@ -47,12 +47,12 @@ PEAK_FALLBACK_GBS = 6650.0
 # whenever a kernel changes; None for workloads that were not captured.
 NCU_TRAFFIC = {
     ("resnet50", "q8"): {
-        "enc_pass1_stats_sign": 262_260_992,
-        "enc_pass2_variance": 191_604_224,
-        "enc_pass3_predict": 340_526_080,
-        "enc_pass4_quantize_pack": 188_978_176,
-        "dec_prefix": 236_544,
-        "dec_reconstruct": 426_964_224,
+        "enc_pass1_stats_sign": 260_293_376,
+        "enc_pass2_variance": 191_903_744,
+        "enc_pass3_predict": 339_045_888,
+        "enc_pass4_quantize_pack": 189_139_456,
+        "dec_prefix": 259_840,
+        "dec_reconstruct": 421_497_088,
     },
 }
 
