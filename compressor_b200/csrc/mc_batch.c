@@ -1697,6 +1697,8 @@ static int dec_segment(MomentumCompressor *mc, const BatchItem *items, size_t n,
         L.tile_count = d_count;
         L.tile_poff = d_poff;
         L.staged = dstaged;
+        L.item0 = 0;
+        L.item1 = (int32_t)n;
         int k = mc_launch_decode(&L, st, tr);
         if (k < 0) { rc = ERROR_DECOMPRESSION; goto fail_arena; }
         mc->last_launches += k;
@@ -1734,6 +1736,8 @@ static int dec_segment(MomentumCompressor *mc, const BatchItem *items, size_t n,
             L.tile_count = d_count;
             L.tile_poff = d_poff;
             L.staged = dstaged;
+            L.item0 = (int32_t)dstart[c];
+            L.item1 = (int32_t)dstart[c + 1];
             all0 += na;
             mom0 += nm;
             int k = mc_launch_decode(&L, st, tr);

@@ -193,9 +193,10 @@ typedef struct {
     int32_t nall_tiles;
     const void *mom_tiles;      /* mc_tile_ref[] of momentum items (prefix kernel) */
     int32_t nmom_tiles;
-    int32_t *tile_count;        /* scratch */
-    int64_t *tile_poff;         /* scratch */
+    int32_t *tile_count;        /* scratch: predicted kernels per momentum tile */
+    int64_t *tile_poff;         /* scratch: first predicted kernel of each momentum tile in the dense signs */
     int32_t staged;             /* 1: stage tiles of aligned items in shared memory (bulk copies) */
+    int32_t item0, item1;       /* items [item0, item1) own this launch's tiles */
     int32_t pad;
 } mc_dec_launch;
 

@@ -313,21 +313,21 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
     return false;
 }
 
-// ------------------------------------------------------- persistent tiles
-// The streaming passes run persistent CTAs: CTA b walks a contiguous range of
-// the launch's tile list (forwards, or backwards so that a pass starts on the
-// tiles the previous pass touched last, which are still in L2) through a
-// pipeline of NST shared-memory stages: while the CTA computes tile i, the
-// bulk copies of tiles i+1 .. i+NST-1 are in flight.  Thread 0 plans and
-// issues; a staged tile's descriptor travels in shared memory, published by
-// the mbarrier arrive.  A tile only writes its outputs and its partials: the
-// per-item reductions run in separate finalize kernels, so the streaming
-// loop has no fences or atomics.
+// ------------------------------------------------------------ tile CTAs
+// The streaming passes run one CTA per tile of the launch's tile list.  A
+// tile only writes its outputs and its partials: the per-item reductions run
+// in separate finalize kernels, so the passes have no fences or atomics.
 #define NSTAGE_ARR 3
+// Bitmap words of one tile: at most 4096 kernels (tiles hold at most
+// STAGE_ELEMS elements of whole kernels, and start on a word boundary).
+#define TILE_WORDS (STAGE_ELEMS / 32)
 
 struct StageDesc {
     const float *src[NSTAGE_ARR];   // global source of every staged array (NULL: not staged)
     int64_t e0, e1;                 // element range of the tile
+    // optional byte range [x0, x1) staged in the byte region behind the
+    // arrays, the byte at address a at offset a - (x0 & ~15)
+    const uint8_t *x0, *x1;
     int gt;                         // tile id
     int ii;                         // item index
 };
@@ -340,36 +340,51 @@ struct TileShared {
 __device__ __forceinline__ uint32_t stage_body_bytes(const StageDesc &d) {
     return (uint32_t)(((d.e1 - d.e0) * 4) & ~(int64_t)15);
 }
+__device__ __forceinline__ uintptr_t up16(const void *p) { return ((uintptr_t)p + 15) & ~(uintptr_t)15; }
+__device__ __forceinline__ uintptr_t dn16(const void *p) { return (uintptr_t)p & ~(uintptr_t)15; }
 
 // Thread 0: start the bulk copies of a tile into a stage buffer of NA
-// arrays; a tile with nothing staged still arrives so that the stage's phase
+// arrays (and the aligned interior of the byte range into the byte region
+// xb); a tile with nothing staged still arrives so that the stage's phase
 // completes.
 template <int NA>
-__device__ void pipe_issue(uint32_t bar, float *buf, const StageDesc &d) {
+__device__ void pipe_issue(uint32_t bar, float *buf, uint8_t *xb, const StageDesc &d) {
     const uint32_t body = stage_body_bytes(d);
     uint32_t total = 0;
 #pragma unroll
     for (int k = 0; k < NA; k++)
         if (d.src[k]) total += body;
-    mbar_expect_tx(bar, total);
+    const uintptr_t xa = d.x0 ? up16(d.x0) : 0, xe = d.x0 ? dn16(d.x1) : 0;
+    const uint32_t xbytes = xe > xa ? (uint32_t)(xe - xa) : 0u;
+    mbar_expect_tx(bar, total + xbytes);
     if (body) {
 #pragma unroll
         for (int k = 0; k < NA; k++)
             if (d.src[k]) bulk_g2s(smem_u32(buf + k * STAGE_ELEMS), d.src[k] + d.e0, body, bar);
     }
+    if (xbytes) bulk_g2s(smem_u32(xb + (xa - dn16(d.x0))), (const void *)xa, xbytes, bar);
 }
 
-// All threads, after the wait: the (< 4) trailing elements of the staged
-// arrays that the bulk copies left out.
+// All threads, while the copies are in flight: what the bulk copies leave
+// out -- the (< 4) trailing elements of the staged arrays and the unaligned
+// head and tail (< 16 bytes each) of the byte range.
 // (visible to the block after the barrier that follows the wait)
 template <int NA>
-__device__ void pipe_tail(float *buf, const StageDesc &d) {
+__device__ void pipe_tail(float *buf, uint8_t *xb, const StageDesc &d) {
     const int64_t t0 = d.e0 + stage_body_bytes(d) / 4;
-    if (t0 >= d.e1) return;
+    if (t0 < d.e1) {
 #pragma unroll
-    for (int k = 0; k < NA; k++) {
-        if (!d.src[k]) continue;
-        for (int64_t e = t0 + threadIdx.x; e < d.e1; e += TPB) buf[k * STAGE_ELEMS + (e - d.e0)] = d.src[k][e];
+        for (int k = 0; k < NA; k++) {
+            if (!d.src[k]) continue;
+            for (int64_t e = t0 + threadIdx.x; e < d.e1; e += TPB) buf[k * STAGE_ELEMS + (e - d.e0)] = d.src[k][e];
+        }
+    }
+    if (d.x0 && threadIdx.x < 32) {
+        const int i = threadIdx.x & 15;
+        const uintptr_t base = dn16(d.x0), xa = up16(d.x0), xe = dn16(d.x1);
+        const uintptr_t a = threadIdx.x < 16 ? (uintptr_t)d.x0 + i : (xe > xa ? xe : xa) + i;
+        const uintptr_t lim = threadIdx.x < 16 ? (xa < (uintptr_t)d.x1 ? xa : (uintptr_t)d.x1) : (uintptr_t)d.x1;
+        if (a < lim) xb[a - base] = *(const uint8_t *)a;
     }
 }
 
@@ -382,30 +397,34 @@ __device__ __forceinline__ const float *staged_or(const StageDesc &d, const floa
 // One CTA per tile: list entry blockIdx.x (counted from the end when
 // REVERSE: CTAs start roughly in index order, so a reversed pass first
 // touches the tiles the previous pass touched last, still in L2) holds the
-// tile id and its item index.  plan(StageDesc&) runs on thread 0 and fills the element range and
-// the arrays to stage (src[k] for k < NA); thread 0 then starts their bulk
-// copies, all threads copy the (< 4) trailing elements the copies leave out
-// and wait (bounded) on the mbarrier, and body(const StageDesc&, const float
-// *buf) runs with the tile in shared memory; pre(const StageDesc&) runs on
-// all threads between the issue and the wait.  A copy that does not complete
-// within the spin limit sets the item's error flag and skips the tile.
+// tile id and its item index.  plan(StageDesc&) runs on thread 0 and fills
+// the element range, the arrays to stage (src[k] for k < NA) and the byte
+// range (x0 / x1, NULL for none; at most the byte region's size less 16);
+// thread 0 then starts their bulk copies, all threads copy what the copies
+// leave out and wait (bounded) on the mbarrier, and body(const StageDesc&,
+// const float *buf) runs with the tile in shared memory (the byte region at
+// buf + NA * STAGE_ELEMS); pre(const StageDesc&) runs on all threads between
+// the issue and the wait.  A copy that does not complete within the spin
+// limit sets the item's error flag and skips the tile.
 template <int NA, bool REVERSE, class Plan, class Pre, class Body>
 __device__ void run_tile(const int2 *list, float *stage_mem, uint64_t *bar, StageDesc *sd, int32_t *err_of_item,
                          int err_stride_words, Plan plan, Pre pre, Body body) {
     const uint32_t b = smem_u32(bar);
+    uint8_t *xb = (uint8_t *)(stage_mem + NA * STAGE_ELEMS);
     if (threadIdx.x == 0) {
         const int2 e = list[REVERSE ? gridDim.x - 1 - blockIdx.x : blockIdx.x];
         StageDesc d;
         d.gt = e.x;
         d.ii = e.y;
+        d.x0 = d.x1 = nullptr;
         plan(d);
         *sd = d;
         mbar_init(b, 1);
-        pipe_issue<NA>(b, stage_mem, d);
+        pipe_issue<NA>(b, stage_mem, xb, d);
     }
     __syncthreads();
     const StageDesc d = *sd;
-    pipe_tail<NA>(stage_mem, d);
+    pipe_tail<NA>(stage_mem, xb, d);
     pre(d);   // the tile's own global reads, while its bulk copies are in flight
     bool ok = mbar_wait(b, 0);
     if (!ok) ok = mbar_wait(b, 0);   // one more bounded wait for the copies in flight
@@ -763,7 +782,7 @@ __device__ __forceinline__ void stage_words(const mc_enc_item &I, int t, uint32_
     const int64_t k0 = (int64_t)t * I.tile_kernels;
     const int64_t k1 = min(k0 + (int64_t)I.tile_kernels, I.K);
     const int64_t wb = k0 >> 5, we = (k1 + 31) >> 5;
-    if (wb + threadIdx.x < we) {
+    if (wb + threadIdx.x < we && threadIdx.x < TILE_WORDS) {
         s_bw[threadIdx.x] = I.bm_words[wb + threadIdx.x];
         s_dw[threadIdx.x] = I.dom_words[wb + threadIdx.x];
     }
@@ -900,7 +919,7 @@ __global__ void __launch_bounds__(TPB) k_enc_final2(mc_enc_launch L) {
 __global__ void __launch_bounds__(TPB, 4) k_enc_pass3(mc_enc_launch L) {
     __shared__ Red red;
     __shared__ TileShared ts;
-    __shared__ uint32_t s_bw[TPB], s_dw[TPB];
+    __shared__ uint32_t s_bw[TILE_WORDS], s_dw[TILE_WORDS];
     extern __shared__ __align__(128) float s_stage[];
     run_tile<3, false>((const int2 *)L.mom_tiles, s_stage, &ts.bar, &ts.d, ENC_ERR(L),
                     [&](StageDesc &d) {
@@ -908,7 +927,7 @@ __global__ void __launch_bounds__(TPB, 4) k_enc_pass3(mc_enc_launch L) {
                         if (stageable(L.staged, I, d)) {
                             d.src[0] = (const float *)I.cur;
                             d.src[1] = I.mem_in;
-                            if (2 * L.tiles[d.gt].P >= (int32_t)I.tile_kernels) d.src[2] = I.prev;
+                            if (L.tiles[d.gt].P > 0) d.src[2] = I.prev;
                         }
                     },
                     [&](const StageDesc &d) {
@@ -1066,8 +1085,16 @@ __device__ __forceinline__ void put_codes(uint8_t *data_out, int codec, int64_t 
 }
 
 // ------------------------------------------------------------------ pass 4
+// Side inputs of a pass-4 tile, read while its bulk copies are in flight:
+// the offset of its first predicted kernel in the dense signs and the
+// position of its block in the bitmap frame.
+struct P4Side {
+    int64_t poff;
+    uint32_t blkpos;
+};
+
 __device__ void pass4_tile(const mc_enc_launch &L, const StageDesc &d, const float *buf, int *scan_sh,
-                           uint32_t *s_sg, const uint32_t *s_bw, const uint32_t *s_dw) {
+                           uint32_t *s_sg, const uint32_t *s_bw, const uint32_t *s_dw, const P4Side &S) {
     const int gt = d.gt;
     const int ii = d.ii;
     const mc_enc_item I = L.items[ii];
@@ -1114,18 +1141,21 @@ __device__ void pass4_tile(const mc_enc_launch &L, const StageDesc &d, const flo
         {
             const int64_t c = (I.K + 7) >> 3;
             const int64_t cb0 = tr.k0 >> 3, cb1 = min((tr.k1 + 7) >> 3, c);
-            const uint32_t pos = I.blk_pos[tr.k0 >> (MC_ZBLOCK_LOG2 + 3)];
+            const uint32_t pos = S.blkpos;
             if (pos != 0xFFFFFFFFu) {
                 uint8_t *dst = I.bm_frame + pos - ((cb0 >> MC_ZBLOCK_LOG2) << MC_ZBLOCK_LOG2);  // + cb
-                const uint8_t *srcb = (const uint8_t *)I.bm_words;
+                // content byte b is byte b & 3 of the staged word (b >> 2) - wb0
+                const int64_t wb0 = tr.k0 >> 5;
                 if ((((uintptr_t)(dst + cb0)) & 3) == 0) {
                     for (int64_t w = (cb0 >> 2) + threadIdx.x; 4 * w < cb1; w += TPB) {
-                        if (4 * w + 4 <= cb1) *(uint32_t *)(dst + 4 * w) = I.bm_words[w];
+                        const uint32_t v = s_bw[w - wb0];
+                        if (4 * w + 4 <= cb1) *(uint32_t *)(dst + 4 * w) = v;
                         else
-                            for (int64_t b = 4 * w; b < cb1; b++) dst[b] = srcb[b];
+                            for (int64_t b = 4 * w; b < cb1; b++) dst[b] = (uint8_t)(v >> (8 * (b & 3)));
                     }
                 } else {
-                    for (int64_t b = cb0 + threadIdx.x; b < cb1; b += TPB) dst[b] = srcb[b];
+                    for (int64_t b = cb0 + threadIdx.x; b < cb1; b += TPB)
+                        dst[b] = (uint8_t)(s_bw[(b >> 2) - wb0] >> (8 * (b & 3)));
                 }
             }
         }
@@ -1137,14 +1167,14 @@ __device__ void pass4_tile(const mc_enc_launch &L, const StageDesc &d, const flo
         s_sg[i] = 0u;
         if (i < 2) s_sg[TPB + i] = 0u;
         uint32_t mw = 0, dv = 0;
-        if (wb + i < we) {
+        if (wb + i < we && i < TILE_WORDS) {
             mw = s_bw[i];
             dv = s_dw[i];
         }
         const int pc = __popc(mw);
         int tot;
         const int off_l = block_excl_scan(pc, scan_sh, &tot);   // also orders the zeroing above
-        const int64_t poff = L.tile_poff[gt];
+        const int64_t poff = S.poff;
         if (pc) {
             const uint32_t bits = pext32(dv, mw);
             const int lb = (int)(poff & 7) + off_l;
@@ -1185,7 +1215,8 @@ __device__ void pass4_tile(const mc_enc_launch &L, const StageDesc &d, const flo
 __global__ void __launch_bounds__(TPB, 5) k_enc_pass4(mc_enc_launch L) {
     __shared__ int scan_sh[NWARP + 1];
     __shared__ uint32_t s_sg[TPB + 2];
-    __shared__ uint32_t s_bw[TPB], s_dw[TPB];
+    __shared__ uint32_t s_bw[TILE_WORDS], s_dw[TILE_WORDS];
+    __shared__ P4Side side;
     __shared__ TileShared ts;
     extern __shared__ __align__(128) float s_stage[];
     run_tile<2, true>((const int2 *)L.all_tiles, s_stage, &ts.bar, &ts.d, ENC_ERR(L),
@@ -1193,15 +1224,22 @@ __global__ void __launch_bounds__(TPB, 5) k_enc_pass4(mc_enc_launch L) {
                         const mc_enc_item &I = enc_plan_range(L, d);
                         if ((I.kind == MC_K_MOMENTUM || I.kind == MC_K_QUANT) && stageable(L.staged, I, d)) {
                             d.src[0] = (const float *)I.cur;
-                            if (I.kind == MC_K_MOMENTUM && 2 * L.tiles[d.gt].P >= (int32_t)I.tile_kernels)
-                                d.src[1] = I.mem_out;
+                            if (I.kind == MC_K_MOMENTUM && L.tiles[d.gt].P > 0) d.src[1] = I.mem_out;
                         }
                     },
                     [&](const StageDesc &d) {
                         const mc_enc_item &I = L.items[d.ii];
-                        if (I.kind == MC_K_MOMENTUM) stage_words(I, d.gt - I.tile_base, s_bw, s_dw);
+                        if (I.kind != MC_K_MOMENTUM) return;
+                        const int t = d.gt - I.tile_base;
+                        stage_words(I, t, s_bw, s_dw);
+                        if (threadIdx.x == 0) {
+                            side.poff = L.tile_poff[d.gt];
+                            side.blkpos = I.blk_pos[((int64_t)t * I.tile_kernels) >> (MC_ZBLOCK_LOG2 + 3)];
+                        }
                     },
-                    [&](const StageDesc &d, const float *buf) { pass4_tile(L, d, buf, scan_sh, s_sg, s_bw, s_dw); });
+                    [&](const StageDesc &d, const float *buf) {
+                        pass4_tile(L, d, buf, scan_sh, s_sg, s_bw, s_dw, side);
+                    });
 }
 
 // ------------------------------------------------------------------ frames
@@ -1366,28 +1404,18 @@ __device__ int64_t check_frame(const uint8_t *f, int mode, int64_t want) {
     return cs;
 }
 
-// Sum of one value per thread over the block (result in every thread).
-__device__ long long block_sum_ll(long long v, long long *sh) {
-    v = warp_sum_ll(v);
-    __syncthreads();
-    if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = v;
-    __syncthreads();
-    long long s = 0;
-#pragma unroll
-    for (int j = 0; j < NWARP; j++) s += sh[j];
-    return s;
-}
-
-// Decoder, first launch (one CTA per momentum tile): predicted kernels of the
-// tile from its bitmap words; the first tile of an item also checks the
+// Decoder, first launch (one warp per momentum tile): predicted kernels of
+// the tile from its bitmap words; the first tile of an item also checks the
 // headers of the frames read in place.
 __global__ void __launch_bounds__(TPB) k_dec_prefix(mc_dec_launch L) {
-    __shared__ long long sh[NWARP];
-    const int2 e = ((const int2 *)L.mom_tiles)[blockIdx.x];
+    const int lane = threadIdx.x & 31;
+    const int j = blockIdx.x * NWARP + (threadIdx.x >> 5);
+    if (j >= L.nmom_tiles) return;
+    const int2 e = ((const int2 *)L.mom_tiles)[j];
     const int gt = e.x, ii = e.y;
-    const mc_dec_item I = L.items[ii];
+    const mc_dec_item &I = L.items[ii];
     const int t = gt - I.tile_base;
-    if (t == 0 && threadIdx.x == 0) {
+    if (t == 0 && lane == 0) {
         int bad = 0;
         if (I.bm_mode != MC_BM_WORDS) bad |= check_frame(I.bm_frame, I.bm_mode, (I.bm_bits + 7) >> 3) < 0;
         if (I.sg_mode != MC_BM_WORDS && I.sg_frame) bad |= check_frame(I.sg_frame, I.sg_mode, I.sg_len) < 0;
@@ -1396,56 +1424,76 @@ __global__ void __launch_bounds__(TPB) k_dec_prefix(mc_dec_launch L) {
     const DecTile tr = dec_range(I, t);
     const int64_t wb = tr.k0 >> 5, we = (tr.k1 + 31) >> 5;
     const int64_t bm_bits = dec_bm_bits(I);
-    int c = 0;
-    for (int64_t w = wb + threadIdx.x; w < we; w += TPB) c += __popc(dec_bm_word(I, w) & word_mask(w, bm_bits));
-    const long long tot = block_sum_ll(c, sh);
-    if (threadIdx.x == 0) L.tile_count[gt] = (int32_t)tot;
+    long long c = 0;
+    for (int64_t w = wb + lane; w < we; w += 32) c += __popc(dec_bm_word(I, w) & word_mask(w, bm_bits));
+    c = warp_sum_ll(c);
+    if (lane == 0) L.tile_count[gt] = (int32_t)c;
 }
 
-// Residual values of one quad from the payload (codes * scale or raw floats).
-__device__ __forceinline__ void dec_resid4(const mc_dec_item &I, int64_t g, int64_t e1, float scale,
-                                           float (&r)[4]) {
+// Decoder, second launch (one CTA per item): offset of each momentum tile's
+// first predicted kernel in the dense signs (exclusive scan of the tile
+// counts, in tile order) and the item's predicted total.
+__global__ void __launch_bounds__(TPB) k_dec_scan(mc_dec_launch L) {
+    __shared__ int scan_sh[NWARP + 1];
+    const int ii = L.item0 + blockIdx.x;
+    const mc_dec_item &I = L.items[ii];
+    if (I.kind != MC_D_MOMENTUM) return;
+    const int64_t P = scan_tile_counts(L.tile_count, 1, I.tile_base, I.ntiles, L.tile_poff, scan_sh);
+    if (threadIdx.x == 0) L.results[ii].P = P;
+}
+
+// Residual values of one quad from the payload (codes * scale or raw floats);
+// `data` is the payload's data pointer or its staged copy (same indexing).
+__device__ __forceinline__ void dec_resid4(const mc_dec_item &I, const uint8_t *data, int64_t g, int64_t e1,
+                                           float scale, float (&r)[4]) {
     if (I.codec == MC_DC_Q8) {
         uint32_t w;
         if (I.vec && g + 4 <= e1) {
-            w = *(const uint32_t *)(I.data + g);
+            w = *(const uint32_t *)(data + g);
         } else {
             w = 0;
             for (int j = 0; j < 4; j++)
-                if (g + j < e1) w |= (uint32_t)I.data[g + j] << (8 * j);
+                if (g + j < e1) w |= (uint32_t)data[g + j] << (8 * j);
         }
 #pragma unroll
         for (int j = 0; j < 4; j++) r[j] = __fmul_rn((float)(int8_t)(uint8_t)(w >> (8 * j)), scale);
     } else if (I.codec == MC_DC_INT4) {
         uint32_t w;
         if (I.vec && g + 4 <= e1) {
-            w = *(const uint16_t *)(I.data + (g >> 1));
+            w = *(const uint16_t *)(data + (g >> 1));
         } else {
-            w = I.data[g >> 1];
-            if (g + 2 < e1) w |= (uint32_t)I.data[(g >> 1) + 1] << 8;
+            w = data[g >> 1];
+            if (g + 2 < e1) w |= (uint32_t)data[(g >> 1) + 1] << 8;
         }
 #pragma unroll
         for (int j = 0; j < 4; j++) r[j] = __fmul_rn((float)((int)((w >> (4 * j)) & 15u) - 8), scale);
     } else {
-        ld4((const float *)I.data, g, e1, I.vec, r);
+        ld4((const float *)data, g, e1, I.vec, r);
     }
 }
 
 // Sign bytes a reconstruct tile needs: its predicted kernels' bits start at
-// bit (tile_poff & 7) of the window; up to 8192 kernels per tile, plus the
+// bit (tile_poff & 7) of the window; up to 4096 kernels per tile, plus the
 // read-ahead of the 5-byte gather.
-#define SIGN_WIN 1040
+#define SIGN_WIN 528
+// Byte region of a reconstruct stage: the tile's q8 / int4 codes (at most
+// STAGE_ELEMS bytes, plus the 15-byte misalignment of their start).
+#define RC_XB 4128
 
 // Momentum tiles of the decoder, before the wait on the tile's bulk copies:
 // the tile's bitmap words, the offset of its first predicted kernel in the
-// dense signs (counts of the item's earlier tiles; the first tile also
-// reports the item's total) and the deposited dominant-sign words, into
-// shared memory (s_m, s_d; word wb = k0 / 32 at index 0).
+// dense signs (from the scan kernel) and the deposited dominant-sign words,
+// into shared memory (s_m, s_d; word wb = k0 / 32 at index 0); every tile
+// also reads the payload's scale header into *s_scale.
 __device__ void recon_pre(const mc_dec_launch &L, const StageDesc &d, uint32_t *s_m, uint32_t *s_d, int *scan_sh,
-                          uint8_t *s_sb, long long *s_ll) {
+                          uint8_t *s_sb, float *s_scale) {
     const int ii = d.ii;
     const mc_dec_item &I = L.items[ii];
     const int t = d.gt - I.tile_base;
+    // the scale header may sit at any byte address (payloads from the caller)
+    if (threadIdx.x == 0)
+        *s_scale = (I.codec == MC_DC_Q8 || I.codec == MC_DC_INT4) ? __uint_as_float(le32((const uint8_t *)I.scale_ptr))
+                                                                  : 1.0f;
     if (I.kind == MC_D_MOMENTUM) {
         const DecTile tr = dec_range(I, t);
         const int64_t wb = tr.k0 >> 5, we = (tr.k1 + 31) >> 5;
@@ -1458,30 +1506,17 @@ __device__ void recon_pre(const mc_dec_launch &L, const StageDesc &d, uint32_t *
             sg_len = *I.sg_len_ptr;
             if (sg_len < 0) sg = nullptr;
         }
+        const int64_t poff = L.tile_poff[d.gt];
         uint32_t m = 0;
-        if (wb + i < we) m = dec_bm_word(I, wb + i) & word_mask(wb + i, bm_bits);
+        if (wb + i < we && i < TILE_WORDS) m = dec_bm_word(I, wb + i) & word_mask(wb + i, bm_bits);
         const int pc = __popc(m);
         int tot;
         const int off_l = block_excl_scan(pc, scan_sh, &tot);
-        // offset of the tile's first predicted kernel in the dense signs: the
-        // counts of the item's earlier tiles; the first tile also reports the
-        // item's total
-        long long before = 0, all = 0;
-        for (int k = threadIdx.x; k < I.ntiles; k += TPB) {
-            const long long c = L.tile_count[I.tile_base + k];
-            if (k < t) before += c;
-            all += c;
-        }
-        const int64_t poff = block_sum_ll(before, s_ll);
-        if (t == 0) {
-            const long long P = block_sum_ll(all, s_ll);
-            if (threadIdx.x == 0) L.results[ii].P = P;
-        }
         // the tile's sign bits, staged as bytes; bytes past the sign content
         // read as 0xFF: missing signs default to +1 (ref :3296-3302)
         const int64_t b0 = poff >> 3;
         const int nb = tot > 0 ? (int)(((poff + tot + 7) >> 3) - b0) : 0;
-        for (int j = threadIdx.x; j < nb + 8; j += TPB) {
+        for (int j = threadIdx.x; j < nb + 8 && j < SIGN_WIN; j += TPB) {
             const int64_t b = b0 + j;
             uint32_t v = 0xFFu;
             if (sg && j < nb && b < sg_len) v = src_byte(sg, I.sg_mode, b);
@@ -1504,20 +1539,21 @@ __device__ void recon_pre(const mc_dec_launch &L, const StageDesc &d, uint32_t *
                 mm &= mm - 1;
             }
         }
-        s_m[i] = m;
-        s_d[i] = dm;
+        if (i < TILE_WORDS) {
+            s_m[i] = m;
+            s_d[i] = dm;
+        }
     }
 }
 
+// `codes`: the tile's payload bytes, staged or in place, indexed like
+// I.data; `scale`: the payload's scale header (1 without one).
 __device__ void recon_tile(const mc_dec_launch &L, const StageDesc &d, const float *buf, const uint32_t *s_m,
-                           const uint32_t *s_d) {
+                           const uint32_t *s_d, const uint8_t *codes, float scale) {
     const int gt = d.gt;
     const int ii = d.ii;
     const mc_dec_item I = L.items[ii];
     const int t = gt - I.tile_base;
-    // the scale header may sit at any byte address (payloads from the caller)
-    const float scale = (I.codec == MC_DC_Q8 || I.codec == MC_DC_INT4)
-                            ? __uint_as_float(le32((const uint8_t *)I.scale_ptr)) : 1.0f;
     float *hist = (float *)I.hist_out;
     float *out = (float *)I.out;
     if (I.kind == MC_D_MOMENTUM) {
@@ -1558,7 +1594,7 @@ __device__ void recon_tile(const mc_dec_launch &L, const StageDesc &d, const flo
             for (int q = threadIdx.x; q < nq; q += TPB) {
                 const QuadBits qb = quad_bits_full(s_m, s_d, (uint32_t)wb, k0, 4u * q, I.ks, I.ksdiv);
                 float r[4];
-                dec_resid4(I, tr.e0 + 4 * q, tr.e1, scale, r);
+                dec_resid4(I, codes, tr.e0 + 4 * q, tr.e1, scale, r);
                 const float4 mv = m4 ? m4[q] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
                 float4 pv = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
                 if (qb.f) pv = p4[q];
@@ -1576,7 +1612,7 @@ __device__ void recon_tile(const mc_dec_launch &L, const StageDesc &d, const flo
         for (int64_t g = gstart + 4 * (int64_t)((threadIdx.x - owner + TPB) % TPB); g < tr.e1; g += 4 * TPB) {
             const QuadBits qb = quad_bits(s_m, s_d, (uint32_t)wb, k0, g, tr.e0, tr.e1, I.ks, I.ksdiv);
             float r[4], m0[4], p[4], mo[4], rec[4];
-            dec_resid4(I, g, tr.e1, scale, r);
+            dec_resid4(I, codes, g, tr.e1, scale, r);
             if (mem_in) ld4(mem_in, g, tr.e1, I.vec, m0);
             else m0[0] = m0[1] = m0[2] = m0[3] = 0.0f;
             if (qb.f) ld4(prev, g, tr.e1, I.vec, p);
@@ -1592,7 +1628,7 @@ __device__ void recon_tile(const mc_dec_launch &L, const StageDesc &d, const flo
     if (I.kind == MC_D_RESIDUAL || I.kind == MC_D_QUANT) {
         for (int64_t g = e0 + 4 * (int64_t)threadIdx.x; g < e1; g += 4 * TPB) {
             float r[4];
-            dec_resid4(I, g, e1, scale, r);
+            dec_resid4(I, I.data, g, e1, scale, r);
             st4(hist, g, e1, I.vec, r);
             if (out) st4(out, g, e1, I.vec, r);
         }
@@ -1651,10 +1687,10 @@ __device__ void recon_tile(const mc_dec_launch &L, const StageDesc &d, const flo
 }
 
 __global__ void __launch_bounds__(TPB, 4) k_dec_recon(mc_dec_launch L) {
-    __shared__ uint32_t s_m[TPB], s_d[TPB];
+    __shared__ uint32_t s_m[TILE_WORDS], s_d[TILE_WORDS];
     __shared__ int scan_sh[NWARP + 1];
     __shared__ uint8_t s_sb[SIGN_WIN];
-    __shared__ long long s_ll[NWARP];
+    __shared__ float s_scale;
     __shared__ TileShared ts;
     extern __shared__ __align__(128) float s_stage[];
     run_tile<2, false>((const int2 *)L.all_tiles, s_stage, &ts.bar, &ts.d, &L.results[0].err,
@@ -1669,15 +1705,28 @@ __global__ void __launch_bounds__(TPB, 4) k_dec_recon(mc_dec_launch L) {
                             d.e1 = tr.e1;
                             if (L.staged && I.vec && d.e1 - d.e0 <= STAGE_ELEMS) {
                                 d.src[0] = I.mem_in;
-                                if (2 * L.tile_count[d.gt] >= (int32_t)I.tile_kernels) d.src[1] = I.prev;
+                                if (L.tile_count[d.gt] > 0) d.src[1] = I.prev;
+                                // the codes, staged behind the arrays
+                                if (I.codec == MC_DC_Q8) {
+                                    d.x0 = I.data + d.e0;
+                                    d.x1 = I.data + d.e1;
+                                } else if (I.codec == MC_DC_INT4) {
+                                    d.x0 = I.data + (d.e0 >> 1);
+                                    d.x1 = I.data + ((d.e1 + 1) >> 1);
+                                }
                             }
                         } else {
                             d.e0 = (int64_t)t * I.tile_kernels;
                             d.e1 = min(d.e0 + (int64_t)I.tile_kernels, I.n);
                         }
                     },
-                    [&](const StageDesc &d) { recon_pre(L, d, s_m, s_d, scan_sh, s_sb, s_ll); },
-                    [&](const StageDesc &d, const float *buf) { recon_tile(L, d, buf, s_m, s_d); });
+                    [&](const StageDesc &d) { recon_pre(L, d, s_m, s_d, scan_sh, s_sb, &s_scale); },
+                    [&](const StageDesc &d, const float *buf) {
+                        const uint8_t *data = L.items[d.ii].data;
+                        const uint8_t *xb = (const uint8_t *)(buf + 2 * STAGE_ELEMS);
+                        const uint8_t *codes = d.x0 ? xb + ((intptr_t)data - (intptr_t)dn16(d.x0)) : data;
+                        recon_tile(L, d, buf, s_m, s_d, codes, s_scale);
+                    });
 }
 
 // ------------------------------------------------------------- aggregate
@@ -1731,7 +1780,7 @@ static void smem_opt_in(int kf, const void *fn, size_t smem) {
 #define P2_SMEM STAGE_BYTES(2)
 #define P3_SMEM STAGE_BYTES(3)
 #define P4_SMEM STAGE_BYTES(2)
-#define RECON_SMEM STAGE_BYTES(2)
+#define RECON_SMEM (STAGE_BYTES(2) + RC_XB)
 
 extern "C" int mc_launch_encode(const mc_enc_launch *L, void *stream, mc_ktrace *tr) {
     cudaStream_t s = (cudaStream_t)stream;
@@ -1779,9 +1828,10 @@ extern "C" int mc_launch_decode(const mc_dec_launch *L, void *stream, mc_ktrace 
     int n = 0;
     if (L->nmom_tiles > 0) {
         tr_begin(tr, MC_KT_DEC_PREFIX, s);
-        k_dec_prefix<<<L->nmom_tiles, TPB, 0, s>>>(*L);
+        k_dec_prefix<<<(L->nmom_tiles + NWARP - 1) / NWARP, TPB, 0, s>>>(*L);
+        k_dec_scan<<<L->item1 - L->item0, TPB, 0, s>>>(*L);
         tr_end(tr, s);
-        n++;
+        n += 2;
     }
     if (L->nall_tiles > 0) {
         smem_opt_in(KF_RECON, (const void *)k_dec_recon, RECON_SMEM);
