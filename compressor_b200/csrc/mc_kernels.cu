@@ -296,9 +296,30 @@ __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
 __device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
 }
-__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar) {
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
-                 ::"r"(dst), "l"(src), "r"(bytes), "r"(bar) : "memory");
+// L2 eviction priorities: a pass keeps in L2 (evict_last) what the next pass
+// of the round reads again, and streams the rest (evict_first).  The passes
+// alternate their tile order, so the next pass starts on the tiles this one
+// touched last.
+__device__ __forceinline__ uint64_t l2_keep() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+__device__ __forceinline__ uint64_t l2_stream() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar,
+                                         uint64_t pol) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;"
+        ::"r"(dst), "l"(src), "r"(bytes), "r"(bar), "l"(pol) : "memory");
+}
+// 16-byte store with an L2 eviction priority.
+__device__ __forceinline__ void st_f4(float4 *p, float4 v, uint64_t pol) {
+    asm volatile("st.global.L2::cache_hint.v4.f32 [%0], {%1, %2, %3, %4}, %5;"
+                 ::"l"(p), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w), "l"(pol) : "memory");
 }
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     uint32_t done;
@@ -330,6 +351,7 @@ struct StageDesc {
     const uint8_t *x0, *x1;
     int gt;                         // tile id
     int ii;                         // item index
+    uint32_t keep;                  // bit k: array k stays in L2 (evict_last), else streamed
 };
 
 struct TileShared {
@@ -357,12 +379,15 @@ __device__ void pipe_issue(uint32_t bar, float *buf, uint8_t *xb, const StageDes
     const uintptr_t xa = d.x0 ? up16(d.x0) : 0, xe = d.x0 ? dn16(d.x1) : 0;
     const uint32_t xbytes = xe > xa ? (uint32_t)(xe - xa) : 0u;
     mbar_expect_tx(bar, total + xbytes);
+    const uint64_t keep = l2_keep(), stream = l2_stream();
     if (body) {
 #pragma unroll
         for (int k = 0; k < NA; k++)
-            if (d.src[k]) bulk_g2s(smem_u32(buf + k * STAGE_ELEMS), d.src[k] + d.e0, body, bar);
+            if (d.src[k])
+                bulk_g2s(smem_u32(buf + k * STAGE_ELEMS), d.src[k] + d.e0, body, bar,
+                         (d.keep >> k) & 1u ? keep : stream);
     }
-    if (xbytes) bulk_g2s(smem_u32(xb + (xa - dn16(d.x0))), (const void *)xa, xbytes, bar);
+    if (xbytes) bulk_g2s(smem_u32(xb + (xa - dn16(d.x0))), (const void *)xa, xbytes, bar, stream);
 }
 
 // All threads, while the copies are in flight: what the bulk copies leave
@@ -417,6 +442,7 @@ __device__ void run_tile(const int2 *list, float *stage_mem, uint64_t *bar, Stag
         d.gt = e.x;
         d.ii = e.y;
         d.x0 = d.x1 = nullptr;
+        d.keep = 0;
         plan(d);
         *sd = d;
         mbar_init(b, 1);
@@ -545,6 +571,7 @@ __device__ void pass1_tile(const mc_enc_launch &L, const StageDesc &d, const flo
             const int len = (int)(tr.e1 - tr.e0), nq = len >> 2;
             const float4 *c4 = (const float4 *)(cur + tr.e0), *p4 = (const float4 *)(prev + tr.e0);
             float4 *h4 = hist ? (float4 *)(hist + tr.e0) : nullptr;
+            const uint64_t hpol = l2_stream();   // the history copy is read next round
             for (int q = threadIdx.x; q < nq; q += TPB) {
                 const float4 c = c4[q], p = p4[q];
                 dd[0] += (double)fabsf(c.x);
@@ -563,7 +590,7 @@ __device__ void pass1_tile(const mc_enc_launch &L, const StageDesc &d, const flo
                 mx = c.z > mx ? c.z : mx;
                 mn = c.w < mn ? c.w : mn;
                 mx = c.w > mx ? c.w : mx;
-                if (h4) h4[q] = c;
+                if (h4) st_f4(h4 + q, c, hpol);
             }
             if ((len & 3) && threadIdx.x == (nq % TPB)) {
                 for (int64_t g = tr.e0 + 4 * (int64_t)nq; g < tr.e1; g++) {
@@ -769,6 +796,7 @@ __global__ void __launch_bounds__(TPB, 4) k_enc_pass1(mc_enc_launch L) {
                     if ((I.kind == MC_K_MOMENTUM || I.kind == MC_K_QUANT) && stageable(L.staged, I, d)) {
                         d.src[0] = (const float *)I.cur;
                         if (I.kind == MC_K_MOMENTUM) d.src[1] = I.prev;
+                        d.keep = 3u;   // pass 2 reads both again
                     }
                 },
                 [](const StageDesc &) {},
@@ -846,6 +874,7 @@ __global__ void __launch_bounds__(TPB, 6) k_enc_pass2(mc_enc_launch L) {
                         if (stageable(L.staged, I, d)) {
                             d.src[0] = (const float *)I.cur;
                             d.src[1] = I.prev;
+                            d.keep = 3u;   // pass 3 reads both again
                         }
                     },
                     [](const StageDesc &) {},
@@ -928,6 +957,7 @@ __global__ void __launch_bounds__(TPB, 4) k_enc_pass3(mc_enc_launch L) {
                             d.src[0] = (const float *)I.cur;
                             d.src[1] = I.mem_in;
                             if (L.tiles[d.gt].P > 0) d.src[2] = I.prev;
+                            d.keep = 1u;   // pass 4 reads the input again
                         }
                     },
                     [&](const StageDesc &d) {
@@ -976,6 +1006,7 @@ __global__ void __launch_bounds__(TPB, 4) k_enc_pass3(mc_enc_launch L) {
                             const float4 *m4 = mem_in ? (const float4 *)(mem_in + tr.e0) : nullptr;
                             const float4 *p4 = (const float4 *)(prev + tr.e0);
                             float4 *o4 = (float4 *)(I.mem_out + tr.e0);
+                            const uint64_t keep = l2_keep();   // pass 4 reads the new memory
                             for (int q = threadIdx.x; q < nq; q += TPB) {
                                 const QuadBits qb = quad_bits_full(s_bw, s_dw, k0 >> 5, k0, 4u * q, I.ks, I.ksdiv);
                                 const float4 cv = c4[q];
@@ -986,7 +1017,7 @@ __global__ void __launch_bounds__(TPB, 4) k_enc_pass3(mc_enc_launch L) {
                                 const float p[4] = {pv.x, pv.y, pv.z, pv.w};
                                 float mo[4];
                                 quad(tr.e0 + 4 * q, qb, c, m0, p, mo, 4);
-                                o4[q] = make_float4(mo[0], mo[1], mo[2], mo[3]);
+                                st_f4(o4 + q, make_float4(mo[0], mo[1], mo[2], mo[3]), keep);
                             }
                         }
                         const int64_t gstart = I.vec ? tr.e0 + 4 * (int64_t)nq : tr.e0;
@@ -1590,6 +1621,7 @@ __device__ void recon_tile(const mc_dec_launch &L, const StageDesc &d, const flo
             const float4 *m4 = mem_in ? (const float4 *)(mem_in + tr.e0) : nullptr;
             const float4 *p4 = (const float4 *)(prev + tr.e0);
             float4 *mo4 = (float4 *)(I.mem_out + tr.e0), *h4 = (float4 *)(hist + tr.e0);
+            const uint64_t spol = l2_stream();   // read again next round only
             float4 *o4 = out ? (float4 *)(out + tr.e0) : nullptr;
             for (int q = threadIdx.x; q < nq; q += TPB) {
                 const QuadBits qb = quad_bits_full(s_m, s_d, (uint32_t)wb, k0, 4u * q, I.ks, I.ksdiv);
@@ -1601,10 +1633,10 @@ __device__ void recon_tile(const mc_dec_launch &L, const StageDesc &d, const flo
                 const float m0[4] = {mv.x, mv.y, mv.z, mv.w}, p[4] = {pv.x, pv.y, pv.z, pv.w};
                 float mo[4], rec[4];
                 quad(qb, r, m0, p, mo, rec);
-                mo4[q] = make_float4(mo[0], mo[1], mo[2], mo[3]);
+                st_f4(mo4 + q, make_float4(mo[0], mo[1], mo[2], mo[3]), spol);
                 const float4 rv = make_float4(rec[0], rec[1], rec[2], rec[3]);
-                h4[q] = rv;
-                if (o4) o4[q] = rv;
+                st_f4(h4 + q, rv, spol);
+                if (o4) st_f4(o4 + q, rv, spol);
             }
         }
         const int64_t gstart = I.vec ? tr.e0 + 4 * (int64_t)nq : tr.e0;
