@@ -653,6 +653,86 @@ def run_federated(args):
     return 0
 
 
+# ------------------------------------------------------------------ replay
+def run_replay(args):
+    """Closed loop on captured rounds: each file (the replay layout of the
+    reference's benchmark_real.c / profile_appfl_hot_rounds.py) is loaded into
+    device memory by the native loader, then compressed on an encoder and
+    decompressed on a decoder instance through the C ABI, one round per step
+    (files in name order, cycled).  Scalar tensors are left out, as FalComC
+    keeps them out of the C codec."""
+    import glob
+    import torch
+    from compressor_b200 import build as B
+    from compressor_b200 import replay as R
+    from compressor_b200.abi import BatchItemC, Codec, NDArrayC
+
+    files = sorted(glob.glob(args.replay))
+    if not files:
+        raise SystemExit(f"no replay files match {args.replay}")
+    torch.cuda.set_device(0)
+    if not os.path.exists(B.OUT):
+        B.build()
+    os.environ.setdefault("FALCOM_LOG_LEVEL", "ERROR")
+    stream = torch.cuda.current_stream()
+    rounds = []
+    for f in files:
+        r = R.ReplayRound(f, "device", 0, B.OUT)
+        keep = [i for i in range(r.n) if r.items[i].gradient.contents.ndim >= 1]
+        items = (BatchItemC * len(keep))()
+        for j, i in enumerate(keep):
+            items[j].layer_name = r.items[i].layer_name
+            items[j].gradient = r.items[i].gradient
+        nbytes = sum(r.items[i].gradient.contents.total_size * r.dtypes[i].itemsize for i in keep)
+        rounds.append((r, items, len(keep), nbytes))
+    client = rounds[0][0].client.encode() or b"Client1"
+    enc = Codec(B.OUT, client=client.decode())
+    dec = Codec(B.OUT, client=client.decode())
+    for c in (enc, dec):
+        assert c.lib.falcom_set_residual_codec(c.h, args.codec.encode()) == 0
+        c.lib.falcom_set_stream(c.h, ctypes.c_void_p(stream.cuda_stream))
+    outs = [(ctypes.POINTER(NDArrayC) * n)() for _, _, n, _ in rounds]
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device="cuda")
+
+    def one(k):
+        _, items, n, nbytes = rounds[k % len(rounds)]
+        o = outs[k % len(rounds)]
+        flush.zero_()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        r1 = enc.lib.momentum_compressor_compress_batch(enc.h, items, n, client)
+        r2 = dec.lib.momentum_compressor_decompress_batch(dec.h, items, n, client, o)
+        e1.record(stream)
+        e1.synchronize()
+        if r1 != 0 or r2 != 0:
+            raise RuntimeError(f"codec failed on {files[k % len(files)]}: {r1} {r2}")
+        enc.lib.falcom_free_batch(items, n, o)
+        return e0.elapsed_time(e1), nbytes
+
+    for k in range(args.warmup):
+        one(k)
+    ms, tot = [], 0
+    for k in range(args.warmup, args.warmup + args.steps):
+        t, nb = one(k)
+        ms.append(t)
+        tot += nb
+    total_ms = sum(ms)
+    print(json.dumps({
+        "metric": "replay closed-loop codec ms/round; raw-update GB/s", "value": round(tot / (total_ms * 1e-3) / 1e9, 3),
+        "unit": "GB/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(total_ms / args.steps, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": f"replay files {args.replay} ({len(files)} rounds)",
+        "config": {"workload": "captured rounds, compress_batch + decompress_batch on device-resident tensors",
+                   "codec": args.codec, "client": client.decode(),
+                   "l2": "flushed between steps (256 MiB write, outside the timed events)"}}))
+    enc.close()
+    dec.close()
+    for r, _, _, _ in rounds:
+        r.close()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -669,10 +749,14 @@ def main():
                     help="federated round (decode + weighted aggregate + all-reduce) also on one GPU")
     ap.add_argument("--clients-per-gpu", type=int, default=1,
                     help="federated round: clients per GPU (64 / N for the 64-client round)")
+    ap.add_argument("--replay", default=None,
+                    help="glob of captured replay rounds (.bin): time the closed loop on them instead")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3) if args.impl == "ours" else args.warmup
     if args.impl == "reference":
         return run_reference(args)
+    if args.replay:
+        return run_replay(args)
     if int(os.environ.get("WORLD_SIZE", "1")) > 1 or args.federated:
         return run_federated(args)
     return run_ours(args)

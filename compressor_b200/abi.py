@@ -331,6 +331,13 @@ class Codec:
             self.lib.momentum_compressor_destroy(self.h)
             self.h = None
 
+    # -- state checkpoint (extension) ---------------------------------------
+    def save_state(self, path: str) -> int:
+        return self.lib.falcom_state_save(self.h, os.fsencode(path))
+
+    def load_state(self, path: str) -> int:
+        return self.lib.falcom_state_load(self.h, os.fsencode(path))
+
     def __del__(self):
         try:
             self.close()
@@ -496,6 +503,27 @@ def bind_extensions(lib: ctypes.CDLL) -> None:
     lib.falcom_set_aggregate.argtypes = [c_vp, c_vp, ctypes.POINTER(ctypes.c_size_t), ctypes.c_size_t,
                                          ctypes.c_float]
     lib.falcom_set_aggregate.restype = ctypes.c_int
+    lib.falcom_state_save.argtypes = [c_vp, ctypes.c_char_p]
+    lib.falcom_state_save.restype = ctypes.c_int
+    lib.falcom_state_load.argtypes = [c_vp, ctypes.c_char_p]
+    lib.falcom_state_load.restype = ctypes.c_int
+    bind_replay(lib)
+
+
+def bind_replay(lib: ctypes.CDLL) -> None:
+    """Replay-round entry points (falcom_replay_*); no instance needed."""
+    c_vp = ctypes.c_void_p
+    lib.falcom_replay_open.argtypes = [ctypes.c_char_p, ctypes.c_int, ctypes.c_int]
+    lib.falcom_replay_open.restype = c_vp
+    for name, rest in (("falcom_replay_count", ctypes.c_size_t), ("falcom_replay_round", ctypes.c_uint32),
+                       ("falcom_replay_client", ctypes.c_char_p), ("falcom_replay_bytes", ctypes.c_size_t),
+                       ("falcom_replay_items", ctypes.POINTER(BatchItemC)), ("falcom_replay_close", None)):
+        fn = getattr(lib, name)
+        fn.argtypes = [c_vp]
+        fn.restype = rest
+    lib.falcom_replay_write.argtypes = [ctypes.c_char_p, ctypes.c_uint32, ctypes.c_char_p,
+                                        ctypes.POINTER(BatchItemC), ctypes.c_size_t]
+    lib.falcom_replay_write.restype = ctypes.c_int
 
 
 def kernel_times(lib: ctypes.CDLL, handle) -> dict:

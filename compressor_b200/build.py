@@ -19,7 +19,7 @@ NVCC = os.path.join(CUDA, "bin", "nvcc")
 CC = "/usr/bin/gcc"
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
-C_SOURCES = ["mc_util.c", "mc_wire.c", "mc_state.c", "mc_batch.c", "mc_api.c"]
+C_SOURCES = ["mc_util.c", "mc_wire.c", "mc_state.c", "mc_batch.c", "mc_api.c", "mc_replay.c", "mc_checkpoint.c"]
 CU_SOURCES = ["mc_kernels.cu", "mc_noalloc.cu"]
 
 

@@ -136,6 +136,54 @@ int falcom_set_aggregate(MomentumCompressor *mc, float *aggregate, const size_t 
 #define FALCOM_NOALLOC_MAX_ELEMS 134217728LL
 int falcom_quantize_residual_noalloc(const float *residual, size_t n, int bits, void *out, void *stream);
 
+/* Replay rounds: one captured client update per file, in the layout the
+ * reference's replay tools read (benchmark_real.c:30-89 load_test_data,
+ * cuda_feasibility/profile_appfl_hot_rounds.py:47-72 read_round):
+ *   u32 round | char client_id[64] | u64 layer_count, then per layer
+ *   char name[256] | u64 shape[8] | u64 ndim | u32 dtype | u64 data_size |
+ *   data_size bytes  (little-endian; dtype = DataType code).
+ *
+ * falcom_replay_open reads a file into one block of host memory
+ * (FALCOM_LOC_HOST, malloc'd) or of device memory of `device`
+ * (FALCOM_LOC_DEVICE; the data streams through pinned staging buffers while
+ * the file is read) and returns the round, or NULL when the file cannot be
+ * opened or is inconsistent (truncated, ndim above 8, unknown dtype,
+ * data_size != numel * element size), as the reference loader returns NULL;
+ * ndim 0 is a scalar.
+ * falcom_replay_items returns falcom_replay_count items whose layer_name and
+ * gradient are set (compressed NULL): ready for
+ * momentum_compressor_compress_batch, valid until falcom_replay_close.
+ * falcom_replay_bytes is the sum of the data sizes.
+ *
+ * falcom_replay_write writes items[0..n) (host or device gradients) as one
+ * round file.  Returns 0, or ERROR_INVALID_PARAM (bad item, file not
+ * writable), ERROR_ALLOCATION (write failed). */
+typedef struct falcom_replay falcom_replay;
+falcom_replay *falcom_replay_open(const char *path, int location, int device);
+size_t falcom_replay_count(const falcom_replay *r);
+uint32_t falcom_replay_round(const falcom_replay *r);
+const char *falcom_replay_client(const falcom_replay *r);
+size_t falcom_replay_bytes(const falcom_replay *r);
+BatchItem *falcom_replay_items(falcom_replay *r);
+void falcom_replay_close(falcom_replay *r);
+int falcom_replay_write(const char *path, uint32_t round, const char *client_id, const BatchItem *items,
+                        size_t n);
+
+/* State checkpoint.  No counterpart in the reference, whose state
+ * (momentum_compressor_openmp_simd_final.c:420-471) lives in process memory
+ * only.
+ *
+ * falcom_state_save writes the instance's whole codec state -- for every
+ * "client:layer" its step count and history head, every prediction memory,
+ * the clients that own memories -- to `path`.  falcom_state_load replaces the
+ * instance's state with a file's contents (on any instance and device), so
+ * the next compress / decompress continues exactly where the saved instance
+ * would; when loading fails the state is left unchanged.  Both wait for the
+ * instance's stream.  Returns 0, or ERROR_NOT_FOUND (no such file),
+ * ERROR_INVALID_PARAM (not a state file / not writable), ERROR_ALLOCATION. */
+int falcom_state_save(MomentumCompressor *mc, const char *path);
+int falcom_state_load(MomentumCompressor *mc, const char *path);
+
 #ifdef __cplusplus
 }
 #endif
