@@ -182,6 +182,8 @@ MC_EXPORT void momentum_compressor_destroy(MomentumCompressor *mc) {
         if (mc->ev_in[i]) cudaEventDestroy(mc->ev_in[i]);
         if (mc->ev_done[i]) cudaEventDestroy(mc->ev_done[i]);
     }
+    for (int k = 0; k < 2; k++)
+        if (mc->tab_ev[k]) cudaEventDestroy(mc->tab_ev[k]);
     for (int i = 0; i < 2 * MC_KTRACE_MAX; i++)
         if (mc->ktrace.ev[i]) cudaEventDestroy((cudaEvent_t)mc->ktrace.ev[i]);
     free(mc->stats.prediction_ratios);

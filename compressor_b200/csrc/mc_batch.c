@@ -48,6 +48,26 @@ static void prof_print(prof_t *p, const char *tag) {
     for (int i = 1; i < p->n; i++) fprintf(stderr, " %s=%.1f", p->what[i], p->t[i] - p->t[i - 1]);
     fprintf(stderr, "\n");
 }
+/* The pinned table buffers (scratch slots SH_TABLES, SH_ACC) are rewritten
+ * by every call; event k marks the last upload out of buffer k, so a call
+ * waits for that copy only, not for other work the caller queued on the
+ * stream. */
+void mc_tables_wait(MomentumCompressor *mc, int k) {
+    if (mc->tab_ev_live[k] && cudaEventSynchronize(mc->tab_ev[k]) != cudaSuccess) {
+        (void)cudaGetLastError();
+        cudaDeviceSynchronize();
+    }
+}
+int mc_tables_mark(MomentumCompressor *mc, int k, cudaStream_t st) {
+    if (!mc->tab_ev[k] && cudaEventCreateWithFlags(&mc->tab_ev[k], cudaEventDisableTiming) != cudaSuccess) {
+        mc->tab_ev[k] = NULL;
+        return -1;
+    }
+    if (cudaEventRecord(mc->tab_ev[k], st) != cudaSuccess) return -1;
+    mc->tab_ev_live[k] = 1;
+    return 0;
+}
+
 #define SLOT_ALIGN 256
 #define TILE_ELEMS 4096
 
@@ -320,6 +340,7 @@ int mc_compress_grouped(MomentumCompressor *mc, BatchItem *items, size_t n, cons
     size_t nruns = 0;
     uint8_t *stage = NULL;
     int rc = ERROR_NONE;
+    CompressedLayerData **outs = NULL, *blk = NULL;   /* result structs (filled while the GPU works) */
     cplan *P = (cplan *)calloc(n, sizeof(cplan));
     cgroup *G = (cgroup *)calloc(n, sizeof(cgroup));
     if (!P || !G) {
@@ -713,7 +734,7 @@ int mc_compress_grouped(MomentumCompressor *mc, BatchItem *items, size_t n, cons
     }
     /* the pinned table buffer is reused by every call: wait for the previous
      * upload from it to finish before rewriting it */
-    cudaStreamSynchronize(st);
+    mc_tables_wait(mc, 0);
     prof_mark(&prof, "t_sync");
     mc_enc_item *hit = (mc_enc_item *)htab;
     for (size_t i = 0; i < n; i++) {
@@ -794,6 +815,7 @@ int mc_compress_grouped(MomentumCompressor *mc, BatchItem *items, size_t n, cons
     }
     prof_mark(&prof, "t_lists");
     if (cudaMemcpyAsync(dtab, htab, tab_items, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+        mc_tables_mark(mc, 0, st) != 0 ||
         cudaMemsetAsync(results, 0, n * sizeof(mc_enc_result), st) != cudaSuccess) {
         rc = ERROR_COMPRESSION;
         goto fail;
@@ -899,6 +921,39 @@ int mc_compress_grouped(MomentumCompressor *mc, BatchItem *items, size_t n, cons
     if (host_arena && nchunks == 1)
         cudaMemcpyAsync(host_arena->ptr, payload_dev, arena_bytes, cudaMemcpyDeviceToHost, st);
     prof_mark(&prof, "launch");
+    /* while the GPU works: the result structs and every field that does not
+     * depend on the device results (they live in one block owned by the
+     * payload arena, released with it once the caller has freed every item) */
+    {
+        mc_arena *arena = dev_arena ? dev_arena : host_arena;
+        uint8_t *base = (uint8_t *)arena->ptr;
+        outs = (CompressedLayerData **)malloc((n ? n : 1) * sizeof(*outs));
+        blk = (CompressedLayerData *)calloc(n ? n : 1, sizeof(CompressedLayerData));
+        if (!outs || !blk) {
+            rc = ERROR_ALLOCATION;
+            goto fail;
+        }
+        for (size_t i = 0; i < n; i++) {
+            cplan *p = &P[i];
+            CompressedLayerData *c = outs[i] = &blk[i];
+            /* fixed strings, all shorter than their fields */
+            strcpy(c->type, p->mode == MODE_DIRECT ? "direct"
+                                                   : (p->mode == MODE_MOMENTUM ? "momentum_predicted"
+                                                                               : "direct_generic"));
+            strcpy(c->codec, p->codec_tag);
+            c->ndim = p->g->ndim;
+            memcpy(c->shape, p->g->shape, p->g->ndim * sizeof(size_t));
+            strcpy(c->original_dtype, mc_dtype_name(p->dt));
+            strcpy(c->stored_dtype, c->original_dtype);
+            c->step = p->local_step;
+            c->data = base + p->off_data;
+            if (p->kind == MC_K_MOMENTUM || p->kind == MC_K_QUANT) c->data_size = residual_bytes(p->dcodec, p->n);
+            else if (p->kind == MC_K_COPY) c->data_size = p->bytes;
+            else c->data_size = MC_ZHDR + 3 * frame_blocks(p->bytes) + p->bytes;
+            if (p->kind == MC_K_MOMENTUM) c->bitmap = base + p->off_bm;
+        }
+    }
+    prof_mark(&prof, "prefill");
     cudaError_t e = cudaStreamSynchronize(st);
     if (nchunks > 1) {
         const cudaError_t e2 = cudaStreamSynchronize(mc->copy_out);
@@ -972,39 +1027,15 @@ int mc_compress_grouped(MomentumCompressor *mc, BatchItem *items, size_t n, cons
     {
         mc_arena *arena = dev_arena ? dev_arena : host_arena;
         uint8_t *base = (uint8_t *)arena->ptr;
-        /* the structs live in one block owned by the payload arena, released
-         * with it once the caller has freed every item */
-        CompressedLayerData **outs = (CompressedLayerData **)malloc(n * sizeof(*outs));
-        CompressedLayerData *blk = (CompressedLayerData *)calloc(n ? n : 1, sizeof(CompressedLayerData));
-        if (!outs || !blk) {
-            free(outs);
-            free(blk);
-            rc = ERROR_ALLOCATION;
-            goto fail;
-        }
-        for (size_t i = 0; i < n; i++) outs[i] = &blk[i];
         arena->objs = blk;
+        blk = NULL;
         const int libz = mc->frame_mode == MC_FRAME_LIBZSTD;
         for (size_t i = 0; i < n; i++) {
             cplan *p = &P[i];
             CompressedLayerData *c = outs[i];
             const mc_enc_result *r = &hres[i];
-            /* fixed strings, all shorter than their fields */
-            strcpy(c->type, p->mode == MODE_DIRECT ? "direct"
-                                                   : (p->mode == MODE_MOMENTUM ? "momentum_predicted"
-                                                                               : "direct_generic"));
-            strcpy(c->codec, p->codec_tag);
-            c->ndim = p->g->ndim;
-            memcpy(c->shape, p->g->shape, p->g->ndim * sizeof(size_t));
-            strcpy(c->original_dtype, mc_dtype_name(p->dt));
-            strcpy(c->stored_dtype, c->original_dtype);
-            c->step = p->local_step;
-            c->data = base + p->off_data;
-            if (p->kind == MC_K_MOMENTUM || p->kind == MC_K_QUANT) c->data_size = residual_bytes(p->dcodec, p->n);
-            else if (p->kind == MC_K_COPY) c->data_size = p->bytes;
-            else c->data_size = libz ? p->fs_data : MC_ZHDR + 3 * frame_blocks(p->bytes) + p->bytes;
+            if (libz && p->kind == MC_K_FRAME) c->data_size = p->fs_data;
             if (p->kind == MC_K_MOMENTUM) {
-                c->bitmap = base + p->off_bm;
                 c->bitmap_size = libz ? p->fs_bm : (size_t)r->bm_size;
                 size_t sgs = libz ? p->fs_sg : (size_t)r->sg_size;
                 c->dominant_signs = sgs ? base + p->off_sg : NULL;
@@ -1041,6 +1072,7 @@ int mc_compress_grouped(MomentumCompressor *mc, BatchItem *items, size_t n, cons
         registry_add_many((const void **)outs, n, arena);
         arena_retain(arena, (int)n - 1);
         free(outs);
+        outs = NULL;
         if (n == 0) arena_release(arena);
     }
     prof_mark(&prof, "commit");
@@ -1062,6 +1094,8 @@ fail:
         if (items[i].error == ERROR_NONE) items[i].error = rc;
     }
 out:
+    free(outs);
+    free(blk);
     free(runs);
     free(P);
     free(G);
@@ -1233,7 +1267,7 @@ static int dec_accumulate(MomentumCompressor *mc, const dplan *D, size_t n, NDAr
     for (size_t i = 0; i < n; i++) {
         if (!out[i] || D[i].dt != DTYPE_FLOAT32 || base + i >= mc->agg_n) continue;
         m++;
-        ntiles += (int)((D[i].n + TILE_ELEMS - 1) / TILE_ELEMS);
+        ntiles += (int)((D[i].n + MC_ACC_TILE - 1) / MC_ACC_TILE);
     }
     if (m == 0 || ntiles == 0) return ERROR_NONE;
     size_t t_items = ALIGN_UP(m * sizeof(mc_acc_item), 256);
@@ -1241,6 +1275,7 @@ static int dec_accumulate(MomentumCompressor *mc, const dplan *D, size_t n, NDAr
     uint8_t *ht = (uint8_t *)scratch_host(&mc->scratch, SH_ACC, t_items + t_ti);
     uint8_t *dt = (uint8_t *)scratch_dev(&mc->scratch, SD_ACC, t_items + t_ti);
     if (!ht || !dt) return ERROR_ALLOCATION;
+    mc_tables_wait(mc, 1);
     mc_acc_item *hi = (mc_acc_item *)ht;
     int32_t *h_ti = (int32_t *)(ht + t_items);
     size_t j = 0;
@@ -1254,12 +1289,13 @@ static int dec_accumulate(MomentumCompressor *mc, const dplan *D, size_t n, NDAr
         A->w = mc->agg_w;
         A->tile_base = tb;
         A->vec = ((((uintptr_t)A->src) | ((uintptr_t)A->dst)) & 15) == 0;
-        const int nt = (int)((D[i].n + TILE_ELEMS - 1) / TILE_ELEMS);
+        const int nt = (int)((D[i].n + MC_ACC_TILE - 1) / MC_ACC_TILE);
         for (int t = 0; t < nt; t++) h_ti[tb + t] = (int32_t)j;
         tb += nt;
         j++;
     }
-    if (cudaMemcpyAsync(dt, ht, t_items + t_ti, cudaMemcpyHostToDevice, mc->stream) != cudaSuccess)
+    if (cudaMemcpyAsync(dt, ht, t_items + t_ti, cudaMemcpyHostToDevice, mc->stream) != cudaSuccess ||
+        mc_tables_mark(mc, 1, mc->stream) != 0)
         return ERROR_DECOMPRESSION;
     mc_ktrace *tr = mc_trace_begin(mc);
     int k = mc_launch_accumulate((const mc_acc_item *)dt, (const int32_t *)(dt + t_items), ntiles, mc->stream, tr);
@@ -1550,7 +1586,7 @@ static int dec_segment(MomentumCompressor *mc, const BatchItem *items, size_t n,
     uint8_t *dt = (uint8_t *)scratch_dev(&mc->scratch, SD_TABLES, tab + dyn);
     if (!ht || !dt || !lc) { rc = ERROR_ALLOCATION; goto fail_arena; }
     prof_mark(&prof, "t_scratch");
-    cudaStreamSynchronize(st);
+    mc_tables_wait(mc, 0);
     prof_mark(&prof, "t_sync");
     if (njobs) memset(ht + t_items, 0, t_jobs);
     mc_dec_item *hi = (mc_dec_item *)ht;
@@ -1664,7 +1700,7 @@ static int dec_segment(MomentumCompressor *mc, const BatchItem *items, size_t n,
             cudaSuccess) { rc = ERROR_DECOMPRESSION; goto fail_arena; }
         lc->sig = sig;
     }
-    if (cudaMemcpyAsync(dt, ht, tab, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+    if (cudaMemcpyAsync(dt, ht, tab, cudaMemcpyHostToDevice, st) != cudaSuccess || mc_tables_mark(mc, 0, st) != 0 ||
         cudaMemsetAsync(d_res, 0, t_res, st) != cudaSuccess) { rc = ERROR_DECOMPRESSION; goto fail_arena; }
 
     prof_mark(&prof, "tables");

@@ -201,7 +201,8 @@ typedef struct {
 } mc_dec_launch;
 
 /* Weighted accumulation of decoded tensors into an aggregate:
- * dst[e] = fma(w, src[e], dst[e]) for e < n; 8192-element tiles. */
+ * dst[e] = fma(w, src[e], dst[e]) for e < n; tiles of MC_ACC_TILE elements. */
+#define MC_ACC_TILE 8192
 typedef struct {
     const float *src;
     float *dst;

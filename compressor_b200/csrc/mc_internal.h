@@ -144,6 +144,11 @@ struct MomentumCompressor {
 #define MC_MAX_CHUNKS 8
     cudaStream_t copy_in, copy_out;
     cudaEvent_t ev_in[MC_MAX_CHUNKS], ev_done[MC_MAX_CHUNKS];
+    /* recorded after the last upload from a pinned table buffer (0: item
+     * tables, 1: aggregate tables): a call waits on it (not on the whole
+     * stream) before rewriting the buffer */
+    cudaEvent_t tab_ev[2];
+    int tab_ev_live[2];
     int residual_codec;      /* MC_CODEC_* */
     int frame_mode;          /* MC_FRAME_GPU / MC_FRAME_LIBZSTD */
     int payload_loc;
@@ -187,6 +192,10 @@ struct MomentumCompressor {
     double ktime_ms[MC_NKERN];
     long long kcount[MC_NKERN];
 };
+
+/* pinned table buffer k: wait for / mark the last upload from it */
+void mc_tables_wait(MomentumCompressor *mc, int k);
+int mc_tables_mark(MomentumCompressor *mc, int k, cudaStream_t st);
 
 /* kernel timing: start a trace for one call / fold it into the totals after
  * the call's stream synchronisation */

@@ -1070,14 +1070,37 @@ __global__ void __launch_bounds__(TPB) k_enc_final3(mc_enc_launch L) {
 
 // Software parallel-bit-extract: the bits of `v` at the set positions of
 // `m`, packed towards bit 0 in ascending position order.
+// Bits of v at the set bits of m, packed from bit 0 (parallel bit extract),
+// one run of consecutive set bits of m per step.
 __device__ __forceinline__ uint32_t pext32(uint32_t v, uint32_t m) {
+    if (m == FULL) return v;
     uint32_t out = 0;
     int j = 0;
     while (m) {
-        const int b = __ffs(m) - 1;
-        out |= ((v >> b) & 1u) << j;
-        j++;
-        m &= m - 1;
+        const int lo = __ffs(m) - 1;
+        const uint32_t t = m >> lo;
+        const int len = t == (FULL >> lo) ? 32 - lo : __ffs(~t) - 1;
+        const uint32_t run = len == 32 ? FULL : (1u << len) - 1u;
+        out |= ((v >> lo) & run) << j;
+        j += len;
+        m &= ~(run << lo);
+    }
+    return out;
+}
+
+// The low bits of v deposited at the set bits of m (parallel bit deposit),
+// one run of consecutive set bits of m per step.
+__device__ __forceinline__ uint32_t pdep32(uint32_t v, uint32_t m) {
+    if (m == FULL) return v;
+    uint32_t out = 0;
+    while (m) {
+        const int lo = __ffs(m) - 1;
+        const uint32_t t = m >> lo;
+        const int len = t == (FULL >> lo) ? 32 - lo : __ffs(~t) - 1;
+        const uint32_t run = len == 32 ? FULL : (1u << len) - 1u;
+        out |= (v & run) << lo;
+        v = len == 32 ? 0u : v >> len;
+        m &= ~(run << lo);
     }
     return out;
 }
@@ -1561,14 +1584,7 @@ __device__ void recon_pre(const mc_dec_launch &L, const StageDesc &d, uint32_t *
             uint64_t w = 0;
 #pragma unroll
             for (int k = 0; k < 5; k++) w |= (uint64_t)s_sb[ob + k] << (8 * k);
-            uint32_t bits = (uint32_t)(w >> (o & 7));
-            uint32_t mm = m;
-            while (mm) {   // deposit the pc sign bits at the set bits of m
-                const int b = __ffs(mm) - 1;
-                dm |= (bits & 1u) << b;
-                bits >>= 1;
-                mm &= mm - 1;
-            }
+            dm = pdep32((uint32_t)(w >> (o & 7)), m);   // the pc sign bits at the set bits of m
         }
         if (i < TILE_WORDS) {
             s_m[i] = m;
@@ -1765,8 +1781,8 @@ __global__ void __launch_bounds__(TPB, 4) k_dec_recon(mc_dec_launch L) {
 __global__ void __launch_bounds__(TPB) k_accumulate(const mc_acc_item *items, const int32_t *tile_item) {
     const int gt = blockIdx.x;
     const mc_acc_item I = items[tile_item[gt]];
-    const int64_t e0 = (int64_t)(gt - I.tile_base) * 8192;
-    const int64_t e1 = min(e0 + 8192, I.n);
+    const int64_t e0 = (int64_t)(gt - I.tile_base) * MC_ACC_TILE;
+    const int64_t e1 = min(e0 + MC_ACC_TILE, I.n);
     for (int64_t g = e0 + 4 * (int64_t)threadIdx.x; g < e1; g += 4 * TPB) {
         float x[4], a[4];
         ld4(I.src, g, e1, I.vec, x);
