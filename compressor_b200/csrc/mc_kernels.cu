@@ -47,6 +47,17 @@ __device__ __forceinline__ uint32_t fdiv32(uint32_t x, mc_fastdiv d) {
     return (uint32_t)(((uint64_t)hi + x) >> d.shift);
 }
 
+// Programmatic dependent launch.  The kernels of one encode (or decode) are
+// launched so that kernel N+1 may start while kernel N is finishing; N+1
+// plans its tiles and starts their bulk copies, then waits (pdl_wait) for N
+// to complete before it reads N's results or writes anything.  Every kernel
+// releases its successor (pdl_release) only after its own wait, so when
+// kernel N+1 starts, kernels N-1, N-2, ... have completed: a prologue may
+// read their outputs.  Both are no-ops for a kernel launched without the
+// attribute.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_release() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ---- deterministic block reductions (result valid in thread 0) ---------
 __device__ __forceinline__ double warp_sum_d(double v) {
 #pragma unroll
@@ -449,6 +460,8 @@ __device__ void run_tile(const int2 *list, float *stage_mem, uint64_t *bar, Stag
         pipe_issue<NA>(b, stage_mem, xb, d);
     }
     __syncthreads();
+    pdl_wait();
+    pdl_release();
     const StageDesc d = *sd;
     pipe_tail<NA>(stage_mem, xb, d);
     pre(d);   // the tile's own global reads, while its bulk copies are in flight
@@ -824,6 +837,8 @@ __global__ void __launch_bounds__(TPB) k_enc_final1(mc_enc_launch L) {
     __shared__ Red red;
     __shared__ int scan_sh[NWARP + 1];
     __shared__ int s_blk[MAX_RLE_BLOCKS + 1];
+    pdl_wait();
+    pdl_release();
     const int ii = L.item0 + blockIdx.x;
     const mc_enc_item I = L.items[ii];
     if (I.wave != L.wave) return;
@@ -920,6 +935,8 @@ __global__ void __launch_bounds__(TPB, 6) k_enc_pass2(mc_enc_launch L) {
 // Per-item results of pass 2: population std of |cur| and |prev|.
 __global__ void __launch_bounds__(TPB) k_enc_final2(mc_enc_launch L) {
     __shared__ Red red;
+    pdl_wait();
+    pdl_release();
     const int ii = L.item0 + blockIdx.x;
     const mc_enc_item I = L.items[ii];
     if (I.wave != L.wave || I.kind != MC_K_MOMENTUM) return;
@@ -1048,6 +1065,8 @@ __global__ void __launch_bounds__(TPB, 4) k_enc_pass3(mc_enc_launch L) {
 // the payload header) and sign mismatches.
 __global__ void __launch_bounds__(TPB) k_enc_final3(mc_enc_launch L) {
     __shared__ Red red;
+    pdl_wait();
+    pdl_release();
     const int ii = L.item0 + blockIdx.x;
     const mc_enc_item I = L.items[ii];
     if (I.wave != L.wave || I.kind != MC_K_MOMENTUM) return;
@@ -1462,6 +1481,8 @@ __device__ int64_t check_frame(const uint8_t *f, int mode, int64_t want) {
 // the tile from its bitmap words; the first tile of an item also checks the
 // headers of the frames read in place.
 __global__ void __launch_bounds__(TPB) k_dec_prefix(mc_dec_launch L) {
+    pdl_wait();
+    pdl_release();
     const int lane = threadIdx.x & 31;
     const int j = blockIdx.x * NWARP + (threadIdx.x >> 5);
     if (j >= L.nmom_tiles) return;
@@ -1489,6 +1510,8 @@ __global__ void __launch_bounds__(TPB) k_dec_prefix(mc_dec_launch L) {
 // counts, in tile order) and the item's predicted total.
 __global__ void __launch_bounds__(TPB) k_dec_scan(mc_dec_launch L) {
     __shared__ int scan_sh[NWARP + 1];
+    pdl_wait();
+    pdl_release();
     const int ii = L.item0 + blockIdx.x;
     const mc_dec_item &I = L.items[ii];
     if (I.kind != MC_D_MOMENTUM) return;
@@ -1809,6 +1832,23 @@ static inline void tr_end(mc_ktrace *tr, cudaStream_t s) {
     }
 }
 
+// Launch of a kernel that may start while the previous kernel on the stream
+// is finishing (programmatic dependent launch; see pdl_wait).
+template <typename... P, typename... A>
+static void launch_pdl(void (*kern)(P...), int grid, size_t smem, cudaStream_t s, A... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3(TPB);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
 // Dynamic shared memory of the staged kernels (one stage of NA arrays),
 // opted in above the 48 KiB default once per kernel and device.
 enum { KF_P1 = 0, KF_P2, KF_P3, KF_P4, KF_RECON, KF_N };
@@ -1839,31 +1879,31 @@ extern "C" int mc_launch_encode(const mc_enc_launch *L, void *stream, mc_ktrace 
         k_enc_pass1<<<L->nall_tiles, TPB, P1_SMEM, s>>>(*L);
         tr_end(tr, s);
         tr_begin(tr, MC_KT_ENC_FINAL, s);
-        k_enc_final1<<<L->nitems, TPB, 0, s>>>(*L);
+        launch_pdl(k_enc_final1, L->nitems, 0, s, *L);
         tr_end(tr, s);
         n += 2;
     }
     if (L->nmom_tiles > 0) {
         smem_opt_in(KF_P2, (const void *)k_enc_pass2, P2_SMEM);
         tr_begin(tr, MC_KT_ENC_PASS2, s);
-        k_enc_pass2<<<L->nmom_tiles, TPB, P2_SMEM, s>>>(*L);
+        launch_pdl(k_enc_pass2, L->nmom_tiles, P2_SMEM, s, *L);
         tr_end(tr, s);
         tr_begin(tr, MC_KT_ENC_FINAL, s);
-        k_enc_final2<<<L->nitems, TPB, 0, s>>>(*L);
+        launch_pdl(k_enc_final2, L->nitems, 0, s, *L);
         tr_end(tr, s);
         smem_opt_in(KF_P3, (const void *)k_enc_pass3, P3_SMEM);
         tr_begin(tr, MC_KT_ENC_PASS3, s);
-        k_enc_pass3<<<L->nmom_tiles, TPB, P3_SMEM, s>>>(*L);
+        launch_pdl(k_enc_pass3, L->nmom_tiles, P3_SMEM, s, *L);
         tr_end(tr, s);
         tr_begin(tr, MC_KT_ENC_FINAL, s);
-        k_enc_final3<<<L->nitems, TPB, 0, s>>>(*L);
+        launch_pdl(k_enc_final3, L->nitems, 0, s, *L);
         tr_end(tr, s);
         n += 4;
     }
     if (L->nall_tiles > 0) {
         smem_opt_in(KF_P4, (const void *)k_enc_pass4, P4_SMEM);
         tr_begin(tr, MC_KT_ENC_PASS4, s);
-        k_enc_pass4<<<L->nall_tiles, TPB, P4_SMEM, s>>>(*L);
+        launch_pdl(k_enc_pass4, L->nall_tiles, P4_SMEM, s, *L);
         tr_end(tr, s);
         n++;
     }
@@ -1877,14 +1917,14 @@ extern "C" int mc_launch_decode(const mc_dec_launch *L, void *stream, mc_ktrace 
     if (L->nmom_tiles > 0) {
         tr_begin(tr, MC_KT_DEC_PREFIX, s);
         k_dec_prefix<<<(L->nmom_tiles + NWARP - 1) / NWARP, TPB, 0, s>>>(*L);
-        k_dec_scan<<<L->item1 - L->item0, TPB, 0, s>>>(*L);
+        launch_pdl(k_dec_scan, L->item1 - L->item0, 0, s, *L);
         tr_end(tr, s);
         n += 2;
     }
     if (L->nall_tiles > 0) {
         smem_opt_in(KF_RECON, (const void *)k_dec_recon, RECON_SMEM);
         tr_begin(tr, MC_KT_DEC_RECON, s);
-        k_dec_recon<<<L->nall_tiles, TPB, RECON_SMEM, s>>>(*L);
+        launch_pdl(k_dec_recon, L->nall_tiles, RECON_SMEM, s, *L);
         tr_end(tr, s);
         n++;
     }
