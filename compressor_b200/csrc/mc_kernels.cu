@@ -92,36 +92,47 @@ struct Red {
     long long l[2][NWARP];
 };
 
-// Reduce up to 4 doubles, 1 min, 2 max floats and 2 integers over the block.
-__device__ void block_reduce(Red &sh, double (&d)[4], int nd, float &mn, float &mx, float &mx2,
-                             long long (&l)[2], int nl) {
+// Reduce ND doubles, the floats selected by F (bit 0 mn: min, bit 1 mx: max,
+// bit 2 mx2: max) and NL integers over the block; the result is valid in
+// thread 0.  Only the selected values are exchanged.
+#define RF_MN 1
+#define RF_MX 2
+#define RF_MX2 4
+template <int ND, int F, int NL>
+__device__ void block_reduce(Red &sh, double (&d)[4], float &mn, float &mx, float &mx2, long long (&l)[2]) {
     const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (int i = 0; i < nd; i++) d[i] = warp_sum_d(d[i]);
-    mn = warp_min_f(mn);
-    mx = warp_max_f(mx);
-    mx2 = warp_max_f(mx2);
-    for (int i = 0; i < nl; i++) l[i] = warp_sum_ll(l[i]);
+#pragma unroll
+    for (int i = 0; i < ND; i++) d[i] = warp_sum_d(d[i]);
+    if (F & RF_MN) mn = warp_min_f(mn);
+    if (F & RF_MX) mx = warp_max_f(mx);
+    if (F & RF_MX2) mx2 = warp_max_f(mx2);
+#pragma unroll
+    for (int i = 0; i < NL; i++) l[i] = warp_sum_ll(l[i]);
     __syncthreads();
     if (lane == 0) {
-        for (int i = 0; i < nd; i++) sh.d[i][w] = d[i];
-        sh.f[0][w] = mn;
-        sh.f[1][w] = mx;
-        sh.f[2][w] = mx2;
-        for (int i = 0; i < nl; i++) sh.l[i][w] = l[i];
+#pragma unroll
+        for (int i = 0; i < ND; i++) sh.d[i][w] = d[i];
+        if (F & RF_MN) sh.f[0][w] = mn;
+        if (F & RF_MX) sh.f[1][w] = mx;
+        if (F & RF_MX2) sh.f[2][w] = mx2;
+#pragma unroll
+        for (int i = 0; i < NL; i++) sh.l[i][w] = l[i];
     }
     __syncthreads();
     if (threadIdx.x == 0) {
-        for (int i = 0; i < nd; i++) {
+#pragma unroll
+        for (int i = 0; i < ND; i++) {
             double s = 0.0;
             for (int j = 0; j < NWARP; j++) s += sh.d[i][j];
             d[i] = s;
         }
         for (int j = 0; j < NWARP; j++) {
-            mn = sh.f[0][j] < mn ? sh.f[0][j] : mn;
-            mx = sh.f[1][j] > mx ? sh.f[1][j] : mx;
-            mx2 = sh.f[2][j] > mx2 ? sh.f[2][j] : mx2;
+            if (F & RF_MN) mn = sh.f[0][j] < mn ? sh.f[0][j] : mn;
+            if (F & RF_MX) mx = sh.f[1][j] > mx ? sh.f[1][j] : mx;
+            if (F & RF_MX2) mx2 = sh.f[2][j] > mx2 ? sh.f[2][j] : mx2;
         }
-        for (int i = 0; i < nl; i++) {
+#pragma unroll
+        for (int i = 0; i < NL; i++) {
             long long s = 0;
             for (int j = 0; j < NWARP; j++) s += sh.l[i][j];
             l[i] = s;
@@ -159,8 +170,18 @@ __device__ __forceinline__ int qmax_of(int codec) {
     return (codec == MC_DC_INT4 || codec == MC_DC_INT4_RAW) ? 7 : 127;
 }
 
-__device__ __forceinline__ int quant1(float r, float scale, float qm) {
-    float v = rintf(__fdiv_rn(r, scale));
+// Residual code rint(r / scale) clamped to [-qm, qm], with the IEEE quotient
+// (ref falcom_cuda_v4_kernels.cu:53-65) but without a division per element:
+// y = r * inv, inv = 1/scale rounded to nearest, is within 2^-22 |r / scale|
+// (plus 2^-149 below the normal range) of the quotient, so within 2^-15 of it
+// wherever |r / scale| < 128, the only range where the code is not clamped.
+// There rint(y) equals rint(r / scale) unless y lies within 2^-15 of a
+// half-integer; those elements (about 6 in 10^5), and every NaN / Inf case
+// (inv = Inf for a subnormal scale), take the exact quotient.
+__device__ __forceinline__ int quant1(float r, float scale, float inv, float qm) {
+    const float y = __fmul_rn(r, inv);
+    float v = rintf(y);
+    if (!(fabsf(fabsf(__fsub_rn(y, v)) - 0.5f) > 3.0517578125e-5f)) v = rintf(__fdiv_rn(r, scale));
     v = fminf(qm, fmaxf(-qm, v));
     return (int)v;
 }
@@ -256,6 +277,17 @@ __device__ __forceinline__ QuadBits quad_bits_full(const uint32_t *bm, const uin
     const uint32_t q = fdiv32(o, ksdiv);
     uint32_t r = o - q * (uint32_t)ks;
     uint32_t k = k0 + q;
+    if (ks >= 4) {
+        // the quad's elements j < s belong to kernel k, the rest (if any) to
+        // kernel k + 1: a quad spans at most two kernels of 4 or more elements
+        const uint32_t s = (uint32_t)ks - r;
+        const uint32_t lo = s >= 4u ? 0xFu : (1u << s) - 1u;
+        const uint32_t k1 = k + (s < 4u ? 1u : 0u);
+        const uint32_t wa = (k >> 5) - wbase, sa = k & 31, wb = (k1 >> 5) - wbase, sb = k1 & 31;
+        b.f = (lo & (0u - ((bm[wa] >> sa) & 1u))) | (~lo & 0xFu & (0u - ((bm[wb] >> sb) & 1u)));
+        b.pos = dom ? (lo & (0u - ((dom[wa] >> sa) & 1u))) | (~lo & 0xFu & (0u - ((dom[wb] >> sb) & 1u))) : 0u;
+        return b;
+    }
     b.f = b.pos = 0u;
 #pragma unroll
     for (int j = 0; j < 4; j++) {
@@ -338,10 +370,22 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
                  "selp.u32 %0, 1, 0, p;\n\t}" : "=r"(done) : "r"(bar), "r"(parity) : "memory");
     return done != 0;
 }
-// Bounded wait for phase `parity`; false when the limit ran out.
+// Bounded wait for phase `parity`, polled with a short sleep between tests
+// (a polling warp takes issue slots from the other CTAs on the SM): at most
+// MBAR_SPIN_LIMIT tests and about two seconds; false when either ran out.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
-    for (uint32_t i = 0; i < MBAR_SPIN_LIMIT; i++)
+    if (mbar_try_wait(bar, parity)) return true;
+    uint64_t t0;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+    for (uint32_t i = 0; i < MBAR_SPIN_LIMIT; i++) {
+        __nanosleep(64);
         if (mbar_try_wait(bar, parity)) return true;
+        if ((i & 15) == 15) {
+            uint64_t t;
+            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+            if (t - t0 > 2000000000ull) return false;
+        }
+    }
     return false;
 }
 
@@ -465,8 +509,13 @@ __device__ void run_tile(const int2 *list, float *stage_mem, uint64_t *bar, Stag
     const StageDesc d = *sd;
     pipe_tail<NA>(stage_mem, xb, d);
     pre(d);   // the tile's own global reads, while its bulk copies are in flight
-    bool ok = mbar_wait(b, 0);
-    if (!ok) ok = mbar_wait(b, 0);   // one more bounded wait for the copies in flight
+    // warp 0 waits for the copies; the other warps wait in the CTA barrier
+    // (which issues nothing) and see the staged tile through it
+    bool ok = true;
+    if (threadIdx.x < 32) {
+        ok = mbar_wait(b, 0);
+        if (!ok) ok = mbar_wait(b, 0);   // one more bounded wait for the copies in flight
+    }
     if (!__syncthreads_and(ok)) {
         if (threadIdx.x == 0) err_of_item[(size_t)d.ii * err_stride_words] = 2;
         return;
@@ -689,7 +738,7 @@ __device__ void pass1_tile(const mc_enc_launch &L, const StageDesc &d, const flo
             }
         }
         l[0] = P;
-        block_reduce(red, dd, 2, mn, mx, mx2, l, 1);
+        block_reduce<2, RF_MN | RF_MX, 1>(red, dd, mn, mx, mx2, l);
         if (threadIdx.x == 0) {
             mc_enc_tile &T = L.tiles[d.gt];
             T.s_cur = dd[0];
@@ -775,7 +824,7 @@ __device__ void pass1_tile(const mc_enc_launch &L, const StageDesc &d, const flo
             if (g + j < e1) mx2 = fmaxf(mx2, fabsf(c[j]));
         if (hist) st4(hist, g, e1, I.vec, c);
     }
-    block_reduce(red, dd, 0, mn, mx, mx2, l, 0);
+    block_reduce<0, RF_MX2, 0>(red, dd, mn, mx, mx2, l);
     if (threadIdx.x == 0) L.tiles[d.gt].maxr = mx2;
 }
 
@@ -854,7 +903,7 @@ __global__ void __launch_bounds__(TPB) k_enc_final1(mc_enc_launch L) {
             tmn = T->mn < tmn ? T->mn : tmn;
             tmx = T->mx > tmx ? T->mx : tmx;
         }
-        block_reduce(red, a, 2, tmn, tmx, t2, z, 0);
+        block_reduce<2, RF_MN | RF_MX, 0>(red, a, tmn, tmx, t2, z);
         const int64_t total = scan_tile_counts(&L.tiles[0].P, (int)(sizeof(mc_enc_tile) / 4), I.tile_base,
                                                I.ntiles, L.tile_poff, scan_sh);
         write_frame_headers(I, L, R, total, s_blk);
@@ -869,7 +918,7 @@ __global__ void __launch_bounds__(TPB) k_enc_final1(mc_enc_launch L) {
     } else if (I.kind == MC_K_QUANT) {
         float m = 0.0f, u0 = FLT_MAX, u1 = -FLT_MAX;
         for (int i = threadIdx.x; i < I.ntiles; i += TPB) m = fmaxf(m, L.tiles[I.tile_base + i].maxr);
-        block_reduce(red, a, 0, u0, u1, m, z, 0);
+        block_reduce<0, RF_MX2, 0>(red, a, u0, u1, m, z);
         if (threadIdx.x == 0) {
             R->maxr = m;
             R->scale = (m == 0.0f) ? 1.0f : __fdiv_rn(m, (float)qmax_of(I.codec));
@@ -924,7 +973,7 @@ __global__ void __launch_bounds__(TPB, 6) k_enc_pass2(mc_enc_launch L) {
                             for (int64_t g = d.e0 + threadIdx.x * 4; g < d.e1; g += 4 * TPB)
                                 for (int64_t e = g; e < g + 4 && e < d.e1; e++) acc(cur[e], prev[e]);
                         }
-                        block_reduce(red, dd, 2, mn, mx, mx2, l, 0);
+                        block_reduce<2, 0, 0>(red, dd, mn, mx, mx2, l);
                         if (threadIdx.x == 0) {
                             L.tiles[d.gt].v_cur = dd[0];
                             L.tiles[d.gt].v_prev = dd[1];
@@ -948,7 +997,7 @@ __global__ void __launch_bounds__(TPB) k_enc_final2(mc_enc_launch L) {
         a[0] += L.tiles[I.tile_base + i].v_cur;
         a[1] += L.tiles[I.tile_base + i].v_prev;
     }
-    block_reduce(red, a, 2, mn, mx, mx2, l, 0);
+    block_reduce<2, 0, 0>(red, a, mn, mx, mx2, l);
     if (threadIdx.x == 0) {
         const double dn = (double)I.n;
         const float cs = __fsqrt_rn(__double2float_rn(__ddiv_rn(a[0], dn)));
@@ -1053,7 +1102,7 @@ __global__ void __launch_bounds__(TPB, 4) k_enc_pass3(mc_enc_launch L) {
                         double dd[4];
                         long long l[2] = {mism, 0};
                         float mn = FLT_MAX, mx = -FLT_MAX;
-                        block_reduce(red, dd, 0, mn, mx, maxr, l, 1);
+                        block_reduce<0, RF_MX2, 1>(red, dd, mn, mx, maxr, l);
                         if (threadIdx.x == 0) {
                             L.tiles[d.gt].maxr = maxr;
                             L.tiles[d.gt].mism = l[0];
@@ -1078,7 +1127,7 @@ __global__ void __launch_bounds__(TPB) k_enc_final3(mc_enc_launch L) {
         m = fmaxf(m, L.tiles[I.tile_base + i].maxr);
         z[0] += L.tiles[I.tile_base + i].mism;
     }
-    block_reduce(red, dd, 0, mn, mx, m, z, 1);
+    block_reduce<0, RF_MX2, 1>(red, dd, mn, mx, m, z);
     if (threadIdx.x == 0) {
         R->maxr = m;
         R->mism = z[0];
@@ -1126,7 +1175,7 @@ __device__ __forceinline__ uint32_t pdep32(uint32_t v, uint32_t m) {
 
 // Writes the residual codes of one quad (4 consecutive elements at g).
 __device__ __forceinline__ void put_codes(uint8_t *data_out, int codec, int64_t g, int64_t e1, bool vec,
-                                          const float (&r)[4], float scale, float qm) {
+                                          const float (&r)[4], float scale, float inv, float qm) {
     if (codec == MC_DC_RAW) {
         st4((float *)data_out, g, e1, vec, r);
     } else if (codec == MC_DC_Q8) {
@@ -1134,7 +1183,7 @@ __device__ __forceinline__ void put_codes(uint8_t *data_out, int codec, int64_t 
         uint32_t word = 0;
 #pragma unroll
         for (int j = 0; j < 4; j++)
-            if (g + j < e1) word |= ((uint32_t)(uint8_t)(int8_t)quant1(r[j], scale, qm)) << (8 * j);
+            if (g + j < e1) word |= ((uint32_t)(uint8_t)(int8_t)quant1(r[j], scale, inv, qm)) << (8 * j);
         if (g + 4 <= e1) *(uint32_t *)(codes + g) = word;
         else
             for (int j = 0; g + j < e1; j++) codes[g + j] = (uint8_t)(word >> (8 * j));
@@ -1142,7 +1191,7 @@ __device__ __forceinline__ void put_codes(uint8_t *data_out, int codec, int64_t 
         uint8_t *packed = data_out + 4;  // byte g/2, 2-byte aligned
         uint32_t nib[4];
 #pragma unroll
-        for (int j = 0; j < 4; j++) nib[j] = (g + j < e1) ? (uint32_t)((quant1(r[j], scale, qm) + 8) & 15) : 0u;
+        for (int j = 0; j < 4; j++) nib[j] = (g + j < e1) ? (uint32_t)((quant1(r[j], scale, inv, qm) + 8) & 15) : 0u;
         const uint32_t b0 = nib[0] | (nib[1] << 4), b1 = nib[2] | (nib[3] << 4);
         if (g + 4 <= e1) *(uint16_t *)(packed + (g >> 1)) = (uint16_t)(b0 | (b1 << 8));
         else {
@@ -1152,7 +1201,7 @@ __device__ __forceinline__ void put_codes(uint8_t *data_out, int codec, int64_t 
     } else {   // Q8_RAW / INT4_RAW: dequantised floats
         float v[4];
 #pragma unroll
-        for (int j = 0; j < 4; j++) v[j] = __fmul_rn((float)quant1(r[j], scale, qm), scale);
+        for (int j = 0; j < 4; j++) v[j] = __fmul_rn((float)quant1(r[j], scale, inv, qm), scale);
         st4((float *)data_out, g, e1, vec, v);
     }
 }
@@ -1177,6 +1226,7 @@ __device__ void pass4_tile(const mc_enc_launch &L, const StageDesc &d, const flo
         const TileRange tr = mom_range(I, t);
         const MomParams mp = {R->cm, R->cs, R->gmin, R->gmax, R->cs > 1e-8f};
         const float scale = R->scale;
+        const float inv = __fdiv_rn(1.0f, scale);
         const float qm = (float)qmax_of(I.codec);
         const float *cur = staged_or(d, buf, 0, (const float *)I.cur);
         const float *mem = staged_or(d, buf, 1, I.mem_out);
@@ -1194,7 +1244,7 @@ __device__ void pass4_tile(const mc_enc_launch &L, const StageDesc &d, const flo
 #pragma unroll
                 for (int j = 0; j < 4; j++)
                     r[j] = ((qb.f >> j) & 1u) ? mom_residual(c[j], m[j], (qb.pos >> j) & 1u, mp) : c[j];
-                put_codes(I.data_out, I.codec, tr.e0 + 4 * q, tr.e1, true, r, scale, qm);
+                put_codes(I.data_out, I.codec, tr.e0 + 4 * q, tr.e1, true, r, scale, inv, qm);
             }
         }
         const int64_t gstart = I.vec ? tr.e0 + 4 * (int64_t)nq : tr.e0;
@@ -1207,7 +1257,7 @@ __device__ void pass4_tile(const mc_enc_launch &L, const StageDesc &d, const flo
 #pragma unroll
             for (int j = 0; j < 4; j++)
                 r[j] = ((qb.f >> j) & 1u) ? mom_residual(c[j], m[j], (qb.pos >> j) & 1u, mp) : c[j];
-            put_codes(I.data_out, I.codec, g, tr.e1, I.vec, r, scale, qm);
+            put_codes(I.data_out, I.codec, g, tr.e1, I.vec, r, scale, inv, qm);
         }
         // bitmap content of this tile into its block of the bitmap frame
         // (ref :2222-2253; RLE blocks were written whole by pass 1)
@@ -1275,12 +1325,13 @@ __device__ void pass4_tile(const mc_enc_launch &L, const StageDesc &d, const flo
         const int64_t e0 = (int64_t)t * I.tile_kernels;
         const int64_t e1 = min(e0 + (int64_t)I.tile_kernels, I.n);
         const float scale = R->scale;
+        const float inv = __fdiv_rn(1.0f, scale);
         const float qm = (float)qmax_of(I.codec);
         const float *cur = staged_or(d, buf, 0, (const float *)I.cur);
         for (int64_t g = e0 + 4 * (int64_t)threadIdx.x; g < e1; g += 4 * TPB) {
             float c[4];
             ld4(cur, g, e1, I.vec, c);
-            put_codes(I.data_out, I.codec, g, e1, I.vec, c, scale, qm);
+            put_codes(I.data_out, I.codec, g, e1, I.vec, c, scale, inv, qm);
         }
     }
 }
