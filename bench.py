@@ -235,6 +235,22 @@ def run_reference(args):
 
 
 # ------------------------------------------------------------------- ours
+class L2Flush:
+    """Empties the L2 between timed steps, outside the timed events: a 256 MiB
+    write (no line of the previous step survives), then a 256 MiB read of a
+    second buffer, which evicts the write's dirty lines too, so no write-back
+    of the flush itself lands inside the next timed step."""
+
+    def __init__(self, torch, device):
+        n = 256 * 1024 * 1024 // 4
+        self.w = torch.empty(n, dtype=torch.float32, device=device)
+        self.r = torch.zeros(n, dtype=torch.float32, device=device)
+
+    def __call__(self):
+        self.w.zero_()
+        self.r.sum()
+
+
 def make_rounds_on_device(torch, model: str, n_rounds: int, seed: int, device):
     """AR(1) Gaussian updates (rho 0.9, sigma 1e-3/sqrt(fan_in)) generated on
     the GPU with a seeded generator, packed in the flat layout."""
@@ -292,7 +308,7 @@ def run_ours(args):
         return enc, dec
 
     client = f"Client{rank + 1}".encode()
-    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+    flush = L2Flush(torch, dev)
 
     def closed_loop(enc, dec, pb, base_ptr, count, e0=None, e1=None):
         """One round through the C ABI; e0/e1 (CUDA events on the library's
@@ -328,7 +344,7 @@ def run_ours(args):
     payload = 0
     with ClockSampler(local) as clk:
         for t in range(1 + Wm, n_rounds):
-            flush.zero_()                       # L2 flush outside the timed events
+            flush()                             # L2 flush outside the timed events
             e0 = torch.cuda.Event(enable_timing=True)
             e1 = torch.cuda.Event(enable_timing=True)
             payload = closed_loop(enc, dec, pb, rounds[t].data_ptr(), cnt, e0, e1)
@@ -359,7 +375,7 @@ def run_ours(args):
     enc.lib.falcom_set_kernel_timing(enc.h, 1)
     dec.lib.falcom_set_kernel_timing(dec.h, 1)
     for t in range(1 + Wm, n_rounds):
-        flush.zero_()
+        flush()
         closed_loop(enc, dec, pb, rounds[t].data_ptr(), [0])
     kt = kernel_times(enc.lib, enc.h)
     kd = kernel_times(dec.lib, dec.h)
@@ -410,7 +426,7 @@ def run_ours(args):
     h2d = d2h = 0
     for j in range(K):
         h = hosts[1 + Wm + j % (len(hosts) - 1 - Wm)]
-        flush.zero_()
+        flush()
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         pbytes = closed_loop(enc2, dec2, pb2, h.data_ptr(), [0], e0, e1)
@@ -448,7 +464,7 @@ def run_ours(args):
                                    f"encoder/decoder instances, residual codec {args.codec}, GPU zstd frames",
                        "elements_per_client": lay.numel, "update_bytes_per_client": upd,
                        "clients_per_gpu": 1, "codec": args.codec,
-                       "l2": "flushed between steps (256 MiB write, outside the timed events)",
+                       "l2": "flushed between steps (256 MiB write, then 256 MiB read of a second buffer; outside the timed events)",
                        "parallelism": f"replicas x{world} (independent clients)"},
             "gpu_launches": launches_timed,
             "payload_bytes_per_round": payload,
@@ -531,7 +547,7 @@ def run_federated(args):
         return encs, dec
 
     agg = torch.zeros(lay.total, dtype=torch.float32, device=dev)
-    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+    flush = L2Flush(torch, dev)
     cids = [f"Client{c + 1}".encode() for c in mine]
 
     def fed_step(encs, dec, pb, ptrs, count, e0=None, ear=None, e1=None):
@@ -569,7 +585,7 @@ def run_federated(args):
     with ClockSampler(local) as clk:
         for _ in range(K):
             next_round()
-            flush.zero_()
+            flush()
             e0, ear, e1 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
             payload = fed_step(encs, dec, pb, [x.data_ptr() for x in xs], cnt, e0, ear, e1)
             e1.synchronize()
@@ -595,7 +611,7 @@ def run_federated(args):
         for h, x in zip(hosts, xs):
             h.copy_(x)
         torch.cuda.synchronize()
-        flush.zero_()
+        flush()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         pbytes = fed_step(encs, dec, pb, [h.data_ptr() for h in hosts], [0], e0)
         agg_host.copy_(agg, non_blocking=True)
@@ -631,7 +647,7 @@ def run_federated(args):
                                    f"the {lay.numel}-element aggregate; residual codec {args.codec}",
                        "clients": n_clients, "clients_per_gpu": args.clients_per_gpu,
                        "elements_per_client": lay.numel, "update_bytes_per_client": upd, "codec": args.codec,
-                       "l2": "flushed between steps (256 MiB write, outside the timed events)",
+                       "l2": "flushed between steps (256 MiB write, then 256 MiB read of a second buffer; outside the timed events)",
                        "parallelism": f"clients sharded over {world} GPU(s), NCCL all-reduce of the aggregate"},
             "gpu_launches": cnt[0],
             "payload_bytes_per_step_rank0": payload,
@@ -692,12 +708,12 @@ def run_replay(args):
         assert c.lib.falcom_set_residual_codec(c.h, args.codec.encode()) == 0
         c.lib.falcom_set_stream(c.h, ctypes.c_void_p(stream.cuda_stream))
     outs = [(ctypes.POINTER(NDArrayC) * n)() for _, _, n, _ in rounds]
-    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device="cuda")
+    flush = L2Flush(torch, "cuda")
 
     def one(k):
         _, items, n, nbytes = rounds[k % len(rounds)]
         o = outs[k % len(rounds)]
-        flush.zero_()
+        flush()
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         e0.record(stream)
@@ -725,7 +741,7 @@ def run_replay(args):
         "vs_baseline": None, "dtype": "f32", "data": f"replay files {args.replay} ({len(files)} rounds)",
         "config": {"workload": "captured rounds, compress_batch + decompress_batch on device-resident tensors",
                    "codec": args.codec, "client": client.decode(),
-                   "l2": "flushed between steps (256 MiB write, outside the timed events)"}}))
+                   "l2": "flushed between steps (256 MiB write, then 256 MiB read of a second buffer; outside the timed events)"}}))
     enc.close()
     dec.close()
     for r, _, _, _ in rounds:

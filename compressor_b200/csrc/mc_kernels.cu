@@ -339,15 +339,13 @@ __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
 __device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
 }
-// L2 eviction priorities: a pass keeps in L2 (evict_last) what the next pass
-// of the round reads again, and streams the rest (evict_first).  The passes
-// alternate their tile order, so the next pass starts on the tiles this one
-// touched last.
-__device__ __forceinline__ uint64_t l2_keep() {
-    uint64_t p;
-    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
-    return p;
-}
+// L2 eviction priority of the staged arrays and the large outputs: streamed
+// (evict_first).  A round's working set (inputs, previous gradients,
+// memories, history copies) is several times the L2; lines kept at a higher
+// priority for a later pass only crowd out the lines in use (measured on
+// ResNet-50: keeping the inputs and previous gradients, or the inputs alone,
+// made the round ~4% slower).  The passes alternate their tile order, so a
+// pass still starts on the tiles the previous one touched last.
 __device__ __forceinline__ uint64_t l2_stream() {
     uint64_t p;
     asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
@@ -406,7 +404,6 @@ struct StageDesc {
     const uint8_t *x0, *x1;
     int gt;                         // tile id
     int ii;                         // item index
-    uint32_t keep;                  // bit k: array k stays in L2 (evict_last), else streamed
 };
 
 struct TileShared {
@@ -434,13 +431,13 @@ __device__ void pipe_issue(uint32_t bar, float *buf, uint8_t *xb, const StageDes
     const uintptr_t xa = d.x0 ? up16(d.x0) : 0, xe = d.x0 ? dn16(d.x1) : 0;
     const uint32_t xbytes = xe > xa ? (uint32_t)(xe - xa) : 0u;
     mbar_expect_tx(bar, total + xbytes);
-    const uint64_t keep = l2_keep(), stream = l2_stream();
+    const uint64_t stream = l2_stream();
     if (body) {
 #pragma unroll
         for (int k = 0; k < NA; k++)
             if (d.src[k])
                 bulk_g2s(smem_u32(buf + k * STAGE_ELEMS), d.src[k] + d.e0, body, bar,
-                         (d.keep >> k) & 1u ? keep : stream);
+                         stream);
     }
     if (xbytes) bulk_g2s(smem_u32(xb + (xa - dn16(d.x0))), (const void *)xa, xbytes, bar, stream);
 }
@@ -497,7 +494,6 @@ __device__ void run_tile(const int2 *list, float *stage_mem, uint64_t *bar, Stag
         d.gt = e.x;
         d.ii = e.y;
         d.x0 = d.x1 = nullptr;
-        d.keep = 0;
         plan(d);
         *sd = d;
         mbar_init(b, 1);
@@ -858,7 +854,6 @@ __global__ void __launch_bounds__(TPB, 4) k_enc_pass1(mc_enc_launch L) {
                     if ((I.kind == MC_K_MOMENTUM || I.kind == MC_K_QUANT) && stageable(L.staged, I, d)) {
                         d.src[0] = (const float *)I.cur;
                         if (I.kind == MC_K_MOMENTUM) d.src[1] = I.prev;
-                        d.keep = 3u;   // pass 2 reads both again
                     }
                 },
                 [](const StageDesc &) {},
@@ -938,7 +933,6 @@ __global__ void __launch_bounds__(TPB, 6) k_enc_pass2(mc_enc_launch L) {
                         if (stageable(L.staged, I, d)) {
                             d.src[0] = (const float *)I.cur;
                             d.src[1] = I.prev;
-                            d.keep = 3u;   // pass 3 reads both again
                         }
                     },
                     [](const StageDesc &) {},
@@ -1023,7 +1017,6 @@ __global__ void __launch_bounds__(TPB, 4) k_enc_pass3(mc_enc_launch L) {
                             d.src[0] = (const float *)I.cur;
                             d.src[1] = I.mem_in;
                             if (L.tiles[d.gt].P > 0) d.src[2] = I.prev;
-                            d.keep = 1u;   // pass 4 reads the input again
                         }
                     },
                     [&](const StageDesc &d) {
@@ -1072,7 +1065,7 @@ __global__ void __launch_bounds__(TPB, 4) k_enc_pass3(mc_enc_launch L) {
                             const float4 *m4 = mem_in ? (const float4 *)(mem_in + tr.e0) : nullptr;
                             const float4 *p4 = (const float4 *)(prev + tr.e0);
                             float4 *o4 = (float4 *)(I.mem_out + tr.e0);
-                            const uint64_t keep = l2_keep();   // pass 4 reads the new memory
+                            const uint64_t spol = l2_stream();
                             for (int q = threadIdx.x; q < nq; q += TPB) {
                                 const QuadBits qb = quad_bits_full(s_bw, s_dw, k0 >> 5, k0, 4u * q, I.ks, I.ksdiv);
                                 const float4 cv = c4[q];
@@ -1083,7 +1076,7 @@ __global__ void __launch_bounds__(TPB, 4) k_enc_pass3(mc_enc_launch L) {
                                 const float p[4] = {pv.x, pv.y, pv.z, pv.w};
                                 float mo[4];
                                 quad(tr.e0 + 4 * q, qb, c, m0, p, mo, 4);
-                                st_f4(o4 + q, make_float4(mo[0], mo[1], mo[2], mo[3]), keep);
+                                st_f4(o4 + q, make_float4(mo[0], mo[1], mo[2], mo[3]), spol);
                             }
                         }
                         const int64_t gstart = I.vec ? tr.e0 + 4 * (int64_t)nq : tr.e0;
