@@ -47,15 +47,14 @@ PEAK_FALLBACK_GBS = 6650.0
 # whenever a kernel changes; None for workloads that were not captured.
 NCU_TRAFFIC = {
     ("resnet50", "q8"): {
-        "enc_pass1_stats_sign": 260_293_376,
-        "enc_pass2_variance": 191_903_744,
-        "enc_pass3_predict": 339_045_888,
-        "enc_pass4_quantize_pack": 189_139_456,
+        "enc_pass1_stats_sign": 246_334_464,
+        "enc_pass2_variance": 193_776_128,
+        "enc_pass3_predict": 342_665_216,
+        "enc_pass4_quantize_pack": 201_771_776,
         "dec_prefix": 259_840,
-        "dec_reconstruct": 421_497_088,
+        "dec_reconstruct": 438_323_456,
     },
 }
-
 
 def log(*a):
     print(*a, file=sys.stderr, flush=True)
@@ -409,7 +408,8 @@ def run_ours(args):
                 "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, one steady-state launch",
                 "algorithmic_bytes_per_launch": int(alg[dom]), "avg_launch_ms": round(avg_ms, 5),
                 "kernel_share": {k: round(v / sum(shares.values()), 4) for k, v in shares.items()},
-                "kernel_ms_per_round": {k: round(v[0] / v[1], 5) for k, v in ktimes.items() if v[1] > 0},
+                "kernel_ms_per_round": {k: round(v[0] / K, 5) for k, v in ktimes.items() if v[1] > 0},
+                "launches_per_round": {k: round(v[1] / K, 2) for k, v in ktimes.items() if v[1] > 0},
                 "closed_loop_algorithmic_bytes": int(ab["bytes_per_round"]),
                 "closed_loop_frac": round(ab["bytes_per_round"] / (ms_per_step * 1e-3) / 1e9 / peak, 4)}
 
