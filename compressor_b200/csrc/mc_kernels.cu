@@ -30,6 +30,8 @@
 #include <float.h>
 #include <stdint.h>
 
+#include <type_traits>
+
 #include "mc_device.h"
 
 #define TPB 256
@@ -1199,6 +1201,50 @@ __device__ __forceinline__ void put_codes(uint8_t *data_out, int codec, int64_t 
     }
 }
 
+// Codes of one whole quad (4 consecutive elements at g, all inside the item;
+// the item's pointers 16-byte aligned), for codec C.  The exact quotient is
+// taken only when a lane of the warp has an element within 2^-15 of a
+// half-integer (see quant1).
+template <int C>
+__device__ __forceinline__ void put_codes_full(uint8_t *data_out, int64_t g, const float (&r)[4], float scale,
+                                               float inv, float qm) {
+    if (C == MC_DC_RAW) {
+        *(float4 *)((float *)data_out + g) = make_float4(r[0], r[1], r[2], r[3]);
+        return;
+    }
+    float v[4];
+    bool need = false;
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        const float y = __fmul_rn(r[j], inv);
+        v[j] = rintf(y);
+        need |= !(fabsf(fabsf(__fsub_rn(y, v[j])) - 0.5f) > 3.0517578125e-5f);
+    }
+    if (__any_sync(__activemask(), need)) {   // the lanes still in the quad loop
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const float y = __fmul_rn(r[j], inv);
+            if (!(fabsf(fabsf(__fsub_rn(y, v[j])) - 0.5f) > 3.0517578125e-5f)) v[j] = rintf(__fdiv_rn(r[j], scale));
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < 4; j++) v[j] = fminf(qm, fmaxf(-qm, v[j]));
+    if (C == MC_DC_Q8) {
+        const uint32_t word = ((uint32_t)(uint8_t)(int8_t)(int)v[0]) | ((uint32_t)(uint8_t)(int8_t)(int)v[1] << 8) |
+                              ((uint32_t)(uint8_t)(int8_t)(int)v[2] << 16) |
+                              ((uint32_t)(uint8_t)(int8_t)(int)v[3] << 24);
+        *(uint32_t *)(data_out + 4 + g) = word;
+    } else if (C == MC_DC_INT4) {
+        const uint32_t b0 = (uint32_t)(((int)v[0] + 8) & 15) | ((uint32_t)(((int)v[1] + 8) & 15) << 4);
+        const uint32_t b1 = (uint32_t)(((int)v[2] + 8) & 15) | ((uint32_t)(((int)v[3] + 8) & 15) << 4);
+        *(uint16_t *)(data_out + 4 + (g >> 1)) = (uint16_t)(b0 | (b1 << 8));
+    } else {   // Q8_RAW / INT4_RAW: dequantised floats (through the integer code, so a code of -0.0 gives +0.0)
+        *(float4 *)((float *)data_out + g) =
+            make_float4(__fmul_rn((float)(int)v[0], scale), __fmul_rn((float)(int)v[1], scale),
+                        __fmul_rn((float)(int)v[2], scale), __fmul_rn((float)(int)v[3], scale));
+    }
+}
+
 // ------------------------------------------------------------------ pass 4
 // Side inputs of a pass-4 tile, read while its bulk copies are in flight:
 // the offset of its first predicted kernel in the dense signs and the
@@ -1227,17 +1273,26 @@ __device__ void pass4_tile(const mc_enc_launch &L, const StageDesc &d, const flo
         const int len = (int)(tr.e1 - tr.e0), nq = len >> 2;
         if (I.vec) {   // whole quads, no range checks
             const float4 *c4 = (const float4 *)(cur + tr.e0), *m4 = (const float4 *)(mem + tr.e0);
-            for (int q = threadIdx.x; q < nq; q += TPB) {
-                const QuadBits qb = quad_bits_full(s_bw, s_dw, k0 >> 5, k0, 4u * q, I.ks, I.ksdiv);
-                const float4 cv = c4[q];
-                float4 mv = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-                if (qb.f) mv = m4[q];
-                const float c[4] = {cv.x, cv.y, cv.z, cv.w}, m[4] = {mv.x, mv.y, mv.z, mv.w};
-                float r[4];
+            auto quads = [&](auto codec) {
+                for (int q = threadIdx.x; q < nq; q += TPB) {
+                    const QuadBits qb = quad_bits_full(s_bw, s_dw, k0 >> 5, k0, 4u * q, I.ks, I.ksdiv);
+                    const float4 cv = c4[q];
+                    float4 mv = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                    if (qb.f) mv = m4[q];
+                    const float c[4] = {cv.x, cv.y, cv.z, cv.w}, m[4] = {mv.x, mv.y, mv.z, mv.w};
+                    float r[4];
 #pragma unroll
-                for (int j = 0; j < 4; j++)
-                    r[j] = ((qb.f >> j) & 1u) ? mom_residual(c[j], m[j], (qb.pos >> j) & 1u, mp) : c[j];
-                put_codes(I.data_out, I.codec, tr.e0 + 4 * q, tr.e1, true, r, scale, inv, qm);
+                    for (int j = 0; j < 4; j++)
+                        r[j] = ((qb.f >> j) & 1u) ? mom_residual(c[j], m[j], (qb.pos >> j) & 1u, mp) : c[j];
+                    put_codes_full<decltype(codec)::value>(I.data_out, tr.e0 + 4 * q, r, scale, inv, qm);
+                }
+            };
+            switch (I.codec) {
+                case MC_DC_Q8: quads(std::integral_constant<int, MC_DC_Q8>()); break;
+                case MC_DC_INT4: quads(std::integral_constant<int, MC_DC_INT4>()); break;
+                case MC_DC_RAW: quads(std::integral_constant<int, MC_DC_RAW>()); break;
+                case MC_DC_Q8_RAW: quads(std::integral_constant<int, MC_DC_Q8_RAW>()); break;
+                default: quads(std::integral_constant<int, MC_DC_INT4_RAW>()); break;
             }
         }
         const int64_t gstart = I.vec ? tr.e0 + 4 * (int64_t)nq : tr.e0;
