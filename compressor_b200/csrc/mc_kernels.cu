@@ -691,10 +691,39 @@ __device__ void pass1_tile(const mc_enc_launch &L, const StageDesc &d, const flo
         const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
         const float inv_ks = __fdiv_rn(1.0f, (float)I.ks);
         int P = 0;
-        if (I.ks == 1) {
+        if (I.ks == 1 && d.src[0]) {
             // one element per kernel: maj = 1, so every kernel has the same
-            // consistency ((1 * 1 - 0.5) * 2) and the dominant sign is
-            // "not negative"
+            // consistency ((1 * 1 - 0.5) * 2) and the dominant sign is "not
+            // negative".  A lane takes 4 kernels (one 16-byte load of the
+            // staged tile; a quad past the tile's end stays inside the
+            // 4096-float stage and its bits are masked off), and each group
+            // of 8 lanes ORs its nibbles into one 32-kernel word.
+            const float half = __fmaf_rn(1.0f, inv_ks, -0.5f);
+            const bool flag = __fadd_rn(half, half) >= I.thr;
+            const uint32_t kt = (uint32_t)(tr.k1 - tr.k0);
+            const float4 *c4 = (const float4 *)(cur + tr.k0);
+            for (uint32_t kb = warp * 128u; kb < kt; kb += NWARP * 128u) {
+                const uint32_t k = kb + 4u * lane;
+                const float4 v = c4[k >> 2];
+                const uint32_t nv = k >= kt ? 0u : (kt - k >= 4u ? 4u : kt - k);
+                const uint32_t vm = (1u << nv) - 1u;
+                const uint32_t nib = ((v.x < 0.0f ? 0u : 1u) | (v.y < 0.0f ? 0u : 2u) | (v.z < 0.0f ? 0u : 4u) |
+                                      (v.w < 0.0f ? 0u : 8u)) & vm;
+                const uint32_t sh = 4u * (lane & 7);
+                uint32_t dw = nib << sh, bw = (flag ? vm : 0u) << sh;
+#pragma unroll
+                for (int o = 1; o < 8; o <<= 1) {
+                    dw |= __shfl_xor_sync(FULL, dw, o);
+                    bw |= __shfl_xor_sync(FULL, bw, o);
+                }
+                const uint32_t kw = kb + 32u * (lane >> 3);
+                if ((lane & 7) == 0 && kw < kt) {
+                    I.bm_words[(tr.k0 + kw) >> 5] = bw;
+                    I.dom_words[(tr.k0 + kw) >> 5] = dw;
+                    P += __popc(bw);
+                }
+            }
+        } else if (I.ks == 1) {
             const float half = __fmaf_rn(1.0f, inv_ks, -0.5f);
             const bool flag = __fadd_rn(half, half) >= I.thr;
             for (int64_t kb = tr.k0 + warp * 32; kb < tr.k1; kb += TPB) {
@@ -708,32 +737,49 @@ __device__ void pass1_tile(const mc_enc_launch &L, const StageDesc &d, const flo
                     P += __popc(b);
                 }
             }
-        }
-        for (int64_t kb = tr.k0 + warp * 32; I.ks != 1 && kb < tr.k1; kb += TPB) {
-            const int64_t k = kb + lane;
-            bool flag = false, dom = false;
-            if (k < tr.k1) {
-                const float *pk = cur + k * I.ks;
-                int pos = 0, neg = 0;
-                for (int j = 0; j < I.ks; j++) {
-                    const float v = pk[j];
-                    pos += v > 0.0f;
-                    neg += v < 0.0f;
+        } else {
+            // kernels of KS elements (KS = 0: the item's ks at run time)
+            auto kernels = [&](auto ks_c) {
+                constexpr int KS = decltype(ks_c)::value;
+                const int ks = KS ? KS : I.ks;
+                for (int64_t kb = tr.k0 + warp * 32; kb < tr.k1; kb += TPB) {
+                    const int64_t k = kb + lane;
+                    bool flag = false, dom = false;
+                    if (k < tr.k1) {
+                        const float *pk = cur + k * ks;
+                        int pos = 0, neg = 0;
+                        if (KS) {
+#pragma unroll
+                            for (int j = 0; j < KS; j++) {
+                                const float v = pk[j];
+                                pos += v > 0.0f;
+                                neg += v < 0.0f;
+                            }
+                        } else {
+                            for (int j = 0; j < ks; j++) {
+                                const float v = pk[j];
+                                pos += v > 0.0f;
+                                neg += v < 0.0f;
+                            }
+                        }
+                        const int zero = ks - pos - neg;
+                        const int maj = (pos >= neg) ? (pos + zero) : (neg + zero);
+                        const float half = __fmaf_rn((float)maj, inv_ks, -0.5f);
+                        const float cons = __fadd_rn(half, half);
+                        flag = cons >= I.thr;
+                        dom = pos >= neg;
+                    }
+                    const uint32_t b = __ballot_sync(FULL, flag);
+                    const uint32_t dw = __ballot_sync(FULL, dom);
+                    if (lane == 0) {
+                        I.bm_words[kb >> 5] = b;
+                        I.dom_words[kb >> 5] = dw;
+                        P += __popc(b);
+                    }
                 }
-                const int zero = I.ks - pos - neg;
-                const int maj = (pos >= neg) ? (pos + zero) : (neg + zero);
-                const float half = __fmaf_rn((float)maj, inv_ks, -0.5f);
-                const float cons = __fadd_rn(half, half);
-                flag = cons >= I.thr;
-                dom = pos >= neg;
-            }
-            const uint32_t b = __ballot_sync(FULL, flag);
-            const uint32_t dw = __ballot_sync(FULL, dom);
-            if (lane == 0) {
-                I.bm_words[kb >> 5] = b;
-                I.dom_words[kb >> 5] = dw;
-                P += __popc(b);
-            }
+            };
+            if (I.ks == 9) kernels(std::integral_constant<int, 9>());
+            else kernels(std::integral_constant<int, 0>());
         }
         l[0] = P;
         block_reduce<2, RF_MN | RF_MX, 1>(red, dd, mn, mx, mx2, l);
