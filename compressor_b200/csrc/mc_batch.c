@@ -69,7 +69,7 @@ int mc_tables_mark(MomentumCompressor *mc, int k, cudaStream_t st) {
 }
 
 #define SLOT_ALIGN 256
-#define TILE_ELEMS 4096
+#define TILE_ELEMS MC_TILE_ELEMS
 
 enum { MODE_DIRECT = 0, MODE_MOMENTUM = 1, MODE_GENERIC = 2 };
 
@@ -292,8 +292,8 @@ static const char *codec_tag_of(int dcodec) {
     }
 }
 
-/* Kernels per momentum tile: the largest power of two with at most 8192
- * elements per tile, at least 32 (one ballot word).  Powers of two make every
+/* Kernels per momentum tile: the largest power of two with at most
+ * TILE_ELEMS elements per tile, at least 32 (one ballot word).  Powers of two make every
  * 2^20-kernel block of the bitmap frame a union of whole tiles. */
 static int tile_kernels_for(size_t ks) {
     size_t tk = TILE_ELEMS;

@@ -121,6 +121,13 @@ enum {
     MC_D_COPY = 3           /* direct, bytes copied (raw floats or lossless content) */
 };
 
+/* Elements of one tile: the unit of work of one CTA of the streaming
+ * kernels and the capacity of one array of its shared-memory stage.  A
+ * momentum tile holds a power-of-two number of whole kernels (at least 32)
+ * with at most MC_TILE_ELEMS elements; other tiles hold MC_TILE_ELEMS
+ * elements (4x that for byte copies). */
+#define MC_TILE_ELEMS 4096
+
 /* zstd framing shared by encoder and decoder: single-segment frame header
  * (magic, descriptor 0xA0 and a 4-byte content size: 9 bytes), then blocks of
  * at most 2^17 content bytes, each behind a 3-byte block header. */

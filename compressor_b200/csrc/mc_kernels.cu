@@ -328,7 +328,7 @@ __device__ int64_t scan_tile_counts(const int32_t *cnt, int stride_words, int ba
 // spending registers on it.  Copies need 16-byte aligned addresses and
 // sizes: the aligned body of the tile is copied in bulk and the remaining
 // (< 4) elements by plain loads.  Every wait on the mbarrier is bounded.
-#define STAGE_ELEMS 4096
+#define STAGE_ELEMS MC_TILE_ELEMS
 #define MBAR_SPIN_LIMIT (1u << 24)
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
@@ -397,6 +397,7 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
 // Bitmap words of one tile: at most 4096 kernels (tiles hold at most
 // STAGE_ELEMS elements of whole kernels, and start on a word boundary).
 #define TILE_WORDS (STAGE_ELEMS / 32)
+static_assert(TILE_WORDS <= TPB, "tile kernels handle one bitmap word per thread");
 
 struct StageDesc {
     const float *src[NSTAGE_ARR];   // global source of every staged array (NULL: not staged)
@@ -1695,12 +1696,12 @@ __device__ __forceinline__ void dec_resid4(const mc_dec_item &I, const uint8_t *
 }
 
 // Sign bytes a reconstruct tile needs: its predicted kernels' bits start at
-// bit (tile_poff & 7) of the window; up to 4096 kernels per tile, plus the
-// read-ahead of the 5-byte gather.
-#define SIGN_WIN 528
+// bit (tile_poff & 7) of the window; up to STAGE_ELEMS kernels per tile, plus
+// the read-ahead of the 5-byte gather.
+#define SIGN_WIN (STAGE_ELEMS / 8 + 16)
 // Byte region of a reconstruct stage: the tile's q8 / int4 codes (at most
 // STAGE_ELEMS bytes, plus the 15-byte misalignment of their start).
-#define RC_XB 4128
+#define RC_XB (STAGE_ELEMS + 32)
 
 // Momentum tiles of the decoder, before the wait on the tile's bulk copies:
 // the tile's bitmap words, the offset of its first predicted kernel in the
