@@ -1178,41 +1178,44 @@ __global__ void __launch_bounds__(TPB) k_enc_final3(mc_enc_launch L) {
     }
 }
 
-// Software parallel-bit-extract: the bits of `v` at the set positions of
-// `m`, packed towards bit 0 in ascending position order.
-// Bits of v at the set bits of m, packed from bit 0 (parallel bit extract),
-// one run of consecutive set bits of m per step.
+// Parallel bit extract / deposit of the bits of v at the set bits of m, by
+// the parallel-suffix method (Hacker's Delight, 2nd ed., 7-4 "compress" and
+// 7-5 "expand"): five fixed steps, no data-dependent loop, so the lanes of a
+// warp stay converged whatever their masks.
 __device__ __forceinline__ uint32_t pext32(uint32_t v, uint32_t m) {
-    if (m == FULL) return v;
-    uint32_t out = 0;
-    int j = 0;
-    while (m) {
-        const int lo = __ffs(m) - 1;
-        const uint32_t t = m >> lo;
-        const int len = t == (FULL >> lo) ? 32 - lo : __ffs(~t) - 1;
-        const uint32_t run = len == 32 ? FULL : (1u << len) - 1u;
-        out |= ((v >> lo) & run) << j;
-        j += len;
-        m &= ~(run << lo);
+    uint32_t x = v & m, mk = ~m << 1;
+#pragma unroll
+    for (int i = 0; i < 5; i++) {
+        uint32_t mp = mk ^ (mk << 1);
+        mp ^= mp << 2;
+        mp ^= mp << 4;
+        mp ^= mp << 8;
+        mp ^= mp << 16;
+        const uint32_t mv = mp & m;
+        m = (m ^ mv) | (mv >> (1 << i));
+        const uint32_t t = x & mv;
+        x = (x ^ t) | (t >> (1 << i));
+        mk &= ~mp;
     }
-    return out;
+    return x;
 }
-
-// The low bits of v deposited at the set bits of m (parallel bit deposit),
-// one run of consecutive set bits of m per step.
 __device__ __forceinline__ uint32_t pdep32(uint32_t v, uint32_t m) {
-    if (m == FULL) return v;
-    uint32_t out = 0;
-    while (m) {
-        const int lo = __ffs(m) - 1;
-        const uint32_t t = m >> lo;
-        const int len = t == (FULL >> lo) ? 32 - lo : __ffs(~t) - 1;
-        const uint32_t run = len == 32 ? FULL : (1u << len) - 1u;
-        out |= (v & run) << lo;
-        v = len == 32 ? 0u : v >> len;
-        m &= ~(run << lo);
+    const uint32_t m0 = m;
+    uint32_t mk = ~m << 1, mvs[5];
+#pragma unroll
+    for (int i = 0; i < 5; i++) {
+        uint32_t mp = mk ^ (mk << 1);
+        mp ^= mp << 2;
+        mp ^= mp << 4;
+        mp ^= mp << 8;
+        mp ^= mp << 16;
+        mvs[i] = mp & m;
+        m = (m ^ mvs[i]) | (mvs[i] >> (1 << i));
+        mk &= ~mp;
     }
-    return out;
+#pragma unroll
+    for (int i = 4; i >= 0; i--) v = (v & ~mvs[i]) | ((v << (1 << i)) & mvs[i]);
+    return v & m0;
 }
 
 // Writes the residual codes of one quad (4 consecutive elements at g).
