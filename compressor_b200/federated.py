@@ -72,3 +72,63 @@ def allreduce_aggregate(aggregate, dist=None, group=None) -> None:
     """Sum of the per-rank aggregates on every rank (no-op on one rank)."""
     if dist is not None and dist.is_initialized() and dist.get_world_size(group) > 1:
         dist.all_reduce(aggregate, op=dist.ReduceOp.SUM, group=group)
+
+
+def layer_chunks(numels: Sequence[int], n_chunks: int) -> List[tuple]:
+    """Splits items 0..len(numels)-1, in order, into at most n_chunks
+    contiguous runs [i0, i1) of about equal element counts (a run ends once
+    it reaches its share of the total; every run holds at least one item)."""
+    n = len(numels)
+    if n == 0:
+        return []
+    n_chunks = max(1, min(int(n_chunks), n))
+    total = float(sum(int(x) for x in numels))
+    out, i0, acc = [], 0, 0
+    for i, x in enumerate(numels):
+        acc += int(x)
+        left_items, left_chunks = n - (i + 1), n_chunks - len(out) - 1
+        if left_chunks > 0 and (acc >= total * (len(out) + 1) / n_chunks or left_items == left_chunks):
+            out.append((i0, i + 1))
+            i0 = i + 1
+    out.append((i0, n))
+    return out
+
+
+class ChunkedAllreduce:
+    """Sum all-reduce of the flat aggregate, one layer chunk at a time.
+
+    The server step decodes the items of chunk 0, then chunk 1, ...; as soon
+    as a chunk's decodes (with their fused aggregate additions) are queued,
+    chunk_done(c) issues the all-reduce of that chunk's region of the
+    aggregate as an asynchronous collective.  Under NCCL it runs on the
+    process group's own stream, which waits only for the work already queued
+    on the caller's stream, so it overlaps the codec work of the later
+    chunks; wait() orders the caller's stream (or, under gloo, the host)
+    after all of them.  Every rank issues the same chunks in the same order.
+    No-op on one rank."""
+
+    def __init__(self, aggregate, layout: AggregateLayout, chunks: Sequence[tuple], dist=None, group=None):
+        self.aggregate = aggregate
+        self.dist = dist
+        self.group = group
+        self.active = dist is not None and dist.is_initialized() and dist.get_world_size(group) > 1
+        self.regions = []
+        for i0, i1 in chunks:
+            lo = layout.offsets[i0]
+            last = i1 - 1
+            hi = layout.offsets[last] + int(np.prod(layout.shapes[last]))
+            self.regions.append((lo, hi))
+        self.works = []
+
+    def chunk_done(self, c: int) -> None:
+        if not self.active:
+            return
+        lo, hi = self.regions[c]
+        if hi > lo:
+            self.works.append(self.dist.all_reduce(self.aggregate[lo:hi], op=self.dist.ReduceOp.SUM,
+                                                   group=self.group, async_op=True))
+
+    def wait(self) -> None:
+        for w in self.works:
+            w.wait()
+        self.works = []

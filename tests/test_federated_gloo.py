@@ -74,3 +74,49 @@ def test_gloo_allreduce_equals_serial_fedavg(tmp_path, n_clients):
     got = [np.load(f"{out}.{r}.npy") for r in range(world)]
     assert np.array_equal(got[0], got[1])            # every rank holds the same global update
     assert np.max(np.abs(got[0] - serial)) <= 1e-9
+
+
+def test_layer_chunks_cover_items_in_order():
+    for numels, g in [([5, 1, 1, 1, 10, 2], 3), ([1] * 5, 8), ([100, 1, 1], 3), ([7], 4), ([3, 3, 3, 3], 2)]:
+        ch = F.layer_chunks(numels, g)
+        assert ch[0][0] == 0 and ch[-1][1] == len(numels)
+        assert all(a[1] == b[0] for a, b in zip(ch, ch[1:]))
+        assert all(i1 > i0 for i0, i1 in ch) and len(ch) <= g
+    assert F.layer_chunks([3, 3, 3, 3], 2) == [(0, 2), (2, 4)]
+    assert F.layer_chunks([], 3) == []
+
+
+def _chunked_worker(rank, world, port, out_path):
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        shapes = [(64, 3, 3, 3), (64,), (128, 64, 1, 1), (10, 7), (5,), (256, 128, 3, 3)]
+        lay = F.AggregateLayout.of([f"t{i}" for i in range(len(shapes))], shapes, align=4)
+        agg = torch.from_numpy(_decoded(rank, 1, lay.total))
+        whole = agg.clone()
+        F.allreduce_aggregate(whole, dist)
+        ar = F.ChunkedAllreduce(agg, lay, F.layer_chunks([int(np.prod(s)) for s in shapes], 3), dist)
+        for c in range(len(ar.regions)):
+            ar.chunk_done(c)
+        ar.wait()
+        ok = all(torch.equal(agg[o:o + int(np.prod(s))], whole[o:o + int(np.prod(s))])
+                 for o, s in zip(lay.offsets, shapes))
+        np.save(f"{out_path}.{rank}.npy", np.array([ok, len(ar.regions)]))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_gloo_chunked_allreduce_equals_whole(tmp_path):
+    """The aggregate all-reduced one layer chunk at a time (asynchronous
+    collectives, waited at the end) equals one all-reduce of the whole
+    aggregate on every item, on every rank."""
+    import torch.multiprocessing as mp
+    world = 2
+    out = str(tmp_path / "chunked")
+    mp.start_processes(_chunked_worker, args=(world, _free_port(), out), nprocs=world, join=True,
+                       start_method="spawn")
+    for r in range(world):
+        ok, n = np.load(f"{out}.{r}.npy")
+        assert ok and n == 3
