@@ -485,10 +485,10 @@ def run_ours(args):
 def run_federated(args):
     """Federated round per step: every rank compresses its clients' updates
     (one encoder instance per client) and decodes them on one server decoder
-    instance whose weighted aggregate is fused into the decode, one layer
-    chunk at a time; the sum all-reduce of each chunk's region of the
-    aggregate is issued over NCCL as soon as that chunk is decoded, so it
-    overlaps the codec work of the later chunks."""
+    instance whose weighted aggregate is fused into the decode, then the sum
+    all-reduce of the aggregate over NCCL.  With --ar-chunks C > 1 the round
+    runs in C layer chunks and each chunk's all-reduce is issued as soon as
+    that chunk is decoded, overlapping the later chunks' codec work."""
     import torch
     import torch.distributed as dist
     from compressor_b200 import build as B
@@ -780,8 +780,9 @@ def main():
                     help="value: only the device-resident timed loop (for profiler runs)")
     ap.add_argument("--federated", action="store_true",
                     help="federated round (decode + weighted aggregate + all-reduce) also on one GPU")
-    ap.add_argument("--ar-chunks", type=int, default=4,
-                    help="federated round on N > 1 GPUs: layer chunks of the pipelined aggregate all-reduce")
+    ap.add_argument("--ar-chunks", type=int, default=1,
+                    help="federated round on N > 1 GPUs: layer chunks of the pipelined aggregate all-reduce "
+                         "(1 = one all-reduce after the whole decode; more chunks measured slower on B200)")
     ap.add_argument("--clients-per-gpu", type=int, default=1,
                     help="federated round: clients per GPU (64 / N for the 64-client round)")
     ap.add_argument("--replay", default=None,
