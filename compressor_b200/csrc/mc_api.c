@@ -985,6 +985,7 @@ MC_EXPORT int falcom_set_aggregate(MomentumCompressor *mc, float *aggregate, con
         mc->agg_off = NULL;
         mc->agg = NULL;
         mc->agg_n = 0;
+        mc->agg_store = 0;
         return ERROR_NONE;
     }
     int d = -1;
@@ -1001,6 +1002,12 @@ MC_EXPORT int falcom_set_aggregate(MomentumCompressor *mc, float *aggregate, con
     mc->agg = aggregate;
     mc->agg_n = n;
     mc->agg_w = weight;
+    return ERROR_NONE;
+}
+
+MC_EXPORT int falcom_set_aggregate_store(MomentumCompressor *mc, int store) {
+    if (!mc || (store != 0 && store != 1)) return ERROR_INVALID_PARAM;
+    mc->agg_store = store;
     return ERROR_NONE;
 }
 

@@ -1287,6 +1287,7 @@ static int dec_accumulate(MomentumCompressor *mc, const dplan *D, size_t n, NDAr
         A->dst = mc->agg + mc->agg_off[base + i];
         A->n = (int64_t)D[i].n;
         A->w = mc->agg_w;
+        A->store = mc->agg_store;
         A->tile_base = tb;
         A->vec = ((((uintptr_t)A->src) | ((uintptr_t)A->dst)) & 15) == 0;
         const int nt = (int)((D[i].n + MC_ACC_TILE - 1) / MC_ACC_TILE);

@@ -208,7 +208,9 @@ typedef struct {
 } mc_dec_launch;
 
 /* Weighted accumulation of decoded tensors into an aggregate:
- * dst[e] = fma(w, src[e], dst[e]) for e < n; tiles of MC_ACC_TILE elements. */
+ * dst[e] = fma(w, src[e], dst[e]) for e < n, or with `store` set
+ * dst[e] = fma(w, src[e], +0) (dst not read: the same bits as clearing dst to
+ * +0 and adding); tiles of MC_ACC_TILE elements. */
 #define MC_ACC_TILE 8192
 typedef struct {
     const float *src;
@@ -217,7 +219,7 @@ typedef struct {
     float w;
     int32_t tile_base;
     int32_t vec;                /* 1: src and dst 16-byte aligned */
-    int32_t pad;
+    int32_t store;              /* 1: dst = w * src (dst not read) */
 } mc_acc_item;
 
 /* Optional per-kernel event trace (events created by the host). */

@@ -184,6 +184,7 @@ struct MomentumCompressor {
     size_t *agg_off;
     size_t agg_n;
     float agg_w;
+    int agg_store;   /* 1: the next batches store weight * decoded instead of adding */
     int agg_failed;
 
     /* per-kernel device time (falcom_set_kernel_timing) */

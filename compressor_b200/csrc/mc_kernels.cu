@@ -1956,9 +1956,9 @@ __global__ void __launch_bounds__(TPB) k_accumulate(const mc_acc_item *items, co
     const int64_t e0 = (int64_t)(gt - I.tile_base) * MC_ACC_TILE;
     const int64_t e1 = min(e0 + MC_ACC_TILE, I.n);
     for (int64_t g = e0 + 4 * (int64_t)threadIdx.x; g < e1; g += 4 * TPB) {
-        float x[4], a[4];
+        float x[4], a[4] = {0.0f, 0.0f, 0.0f, 0.0f};
         ld4(I.src, g, e1, I.vec, x);
-        ld4(I.dst, g, e1, I.vec, a);
+        if (!I.store) ld4(I.dst, g, e1, I.vec, a);
 #pragma unroll
         for (int j = 0; j < 4; j++) a[j] = __fmaf_rn(I.w, x[j], a[j]);
         st4(I.dst, g, e1, I.vec, a);

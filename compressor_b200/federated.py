@@ -68,6 +68,15 @@ def set_client_weight(lib, decoder_handle, aggregate_ptr: int, c_offsets, n: int
         raise RuntimeError(f"falcom_set_aggregate failed ({rc}): {lib.falcom_last_error(decoder_handle)}")
 
 
+def set_aggregate_store(lib, decoder_handle, store: bool) -> None:
+    """Store mode of the decoder's fused aggregate: True for the first client
+    of a round (the aggregate region is written, not read, so it needs no
+    clearing), False for the clients that follow (added)."""
+    rc = lib.falcom_set_aggregate_store(decoder_handle, 1 if store else 0)
+    if rc != 0:
+        raise RuntimeError(f"falcom_set_aggregate_store failed ({rc})")
+
+
 def allreduce_aggregate(aggregate, dist=None, group=None) -> None:
     """Sum of the per-rank aggregates on every rank (no-op on one rank)."""
     if dist is not None and dist.is_initialized() and dist.get_world_size(group) > 1:

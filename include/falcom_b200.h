@@ -99,6 +99,18 @@ const char *falcom_kernel_name(int id);
 int falcom_set_aggregate(MomentumCompressor *mc, float *aggregate, const size_t *offsets, size_t n,
                          float weight);
 
+/* Store mode of the weighted aggregate.  No counterpart in the reference.
+ *   store = 0  (default) aggregate[...] += weight * decoded
+ *   store = 1  aggregate[...] = weight * decoded, computed as
+ *              fma(weight, decoded, +0): the same bits as clearing the region
+ *              to +0 and adding, without the clear or the read of the old
+ *              value.  For the first client of a round.
+ * Applies to the following decompress_batch calls until changed;
+ * falcom_set_aggregate(mc, NULL, ...) resets it to 0.  In store mode an item
+ * that is not added (failed, or not float32) leaves its region as it was.
+ * Returns 0, or ERROR_INVALID_PARAM for mc NULL or store not 0 / 1. */
+int falcom_set_aggregate_store(MomentumCompressor *mc, int store);
+
 /* Residual quantiser that allocates no memory.  No counterpart in the
  * reference interface.
  *

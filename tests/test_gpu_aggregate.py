@@ -109,3 +109,43 @@ def test_aggregate_with_device_inputs_and_outputs(product_lib):
     assert rel_l2(got, want) <= 1e-6, rel_l2(got, want)
     for c in (enc, dec, henc, hdec):
         c.close()
+
+
+def test_store_mode_equals_clear_then_add(product_lib):
+    """falcom_set_aggregate_store: the first client stored (weight * decoded)
+    into a buffer full of NaN, the others added, gives the same bits as
+    clearing the buffer and adding every client; regions of items that are
+    not added (int64) keep their old contents in store mode.  Two rounds."""
+    names = [n for n, _ in SHAPES]
+    sizes = [int(np.prod(s)) for _, s in SHAPES]
+    offsets = np.concatenate([[0], np.cumsum(sizes)[:-1]]).astype(np.uint64)
+    total = int(sum(sizes))
+    weights = [0.5, 0.3, 0.2]
+    encs = [Codec(product_lib, client=f"c{c}", param_count_threshold=16) for c in range(3)]
+    add_srv = Codec(product_lib, client="server", param_count_threshold=16)
+    st_srv = Codec(product_lib, client="server", param_count_threshold=16)
+    assert st_srv.lib.falcom_set_aggregate_store(st_srv.h, 2) == -4
+    off_c = (ctypes.c_size_t * len(names))(*[int(o) for o in offsets])
+    for t in range(2):
+        a = torch.zeros(total, dtype=torch.float32, device="cuda")
+        b = torch.full((total,), float("nan"), dtype=torch.float32, device="cuda")
+        for c in range(3):
+            ret, layers, errs = encs[c].compress_batch(names, _round_inputs(c, t))
+            assert ret == 0, errs
+            for srv, buf in ((add_srv, a), (st_srv, b)):
+                assert srv.lib.falcom_set_aggregate(srv.h, ctypes.c_void_p(buf.data_ptr()), off_c, len(names),
+                                                    weights[c]) == 0
+            assert st_srv.lib.falcom_set_aggregate_store(st_srv.h, 1 if c == 0 else 0) == 0
+            assert add_srv.decompress_batch(names, layers, client=f"c{c}")[0] == 0
+            assert st_srv.decompress_batch(names, layers, client=f"c{c}")[0] == 0
+        torch.cuda.synchronize()
+        ga, gb = a.cpu().numpy(), b.cpu().numpy()
+        for i, (name, _) in enumerate(SHAPES):
+            ra, rb = ga[offsets[i]:offsets[i] + sizes[i]], gb[offsets[i]:offsets[i] + sizes[i]]
+            if name.endswith("num_batches_tracked"):
+                assert np.isnan(rb).all()                  # not added: left as it was
+            else:
+                assert np.array_equal(ra.view(np.uint32), rb.view(np.uint32)), name
+    assert st_srv.lib.falcom_set_aggregate(st_srv.h, None, None, 0, 0.0) == 0   # also resets the store mode
+    for e in encs:
+        e.close()
