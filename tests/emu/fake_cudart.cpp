@@ -224,3 +224,11 @@ cudaError_t cudaGetDriverEntryPoint(const char *, void **fp, unsigned long long,
 }
 
 }  // extern "C"
+
+// Test hooks of the emulation library: "device" memory for arguments that
+// the library checks to be device memory (the fused aggregate).
+extern "C" __attribute__((visibility("default"))) void *emu_device_alloc(size_t n) {
+    void *p = nullptr;
+    return cudaMalloc(&p, n) == cudaSuccess ? p : nullptr;
+}
+extern "C" __attribute__((visibility("default"))) void emu_device_free(void *p) { cudaFree(p); }

@@ -89,3 +89,59 @@ def test_emulated_noalloc_matches_batch_payload(emu_lib):
     es, ec = ob.quantize(x, 127)
     assert scale == es and np.array_equal(codes, ec)
     c.close()
+
+
+def test_emulated_aggregate_add_and_store(emu_lib):
+    """Fused weighted aggregate of the decoder (k_accumulate): three clients
+    added into a cleared buffer equal the host's fma chain bit for bit, and
+    the first client in store mode over a NaN-filled buffer gives the same
+    bits; the int64 item is never added."""
+    import ctypes
+    lib = ctypes.CDLL(emu_lib)
+    lib.emu_device_alloc.restype = ctypes.c_void_p
+    lib.emu_device_alloc.argtypes = [ctypes.c_size_t]
+    lib.emu_device_free.argtypes = [ctypes.c_void_p]
+    shapes = [("l1.conv.weight", (16, 8, 3, 3)), ("l1.bn.bias", (16,)), ("l2.conv.weight", (32, 16, 1, 1)),
+              ("fc.weight", (10, 64)), ("l1.bn.num_batches_tracked", (1,))]
+    names = [n for n, _ in shapes]
+    sizes = [int(np.prod(s)) for _, s in shapes]
+    offs = np.concatenate([[0], np.cumsum(sizes)[:-1]]).astype(int)
+    total = int(sum(sizes))
+    off_c = (ctypes.c_size_t * len(names))(*[int(o) for o in offs])
+    weights = [0.5, 0.3, 0.2]
+    encs = [Codec(emu_lib, client=f"c{c}", param_count_threshold=16) for c in range(3)]
+    add_srv = Codec(emu_lib, client="server", param_count_threshold=16)
+    st_srv = Codec(emu_lib, client="server", param_count_threshold=16)
+    pa, pb = lib.emu_device_alloc(4 * total), lib.emu_device_alloc(4 * total)
+    a = np.ctypeslib.as_array((ctypes.c_float * total).from_address(pa))
+    b = np.ctypeslib.as_array((ctypes.c_float * total).from_address(pb))
+    rng = np.random.default_rng(3)
+    for t in range(2):
+        a[:] = 0.0
+        b[:] = np.nan
+        want = np.zeros(total, np.float32)
+        for c in range(3):
+            xs = [np.array([t + 1], np.int64) if n.endswith("tracked") else
+                  (rng.standard_normal(s) * 1e-3).astype(np.float32) for n, s in shapes]
+            ret, layers, errs = encs[c].compress_batch(names, xs)
+            assert ret == 0, errs
+            for srv, p in ((add_srv, pa), (st_srv, pb)):
+                assert srv.lib.falcom_set_aggregate(srv.h, ctypes.c_void_p(p), off_c, len(names), weights[c]) == 0
+            assert st_srv.lib.falcom_set_aggregate_store(st_srv.h, 1 if c == 0 else 0) == 0
+            ret, outs = add_srv.decompress_batch(names, layers, client=f"c{c}")
+            assert ret == 0 and st_srv.decompress_batch(names, layers, client=f"c{c}")[0] == 0
+            for i, o in enumerate(outs):
+                if o.dtype == np.float32:   # the kernel's fma chain, restated with exact float64 products
+                    seg = want[offs[i]:offs[i] + sizes[i]]
+                    seg[:] = (np.float64(np.float32(weights[c])) * o.reshape(-1) + seg).astype(np.float32)
+        for i, (n, _) in enumerate(shapes):
+            ra, rb, rw = (v[offs[i]:offs[i] + sizes[i]] for v in (a, b, want))
+            if n.endswith("tracked"):
+                assert not ra.any() and np.isnan(rb).all()
+            else:
+                assert np.array_equal(ra.view(np.uint32), rb.view(np.uint32)), n
+                assert np.array_equal(ra.view(np.uint32), rw.view(np.uint32)), n
+    for c in encs + [add_srv, st_srv]:
+        c.close()
+    lib.emu_device_free(pa)
+    lib.emu_device_free(pb)
