@@ -505,6 +505,8 @@ def bind_extensions(lib: ctypes.CDLL) -> None:
     lib.falcom_set_aggregate.restype = ctypes.c_int
     lib.falcom_set_aggregate_store.argtypes = [c_vp, ctypes.c_int]
     lib.falcom_set_aggregate_store.restype = ctypes.c_int
+    lib.falcom_set_aggregate_only.argtypes = [c_vp, ctypes.c_int]
+    lib.falcom_set_aggregate_only.restype = ctypes.c_int
     lib.falcom_state_save.argtypes = [c_vp, ctypes.c_char_p]
     lib.falcom_state_save.restype = ctypes.c_int
     lib.falcom_state_load.argtypes = [c_vp, ctypes.c_char_p]

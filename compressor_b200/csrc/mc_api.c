@@ -182,8 +182,7 @@ MC_EXPORT void momentum_compressor_destroy(MomentumCompressor *mc) {
         if (mc->ev_in[i]) cudaEventDestroy(mc->ev_in[i]);
         if (mc->ev_done[i]) cudaEventDestroy(mc->ev_done[i]);
     }
-    for (int k = 0; k < 2; k++)
-        if (mc->tab_ev[k]) cudaEventDestroy(mc->tab_ev[k]);
+    if (mc->tab_ev[0]) cudaEventDestroy(mc->tab_ev[0]);
     for (int i = 0; i < 2 * MC_KTRACE_MAX; i++)
         if (mc->ktrace.ev[i]) cudaEventDestroy((cudaEvent_t)mc->ktrace.ev[i]);
     free(mc->stats.prediction_ratios);
@@ -986,6 +985,7 @@ MC_EXPORT int falcom_set_aggregate(MomentumCompressor *mc, float *aggregate, con
         mc->agg = NULL;
         mc->agg_n = 0;
         mc->agg_store = 0;
+        mc->agg_no_output = 0;
         return ERROR_NONE;
     }
     int d = -1;
@@ -1011,9 +1011,15 @@ MC_EXPORT int falcom_set_aggregate_store(MomentumCompressor *mc, int store) {
     return ERROR_NONE;
 }
 
+MC_EXPORT int falcom_set_aggregate_only(MomentumCompressor *mc, int on) {
+    if (!mc || (on != 0 && on != 1)) return ERROR_INVALID_PARAM;
+    mc->agg_no_output = on;
+    return ERROR_NONE;
+}
+
 /* ----------------------------------------------------------- kernel timing */
 static const char *k_names[MC_NKERN] = {"enc_pass1_stats_sign", "enc_pass2_variance", "enc_pass3_predict",
-                                        "enc_pass4_quantize_pack", "dec_accumulate", "frames_expand",
+                                        "enc_pass4_quantize_pack", "frames_expand",
                                         "dec_prefix", "dec_reconstruct", "enc_finalize"};
 
 mc_ktrace *mc_trace_begin(MomentumCompressor *mc) {

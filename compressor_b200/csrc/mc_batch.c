@@ -48,10 +48,9 @@ static void prof_print(prof_t *p, const char *tag) {
     for (int i = 1; i < p->n; i++) fprintf(stderr, " %s=%.1f", p->what[i], p->t[i] - p->t[i - 1]);
     fprintf(stderr, "\n");
 }
-/* The pinned table buffers (scratch slots SH_TABLES, SH_ACC) are rewritten
- * by every call; event k marks the last upload out of buffer k, so a call
- * waits for that copy only, not for other work the caller queued on the
- * stream. */
+/* The pinned table buffer (scratch slot SH_TABLES) is rewritten by every
+ * call; event k (k = 0) marks the last upload out of it, so a call waits
+ * for that copy only, not for other work the caller queued on the stream. */
 void mc_tables_wait(MomentumCompressor *mc, int k) {
     if (mc->tab_ev_live[k] && cudaEventSynchronize(mc->tab_ev[k]) != cudaSuccess) {
         (void)cudaGetLastError();
@@ -86,9 +85,8 @@ enum {
     SD_DSTAGE,       /* decoder: staged payload bytes */
     SD_DOUT,         /* decoder: contiguous decoded output before the host copy */
     SD_DCONTENT,     /* decoder: frame contents expanded on the device */
-    SD_ACC,          /* decoder: aggregate accumulation tables */
 };
-enum { SH_TABLES = 0, SH_RESULTS, SH_STAGE, SH_ACC };
+enum { SH_TABLES = 0, SH_RESULTS, SH_STAGE };
 
 /* ------------------------------------------------------------ list cache */
 static uint64_t sig_mix(uint64_t h, uint64_t v) {
@@ -1134,6 +1132,8 @@ typedef struct {
     int data_mode;            /* lossless frame: MC_BM_* */
     size_t sg_len;            /* sign content bytes of a Raw-block sign frame */
     int foreign;              /* a frame lives in device memory the library does not own */
+    float *agg;               /* fused aggregate region of this item (float32 items), NULL */
+    int agg_only;             /* decoded into the aggregate only: no output array */
     const char *why;
 } dplan;
 
@@ -1255,60 +1255,6 @@ static size_t sign_content_len(size_t size) {
     return (s > 0 && frame_blocks(s) == nb) ? s : 0;
 }
 
-
-/* Adds agg_w * (decoded item) into the instance's aggregate for every
- * decoded float32 item of a segment whose batch index has an offset.  The
- * source is the device copy of the decoded tensor; queued on the instance's
- * stream after the segment's commit, so only successful items contribute. */
-static int dec_accumulate(MomentumCompressor *mc, const dplan *D, size_t n, NDArray **out, size_t base,
-                          const uint8_t *dout) {
-    size_t m = 0;
-    int ntiles = 0;
-    for (size_t i = 0; i < n; i++) {
-        if (!out[i] || D[i].dt != DTYPE_FLOAT32 || base + i >= mc->agg_n) continue;
-        m++;
-        ntiles += (int)((D[i].n + MC_ACC_TILE - 1) / MC_ACC_TILE);
-    }
-    if (m == 0 || ntiles == 0) return ERROR_NONE;
-    size_t t_items = ALIGN_UP(m * sizeof(mc_acc_item), 256);
-    size_t t_ti = ALIGN_UP((size_t)ntiles * 4, 256);
-    uint8_t *ht = (uint8_t *)scratch_host(&mc->scratch, SH_ACC, t_items + t_ti);
-    uint8_t *dt = (uint8_t *)scratch_dev(&mc->scratch, SD_ACC, t_items + t_ti);
-    if (!ht || !dt) return ERROR_ALLOCATION;
-    mc_tables_wait(mc, 1);
-    mc_acc_item *hi = (mc_acc_item *)ht;
-    int32_t *h_ti = (int32_t *)(ht + t_items);
-    size_t j = 0;
-    int tb = 0;
-    for (size_t i = 0; i < n; i++) {
-        if (!out[i] || D[i].dt != DTYPE_FLOAT32 || base + i >= mc->agg_n) continue;
-        mc_acc_item *A = &hi[j];
-        A->src = (const float *)(dout + D[i].out_off);
-        A->dst = mc->agg + mc->agg_off[base + i];
-        A->n = (int64_t)D[i].n;
-        A->w = mc->agg_w;
-        A->store = mc->agg_store;
-        A->tile_base = tb;
-        A->vec = ((((uintptr_t)A->src) | ((uintptr_t)A->dst)) & 15) == 0;
-        const int nt = (int)((D[i].n + MC_ACC_TILE - 1) / MC_ACC_TILE);
-        for (int t = 0; t < nt; t++) h_ti[tb + t] = (int32_t)j;
-        tb += nt;
-        j++;
-    }
-    if (cudaMemcpyAsync(dt, ht, t_items + t_ti, cudaMemcpyHostToDevice, mc->stream) != cudaSuccess ||
-        mc_tables_mark(mc, 1, mc->stream) != 0)
-        return ERROR_DECOMPRESSION;
-    mc_ktrace *tr = mc_trace_begin(mc);
-    int k = mc_launch_accumulate((const mc_acc_item *)dt, (const int32_t *)(dt + t_items), ntiles, mc->stream, tr);
-    if (k < 0) return ERROR_DECOMPRESSION;
-    if (tr) {
-        cudaStreamSynchronize(mc->stream);
-        mc_trace_end(mc);
-    }
-    mc->last_launches += k;
-    mc->total_launches += k;
-    return ERROR_NONE;
-}
 
 #define DEC_RETRY_EXPAND 1
 static int dec_segment(MomentumCompressor *mc, const BatchItem *items, size_t n, const char *client,
@@ -1539,8 +1485,15 @@ static int dec_segment(MomentumCompressor *mc, const BatchItem *items, size_t n,
         }
         d->tile_base = ntiles;
         ntiles += d->ntiles;
+        /* float32 items with an aggregate offset are added into the fused
+         * aggregate by the reconstruct kernel; without decode outputs they
+         * get no output slot */
+        if (mc->agg && d->dt == DTYPE_FLOAT32 && base + i < mc->agg_n) {
+            d->agg = mc->agg + mc->agg_off[base + i];
+            d->agg_only = mc->agg_no_output;
+        }
         d->out_off = out_bytes;
-        out_bytes = ALIGN_UP(out_bytes + d->bytes, SLOT_ALIGN);
+        if (!d->agg_only) out_bytes = ALIGN_UP(out_bytes + d->bytes, SLOT_ALIGN);
     }
     uint8_t *content = content_bytes ? (uint8_t *)scratch_dev(&mc->scratch, SD_DCONTENT, content_bytes) : NULL;
     mc_arena *oarena = NULL;
@@ -1612,7 +1565,13 @@ static int dec_segment(MomentumCompressor *mc, const BatchItem *items, size_t n,
         I->tile_base = d->tile_base;
         I->elem_bytes = (int32_t)mc_dtype_size(d->dt);
         I->hist_out = d->hist->dev;
-        I->out = dout + d->out_off;
+        I->out = d->agg_only ? NULL : dout + d->out_off;
+        if (d->agg) {
+            I->agg = d->agg;
+            I->agg_w = mc->agg_w;
+            I->agg_store = mc->agg_store;
+            I->agg_vec = (((uintptr_t)d->agg) & 15) == 0;
+        }
         if (d->dcodec == MC_DC_Q8 || d->dcodec == MC_DC_INT4) {
             I->scale_ptr = (const float *)d->d_data;
             I->data = d->d_data + 4;
@@ -1756,6 +1715,7 @@ static int dec_segment(MomentumCompressor *mc, const BatchItem *items, size_t n,
                 if (!D[i].ok) continue;
                 na += D[i].ntiles;
                 if (D[i].kind == MC_D_MOMENTUM) nm += D[i].ntiles;
+                if (D[i].agg_only) continue;
                 if (o0 == (size_t)-1) o0 = D[i].out_off;
                 o1 = D[i].out_off + D[i].bytes;
             }
@@ -1843,6 +1803,10 @@ static int dec_segment(MomentumCompressor *mc, const BatchItem *items, size_t n,
             d->ok = 0;
             continue;
         }
+        if (d->agg_only) {
+            /* decoded into the aggregate only: no array, the state commits */
+            (*n_ok)++;
+        } else {
         if (!oarena->objs) {   /* arrays and shapes: one block owned by the output arena */
             oarena->objs = calloc(n, sizeof(NDArray) + MAX_NDIM * sizeof(size_t));
             if (!oarena->objs) { rc = ERROR_ALLOCATION; goto fail_arena; }
@@ -1858,6 +1822,7 @@ static int dec_segment(MomentumCompressor *mc, const BatchItem *items, size_t n,
         out[i] = a;
         handed++;
         (*n_ok)++;
+        }
         int commit_hist = 1;
         if (d->kind == MC_D_MOMENTUM) {
             /* reference :3266-3269: no predicted kernel -> residual returned,
@@ -1890,11 +1855,6 @@ static int dec_segment(MomentumCompressor *mc, const BatchItem *items, size_t n,
     if (handed > 0) arena_retain(oarena, handed - 1);
     else arena_release(oarena);
     oarena = NULL;
-    if (mc->agg && dec_accumulate(mc, D, n, out, base, dout) != ERROR_NONE) {
-        /* outputs and state stand; the call reports the failed aggregate */
-        mc_set_error(mc, "Batch decompress: aggregate update failed");
-        mc->agg_failed = 1;
-    }
     prof_mark(&prof, "commit");
     prof_print(&prof, "decompress");
     if (prof.on) {
@@ -1962,7 +1922,17 @@ int mc_decompress_items(MomentumCompressor *mc, const BatchItem *items, size_t n
         }
         if (b == a) b = a + 1;
         int r = dec_segment(mc, items + a, b - a, client, out + a, out_loc, &ok, 0, a);
-        if (r == DEC_RETRY_EXPAND) r = dec_segment(mc, items + a, b - a, client, out + a, out_loc, &ok, 1, a);
+        if (r == DEC_RETRY_EXPAND) {
+            /* the first attempt's reconstruct kernel already added into the
+             * aggregate: in add mode the retry cannot undo that, so the
+             * call reports the aggregate as invalid (store mode rewrites
+             * the same values) */
+            if (mc->agg && !mc->agg_store) {
+                mc_set_error(mc, "Batch decompress: aggregate invalid (frames re-read after a failed check)");
+                mc->agg_failed = 1;
+            }
+            r = dec_segment(mc, items + a, b - a, client, out + a, out_loc, &ok, 1, a);
+        }
         if (r != ERROR_NONE) {
             rc = r;
             for (size_t j = a; j < b; j++) {

@@ -156,6 +156,15 @@ typedef struct {
     float *mem_out;
     void *hist_out;             /* decoded tensor (becomes the history head) */
     void *out;                  /* optional second copy (device output), NULL */
+    /* fused server-side weighted aggregate of a float32 item (NULL: none):
+     * agg[e] = fma(agg_w, decoded[e], agg[e]), or with agg_store set
+     * fma(agg_w, decoded[e], +0) (agg not read: the bits of clearing to +0
+     * and adding) */
+    float *agg;
+    float agg_w;
+    int32_t agg_store;
+    int32_t agg_vec;            /* 1: agg is 16-byte aligned */
+    int32_t pad3;
     int64_t n;
     int64_t K;
     int64_t bm_bits;            /* min(bitmap content bytes*8, K) */
@@ -207,24 +216,10 @@ typedef struct {
     int32_t pad;
 } mc_dec_launch;
 
-/* Weighted accumulation of decoded tensors into an aggregate:
- * dst[e] = fma(w, src[e], dst[e]) for e < n, or with `store` set
- * dst[e] = fma(w, src[e], +0) (dst not read: the same bits as clearing dst to
- * +0 and adding); tiles of MC_ACC_TILE elements. */
-#define MC_ACC_TILE 8192
-typedef struct {
-    const float *src;
-    float *dst;
-    int64_t n;
-    float w;
-    int32_t tile_base;
-    int32_t vec;                /* 1: src and dst 16-byte aligned */
-    int32_t store;              /* 1: dst = w * src (dst not read) */
-} mc_acc_item;
 
 /* Optional per-kernel event trace (events created by the host). */
 enum {
-    MC_KT_ENC_PASS1 = 0, MC_KT_ENC_PASS2, MC_KT_ENC_PASS3, MC_KT_ENC_PASS4, MC_KT_ACCUM,
+    MC_KT_ENC_PASS1 = 0, MC_KT_ENC_PASS2, MC_KT_ENC_PASS3, MC_KT_ENC_PASS4,
     MC_KT_UNFRAME, MC_KT_DEC_PREFIX, MC_KT_DEC_RECON, MC_KT_ENC_FINAL, MC_NKERN
 };
 #define MC_KTRACE_MAX 64
@@ -239,8 +234,6 @@ typedef struct {
 int mc_launch_encode(const mc_enc_launch *L, void *stream, mc_ktrace *tr);
 int mc_launch_decode(const mc_dec_launch *L, void *stream, mc_ktrace *tr);
 int mc_launch_unframe(const mc_unframe_job *jobs, int njobs, void *stream, mc_ktrace *tr);
-int mc_launch_accumulate(const mc_acc_item *items, const int32_t *tile_item, int ntiles, void *stream,
-                         mc_ktrace *tr);
 
 /* Reusable device / pinned scratch owned by one compressor instance. */
 typedef struct {

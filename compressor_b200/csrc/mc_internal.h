@@ -144,11 +144,10 @@ struct MomentumCompressor {
 #define MC_MAX_CHUNKS 8
     cudaStream_t copy_in, copy_out;
     cudaEvent_t ev_in[MC_MAX_CHUNKS], ev_done[MC_MAX_CHUNKS];
-    /* recorded after the last upload from a pinned table buffer (0: item
-     * tables, 1: aggregate tables): a call waits on it (not on the whole
-     * stream) before rewriting the buffer */
-    cudaEvent_t tab_ev[2];
-    int tab_ev_live[2];
+    /* recorded after the last upload from the pinned table buffer: a call
+     * waits on it (not on the whole stream) before rewriting the buffer */
+    cudaEvent_t tab_ev[1];
+    int tab_ev_live[1];
     int residual_codec;      /* MC_CODEC_* */
     int frame_mode;          /* MC_FRAME_GPU / MC_FRAME_LIBZSTD */
     int payload_loc;
@@ -179,12 +178,14 @@ struct MomentumCompressor {
     mc_scratch scratch;
 
     /* server-side aggregate (falcom_set_aggregate): decoded float32 item i
-     * of every batch decompress is added, times agg_w, at agg + agg_off[i] */
+     * of every batch decompress is added, times agg_w, at agg + agg_off[i],
+     * by the reconstruct kernel itself */
     float *agg;
     size_t *agg_off;
     size_t agg_n;
     float agg_w;
-    int agg_store;   /* 1: the next batches store weight * decoded instead of adding */
+    int agg_store;      /* 1: the next batches store weight * decoded instead of adding */
+    int agg_no_output;  /* 1: items added into the aggregate get no decoded array */
     int agg_failed;
 
     /* per-kernel device time (falcom_set_kernel_timing) */

@@ -1698,6 +1698,18 @@ __device__ __forceinline__ void dec_resid4(const mc_dec_item &I, const uint8_t *
     }
 }
 
+// Fused server-side aggregate of a decoded quad at element g (I.agg != NULL):
+// agg = fma(w, decoded, agg), or fma(w, decoded, +0) in store mode (the old
+// value not read).  One rounding per element and client, the same bits as a
+// separate accumulate pass over the decoded tensor.
+__device__ __forceinline__ void agg_quad(const mc_dec_item &I, int64_t g, int64_t e1, const float (&v)[4]) {
+    float a[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    if (!I.agg_store) ld4(I.agg, g, e1, I.agg_vec != 0, a);
+#pragma unroll
+    for (int j = 0; j < 4; j++) a[j] = __fmaf_rn(I.agg_w, v[j], a[j]);
+    st4(I.agg, g, e1, I.agg_vec != 0, a);
+}
+
 // Sign bytes a reconstruct tile needs: its predicted kernels' bits start at
 // bit (tile_poff & 7) of the window; up to STAGE_ELEMS kernels per tile, plus
 // the read-ahead of the 5-byte gather.
@@ -1810,22 +1822,43 @@ __device__ void recon_tile(const mc_dec_launch &L, const StageDesc &d, const flo
             const float4 *p4 = (const float4 *)(prev + tr.e0);
             float4 *mo4 = (float4 *)(I.mem_out + tr.e0), *h4 = (float4 *)(hist + tr.e0);
             const uint64_t spol = l2_stream();   // read again next round only
-            float4 *o4 = out ? (float4 *)(out + tr.e0) : nullptr;
-            for (int q = threadIdx.x; q < nq; q += TPB) {
-                const QuadBits qb = quad_bits_full(s_m, s_d, (uint32_t)wb, k0, 4u * q, I.ks, I.ksdiv);
-                float r[4];
-                dec_resid4(I, codes, tr.e0 + 4 * q, tr.e1, scale, r);
-                const float4 mv = m4 ? m4[q] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-                float4 pv = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-                if (qb.f) pv = p4[q];
-                const float m0[4] = {mv.x, mv.y, mv.z, mv.w}, p[4] = {pv.x, pv.y, pv.z, pv.w};
-                float mo[4], rec[4];
-                quad(qb, r, m0, p, mo, rec);
-                st_f4(mo4 + q, make_float4(mo[0], mo[1], mo[2], mo[3]), spol);
-                const float4 rv = make_float4(rec[0], rec[1], rec[2], rec[3]);
-                st_f4(h4 + q, rv, spol);
-                if (o4) st_f4(o4 + q, rv, spol);
-            }
+            // one loop per destination set, so each keeps only the pointers it
+            // writes live: 0 output copy (or none), 1 aggregate, 2 both
+            auto quads = [&](auto dst) {
+                constexpr int M = decltype(dst)::value;
+                float4 *o4 = (M != 1 && out) ? (float4 *)(out + tr.e0) : nullptr;
+                float4 *a4 = M != 0 ? (float4 *)(I.agg + tr.e0) : nullptr;
+                const float aw = I.agg_w;
+                const bool astore = I.agg_store != 0, avec = I.agg_vec != 0;
+                for (int q = threadIdx.x; q < nq; q += TPB) {
+                    const QuadBits qb = quad_bits_full(s_m, s_d, (uint32_t)wb, k0, 4u * q, I.ks, I.ksdiv);
+                    float r[4];
+                    dec_resid4(I, codes, tr.e0 + 4 * q, tr.e1, scale, r);
+                    const float4 mv = m4 ? m4[q] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                    float4 pv = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                    if (qb.f) pv = p4[q];
+                    const float m0[4] = {mv.x, mv.y, mv.z, mv.w}, p[4] = {pv.x, pv.y, pv.z, pv.w};
+                    float mo[4], rec[4];
+                    quad(qb, r, m0, p, mo, rec);
+                    st_f4(mo4 + q, make_float4(mo[0], mo[1], mo[2], mo[3]), spol);
+                    const float4 rv = make_float4(rec[0], rec[1], rec[2], rec[3]);
+                    st_f4(h4 + q, rv, spol);
+                    if (M != 1 && o4) st_f4(o4 + q, rv, spol);
+                    if (M != 0) {
+                        if (avec) {
+                            float4 a = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                            if (!astore) a = a4[q];
+                            a4[q] = make_float4(__fmaf_rn(aw, rec[0], a.x), __fmaf_rn(aw, rec[1], a.y),
+                                                __fmaf_rn(aw, rec[2], a.z), __fmaf_rn(aw, rec[3], a.w));
+                        } else {
+                            agg_quad(I, tr.e0 + 4 * q, tr.e1, rec);
+                        }
+                    }
+                }
+            };
+            if (!I.agg) quads(std::integral_constant<int, 0>());
+            else if (!out) quads(std::integral_constant<int, 1>());
+            else quads(std::integral_constant<int, 2>());
         }
         const int64_t gstart = I.vec ? tr.e0 + 4 * (int64_t)nq : tr.e0;
         const int owner = I.vec ? nq % TPB : 0;
@@ -1841,6 +1874,15 @@ __device__ void recon_tile(const mc_dec_launch &L, const StageDesc &d, const flo
             st4(hist, g, tr.e1, I.vec, rec);
             if (out) st4(out, g, tr.e1, I.vec, rec);
         }
+        if (I.agg) {
+            // the aggregate of the same quads, from this thread's own history
+            // writes (kept out of the loop above, which holds more live values)
+            for (int64_t g = gstart + 4 * (int64_t)((threadIdx.x - owner + TPB) % TPB); g < tr.e1; g += 4 * TPB) {
+                float rec[4];
+                ld4(hist, g, tr.e1, I.vec, rec);
+                agg_quad(I, g, tr.e1, rec);
+            }
+        }
         return;
     }
     const int64_t e0 = (int64_t)t * I.tile_kernels;
@@ -1851,57 +1893,74 @@ __device__ void recon_tile(const mc_dec_launch &L, const StageDesc &d, const flo
             dec_resid4(I, I.data, g, e1, scale, r);
             st4(hist, g, e1, I.vec, r);
             if (out) st4(out, g, e1, I.vec, r);
+            if (I.agg) agg_quad(I, g, e1, r);
         }
         return;
     }
     // MC_D_COPY: bytes (tile in bytes)
-    const uint8_t *src = I.data;
-    uint8_t *h8 = (uint8_t *)I.hist_out, *o8 = (uint8_t *)I.out;
-    if (I.data_mode != MC_BM_WORDS) {
-        // lossless frame read in place: check the header the host assumed;
-        // a tile (at most 2^15 bytes) lies inside one block of the frame
-        if (t == 0 && threadIdx.x == 0 && check_frame(I.data_frame, I.data_mode, I.n) < 0)
-            L.results[ii].err = 1;
-        if (I.data_mode == MC_BM_RLE) {
-            const uint8_t v = (uint8_t)src_byte(I.data_frame, MC_BM_RLE, e0);
-            for (int64_t e = e0 + threadIdx.x; e < e1; e += TPB) {
-                h8[e] = v;
-                if (o8) o8[e] = v;
+    auto copy_tile = [&]() {
+        const uint8_t *src = I.data;
+        uint8_t *h8 = (uint8_t *)I.hist_out, *o8 = (uint8_t *)I.out;
+        if (I.data_mode != MC_BM_WORDS) {
+            // lossless frame read in place: check the header the host assumed;
+            // a tile (at most 2^15 bytes) lies inside one block of the frame
+            if (t == 0 && threadIdx.x == 0 && check_frame(I.data_frame, I.data_mode, I.n) < 0)
+                L.results[ii].err = 1;
+            if (I.data_mode == MC_BM_RLE) {
+                const uint8_t v = (uint8_t)src_byte(I.data_frame, MC_BM_RLE, e0);
+                for (int64_t e = e0 + threadIdx.x; e < e1; e += TPB) {
+                    h8[e] = v;
+                    if (o8) o8[e] = v;
+                }
+                return;
+            }
+            src = I.data_frame + fpos_raw(e0) - e0;   // byte e of this tile at src[e]
+        }
+        if (!I.vec && ((((uintptr_t)src | (uintptr_t)h8 | (uintptr_t)o8) & 3) == 0)) {
+            // 4-byte words (tiles are multiples of 16 bytes)
+            const int64_t w0 = e0 >> 2, w1 = e1 >> 2;
+            for (int64_t w = w0 + threadIdx.x; w < w1; w += TPB) {
+                const uint32_t x = ((const uint32_t *)src)[w];
+                ((uint32_t *)h8)[w] = x;
+                if (o8) ((uint32_t *)o8)[w] = x;
+            }
+            for (int64_t e = (w1 << 2) + threadIdx.x; e < e1; e += TPB) {
+                h8[e] = src[e];
+                if (o8) o8[e] = src[e];
             }
             return;
         }
-        src = I.data_frame + fpos_raw(e0) - e0;   // byte e of this tile at src[e]
-    }
-    if (!I.vec && ((((uintptr_t)src | (uintptr_t)h8 | (uintptr_t)o8) & 3) == 0)) {
-        // 4-byte words (tiles are multiples of 16 bytes)
-        const int64_t w0 = e0 >> 2, w1 = e1 >> 2;
-        for (int64_t w = w0 + threadIdx.x; w < w1; w += TPB) {
-            const uint32_t x = ((const uint32_t *)src)[w];
-            ((uint32_t *)h8)[w] = x;
-            if (o8) ((uint32_t *)o8)[w] = x;
+        if (I.vec) {
+            const int64_t v0 = e0 >> 4, v1 = e1 >> 4;
+            for (int64_t v = v0 + threadIdx.x; v < v1; v += TPB) {
+                const uint4 x = ((const uint4 *)src)[v];
+                ((uint4 *)h8)[v] = x;
+                if (o8) ((uint4 *)o8)[v] = x;
+            }
+            for (int64_t e = (v1 << 4) + threadIdx.x; e < e1; e += TPB) {
+                h8[e] = src[e];
+                if (o8) o8[e] = src[e];
+            }
+        } else {
+            for (int64_t e = e0 + threadIdx.x; e < e1; e += TPB) {
+                const uint8_t v = src[e];
+                h8[e] = v;
+                if (o8) o8[e] = v;
+            }
         }
-        for (int64_t e = (w1 << 2) + threadIdx.x; e < e1; e += TPB) {
-            h8[e] = src[e];
-            if (o8) o8[e] = src[e];
-        }
-        return;
-    }
-    if (I.vec) {
-        const int64_t v0 = e0 >> 4, v1 = e1 >> 4;
-        for (int64_t v = v0 + threadIdx.x; v < v1; v += TPB) {
-            const uint4 x = ((const uint4 *)src)[v];
-            ((uint4 *)h8)[v] = x;
-            if (o8) ((uint4 *)o8)[v] = x;
-        }
-        for (int64_t e = (v1 << 4) + threadIdx.x; e < e1; e += TPB) {
-            h8[e] = src[e];
-            if (o8) o8[e] = src[e];
-        }
-    } else {
-        for (int64_t e = e0 + threadIdx.x; e < e1; e += TPB) {
-            const uint8_t v = src[e];
-            h8[e] = v;
-            if (o8) o8[e] = v;
+    };
+    copy_tile();
+    if (I.agg) {
+        // float32 item: the aggregate from the history copy this CTA just
+        // wrote (visible to the whole CTA after the barrier); byte tiles
+        // of a float32 item start and end on element boundaries
+        __syncthreads();
+        const float *hf = (const float *)I.hist_out;
+        const int64_t f0 = e0 >> 2, f1 = e1 >> 2;
+        for (int64_t g = f0 + 4 * (int64_t)threadIdx.x; g < f1; g += 4 * TPB) {
+            float v[4];
+            ld4(hf, g, f1, true, v);
+            agg_quad(I, g, f1, v);
         }
     }
 }
@@ -1947,22 +2006,6 @@ __global__ void __launch_bounds__(TPB, 4) k_dec_recon(mc_dec_launch L) {
                         const uint8_t *codes = d.x0 ? xb + ((intptr_t)data - (intptr_t)dn16(d.x0)) : data;
                         recon_tile(L, d, buf, s_m, s_d, codes, s_scale);
                     });
-}
-
-// ------------------------------------------------------------- aggregate
-__global__ void __launch_bounds__(TPB) k_accumulate(const mc_acc_item *items, const int32_t *tile_item) {
-    const int gt = blockIdx.x;
-    const mc_acc_item I = items[tile_item[gt]];
-    const int64_t e0 = (int64_t)(gt - I.tile_base) * MC_ACC_TILE;
-    const int64_t e1 = min(e0 + MC_ACC_TILE, I.n);
-    for (int64_t g = e0 + 4 * (int64_t)threadIdx.x; g < e1; g += 4 * TPB) {
-        float x[4], a[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-        ld4(I.src, g, e1, I.vec, x);
-        if (!I.store) ld4(I.dst, g, e1, I.vec, a);
-#pragma unroll
-        for (int j = 0; j < 4; j++) a[j] = __fmaf_rn(I.w, x[j], a[j]);
-        st4(I.dst, g, e1, I.vec, a);
-    }
 }
 
 }  // namespace
@@ -2086,17 +2129,6 @@ extern "C" int mc_launch_unframe(const mc_unframe_job *jobs, int njobs, void *st
     cudaStream_t s = (cudaStream_t)stream;
     tr_begin(tr, MC_KT_UNFRAME, s);
     k_unframe<<<njobs, TPB, 0, s>>>(jobs);
-    tr_end(tr, s);
-    if (cudaGetLastError() != cudaSuccess) return -1;
-    return 1;
-}
-
-extern "C" int mc_launch_accumulate(const mc_acc_item *items, const int32_t *tile_item, int ntiles, void *stream,
-                                    mc_ktrace *tr) {
-    if (ntiles <= 0) return 0;
-    cudaStream_t s = (cudaStream_t)stream;
-    tr_begin(tr, MC_KT_ACCUM, s);
-    k_accumulate<<<ntiles, TPB, 0, s>>>(items, tile_item);
     tr_end(tr, s);
     if (cudaGetLastError() != cudaSuccess) return -1;
     return 1;

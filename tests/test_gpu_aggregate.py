@@ -149,3 +149,59 @@ def test_store_mode_equals_clear_then_add(product_lib):
     assert st_srv.lib.falcom_set_aggregate(st_srv.h, None, None, 0, 0.0) == 0   # also resets the store mode
     for e in encs:
         e.close()
+
+
+def test_aggregate_only_device_path_exact(product_lib):
+    """Aggregate-only decoding (falcom_set_aggregate_only) on device-resident
+    inputs and payloads, the federated server's path: no decoded arrays are
+    returned, the history still advances, and with two clients of weight 0.5
+    (first stored, second added) the aggregate equals 0.5 * (x1 + x2) in
+    float32 bit for bit, x1 / x2 being the same clients' decodes from a
+    second server that returns arrays.  Three rounds, so rounds 2 and 3
+    decode momentum-predicted layers against the aggregate-only server's own
+    history."""
+    from compressor_b200.abi import PreparedBatch, ndarray_to_numpy
+    names = [n for n, s in SHAPES if not n.endswith("num_batches_tracked")]
+    shapes = [s for n, s in SHAPES if not n.endswith("num_batches_tracked")]
+    sizes = [int(np.prod(s)) for s in shapes]
+    # offsets padded to 4 elements (16-byte aligned regions, vector stores)
+    offs, o = [], 0
+    for n_ in sizes:
+        offs.append(o)
+        o = (o + n_ + 3) // 4 * 4
+    total = o
+    encs = [Codec(product_lib, client=f"c{c}", param_count_threshold=16) for c in range(2)]
+    srv = Codec(product_lib, client="server", param_count_threshold=16)
+    ref = Codec(product_lib, client="server", param_count_threshold=16)
+    assert ref.lib.falcom_set_output_location(ref.h, 1) == 0            # decoded arrays in host memory
+    pb = PreparedBatch(srv.lib, names, shapes)
+    off_c = (ctypes.c_size_t * len(names))(*offs)
+    agg = torch.full((total,), float("nan"), dtype=torch.float32, device="cuda")
+    for t in range(3):
+        decoded = []
+        for c in range(2):
+            xs = [seeded(s, 900 + 100 * c + 10 * t + i) for i, s in enumerate(shapes)]
+            flat = torch.from_numpy(np.concatenate([x.reshape(-1) for x in xs])).cuda()
+            torch.cuda.synchronize()
+            pb.set_pointers(flat.data_ptr(), [4 * int(v) for v in np.concatenate([[0], np.cumsum(sizes)[:-1]])])
+            assert pb.compress(encs[c].h, f"c{c}".encode()) == 0
+            assert srv.lib.falcom_set_aggregate(srv.h, ctypes.c_void_p(agg.data_ptr()), off_c, len(names), 0.5) == 0
+            assert srv.lib.falcom_set_aggregate_store(srv.h, 1 if c == 0 else 0) == 0
+            assert srv.lib.falcom_set_aggregate_only(srv.h, 1) == 0
+            assert pb.decompress(srv.h, f"c{c}".encode()) == 0
+            assert all(not pb.outs[i] for i in range(len(names)))      # no decoded arrays
+            # the same payloads through a server that returns arrays
+            rc = ref.lib.momentum_compressor_decompress_batch(ref.h, pb.items, len(names), f"c{c}".encode(),
+                                                              pb.outs)
+            assert rc == 0
+            torch.cuda.synchronize()
+            decoded.append([ndarray_to_numpy(pb.outs[i]).reshape(-1).copy() for i in range(len(names))])
+            pb.release()
+        got = agg.cpu().numpy()
+        for i in range(len(names)):
+            want = np.float32(0.5) * (decoded[0][i] + decoded[1][i])
+            seg = got[offs[i]:offs[i] + sizes[i]]
+            assert np.array_equal(seg.view(np.uint32), want.astype(np.float32).view(np.uint32)), (t, names[i])
+    assert srv.lib.falcom_set_aggregate_only(srv.h, 2) == -4
+    for c in encs + [srv, ref]:
+        c.close()

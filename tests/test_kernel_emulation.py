@@ -92,10 +92,12 @@ def test_emulated_noalloc_matches_batch_payload(emu_lib):
 
 
 def test_emulated_aggregate_add_and_store(emu_lib):
-    """Fused weighted aggregate of the decoder (k_accumulate): three clients
-    added into a cleared buffer equal the host's fma chain bit for bit, and
-    the first client in store mode over a NaN-filled buffer gives the same
-    bits; the int64 item is never added."""
+    """Weighted aggregate fused into the decoder's reconstruct kernel: three
+    clients added into a cleared buffer equal the host's fma chain bit for
+    bit; the first client in store mode over a NaN-filled buffer gives the
+    same bits, and so does a third server in aggregate-only mode (no decoded
+    arrays for the float32 items, the int64 item still returned); the int64
+    item is never added."""
     import ctypes
     lib = ctypes.CDLL(emu_lib)
     lib.emu_device_alloc.restype = ctypes.c_void_p
@@ -112,36 +114,46 @@ def test_emulated_aggregate_add_and_store(emu_lib):
     encs = [Codec(emu_lib, client=f"c{c}", param_count_threshold=16) for c in range(3)]
     add_srv = Codec(emu_lib, client="server", param_count_threshold=16)
     st_srv = Codec(emu_lib, client="server", param_count_threshold=16)
-    pa, pb = lib.emu_device_alloc(4 * total), lib.emu_device_alloc(4 * total)
+    ao_srv = Codec(emu_lib, client="server", param_count_threshold=16)
+    pa, pb, pc = (lib.emu_device_alloc(4 * total) for _ in range(3))
     a = np.ctypeslib.as_array((ctypes.c_float * total).from_address(pa))
     b = np.ctypeslib.as_array((ctypes.c_float * total).from_address(pb))
+    ao = np.ctypeslib.as_array((ctypes.c_float * total).from_address(pc))
     rng = np.random.default_rng(3)
     for t in range(2):
         a[:] = 0.0
         b[:] = np.nan
+        ao[:] = np.nan
         want = np.zeros(total, np.float32)
         for c in range(3):
             xs = [np.array([t + 1], np.int64) if n.endswith("tracked") else
                   (rng.standard_normal(s) * 1e-3).astype(np.float32) for n, s in shapes]
             ret, layers, errs = encs[c].compress_batch(names, xs)
             assert ret == 0, errs
-            for srv, p in ((add_srv, pa), (st_srv, pb)):
+            for srv, p in ((add_srv, pa), (st_srv, pb), (ao_srv, pc)):
                 assert srv.lib.falcom_set_aggregate(srv.h, ctypes.c_void_p(p), off_c, len(names), weights[c]) == 0
-            assert st_srv.lib.falcom_set_aggregate_store(st_srv.h, 1 if c == 0 else 0) == 0
+            for srv in (st_srv, ao_srv):
+                assert srv.lib.falcom_set_aggregate_store(srv.h, 1 if c == 0 else 0) == 0
+            assert ao_srv.lib.falcom_set_aggregate_only(ao_srv.h, 1) == 0
             ret, outs = add_srv.decompress_batch(names, layers, client=f"c{c}")
             assert ret == 0 and st_srv.decompress_batch(names, layers, client=f"c{c}")[0] == 0
+            ret, ao_outs = ao_srv.decompress_batch(names, layers, client=f"c{c}")
+            assert ret == 0
+            for (n, _), o in zip(shapes, ao_outs):
+                assert (o is not None) == n.endswith("tracked"), n
             for i, o in enumerate(outs):
                 if o.dtype == np.float32:   # the kernel's fma chain, restated with exact float64 products
                     seg = want[offs[i]:offs[i] + sizes[i]]
                     seg[:] = (np.float64(np.float32(weights[c])) * o.reshape(-1) + seg).astype(np.float32)
         for i, (n, _) in enumerate(shapes):
-            ra, rb, rw = (v[offs[i]:offs[i] + sizes[i]] for v in (a, b, want))
+            ra, rb, rc, rw = (v[offs[i]:offs[i] + sizes[i]] for v in (a, b, ao, want))
             if n.endswith("tracked"):
-                assert not ra.any() and np.isnan(rb).all()
+                assert not ra.any() and np.isnan(rb).all() and np.isnan(rc).all()
             else:
                 assert np.array_equal(ra.view(np.uint32), rb.view(np.uint32)), n
+                assert np.array_equal(ra.view(np.uint32), rc.view(np.uint32)), n
                 assert np.array_equal(ra.view(np.uint32), rw.view(np.uint32)), n
-    for c in encs + [add_srv, st_srv]:
+    for c in encs + [add_srv, st_srv, ao_srv]:
         c.close()
-    lib.emu_device_free(pa)
-    lib.emu_device_free(pb)
+    for p in (pa, pb, pc):
+        lib.emu_device_free(p)
