@@ -16,14 +16,16 @@
 // call; this entry point only launches kernels on the caller's stream.
 //
 // Scratch lives in a file-scope __device__ array (g_quant_scratch, 65,792
-// bytes per device): one max|r| slot per 8192-element tile, an arrival
-// counter and the scale.  Its size bounds n at FALCOM_NOALLOC_MAX_ELEMS.
+// bytes per device): one max|r| slot per 8192-element tile and the scale.
+// Its size bounds n at FALCOM_NOALLOC_MAX_ELEMS.  Every call writes each slot
+// it reads before reading it, so nothing has to start at zero and a call
+// that was cut short leaves nothing behind that a later call depends on.
 //
-// Two kernels, both on the caller's stream:
-//   k_na_scale  per-tile max|r|; the last tile to finish reduces the tile
-//               maxima, computes the scale, writes it to out[0..4) and
-//               returns the arrival counter to zero
-//   k_na_codes  codes from the scale
+// Three kernels, all on the caller's stream:
+//   k_na_tiles   per-tile max|r| into the tile's slot
+//   k_na_scale   one CTA: max over the tile slots, the scale into out[0..4)
+//                and into the scale slot
+//   k_na_codes   codes from the scale
 // HBM-bound: 4 bytes read twice and 1 (q8) or 1/2 (int4) byte written per
 // element; the second read of a residual under the 126 MB L2 hits in L2.
 
@@ -31,7 +33,6 @@
 #include <stdint.h>
 #include <stdio.h>
 
-#include <atomic>
 #include <mutex>
 
 #include "falcom_b200.h"
@@ -44,12 +45,11 @@
 
 static_assert(NA_MAX_ELEMS == FALCOM_NOALLOC_MAX_ELEMS, "scratch bound and public limit differ");
 
-// Words [0, NA_MAX_TILES): per-tile max|r| (float bits).  Word NA_MAX_TILES:
-// arrival counter of k_na_scale, which must be zero when a call starts; it is
-// zero at module load and k_na_scale's last tile sets it back to zero.  Word
-// NA_MAX_TILES + 1: the scale of the current call.  The rest is padding.
-#define NA_TICKET NA_MAX_TILES
-#define NA_SCALE (NA_MAX_TILES + 1)
+// Words [0, NA_MAX_TILES): per-tile max|r| (float bits), written by
+// k_na_tiles for the call's tiles before k_na_scale reads them.  Word
+// NA_SCALE: the scale of the current call, written by k_na_scale before
+// k_na_codes reads it.  The rest is padding.
+#define NA_SCALE NA_MAX_TILES
 #define NA_SCRATCH_WORDS (NA_MAX_TILES + 64)
 static __device__ __align__(256) uint32_t g_quant_scratch[NA_SCRATCH_WORDS];
 
@@ -78,12 +78,10 @@ __device__ __forceinline__ int na_quant(float r, float scale, float qm) {
     return (int)v;
 }
 
-__global__ void __launch_bounds__(NA_TPB) k_na_scale(const float *__restrict__ x, int64_t n, int vec, int qmax,
-                                                     uint8_t *__restrict__ out, uint32_t *__restrict__ scratch) {
+__global__ void __launch_bounds__(NA_TPB) k_na_tiles(const float *__restrict__ x, int64_t n, int vec,
+                                                     uint32_t *__restrict__ scratch) {
     __shared__ float sh[NA_TPB / 32];
-    __shared__ int last;
     const int t = blockIdx.x;
-    const int ntiles = gridDim.x;
     const int64_t e0 = (int64_t)t * NA_TILE;
     const int64_t e1 = min(e0 + (int64_t)NA_TILE, n);
     float m = 0.0f;
@@ -100,14 +98,13 @@ __global__ void __launch_bounds__(NA_TPB) k_na_scale(const float *__restrict__ x
         for (int64_t g = e0 + threadIdx.x; g < e1; g += NA_TPB) m = fmaxf(m, fabsf(x[g]));
     }
     m = na_block_max(m, sh);
-    if (threadIdx.x == 0) {
-        scratch[t] = __float_as_uint(m);
-        __threadfence();
-        last = atomicAdd(&scratch[NA_TICKET], 1u) == (uint32_t)(ntiles - 1);
-    }
-    __syncthreads();
-    if (!last) return;
-    __threadfence();
+    if (threadIdx.x == 0) scratch[t] = __float_as_uint(m);
+}
+
+// One CTA: max over the ntiles tile slots, then the scale.
+__global__ void __launch_bounds__(NA_TPB) k_na_scale(int ntiles, int qmax, uint8_t *__restrict__ out,
+                                                     uint32_t *__restrict__ scratch) {
+    __shared__ float sh[NA_TPB / 32];
     float a = 0.0f;
     for (int i = threadIdx.x; i < ntiles; i += NA_TPB) a = fmaxf(a, __uint_as_float(__ldcg(&scratch[i])));
     a = na_block_max(a, sh);
@@ -119,7 +116,6 @@ __global__ void __launch_bounds__(NA_TPB) k_na_scale(const float *__restrict__ x
         out[2] = (uint8_t)(b >> 16);
         out[3] = (uint8_t)(b >> 24);
         scratch[NA_SCALE] = b;
-        scratch[NA_TICKET] = 0u;
     }
 }
 
@@ -160,10 +156,38 @@ __global__ void __launch_bounds__(NA_TPB) k_na_codes(const float *__restrict__ x
 }
 
 std::mutex g_setup_mu;
-std::atomic<uint32_t *> g_scratch_ptr[NA_MAX_DEVICES];
+struct ScratchSlot {
+    void *ctx;            // CUDA context the address belongs to
+    uint32_t *ptr;        // device address of g_quant_scratch in it
+};
+ScratchSlot g_scratch[NA_MAX_DEVICES];
+
+// CUcontext of the calling thread through the driver entry point (the
+// library links the static runtime only); NULL when it cannot be had, and
+// the cache is then kept per device alone.
+void *current_context() {
+    typedef int (*ctx_get_fn)(void **);
+    static ctx_get_fn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *fp = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &fp, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = (ctx_get_fn)fp;
+        else
+            (void)cudaGetLastError();
+    });
+    void *ctx = nullptr;
+    if (fn && fn(&ctx) != 0) ctx = nullptr;
+    return ctx;
+}
 
 // Device address of g_quant_scratch on the current device, looked up once
-// per device.  NULL on failure (message on stderr).
+// per device and context (cudaGetSymbolAddress, with that device current);
+// a call from another context (a context the caller created, or a primary
+// context created again) looks it up anew.  NULL on failure (message on
+// stderr).
 uint32_t *scratch_of_current_device() {
     int dev = -1;
     cudaError_t e = cudaGetDevice(&dev);
@@ -172,18 +196,19 @@ uint32_t *scratch_of_current_device() {
                 e != cudaSuccess ? cudaGetErrorString(e) : "ordinal out of range");
         return nullptr;
     }
-    uint32_t *p = g_scratch_ptr[dev].load(std::memory_order_acquire);
-    if (p) return p;
+    void *ctx = current_context();
     std::lock_guard<std::mutex> lock(g_setup_mu);
-    p = g_scratch_ptr[dev].load(std::memory_order_relaxed);
-    if (p) return p;
+    ScratchSlot &slot = g_scratch[dev];
+    if (slot.ptr && slot.ctx == ctx) return slot.ptr;
+    uint32_t *p = nullptr;
     e = cudaGetSymbolAddress((void **)&p, g_quant_scratch);
     if (e != cudaSuccess || !p) {
         fprintf(stderr, "[ERROR] falcom_quantize_residual_noalloc: scratch set-up failed on device %d: %s\n", dev,
                 cudaGetErrorString(e));
         return nullptr;
     }
-    g_scratch_ptr[dev].store(p, std::memory_order_release);
+    slot.ctx = ctx;
+    slot.ptr = p;
     return p;
 }
 
@@ -215,9 +240,23 @@ extern "C" __attribute__((visibility("default"))) int falcom_quantize_residual_n
     const uintptr_t xa = (uintptr_t)residual, oa = (uintptr_t)out + 4;
     const int vec = (xa & 15) == 0 && (bits == 4 || (oa & 3) == 0);
     cudaStream_t s = (cudaStream_t)stream;
-    k_na_scale<<<ntiles, NA_TPB, 0, s>>>(residual, (int64_t)n, vec, qmax, (uint8_t *)out, scratch);
-    k_na_codes<<<ntiles, NA_TPB, 0, s>>>(residual, (int64_t)n, vec, qmax, (uint8_t *)out, scratch);
-    const cudaError_t e = cudaGetLastError();
+    // an error left pending by the caller's earlier work stays the caller's:
+    // nothing is launched, and it is not cleared
+    cudaError_t e = cudaPeekAtLastError();
+    if (e != cudaSuccess) {
+        fprintf(stderr, "[ERROR] falcom_quantize_residual_noalloc: a CUDA error is already pending (%s); "
+                        "nothing launched\n", cudaGetErrorString(e));
+        return ERROR_COMPRESSION;
+    }
+    k_na_tiles<<<ntiles, NA_TPB, 0, s>>>(residual, (int64_t)n, vec, scratch);
+    if ((e = cudaGetLastError()) == cudaSuccess) {
+        k_na_scale<<<1, NA_TPB, 0, s>>>(ntiles, qmax, (uint8_t *)out, scratch);
+        e = cudaGetLastError();
+    }
+    if (e == cudaSuccess) {
+        k_na_codes<<<ntiles, NA_TPB, 0, s>>>(residual, (int64_t)n, vec, qmax, (uint8_t *)out, scratch);
+        e = cudaGetLastError();
+    }
     if (e != cudaSuccess) {
         fprintf(stderr, "[ERROR] falcom_quantize_residual_noalloc: launch failed: %s\n", cudaGetErrorString(e));
         return ERROR_COMPRESSION;

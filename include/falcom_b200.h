@@ -87,15 +87,18 @@ const char *falcom_kernel_name(int id);
  *
  * While set, every momentum_compressor_decompress_batch call on `mc` also
  * adds weight * (decoded item i) into aggregate[offsets[i] ...
- * offsets[i] + numel_i) for every item i < n that decodes successfully and is
- * float32 (other dtypes are not added).  `aggregate` is float32 device memory
- * of the instance's device, `offsets` element offsets (copied); items must
- * not overlap in the aggregate.  The addition (one fma per element) is queued
- * on the instance's stream after the call's own work and may still run when
- * the call returns: synchronise that stream, or order later work on it,
- * before reading the aggregate.  Set it again to change the weight (one call
- * per client); aggregate = NULL stops it.  Returns 0, or ERROR_INVALID_PARAM
- * when aggregate is not device memory of the instance's device. */
+ * offsets[i] + numel_i) for every item i < n that is float32 (other dtypes
+ * are not added).  The addition (one fma per element) is done by the
+ * decoder's reconstruct kernel as it writes each decoded element, so the
+ * aggregate costs no pass of its own and is complete when the call
+ * returns.  `aggregate` is float32 device memory of the instance's device,
+ * `offsets` element offsets (copied); items must not overlap in the
+ * aggregate; a region 16-byte aligned is written with vector stores.  Set it
+ * again to change the weight (one call per client); aggregate = NULL stops
+ * it.  The aggregate is valid when the call returns 0: an item that fails
+ * after its reconstruction ran may already have written its region, and the
+ * call then reports the failure.  Returns 0, or ERROR_INVALID_PARAM when
+ * aggregate is not device memory of the instance's device. */
 int falcom_set_aggregate(MomentumCompressor *mc, float *aggregate, const size_t *offsets, size_t n,
                          float weight);
 
@@ -106,10 +109,25 @@ int falcom_set_aggregate(MomentumCompressor *mc, float *aggregate, const size_t 
  *              to +0 and adding, without the clear or the read of the old
  *              value.  For the first client of a round.
  * Applies to the following decompress_batch calls until changed;
- * falcom_set_aggregate(mc, NULL, ...) resets it to 0.  In store mode an item
- * that is not added (failed, or not float32) leaves its region as it was.
+ * falcom_set_aggregate(mc, NULL, ...) resets it to 0.  Items that are not
+ * float32 leave their region as it was.
  * Returns 0, or ERROR_INVALID_PARAM for mc NULL or store not 0 / 1. */
 int falcom_set_aggregate_store(MomentumCompressor *mc, int store);
+
+/* Aggregate-only decoding.  No counterpart in the reference.
+ *   on = 1  items that go into the aggregate (float32 items with an offset)
+ *           get no decoded array: decompress_batch sets out[i] = NULL for
+ *           them, writes neither a device nor a host copy of the decoded
+ *           tensor, and still updates the instance's history and memory
+ *           (the next round decodes against them).  A server that only needs
+ *           the aggregate saves one 4-byte write (and, for host outputs, the
+ *           device-to-host copy) per element and client.  The call's return
+ *           code reports success as before; items not added keep their
+ *           arrays.
+ *   on = 0  (default) every decoded item is returned.
+ * falcom_set_aggregate(mc, NULL, ...) resets it to 0.  Returns 0, or
+ * ERROR_INVALID_PARAM for mc NULL or on not 0 / 1. */
+int falcom_set_aggregate_only(MomentumCompressor *mc, int on);
 
 /* Residual quantiser that allocates no memory.  No counterpart in the
  * reference interface.
@@ -128,15 +146,18 @@ int falcom_set_aggregate_store(MomentumCompressor *mc, int store);
  * caching allocator, which must account for every byte), and
  * latency-critical paths, where cudaMalloc / cudaFree would stall the GPU
  * (cudaFree synchronises the device).  The batch entry points above grow
- * device pools of their own on demand; this one only launches two kernels.
+ * device pools of their own on demand; this one only launches three kernels.
  *
  * Scratch is a fixed 65,792-byte __device__ array inside the library, one per
- * device, which bounds n at FALCOM_NOALLOC_MAX_ELEMS (8192-element tiles x
- * 16384 tiles).  Its arrival counter must be zero when a call starts: it is
- * zero when the library is loaded and every completed call leaves it at
- * zero.  The first call on each device does a one-time set-up (looks up the
- * scratch address with cudaGetSymbolAddress); make that call before any
- * stream capture begins -- n = 0 does the set-up only.
+ * device (every GPU that loads the library holds it until exit), which bounds
+ * n at FALCOM_NOALLOC_MAX_ELEMS (8192-element tiles x 16384 tiles).  Each call
+ * writes every scratch word it reads before reading it, so no word has to
+ * start at zero, and a call cut short leaves nothing a later call depends on.
+ * The first call on each device (and in each CUDA context) does a one-time
+ * set-up: it looks up the array's device address with cudaGetSymbolAddress;
+ * make that call before any stream capture begins -- n = 0 does the set-up
+ * only.  cudaDeviceReset destroys the array with its context; a call after a
+ * reset in the same process is not supported.
  *
  * Calls share the scratch of their device, so calls on one device must not
  * overlap: issue them on one stream, or order them with events.  Two calls
@@ -144,7 +165,9 @@ int falcom_set_aggregate_store(MomentumCompressor *mc, int store);
  *
  * Returns 0; ERROR_INVALID_PARAM (message on stderr) when bits is not 8 or
  * 4, n > FALCOM_NOALLOC_MAX_ELEMS, or a pointer is NULL with n > 0;
- * ERROR_COMPRESSION when set-up or the launch fails. */
+ * ERROR_COMPRESSION when set-up or a launch fails, or when a CUDA error from
+ * the caller's earlier work is already pending on the calling thread (then
+ * nothing is launched and that error is left pending for its owner). */
 #define FALCOM_NOALLOC_MAX_ELEMS 134217728LL
 int falcom_quantize_residual_noalloc(const float *residual, size_t n, int bits, void *out, void *stream);
 

@@ -204,6 +204,7 @@ cudaError_t cudaGetDeviceCount(int *n) {
 }
 cudaError_t cudaDeviceSynchronize(void) { return cudaSuccess; }
 cudaError_t cudaGetLastError(void) { return cudaSuccess; }
+cudaError_t cudaPeekAtLastError(void) { return cudaSuccess; }
 const char *cudaGetErrorString(cudaError_t) { return "emulated CUDA error"; }
 cudaError_t cudaGetDeviceProperties_v2(cudaDeviceProp *p, int) {
     memset(p, 0, sizeof(*p));

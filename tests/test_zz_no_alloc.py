@@ -1,8 +1,12 @@
 """GPU test of falcom_quantize_residual_noalloc, the quantiser that uses a
-fixed __device__ scratch array instead of allocating.  Its output must equal
-the data payload that momentum_compressor_compress_batch writes for the same
-tensor (a lossy float32 tensor with no history is quantised directly), on
-two calls in a row, so the scratch left by one call serves the next.
+fixed __device__ scratch array instead of allocating, for callers that cannot
+allocate device memory (a framework's caching allocator owns it, or a
+latency-critical path cannot afford cudaMalloc / cudaFree).  Its output must
+equal the data payload that momentum_compressor_compress_batch writes for the
+same tensor (a lossy float32 tensor with no history is quantised directly)
+and the oracle's quantisation of the tensor, on two calls in a row, so the
+scratch left by one call serves the next; and the device's free memory must
+not change across calls.
 
 The file name sorts last so it also runs after every other GPU test in one
 process; it passes alone too."""
@@ -12,6 +16,7 @@ import numpy as np
 import pytest
 
 from compressor_b200.abi import Codec
+from oracle import binding as ob
 from tests.helpers import seeded
 
 pytestmark = pytest.mark.gpu
@@ -81,8 +86,34 @@ def test_noalloc_matches_batch_payload_twice(product_lib, bits, codec, n):
     for x, o in zip(xd, outs):   # two calls in a row on one stream
         assert _noalloc(lib, x.data_ptr(), n, bits, o.data_ptr(), stream.cuda_stream) == 0
     stream.synchronize()
-    for o, w in zip(outs, want):
-        _check(o.cpu().numpy().tobytes(), w, bits)
+    for o, w, x in zip(outs, want, xs):
+        got = o.cpu().numpy().tobytes()
+        _check(got, w, bits)
+        # and directly against the oracle's quantiser (scale bit-exact, codes equal)
+        es, ec = ob.quantize(x, 127 if bits == 8 else 7)
+        assert np.frombuffer(got[:4], np.float32)[0] == es
+        codes = (np.frombuffer(got[4:], np.int8) if bits == 8
+                 else ob.unpack_int4(np.frombuffer(got[4:], np.uint8), n))
+        assert np.array_equal(codes.astype(np.int32), ec.astype(np.int32))
+
+
+def test_noalloc_device_memory_unchanged(product_lib):
+    """After a first call (set-up and the module's lazy loading), further
+    calls leave the device's free memory exactly as it was: the entry point
+    allocates nothing."""
+    lib = _lib(product_lib)
+    n = 2_000_000
+    x = torch.from_numpy(seeded((n,), 5)).cuda()
+    o = torch.empty(_payload_len(n, 8), dtype=torch.uint8, device="cuda")
+    s = torch.cuda.current_stream().cuda_stream
+    assert _noalloc(lib, x.data_ptr(), n, 8, o.data_ptr(), s) == 0
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info()
+    for bits in (8, 4, 8):
+        assert _noalloc(lib, x.data_ptr(), n, bits, o.data_ptr(), s) == 0
+    torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info()
+    assert free1 == free0
 
 
 def test_noalloc_unaligned_buffers_and_zero_residual(product_lib):
