@@ -1,25 +1,34 @@
 #!/usr/bin/env python
-"""Benchmark of the B200 FalCom codec on the ResNet-50 closed loop.
+"""Benchmark of the B200 FalCom codec.
 
-One step = one hot round of one client's ResNet-50 update (266 tensors,
-23,573,952 fp32): momentum_compressor_compress_batch on the client's encoder
-instance followed by momentum_compressor_decompress_batch on a separate
-server-side decoder instance, through the C ABI.  Residual codec q8.
+Headline step (every N): one federated round with one client per GPU, the
+ResNet-50 closed loop (266 tensors, 23,573,952 fp32, residual codec q8):
+momentum_compressor_compress_batch on the client's encoder instance, then
+momentum_compressor_decompress_batch on a separate server decoder instance
+that writes the decoded update straight into the server's aggregate (weight
+1/N, fused into the reconstruct kernel, aggregate-only: no separate decoded
+copy), then, for N > 1, the NCCL sum all-reduce of the 94.3 MB aggregate.  At
+N = 1 the weight is 1 and the aggregate is the decoded update itself, bit for
+bit: the single-client closed loop.  Same step at every N (weak scaling).
 
-  value    raw-update GB/s over all ranks (update bytes / device time of the
-           step, max over ranks), inputs resident in HBM, payloads and
-           decoded outputs in device memory
-  e2e      the same round with host buffers: pinned host inputs, payloads
-           returned to host memory, decoded outputs in host memory, so the
-           host<->device copies are inside the timed step
+  value    raw-update GB/s over all ranks (N x 94.3 MB / device time of the
+           step, max over ranks), inputs resident in HBM
+  e2e      the same step with host buffers: pinned host inputs, payloads
+           returned to host memory and sent back up to the server, the
+           aggregate read back to host memory, copies inside the timed step
   roofline dominant kernel: algorithmic bytes per launch / mean launch time
            (CUDA events on the library's stream), against the measured HBM
            copy bandwidth
   cpu_baseline  the reference's own grouped OpenMP codec (built from its
            sources, SZ3 stubbed) on the same workload on this host's cores
 
-Multi-GPU (torchrun): every rank runs its own client (weak scaling, no data
-collective); device times are reduced with MAX over ranks.
+Nested lines: ``federated_64`` (64 ResNet-50 clients over the N GPUs, 64/N
+per GPU, NCCL aggregate checked against a float64 FedAvg), ``gpt2_medium_16``
+(16 GPT-2-medium clients, q8), and at N = 1 ``resnet18``, ``int4``,
+``microbench_512x512x3x3`` (per-kernel GB/s beside the reference's own
+microbenchmark), ``per_layer_api`` (the path FalComC.py calls),
+``reference_gpu_v4`` (the reference's q8 GPU codec built for sm_100a),
+``pcie`` and the CPU baseline at 8 threads and at all host threads.
 """
 from __future__ import annotations
 
@@ -56,6 +65,7 @@ NCU_TRAFFIC = {
     },
 }
 
+
 def log(*a):
     print(*a, file=sys.stderr, flush=True)
 
@@ -71,23 +81,39 @@ def measured_peak():
         return PEAK_FALLBACK_GBS, "fallback"
 
 
+def cpu_model() -> str:
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled during a timed region."""
+    """nvidia-smi clocks and throttle reasons of the given GPUs, sampled by one
+    process during a timed region (rank 0 samples every local GPU)."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, gpu_index: int):
-        self.gpu = gpu_index
+    def __init__(self, gpus, interval_ms: int = 20, enabled: bool = True):
+        self.gpus = ",".join(str(g) for g in gpus)
+        self.interval = interval_ms
+        self.enabled = enabled
         self.proc = None
         self.lines = []
 
     def __enter__(self):
+        if not self.enabled:
+            return self
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "20"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                ["nvidia-smi", "-i", self.gpus, f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", str(self.interval)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
             t0 = time.time()   # sampling is running once the first line is in
@@ -103,8 +129,8 @@ class ClockSampler:
 
     def __exit__(self, *exc):
         if self.proc:
-            # a short timed region can end before the first sample: wait for
-            # one more sample (taken as the region ends) before stopping
+            # a short timed region can end before the next sample: wait for
+            # one more (taken as the region ends) before stopping
             n0, t0 = len(self.lines), time.time()
             while len(self.lines) <= n0 and time.time() - t0 < 1.0:
                 time.sleep(0.005)
@@ -130,7 +156,286 @@ class ClockSampler:
                 if v.lower().startswith("active"):
                     reasons.add(nm)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "reasons": sorted(reasons), "samples": len(sm), "gpus": self.gpus}
+
+
+class L2Flush:
+    """Empties the L2 between timed steps, outside the timed events: a 256 MiB
+    write (no line of the previous step survives), then a 256 MiB read of a
+    second buffer, which evicts the write's dirty lines too, so no write-back
+    of the flush itself lands inside the next timed step."""
+
+    def __init__(self, torch, device):
+        n = 256 * 1024 * 1024 // 4
+        self.w = torch.empty(n, dtype=torch.float32, device=device)
+        self.r = torch.zeros(n, dtype=torch.float32, device=device)
+
+    def __call__(self):
+        self.w.zero_()
+        self.r.sum()
+
+
+class DevView:
+    """Zero-copy torch view of float32 device memory the library owns (the
+    CUDA array interface), for checks on decoded arrays."""
+
+    def __init__(self, ptr: int, n: int):
+        self.__cuda_array_interface__ = {"shape": (int(n),), "typestr": "<f4", "data": (int(ptr), False),
+                                         "version": 3}
+
+
+# ------------------------------------------------------------ distributed
+class Dist:
+    """One process per GPU under torchrun (NCCL); a single process otherwise."""
+
+    def __init__(self):
+        import torch
+        self.torch = torch
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        torch.cuda.set_device(self.local)
+        self.dev = torch.device("cuda", self.local)
+        # one stream for everything: torch's work (data, flushes, checks,
+        # events) and the library's (falcom_set_stream), so every step is
+        # ordered on it; the legacy default stream would leave the library
+        # on its own non-blocking stream, unordered with torch's work
+        self.stream = torch.cuda.Stream(device=self.dev)
+        torch.cuda.set_stream(self.stream)
+        self.dist = None
+        if self.world > 1:
+            import datetime
+            import torch.distributed as dist
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=self.dev)
+            self.dist = dist
+
+    def barrier(self):
+        """Host-side alignment of the ranks (device idle on both sides)."""
+        self.torch.cuda.synchronize()
+        if self.dist:
+            self.dist.barrier()
+            self.torch.cuda.synchronize()
+
+    def max(self, x: float) -> float:
+        t = self.torch.tensor([float(x)], dtype=self.torch.float64, device=self.dev)
+        if self.dist:
+            self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def sum_(self, t):
+        if self.dist:
+            self.dist.all_reduce(t, op=self.dist.ReduceOp.SUM)
+
+    def close(self):
+        if self.dist:
+            self.dist.barrier()
+            self.dist.destroy_process_group()
+
+
+# ---------------------------------------------------------- synthetic data
+class DeviceUpdates:
+    """Seeded synthetic client updates generated on the GPU, one flat float32
+    buffer per client in the model's packed layout (offsets aligned to 64
+    elements).  ResNet / microbench: AR(1) Gaussian (rho 0.9, sigma
+    1e-3/sqrt(fan_in), or 1e-4 for the microbench tensor); GPT-2-medium:
+    Student-t nu = 3 scaled by 1e-4, rho 0.8 (t = z0 / sqrt((z1^2+z2^2+z3^2)/3));
+    `common_std` > 0 adds a shared N(0, common_std^2) component drawn once per
+    round with the same seed on every rank."""
+
+    def __init__(self, torch, model: str, clients, dev, common_std: float = 0.0, seed0: int = 50_000):
+        from compressor_b200 import workloads as W
+        self.torch = torch
+        self.lay = W.Layout.of(model)
+        self.student = model == "gpt2-medium"
+        self.rho = 0.8 if self.student else 0.9
+        lay = self.lay
+        self.sigma = torch.zeros(lay.total, device=dev)
+        for o, sh in zip(lay.offsets, lay.shapes):
+            n = int(np.prod(sh))
+            s = 1e-4 if (self.student or model == "microbench") else 1e-3 / float(np.sqrt(W.fan_in(sh)))
+            self.sigma[o:o + n] = s
+        self.gens = []
+        for c in clients:
+            g = torch.Generator(device=dev)
+            g.manual_seed(seed0 + int(c))
+            self.gens.append(g)
+        self.common_std = common_std
+        self.gcom = torch.Generator(device=dev)
+        self.gcom.manual_seed(seed0 - 1)
+        self.state = [torch.zeros(lay.total, device=dev) for _ in clients]
+        self.x = [s if common_std == 0.0 else torch.empty(lay.total, device=dev) for s in self.state]
+        self.started = False
+        self.dev = dev
+
+    def _noise(self, g):
+        t = self.torch
+        n = self.lay.total
+        if not self.student:
+            return t.randn(n, device=self.dev, generator=g).mul_(self.sigma)
+        z = t.randn(4, n, device=self.dev, generator=g)
+        chi = z[1].square_().add_(z[2].square_()).add_(z[3].square_()).div_(3.0).sqrt_()
+        return z[0].div_(chi).mul_(self.sigma)
+
+    def next_round(self):
+        common = None
+        if self.common_std:
+            common = self.torch.randn(self.lay.total, device=self.dev, generator=self.gcom).mul_(self.common_std)
+        for j, g in enumerate(self.gens):
+            noise = self._noise(g)
+            if self.started:
+                self.state[j].mul_(self.rho).add_(noise)
+            else:
+                self.state[j].copy_(noise)
+            if common is not None:
+                self.torch.add(self.state[j], common, out=self.x[j])
+            del noise
+        self.started = True
+
+    def ptrs(self):
+        return [x.data_ptr() for x in self.x]
+
+
+# ------------------------------------------------------------ the round
+class FedRound:
+    """One federated round on this rank: every local client's update through
+    its own encoder instance (compress_batch), then through this rank's server
+    decoder (decompress_batch) with the weighted aggregate fused into the
+    reconstruct kernel (first client stored, the others added,
+    aggregate-only: no separate decoded copy), then the NCCL sum all-reduce of
+    the aggregate over the ranks (N > 1)."""
+
+    def __init__(self, torch, D: Dist, model: str, clients, n_total: int, codec: str, stream, so_path,
+                 host_inputs: bool = False):
+        from compressor_b200 import workloads as W
+        from compressor_b200.abi import Codec, PreparedBatch
+        self.torch, self.D, self.model = torch, D, model
+        self.lay = W.Layout.of(model)
+        self.clients = list(clients)
+        self.cids = [f"Client{c + 1}".encode() for c in self.clients]
+        self.w = 1.0 / float(n_total)
+        self.stream = stream
+        self.host_inputs = host_inputs
+
+        def mk(cid):
+            c = Codec(so_path, client=cid)
+            assert c.lib.falcom_set_residual_codec(c.h, codec.encode()) == 0
+            c.lib.falcom_set_stream(c.h, ctypes.c_void_p(stream.cuda_stream))
+            return c
+        self.encs = [mk(cid.decode()) for cid in self.cids]
+        self.srv = mk("server")
+        # one prepared batch per client, its input pointers set once (the
+        # inputs stay in place from round to round)
+        self.pbs = [PreparedBatch(self.srv.lib, self.lay.names, self.lay.shapes) for _ in self.cids]
+        self.bound = [None] * len(self.cids)
+        self.offs_b = [4 * o for o in self.lay.offsets]
+        self.c_offs = (ctypes.c_size_t * len(self.lay.offsets))(*self.lay.offsets)
+        self.agg = torch.zeros(self.lay.total, dtype=torch.float32, device=D.dev)
+        self.upd = self.lay.numel * 4
+        self.launches = 0
+        self.payload = 0
+
+    def close(self):
+        for c in self.encs + [self.srv]:
+            c.close()
+
+    def codec_part(self, ptrs, outputs: bool = False, check64=None, count_payload: bool = False):
+        """Compress + decode of every local client (queued on the stream,
+        each call synchronous with the host).  With `outputs` the server also
+        returns decoded device arrays, and `check64` (float64, aggregate
+        layout) accumulates weight * decoded for the FedAvg check;
+        `count_payload` adds up the payload bytes (host work kept out of the
+        timed steps)."""
+        lib, srv = self.srv.lib, self.srv
+        if count_payload:
+            self.payload = 0
+        for j, cid in enumerate(self.cids):
+            pb = self.pbs[j]
+            if self.bound[j] != ptrs[j]:
+                pb.set_pointers(ptrs[j], self.offs_b)
+                self.bound[j] = ptrs[j]
+            r1 = pb.compress(self.encs[j].h, cid)
+            assert lib.falcom_set_aggregate(srv.h, ctypes.c_void_p(self.agg.data_ptr()), self.c_offs,
+                                            len(self.lay.offsets), self.w) == 0
+            lib.falcom_set_aggregate_store(srv.h, 1 if j == 0 else 0)
+            lib.falcom_set_aggregate_only(srv.h, 0 if outputs else 1)
+            r2 = pb.decompress(srv.h, cid)
+            if r1 != 0 or r2 != 0:
+                raise RuntimeError(f"codec failed on rank {self.D.rank} client {cid}: {r1} {r2} "
+                                   f"{self.encs[j].lib.falcom_last_error(self.encs[j].h)} "
+                                   f"{lib.falcom_last_error(srv.h)}")
+            if count_payload:
+                self.payload += pb.payload_bytes()
+            self.launches += (self.encs[j].lib.falcom_last_launches(self.encs[j].h) +
+                              lib.falcom_last_launches(srv.h))
+            if check64 is not None:
+                for i, o in enumerate(self.lay.offsets):
+                    a = pb.outs[i].contents
+                    v = self.torch.as_tensor(DevView(a.data, a.total_size), device=self.D.dev)
+                    check64[o:o + a.total_size].add_(v.double(), alpha=self.w)
+                # the views are read on the stream before release hands the
+                # arrays back to the library (ordered anyway: one stream)
+                self.torch.cuda.current_stream().synchronize()
+            pb.release()
+
+    def allreduce(self):
+        self.D.sum_(self.agg)
+
+
+def timed_rounds(torch, D: Dist, fr: FedRound, data: DeviceUpdates, K: int, W: int, flush, clk=None,
+                 split: bool = False):
+    """W untimed rounds, then K rounds each bracketed by CUDA events on the
+    library's stream (L2 flush and rank alignment outside them).  Returns
+    per-step ms, codec-part ms and all-reduce ms (rank-local)."""
+    stream = fr.stream
+    for w in range(W):
+        data.next_round()
+        fr.codec_part(data.ptrs(), count_payload=(w == W - 1))
+        fr.allreduce()
+    torch.cuda.synchronize()
+    step, codec, ar, wait = [], [], [], []
+    fr.launches = 0
+    tiny = torch.zeros(1, device=D.dev)
+    for _ in range(K):
+        data.next_round()
+        # ranks aligned on the host first; the flush that follows gives the
+        # host time to plan the step's first call while the GPU is still busy
+        D.barrier()
+        flush()
+        e = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+        e[0].record(stream)
+        fr.codec_part(data.ptrs())
+        e[1].record(stream)
+        if split:
+            D.sum_(tiny)             # completes once every rank has arrived
+        e[2].record(stream)
+        fr.allreduce()
+        e[3].record(stream)
+        e[3].synchronize()
+        step.append(e[0].elapsed_time(e[3]))
+        codec.append(e[0].elapsed_time(e[1]))
+        wait.append(e[1].elapsed_time(e[2]))
+        ar.append(e[2].elapsed_time(e[3]))
+    torch.cuda.synchronize()
+    return step, codec, wait, ar
+
+
+def fedavg_check(torch, D: Dist, fr: FedRound, data: DeviceUpdates):
+    """One more round in which the server also returns the decoded arrays:
+    rank 0 compares the NCCL-reduced float32 aggregate with the float64 sum
+    over all clients of weight * decoded (all-reduced in float64)."""
+    acc = torch.zeros(fr.lay.total, dtype=torch.float64, device=D.dev)
+    data.next_round()
+    fr.codec_part(data.ptrs(), outputs=True, check64=acc)
+    fr.allreduce()
+    D.sum_(acc)
+    torch.cuda.synchronize()
+    a = fr.agg.double()
+    num = float(torch.linalg.vector_norm(a - acc).item())
+    den = float(torch.linalg.vector_norm(acc).item())
+    exact = bool(torch.equal(fr.agg, acc.float())) if D.world == 1 and len(fr.clients) == 1 else None
+    rel = num / den if den > 0 else num
+    return {"rel_l2": rel, "pass": rel <= 1e-6, "bar": 1e-6, "bit_exact_single_client": exact,
+            "against": "float64 sum over all clients of weight x decoded update (FedAvg), all-reduced in float64"}
 
 
 # ------------------------------------------------------------ reference CPU
@@ -149,7 +454,7 @@ def cpu_reference_loop(model: str, steps: int, warmup: int, threads: int, budget
     os.environ.setdefault("OMP_PLACES", "cores")
     os.environ.setdefault("FALCOM_LOG_LEVEL", "ERROR")
     from compressor_b200 import workloads as W
-    from compressor_b200.abi import Codec, HostArray
+    from compressor_b200.abi import Codec, HostArray, NDArrayC
     so = ref_library()
     gomp = ctypes.CDLL("libgomp.so.1")
     gomp.omp_set_num_threads(int(threads))
@@ -172,7 +477,6 @@ def cpu_reference_loop(model: str, steps: int, warmup: int, threads: int, budget
             hs = [HostArray(v) for v in lay.views(flat)]
             t0 = time.perf_counter()
             ret, items = enc.compress_batch_raw(names, hs)
-            from compressor_b200.abi import BatchItemC, NDArrayC
             n = len(names)
             outs = (ctypes.POINTER(NDArrayC) * n)()
             r2 = dec.lib.momentum_compressor_decompress_batch(dec.h, items, n, b"Client1", outs)
@@ -204,6 +508,17 @@ def update_bytes(model: str) -> int:
     return W.Layout.of(model).numel * 4
 
 
+def cpu_baseline_entry(model: str, threads: int, budget_s: float):
+    ct = cpu_reference_loop(model, 20, 1, threads, budget_s=budget_s)
+    cms = 1e3 * statistics.median(ct)
+    return {"value": round(update_bytes(model) / (cms * 1e-3) / 1e9, 5), "unit": "GB/s", "cores": threads,
+            "kind": "reference", "ms_per_round": round(cms, 2), "cpu_model": cpu_model(),
+            "host_threads_available": os.cpu_count(),
+            "sample": f"{len(ct)} full {model} closed-loop rounds (compress_batch + decompress_batch) of the "
+                      f"reference grouped OpenMP build, SZ3 stubbed (sz3_memcpy), OMP_PROC_BIND=close "
+                      f"OMP_PLACES=cores, {threads} threads, median, after 1 warm-up round"}
+
+
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -226,6 +541,7 @@ def run_reference(args):
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded AR(1) Gaussian updates, ResNet-50 state-dict shapes)", "config": cfg,
         "cpu_baseline": {"value": round(gbs, 5), "unit": "GB/s", "cores": threads, "kind": "reference",
+                         "cpu_model": cpu_model(),
                          "sample": f"{len(times)} full closed-loop rounds after {args.warmup} warm-up rounds"},
         "e2e": {"value": round(gbs, 5), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -233,462 +549,436 @@ def run_reference(args):
     return 0
 
 
-# ------------------------------------------------------------------- ours
-class L2Flush:
-    """Empties the L2 between timed steps, outside the timed events: a 256 MiB
-    write (no line of the previous step survives), then a 256 MiB read of a
-    second buffer, which evicts the write's dirty lines too, so no write-back
-    of the flush itself lands inside the next timed step."""
-
-    def __init__(self, torch, device):
-        n = 256 * 1024 * 1024 // 4
-        self.w = torch.empty(n, dtype=torch.float32, device=device)
-        self.r = torch.zeros(n, dtype=torch.float32, device=device)
-
-    def __call__(self):
-        self.w.zero_()
-        self.r.sum()
-
-
-def make_rounds_on_device(torch, model: str, n_rounds: int, seed: int, device):
-    """AR(1) Gaussian updates (rho 0.9, sigma 1e-3/sqrt(fan_in)) generated on
-    the GPU with a seeded generator, packed in the flat layout."""
-    from compressor_b200 import workloads as W
-    lay = W.Layout.of(model)
-    sigma = torch.zeros(lay.total, device=device)
-    for o, s in zip(lay.offsets, lay.shapes):
-        n = int(np.prod(s))
-        sigma[o:o + n] = 1e-3 / float(np.sqrt(W.fan_in(s)))
-    g = torch.Generator(device=device)
-    g.manual_seed(seed)
-    out = []
-    state = None
-    for _ in range(n_rounds):
-        noise = torch.randn(lay.total, device=device, generator=g) * sigma
-        state = noise if state is None else 0.9 * state + noise
-        out.append(state.clone())
-    return lay, out
-
-
-def run_ours(args):
-    import torch
-    import torch.distributed as dist
-
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        import datetime
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=dev)
-
-    from compressor_b200 import build as B
-    from compressor_b200.abi import Codec, PreparedBatch, kernel_times
-    if not os.path.exists(B.OUT):
-        B.build()
-    os.environ.setdefault("FALCOM_LOG_LEVEL", "ERROR")
-
-    model = args.model
-    K, Wm = args.steps, args.warmup
-    n_rounds = 1 + Wm + K
-    lay, rounds = make_rounds_on_device(torch, model, n_rounds, seed=1000 + rank, device=dev)
-    offs_b = [4 * o for o in lay.offsets]
-    upd = lay.numel * 4
-    stream = torch.cuda.current_stream()
-
-    def new_pair():
-        enc = Codec(B.OUT, client=f"Client{rank + 1}")
-        dec = Codec(B.OUT, client=f"Client{rank + 1}")
-        for c in (enc, dec):
-            assert c.lib.falcom_set_residual_codec(c.h, args.codec.encode()) == 0
-            c.lib.falcom_set_stream(c.h, ctypes.c_void_p(stream.cuda_stream))
-        return enc, dec
-
-    client = f"Client{rank + 1}".encode()
-    flush = L2Flush(torch, dev)
-
-    def closed_loop(enc, dec, pb, base_ptr, count, e0=None, e1=None):
-        """One round through the C ABI; e0/e1 (CUDA events on the library's
-        stream) bracket exactly the two codec calls."""
-        pb.set_pointers(base_ptr, offs_b)
-        if e0 is not None:
-            e0.record(stream)
-        r1 = pb.compress(enc.h, client)
-        r2 = pb.decompress(dec.h, client)
-        if e1 is not None:
-            e1.record(stream)
-        if r1 != 0 or r2 != 0:
-            raise RuntimeError(f"codec failed: {r1} {r2} {enc.lib.falcom_last_error(enc.h)} "
-                               f"{dec.lib.falcom_last_error(dec.h)}")
-        nbytes = pb.payload_bytes()
-        launches = enc.lib.falcom_last_launches(enc.h) + dec.lib.falcom_last_launches(dec.h)
-        pb.release()
-        count[0] += launches
-        return nbytes
-
-    # ------------------------------------------------ device-resident value
-    enc, dec = new_pair()
-    pb = PreparedBatch(enc.lib, lay.names, lay.shapes)
-    cnt = [0]
-    closed_loop(enc, dec, pb, rounds[0].data_ptr(), cnt)          # round 0: direct
-    for t in range(1, 1 + Wm):
-        closed_loop(enc, dec, pb, rounds[t].data_ptr(), cnt)
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    step_ms = []
-    cnt = [0]
-    payload = 0
-    with ClockSampler(local) as clk:
-        for t in range(1 + Wm, n_rounds):
-            flush()                             # L2 flush outside the timed events
-            e0 = torch.cuda.Event(enable_timing=True)
-            e1 = torch.cuda.Event(enable_timing=True)
-            payload = closed_loop(enc, dec, pb, rounds[t].data_ptr(), cnt, e0, e1)
-            e1.synchronize()
-            step_ms.append(e0.elapsed_time(e1))
-    torch.cuda.synchronize()
-    tot = torch.tensor([sum(step_ms)], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(tot, op=dist.ReduceOp.MAX)
-    total_ms = float(tot.item())
-    ms_per_step = total_ms / K
-    value = world * upd / (ms_per_step * 1e-3) / 1e9
-    launches_timed = cnt[0]
-
-    if args.mode == "value":
-        enc.close()
-        dec.close()
-        if rank == 0:
-            print(json.dumps({"metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world,
-                              "steps": K, "warmup": Wm, "ms_per_step": round(ms_per_step, 4),
-                              "mode": "value-only (profiler run)"}))
-        if world > 1:
-            dist.barrier()
-            dist.destroy_process_group()
-        return 0
-
-    # ------------------------------------------------- per-kernel roofline
-    enc.lib.falcom_set_kernel_timing(enc.h, 1)
-    dec.lib.falcom_set_kernel_timing(dec.h, 1)
-    for t in range(1 + Wm, n_rounds):
-        flush()
-        closed_loop(enc, dec, pb, rounds[t].data_ptr(), [0])
-    kt = kernel_times(enc.lib, enc.h)
-    kd = kernel_times(dec.lib, dec.h)
-    ktimes = {k: (v[0] + kd[k][0], v[1] + kd[k][1]) for k, v in kt.items()}
-    enc.close()
-    dec.close()
-
+# ------------------------------------------------------------- sub-benches
+def kernel_roofline(torch, D, fr: FedRound, data: DeviceUpdates, K: int, flush, codec: str):
+    """Per-kernel CUDA-event times of the codec kernels over K more rounds
+    (events bracket every launch inside the library), and the dominant
+    kernel's algorithmic bytes per launch / mean launch time."""
     from compressor_b200 import workloads as Wl
-    ab = Wl.algorithmic_bytes(model, args.codec)
-    q = {"q8": 1.0, "int4": 0.5, "raw": 4.0}[args.codec]
+    from compressor_b200.abi import kernel_times
+    insts = fr.encs + [fr.srv]
+    for c in insts:
+        c.lib.falcom_set_kernel_timing(c.h, 1)
+    for _ in range(K):
+        data.next_round()
+        flush()
+        fr.codec_part(data.ptrs())
+        fr.allreduce()
+    torch.cuda.synchronize()
+    tot = {}
+    for c in insts:
+        for k, v in kernel_times(c.lib, c.h).items():
+            a = tot.get(k, (0.0, 0))
+            tot[k] = (a[0] + v[0], a[1] + v[1])
+        c.lib.falcom_set_kernel_timing(c.h, 0)
+    ab = Wl.algorithmic_bytes(fr.model, codec)
+    q = {"q8": 1.0, "int4": 0.5, "raw": 4.0}[codec]
     me, de = ab["momentum_elements"], ab["direct_elements"]
-    # algorithmic bytes per launch of each kernel (all kernels predicted):
+    nc = len(fr.clients)
+    # algorithmic bytes per launch of each kernel (all kernels predicted);
+    # the decoder writes memory, history and the aggregate (store mode: the
+    # old value is not read; first client of a round)
     alg = {
         "enc_pass1_stats_sign": me * 12 + de * 8,          # read cur, prev; write history copy
         "enc_pass2_variance": me * 8,                       # read cur, prev
         "enc_pass3_predict": me * 16,                       # read cur, prev, mem; write mem
         "enc_pass4_quantize_pack": me * (8 + q) + de * (4 + q),   # read cur, mem; write codes
-        "dec_reconstruct": me * (20 + q) + de * (8 + q),    # read q, prev, mem; write mem, history, output
+        "dec_reconstruct": me * (20 + q) + de * (8 + q),    # read q, prev, mem; write mem, history, aggregate
         "dec_prefix": ab["kernels"] / 8,
-        "frames_write": ab["kernels"] / 8 * 2 * 2,
         "frames_expand": ab["kernels"] / 8 * 2 * 2,
     }
-    shares = {k: v[0] for k, v in ktimes.items() if v[1] > 0}
-    dom = max(shares, key=shares.get)
-    avg_ms = ktimes[dom][0] / ktimes[dom][1]
+    shares = {k: v[0] for k, v in tot.items() if v[1] > 0}
+    dom = max((k for k in shares if k in alg), key=shares.get)
+    avg_ms = tot[dom][0] / tot[dom][1]
     achieved = alg[dom] / (avg_ms * 1e-3) / 1e9
     peak, peak_kind = measured_peak()
-    roofline = {"bound": "hbm", "kernel": dom, "achieved": round(achieved, 1), "peak": peak,
-                "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4),
-                "traffic": NCU_TRAFFIC.get((model, args.codec), {}).get(dom),
-                "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, one steady-state launch",
-                "algorithmic_bytes_per_launch": int(alg[dom]), "avg_launch_ms": round(avg_ms, 5),
-                "kernel_share": {k: round(v / sum(shares.values()), 4) for k, v in shares.items()},
-                "kernel_ms_per_round": {k: round(v[0] / K, 5) for k, v in ktimes.items() if v[1] > 0},
-                "launches_per_round": {k: round(v[1] / K, 2) for k, v in ktimes.items() if v[1] > 0},
-                "closed_loop_algorithmic_bytes": int(ab["bytes_per_round"]),
-                "closed_loop_frac": round(ab["bytes_per_round"] / (ms_per_step * 1e-3) / 1e9 / peak, 4)}
-
-    # ------------------------------------------------------------ e2e (host)
-    enc2, dec2 = new_pair()
-    pb2 = PreparedBatch(enc2.lib, lay.names, lay.shapes)
-    hosts = [torch.empty(lay.total, dtype=torch.float32, pin_memory=True) for _ in range(min(K, 8) + 1 + Wm)]
-    for i, h in enumerate(hosts):
-        h.copy_(rounds[min(i, n_rounds - 1)])
-    torch.cuda.synchronize()
-    for i in range(1 + Wm):
-        closed_loop(enc2, dec2, pb2, hosts[i].data_ptr(), [0])
-    e2e_ms = []
-    h2d = d2h = 0
-    for j in range(K):
-        h = hosts[1 + Wm + j % (len(hosts) - 1 - Wm)]
-        flush()
-        e0 = torch.cuda.Event(enable_timing=True)
-        e1 = torch.cuda.Event(enable_timing=True)
-        pbytes = closed_loop(enc2, dec2, pb2, h.data_ptr(), [0], e0, e1)
-        e1.synchronize()
-        e2e_ms.append(e0.elapsed_time(e1))
-        h2d = upd + pbytes          # inputs up; payloads up for the decoder
-        d2h = pbytes + upd          # payloads down; decoded update down
-    enc2.close()
-    dec2.close()
-    e2e_t = torch.tensor([sum(e2e_ms)], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(e2e_t, op=dist.ReduceOp.MAX)
-    e2e_ms_step = float(e2e_t.item()) / K
-    e2e_val = world * upd / (e2e_ms_step * 1e-3) / 1e9
-
-    out = None
-    if rank == 0:
-        cpu = None
-        if world == 1 and not args.skip_cpu_baseline and ref_library():
-            threads = os.cpu_count() or 1
-            ct = cpu_reference_loop(model, 20, 1, threads, budget_s=args.cpu_budget_s)
-            cms = 1e3 * statistics.mean(ct)
-            cpu = {"value": round(upd / (cms * 1e-3) / 1e9, 5), "unit": "GB/s", "cores": threads,
-                   "kind": "reference", "ms_per_round": round(cms, 2),
-                   "sample": f"{len(ct)} full ResNet-50 closed-loop rounds (compress_batch + decompress_batch) "
-                             f"of the reference grouped OpenMP build, SZ3 stubbed, after 1 warm-up round"}
-        out = {
-            "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world, "steps": K,
-            "warmup": Wm, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic (seeded AR(1) Gaussian updates rho=0.9, sigma=1e-3/sqrt(fan_in), "
-                    "ResNet-50 state-dict shapes)",
-            "config": {"workload": f"{model} single-client closed loop per GPU: compress_batch + "
-                                   f"decompress_batch of 266 tensors through the C ABI, separate "
-                                   f"encoder/decoder instances, residual codec {args.codec}, GPU zstd frames",
-                       "elements_per_client": lay.numel, "update_bytes_per_client": upd,
-                       "clients_per_gpu": 1, "codec": args.codec,
-                       "l2": "flushed between steps (256 MiB write, then 256 MiB read of a second buffer; outside the timed events)",
-                       "parallelism": f"replicas x{world} (independent clients)"},
-            "gpu_launches": launches_timed,
-            "payload_bytes_per_round": payload,
-            "roofline": roofline,
-            "e2e": {"value": round(e2e_val, 3), "unit": "GB/s", "ms_per_step": round(e2e_ms_step, 4),
-                    "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h)},
-            "clocks": clk.summary(),
-            "cpu_baseline": cpu,
-        }
-        print(json.dumps(out))
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
-    return 0
+    return {"bound": "hbm", "kernel": dom, "achieved": round(achieved, 1), "peak": peak,
+            "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4),
+            "traffic": NCU_TRAFFIC.get((fr.model, codec), {}).get(dom),
+            "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, one steady-state launch",
+            "algorithmic_bytes_per_launch": int(alg[dom]), "avg_launch_ms": round(avg_ms, 5),
+            "kernel_share": {k: round(v / sum(shares.values()), 4) for k, v in shares.items()},
+            "kernel_ms_per_round": {k: round(v[0] / K, 5) for k, v in tot.items() if v[1] > 0},
+            "launches_per_round": {k: round(v[1] / K, 2) for k, v in tot.items() if v[1] > 0},
+            "kernel_gbs": {k: round(alg[k] * nc / (tot[k][0] / K * 1e-3) / 1e9, 1)
+                           for k in alg if k in tot and tot[k][1] > 0},
+            "closed_loop_algorithmic_bytes": int(ab["bytes_per_round"])}
 
 
-# --------------------------------------------------------------- federated
-def run_federated(args):
-    """Federated round per step: every rank compresses its clients' updates
-    (one encoder instance per client) and decodes them on one server decoder
-    instance whose weighted aggregate is fused into the decode, then the sum
-    all-reduce of the aggregate over NCCL.  With --ar-chunks C > 1 the round
-    runs in C layer chunks and each chunk's all-reduce is issued as soon as
-    that chunk is decoded, overlapping the later chunks' codec work."""
-    import torch
-    import torch.distributed as dist
-    from compressor_b200 import build as B
+def closed_loop_line(torch, D, model, codec, K, W, flush, so, stream):
+    """Single-client closed loop (the headline step at N = 1) of another model
+    or codec: ms per round and raw-update GB/s."""
+    from compressor_b200 import workloads as Wl
+    fr = FedRound(torch, D, model, [0], 1, codec, stream, so)
+    data = DeviceUpdates(torch, model, [0], D.dev, seed0=7000)
+    step, codec_ms, _, _ = timed_rounds(torch, D, fr, data, K, W, flush)
+    ms = statistics.mean(step)
+    ab = Wl.algorithmic_bytes(model, codec)
+    peak, _ = measured_peak()
+    out = {"ms_per_step": round(ms, 4), "value": round(fr.upd / (ms * 1e-3) / 1e9, 3), "unit": "GB/s",
+           "steps": K, "warmup": W, "codec": codec, "elements": fr.lay.numel,
+           "closed_loop_frac": round(ab["bytes_per_round"] / (ms * 1e-3) / 1e9 / peak, 4),
+           "payload_bytes_per_round": fr.payload}
+    fr.close()
+    return out
+
+
+def federated_line(torch, D, model, n_clients, codec, K, W, flush, so, stream, common_std):
+    """n_clients clients block-distributed over the ranks; per step: every
+    local client's compress + decode into the aggregate, then the NCCL
+    all-reduce; value = all clients' update bytes / max-over-ranks step time.
+    Ends with the FedAvg check of the reduced aggregate."""
     from compressor_b200 import federated as F
-    from compressor_b200 import workloads as W
-    from compressor_b200.abi import Codec, PreparedBatch
+    mine = list(F.shard(n_clients, D.world, D.rank))
+    fr = FedRound(torch, D, model, mine, n_clients, codec, stream, so)
+    data = DeviceUpdates(torch, model, mine, D.dev, common_std=common_std)
+    step, codec_ms, wait, ar = timed_rounds(torch, D, fr, data, K, W, flush, split=D.world > 1)
+    total = D.max(sum(step))
+    ms = total / K
+    check = fedavg_check(torch, D, fr, data)
+    out = {"ms_per_step": round(ms, 4), "value": round(n_clients * fr.upd / (ms * 1e-3) / 1e9, 3),
+           "unit": "GB/s", "scaling": "strong", "clients": n_clients, "clients_per_gpu": len(mine),
+           "steps": K, "warmup": W, "codec": codec, "elements_per_client": fr.lay.numel,
+           "codec_ms_per_client_rank0": round(statistics.mean(codec_ms) / max(1, len(mine)), 4),
+           "peer_wait_ms_rank0": round(statistics.mean(wait), 4) if D.world > 1 else 0.0,
+           "allreduce_ms_rank0": round(statistics.mean(ar), 4) if D.world > 1 else 0.0,
+           "allreduce_bytes": 4 * fr.lay.total if D.world > 1 else 0,
+           "aggregate_check": check, "gpu_launches_per_step_rank0": fr.launches // max(1, K)}
+    fr.close()
+    del data
+    torch.cuda.empty_cache()
+    return out
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        import datetime
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+
+def microbench_line(torch, D, K, flush, so, stream, codec="q8"):
+    """Config 3: one 512x512x3x3 fp32 tensor, N(0, (1e-4)^2) AR(1) rho 0.9
+    updates, closed loop over K rounds; per-kernel CUDA-event times and GB/s
+    of algorithmic bytes, beside the reference's own six-kernel
+    microbenchmark built for sm_100a (oracle/_ref/falcom_cuda_microbench)
+    when present."""
+    from compressor_b200.abi import kernel_times
+    fr = FedRound(torch, D, "microbench", [0], 1, codec, stream, so)
+    data = DeviceUpdates(torch, "microbench", [0], D.dev, seed0=3000)
+    step, _, _, _ = timed_rounds(torch, D, fr, data, K, 3, flush)
+    insts = fr.encs + [fr.srv]
+    for c in insts:
+        c.lib.falcom_set_kernel_timing(c.h, 1)
+    for _ in range(K):
+        data.next_round()
+        flush()
+        fr.codec_part(data.ptrs())
+    torch.cuda.synchronize()
+    tot = {}
+    for c in insts:
+        for k, v in kernel_times(c.lib, c.h).items():
+            a = tot.get(k, (0.0, 0))
+            tot[k] = (a[0] + v[0], a[1] + v[1])
+    n = 512 * 512 * 9
+    kern = 512 * 512
+    # algorithmic bytes per launch (all kernels predicted) and the reference
+    # microbench kernels each of ours covers
+    alg = {
+        "enc_pass1_stats_sign": (12 * n + kern / 8 * 2, "threshold_scan + bitmap_pack (+ stats sums, history copy)"),
+        "enc_pass2_variance": (8 * n, "(stats second pass)"),
+        "enc_pass3_predict": (16 * n, "momentum_update + residual_predmem_update"),
+        "enc_pass4_quantize_pack": (9 * n + kern / 8 * 2, "dominant_sign_pack (+ q8 codes, bitmap frame)"),
+        "dec_reconstruct": (21 * n, "decompress_reconstruct (+ q8 decode, memory update)"),
+    }
+    kernels = {}
+    for k, (b, covers) in alg.items():
+        if k in tot and tot[k][1] > 0:
+            ms = tot[k][0] / tot[k][1]
+            kernels[k] = {"us_per_launch": round(ms * 1e3, 2), "algorithmic_bytes": int(b),
+                          "gbs": round(b / (ms * 1e-3) / 1e9, 1), "covers": covers}
+    out = {"ms_per_round": round(statistics.mean(step), 4), "rounds": K, "elements": n, "conv_kernels": kern,
+           "l2": "flushed before every round", "kernels": kernels}
+    fr.close()
+    mb = os.path.join(ROOT, "oracle", "_ref", "falcom_cuda_microbench")
+    if os.path.exists(mb):
+        try:
+            r = subprocess.run([mb, "--numel", str(n), "--iters", "200"], capture_output=True, text=True,
+                               timeout=300)
+            rows = {}
+            lines = r.stdout.strip().splitlines()
+            hdr = lines[0].split(",")
+            for line in lines[1:]:
+                v = dict(zip(hdr, line.split(",")))
+                g = float(v["gpu_only_ms"])
+                rows[v["kernel"]] = {"gpu_only_us": round(g * 1e3, 2), "cpu_ms": float(v["cpu_ms"]),
+                                     "h2d_gpu_d2h_ms": float(v["h2d_gpu_d2h_ms"])}
+            out["reference_microbench_b200"] = {
+                "rows": rows, "rc": r.returncode,
+                "how": "the reference's falcom_cuda_microbench.cu built for sm_100a, --numel 2359296 --iters "
+                       "200: back-to-back launches on one resident 9.4 MB input (L2-resident on B200)"}
+        except Exception as e:   # a missing or failing baseline does not stop the bench
+            out["reference_microbench_b200"] = {"error": str(e)[:200]}
+    return out
+
+
+def per_layer_line(torch, so, rounds: int = 4):
+    """The path FalComC.py drives (FalComC.py:545,659): 266 separate
+    momentum_compressor_compress_layer calls on host arrays, then 266
+    decompress_layer calls on a second instance; host wall time per round."""
+    from compressor_b200 import workloads as W
+    from compressor_b200.abi import Codec, HostArray
+    lay = W.Layout.of("resnet50")
+    data = W.rounds("resnet50", rounds + 2, seed=4321)
+    enc, dec = Codec(so, client="Client1"), Codec(so, client="Client1")
+    names = [nm.encode() for nm in lay.names]
+    ts = []
+    for t, flat in enumerate(data):
+        hs = [HostArray(v) for v in lay.views(flat)]
+        t0 = time.perf_counter()
+        for i, nm in enumerate(names):
+            p = enc.lib.momentum_compressor_compress_layer(enc.h, nm, ctypes.byref(hs[i].c))
+            if not p:
+                raise RuntimeError("compress_layer failed")
+            o = dec.lib.momentum_compressor_decompress_layer(dec.h, p, b"Client1", nm)
+            if not o:
+                raise RuntimeError("decompress_layer failed")
+            dec.lib.ndarray_destroy(o)
+            enc.lib.compressed_layer_data_free(p)
+        if t >= 2:
+            ts.append(time.perf_counter() - t0)
+    enc.close()
+    dec.close()
+    ms = 1e3 * statistics.median(ts)
+    return {"ms_per_round": round(ms, 3), "value": round(lay.numel * 4 / (ms * 1e-3) / 1e9, 3), "unit": "GB/s",
+            "calls_per_round": 2 * len(names), "rounds": len(ts),
+            "how": "host wall clock; host float32 inputs, host payloads, host decoded arrays (FalComC's "
+                   "memory kinds); compress_layer and decompress_layer per tensor"}
+
+
+def pcie_line(torch, dev):
+    """Pinned host <-> device copy bandwidth (256 MiB, CUDA events, best of 5),
+    one direction at a time and both at once on two streams."""
+    n = 256 * 1024 * 1024
+    h1 = torch.empty(n, dtype=torch.uint8, pin_memory=True)
+    h2 = torch.empty(n, dtype=torch.uint8, pin_memory=True)
+    d1 = torch.empty(n, dtype=torch.uint8, device=dev)
+    d2 = torch.empty(n, dtype=torch.uint8, device=dev)
+    s1, s2 = torch.cuda.Stream(), torch.cuda.Stream()
+
+    def one(fn):
+        best = 1e9
+        for _ in range(5):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda.synchronize()
+            e0.record()
+            fn()
+            e1.record()
+            e1.synchronize()
+            best = min(best, e0.elapsed_time(e1))
+        return best
+
+    h2d = one(lambda: d1.copy_(h1, non_blocking=True))
+    d2h = one(lambda: h2.copy_(d2, non_blocking=True))
+
+    def both():
+        cur = torch.cuda.current_stream()
+        for s in (s1, s2):
+            s.wait_stream(cur)
+        with torch.cuda.stream(s1):
+            d1.copy_(h1, non_blocking=True)
+        with torch.cuda.stream(s2):
+            h2.copy_(d2, non_blocking=True)
+        cur.wait_stream(s1)
+        cur.wait_stream(s2)
+    duplex = one(both)
+    return {"h2d_gbs": round(n / (h2d * 1e-3) / 1e9, 2), "d2h_gbs": round(n / (d2h * 1e-3) / 1e9, 2),
+            "duplex_gbs": round(2 * n / (duplex * 1e-3) / 1e9, 2), "bytes": n}
+
+
+def reference_v4_line(torch, dev, rounds: int = 5):
+    """The reference's fused q8 GPU codec (cuda_feasibility/falcom_cuda_v4,
+    encode_q8_batch / decode_q8_batch) built from its own sources for sm_100a
+    (oracle/build_ref_gpu.py), on the same ResNet-50 rounds: encode of the
+    266 device tensors against the previous round (delta q8, one host sync
+    per layer, payload blob copied to pinned host memory), then decode from
+    that blob.  Host wall clock per round, the way the reference times it."""
+    import importlib.machinery
+    import importlib.util
+    so = os.path.join(ROOT, "oracle", "_ref", "v4", "_falcom_cuda_v4.so")
+    if not os.path.exists(so):
+        return {"unavailable": "oracle/_ref/v4 not built"}
+    spec = importlib.util.spec_from_file_location("_falcom_cuda_v4", so,
+                                                  loader=importlib.machinery.ExtensionFileLoader("_falcom_cuda_v4", so))
+    m = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(m)
+    data = DeviceUpdates(torch, "resnet50", [0], dev, seed0=8000)
+    lay = data.lay
+    shapes = [list(s) for s in lay.shapes]
+    flags = torch.ones(len(shapes), dtype=torch.uint8)
+    prev = None
+    ts = []
+    for t in range(rounds + 2):
+        data.next_round()
+        cur = [data.x[0][o:o + int(np.prod(s))].view(*s).clone() for o, s in zip(lay.offsets, lay.shapes)]
+        if prev is not None:
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            blob, offs, lens, scales, cands, _ = m.encode_q8_batch(cur, prev, flags)
+            dec, _ = m.decode_q8_batch(blob, offs, lens, scales, shapes, prev, flags, dev.index or 0)
+            torch.cuda.synchronize()
+            if t >= 2:
+                ts.append(time.perf_counter() - t0)
+        prev = cur
+    ms = 1e3 * statistics.median(ts)
+    return {"ms_per_round": round(ms, 3), "value": round(lay.numel * 4 / (ms * 1e-3) / 1e9, 3), "unit": "GB/s",
+            "rounds": len(ts),
+            "how": "reference v4 encode_q8_batch + decode_q8_batch (delta q8 in its own envelope, not the C wire "
+                   "format), device tensors in, pinned host blob between them, host wall clock"}
+
+
+# ------------------------------------------------------------------- ours
+def run_ours(args):
+    import torch
+    D = Dist()
+    from compressor_b200 import build as B
     if not os.path.exists(B.OUT):
         B.build()
     os.environ.setdefault("FALCOM_LOG_LEVEL", "ERROR")
-    model = args.model
+    so = B.OUT
+    stream = D.stream
+    assert stream.cuda_stream != 0
+    flush = L2Flush(torch, D.dev)
     K, Wm = args.steps, args.warmup
-    lay = W.Layout.of(model)
-    n_clients = args.clients_per_gpu * world
-    mine = list(F.shard(n_clients, world, rank))
-    weights = F.uniform_weights(n_clients)
-    upd = lay.numel * 4
-    offs_b = [4 * o for o in lay.offsets]
-    stream = torch.cuda.current_stream()
-    # layer chunks of the pipelined all-reduce (one chunk on a single GPU:
-    # nothing to overlap)
-    chunks = F.layer_chunks([int(np.prod(s)) for s in lay.shapes], args.ar_chunks if world > 1 else 1)
-    agg_layout = F.AggregateLayout(list(lay.names), [tuple(s) for s in lay.shapes], list(lay.offsets), lay.total)
-    chunk_offs_b = [offs_b[i0:i1] for i0, i1 in chunks]
-    chunk_c_offs = [(ctypes.c_size_t * (i1 - i0))(*lay.offsets[i0:i1]) for i0, i1 in chunks]
+    model, codec = args.model, args.codec
+    world = D.world
 
-    def prepared(lib):
-        return [PreparedBatch(lib, list(lay.names[i0:i1]), list(lay.shapes[i0:i1])) for i0, i1 in chunks]
-
-    # per-client AR(1) rho 0.9 (own seed) plus a common N(0, 1e-3^2) component
-    # drawn once per round with the same seed on every rank
-    sigma = torch.zeros(lay.total, device=dev)
-    for o, sh in zip(lay.offsets, lay.shapes):
-        sigma[o:o + int(np.prod(sh))] = 1e-3 / float(np.sqrt(W.fan_in(sh)))
-    gens = []
-    for c in mine:
-        g = torch.Generator(device=dev)
-        g.manual_seed(50_000 + c)
-        gens.append(g)
-    gcom = torch.Generator(device=dev)
-    gcom.manual_seed(49_999)
-    states = [None] * len(mine)
-    xs = [torch.empty(lay.total, device=dev) for _ in mine]
-
-    def next_round():
-        common = torch.randn(lay.total, device=dev, generator=gcom) * 1e-3
-        for j in range(len(mine)):
-            noise = torch.randn(lay.total, device=dev, generator=gens[j]) * sigma
-            states[j] = noise if states[j] is None else states[j].mul_(0.9).add_(noise)
-            torch.add(states[j], common, out=xs[j])
-
-    def new_instances():
-        encs = [Codec(B.OUT, client=f"Client{c + 1}") for c in mine]
-        dec = Codec(B.OUT, client="server")
-        for c in encs + [dec]:
-            assert c.lib.falcom_set_residual_codec(c.h, args.codec.encode()) == 0
-            c.lib.falcom_set_stream(c.h, ctypes.c_void_p(stream.cuda_stream))
-        return encs, dec
-
-    agg = torch.zeros(lay.total, dtype=torch.float32, device=dev)
-    flush = L2Flush(torch, dev)
-    cids = [f"Client{c + 1}".encode() for c in mine]
-
-    def fed_step(encs, dec, pbs, ptrs, count, e0=None, ear=None, e1=None):
-        if e0 is not None:
-            e0.record(stream)
-        # the first client's decode stores its weighted update (store mode of
-        # the fused aggregate), so the aggregate needs no clearing; the
-        # padding between tensors is never written and stays zero
-        if not mine:
-            agg.zero_()
-        ar = F.ChunkedAllreduce(agg, agg_layout, chunks, dist)
-        payload = 0
-        for g, (i0, i1) in enumerate(chunks):
-            pb = pbs[g]
-            for j, c in enumerate(mine):
-                pb.set_pointers(ptrs[j], chunk_offs_b[g])
-                r1 = pb.compress(encs[j].h, cids[j])
-                F.set_client_weight(dec.lib, dec.h, agg.data_ptr(), chunk_c_offs[g], i1 - i0, weights[c])
-                F.set_aggregate_store(dec.lib, dec.h, j == 0)
-                r2 = pb.decompress(dec.h, cids[j])
-                if r1 != 0 or r2 != 0:
-                    raise RuntimeError(f"codec failed on rank {rank} client {c}: {r1} {r2}")
-                payload += pb.payload_bytes()
-                count[0] += encs[j].lib.falcom_last_launches(encs[j].h) + dec.lib.falcom_last_launches(dec.h)
-                pb.release()
-            if ear is not None and g == len(chunks) - 1:
-                ear.record(stream)
-            ar.chunk_done(g)
-        ar.wait()
-        if e1 is not None:
-            e1.record(stream)
-        return payload
-
-    # ------------------------------------------------ device-resident value
-    encs, dec = new_instances()
-    pbs = prepared(encs[0].lib)
-    for _ in range(1 + Wm):
-        next_round()
-        fed_step(encs, dec, pbs, [x.data_ptr() for x in xs], [0])
-    torch.cuda.synchronize()
+    # ------------------------------------------------ headline (device value)
+    fr = FedRound(torch, D, model, [D.rank], world, codec, stream, so)
+    data = DeviceUpdates(torch, model, [D.rank], D.dev, seed0=1000)
+    local_gpus = list(range(int(os.environ.get("LOCAL_WORLD_SIZE", world))))
+    with ClockSampler(local_gpus, interval_ms=20 if world == 1 else 50, enabled=D.local == 0) as clk:
+        step, codec_ms, _, ar = timed_rounds(torch, D, fr, data, K, Wm, flush)
+    total_ms = D.max(sum(step))
+    ms_per_step = total_ms / K
+    value = world * fr.upd / (ms_per_step * 1e-3) / 1e9
+    launches_timed = fr.launches
+    payload = fr.payload
+    if args.mode == "value":
+        fr.close()
+        if D.rank == 0:
+            print(json.dumps({"metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world,
+                              "steps": K, "warmup": Wm, "ms_per_step": round(ms_per_step, 4),
+                              "mode": "value-only (profiler run)"}))
+        D.close()
+        return 0
+    codec_max = D.max(statistics.mean(codec_ms))
+    # peer wait vs transfer of the all-reduce, in separate diagnostic rounds
+    split = None
     if world > 1:
-        dist.barrier()
-    step_ms, ar_ms, cnt, payload = [], [], [0], 0
-    with ClockSampler(local) as clk:
-        for _ in range(K):
-            next_round()
-            flush()
-            e0, ear, e1 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
-            payload = fed_step(encs, dec, pbs, [x.data_ptr() for x in xs], cnt, e0, ear, e1)
-            e1.synchronize()
-            step_ms.append(e0.elapsed_time(e1))
-            ar_ms.append(ear.elapsed_time(e1))
-    torch.cuda.synchronize()
-    tot = torch.tensor([sum(step_ms)], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(tot, op=dist.ReduceOp.MAX)
-    ms_per_step = float(tot.item()) / K
-    value = n_clients * upd / (ms_per_step * 1e-3) / 1e9
-    for c in encs + [dec]:
-        c.close()
+        s2, c2, w2, a2 = timed_rounds(torch, D, fr, data, min(K, 10), 0, flush, split=True)
+        split = {"steps": len(s2), "peer_wait_ms_rank0": round(statistics.mean(w2), 4),
+                 "transfer_ms_rank0": round(statistics.mean(a2), 4),
+                 "transfer_ms_max": round(D.max(statistics.mean(a2)), 4),
+                 "how": "a 1-element all-reduce after the decode ends when every rank has arrived (peer wait); "
+                        "the aggregate all-reduce follows (transfer); rounds outside the timed ones"}
+    roofline = kernel_roofline(torch, D, fr, data, K, flush, codec)
+    peak = roofline["peak"]
+    roofline["closed_loop_frac"] = round(roofline["closed_loop_algorithmic_bytes"] /
+                                         (codec_max * 1e-3) / 1e9 / peak, 4)
+    check = fedavg_check(torch, D, fr, data)
+    fr.close()
 
     # ------------------------------------------------------------ e2e (host)
-    encs, dec = new_instances()
-    pbs = prepared(encs[0].lib)
-    hosts = [torch.empty(lay.total, dtype=torch.float32, pin_memory=True) for _ in mine]
-    agg_host = torch.empty(lay.total, dtype=torch.float32, pin_memory=True)
-    e2e_ms, h2d, d2h = [], 0, 0
-    for it in range(1 + Wm + K):
-        next_round()
-        for h, x in zip(hosts, xs):
-            h.copy_(x)
-        torch.cuda.synchronize()
+    fr2 = FedRound(torch, D, model, [D.rank], world, codec, stream, so, host_inputs=True)
+    n_host = min(K, 8) + 1
+    hosts = [torch.empty(fr2.lay.total, dtype=torch.float32, pin_memory=True) for _ in range(n_host)]
+    agg_host = torch.empty(fr2.lay.total, dtype=torch.float32, pin_memory=True)
+    for i, h in enumerate(hosts):
+        data.next_round()
+        h.copy_(data.x[0])
+    torch.cuda.synchronize()
+    for i in range(1 + Wm):
+        fr2.codec_part([hosts[i % n_host].data_ptr()], count_payload=(i == Wm))
+        fr2.allreduce()
+    e2e_ms = []
+    for j in range(K):
+        h = hosts[(1 + Wm + j) % n_host]
+        D.barrier()
         flush()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        pbytes = fed_step(encs, dec, pbs, [h.data_ptr() for h in hosts], [0], e0)
-        agg_host.copy_(agg, non_blocking=True)
+        e0.record(stream)
+        fr2.codec_part([h.data_ptr()])
+        fr2.allreduce()
+        agg_host.copy_(fr2.agg, non_blocking=True)
         e1.record(stream)
         e1.synchronize()
-        if it >= 1 + Wm:
-            e2e_ms.append(e0.elapsed_time(e1))
-            h2d = len(mine) * upd + pbytes       # inputs up, payloads up for the decoder
-            d2h = pbytes + len(mine) * upd + 4 * lay.total   # payloads and decoded outputs down, aggregate
-    for c in encs + [dec]:
-        c.close()
-    e2e_t = torch.tensor([sum(e2e_ms)], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(e2e_t, op=dist.ReduceOp.MAX)
-    e2e_step = float(e2e_t.item()) / K
-    e2e_val = n_clients * upd / (e2e_step * 1e-3) / 1e9
+        e2e_ms.append(e0.elapsed_time(e1))
+    pbytes = fr2.payload
+    fr2.close()
+    e2e_step = D.max(sum(e2e_ms)) / K
+    e2e_val = world * fr2.upd / (e2e_step * 1e-3) / 1e9
+    h2d = fr2.upd + pbytes            # inputs up; payloads up for the server
+    d2h = pbytes + 4 * fr2.lay.total  # payloads down; the aggregate down
+    del hosts, agg_host
+    torch.cuda.empty_cache()
 
-    if rank == 0:
-        peak, peak_kind = measured_peak()
-        ab = W.algorithmic_bytes(model, args.codec)
-        # per client: the closed loop's bytes plus the fused aggregate (read
-        # the decoded tensor, read and write the aggregate: 12 B / element;
-        # the first client stores without reading the aggregate: 8 B)
-        alg = len(mine) * (ab["bytes_per_round"] + 12 * lay.numel) - (4 * lay.numel if mine else 0)
+    # --------------------------------------------------- nested configs
+    nested = {}
+    common = 1e-3
+    if not args.skip_configs:
+        # warm-up rounds: round 0 is direct, the first momentum rounds
+        # allocate the state buffers; steady state from the fourth round
+        nested["federated_64"] = federated_line(torch, D, "resnet50", 64, codec, min(K, 5), 4, flush, so, stream,
+                                                common)
+        nested["gpt2_medium_16"] = federated_line(torch, D, "gpt2-medium", 16, "q8", min(K, 3), 3, flush, so,
+                                                  stream, 0.0)
+    if world == 1 and not args.skip_configs:
+        nested["resnet18"] = closed_loop_line(torch, D, "resnet18", codec, K, Wm, flush, so, stream)
+        nested["int4"] = closed_loop_line(torch, D, "resnet50", "int4", K, Wm, flush, so, stream)
+        nested["microbench_512x512x3x3"] = microbench_line(torch, D, 20, flush, so, stream)
+        nested["per_layer_api"] = per_layer_line(torch, so)
+        nested["pcie"] = pcie_line(torch, D.dev)
+        try:
+            nested["reference_gpu_v4"] = reference_v4_line(torch, D.dev)
+        except Exception as e:   # the baseline is reported, not required
+            nested["reference_gpu_v4"] = {"error": str(e)[:300]}
+    out = None
+    if D.rank == 0:
+        cpu, cpu8 = None, None
+        if world == 1 and not args.skip_cpu_baseline and ref_library():
+            threads = os.cpu_count() or 1
+            cpu = cpu_baseline_entry(model, threads, args.cpu_budget_s)
+            cpu8 = cpu_baseline_entry(model, 8, args.cpu_budget_s)
+        ab_gpu = {"bound": "hbm"}
         out = {
             "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world, "steps": K,
             "warmup": Wm, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic (per-client seeded AR(1) Gaussian updates rho=0.9, sigma=1e-3/sqrt(fan_in), "
-                    "plus a shared N(0, 1e-3^2) component per round; ResNet-50 state-dict shapes)",
-            "config": {"workload": f"federated round of {n_clients} {model} clients, {args.clients_per_gpu} per "
-                                   f"GPU: compress_batch per client, decompress_batch on one server decoder "
-                                   f"per GPU with the weighted aggregate fused in, NCCL sum all-reduce of "
-                                   f"the {lay.numel}-element aggregate in {len(chunks)} layer chunk(s), each "
-                                   f"issued once decoded; residual codec {args.codec}",
-                       "clients": n_clients, "clients_per_gpu": args.clients_per_gpu,
-                       "allreduce_chunks": len(chunks),
-                       "elements_per_client": lay.numel, "update_bytes_per_client": upd, "codec": args.codec,
-                       "l2": "flushed between steps (256 MiB write, then 256 MiB read of a second buffer; outside the timed events)",
-                       "parallelism": f"clients sharded over {world} GPU(s), NCCL all-reduce of the aggregate"},
-            "gpu_launches": cnt[0],
-            "payload_bytes_per_step_rank0": payload,
-            # all-reduce time left after the last chunk's decode (the rest overlaps the codec)
-            "allreduce_exposed_ms_rank0": round(statistics.mean(ar_ms), 4),
-            "roofline": {"bound": "hbm", "kernel": "federated step (all codec kernels + aggregate)",
-                         "achieved": round(alg / (ms_per_step * 1e-3) / 1e9, 1), "peak": peak,
-                         "peak_kind": peak_kind, "unit": "GB/s",
-                         "frac": round(alg / (ms_per_step * 1e-3) / 1e9 / peak, 4), "traffic": None,
-                         "algorithmic_bytes_per_step_per_gpu": int(alg)},
+            "data": "synthetic (seeded AR(1) Gaussian updates rho=0.9, sigma=1e-3/sqrt(fan_in), ResNet-50 "
+                    "state-dict shapes, generated on the GPU)",
+            "config": {"workload": f"{model} closed loop, one client per GPU: compress_batch on the client's "
+                                   f"encoder + decompress_batch on a separate server decoder writing the decoded "
+                                   f"update into the server aggregate (weight 1/{world}, fused into the "
+                                   f"reconstruct kernel, no separate decoded copy)"
+                                   + (", NCCL sum all-reduce of the aggregate" if world > 1 else
+                                      "; at one GPU the aggregate is the decoded update itself"),
+                       "elements_per_client": fr.lay.numel, "update_bytes_per_client": fr.upd,
+                       "clients_per_gpu": 1, "codec": codec, "frames": "GPU zstd frames (Raw / RLE blocks)",
+                       "l2": "flushed between steps (256 MiB write, then 256 MiB read of a second buffer; "
+                             "outside the timed events)",
+                       "parallelism": f"clients sharded over {world} GPU(s)" +
+                                      (", NCCL all-reduce of the aggregate" if world > 1 else "")},
+            "gpu_launches": launches_timed,
+            "payload_bytes_per_round": payload,
+            "codec_ms_per_step_max": round(codec_max, 4),
+            "allreduce_ms_rank0": round(statistics.mean(ar), 4) if world > 1 else 0.0,
+            "allreduce_split": split,
+            "aggregate_check": check,
+            "roofline": roofline,
             "e2e": {"value": round(e2e_val, 3), "unit": "GB/s", "ms_per_step": round(e2e_step, 4),
                     "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h)},
             "clocks": clk.summary(),
-            "cpu_baseline": None,
+            "cpu_baseline": cpu,
+            "cpu_baseline_8_threads": cpu8,
         }
+        del ab_gpu
+        out.update(nested)
         print(json.dumps(out))
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
+    D.close()
     return 0
 
 
@@ -713,7 +1003,8 @@ def run_replay(args):
     if not os.path.exists(B.OUT):
         B.build()
     os.environ.setdefault("FALCOM_LOG_LEVEL", "ERROR")
-    stream = torch.cuda.current_stream()
+    stream = torch.cuda.Stream()      # shared by torch's work and the library's
+    torch.cuda.set_stream(stream)
     rounds = []
     for f in files:
         r = R.ReplayRound(f, "device", 0, B.OUT)
@@ -781,16 +1072,11 @@ def main():
     ap.add_argument("--model", default="resnet50")
     ap.add_argument("--codec", default="q8", choices=["q8", "int4", "raw"])
     ap.add_argument("--skip-cpu-baseline", action="store_true")
-    ap.add_argument("--cpu-budget-s", type=float, default=20.0)
+    ap.add_argument("--skip-configs", action="store_true",
+                    help="headline step only (no federated / GPT-2 / per-config lines)")
+    ap.add_argument("--cpu-budget-s", type=float, default=12.0)
     ap.add_argument("--mode", default="full", choices=["full", "value"],
                     help="value: only the device-resident timed loop (for profiler runs)")
-    ap.add_argument("--federated", action="store_true",
-                    help="federated round (decode + weighted aggregate + all-reduce) also on one GPU")
-    ap.add_argument("--ar-chunks", type=int, default=1,
-                    help="federated round on N > 1 GPUs: layer chunks of the pipelined aggregate all-reduce "
-                         "(1 = one all-reduce after the whole decode; more chunks measured slower on B200)")
-    ap.add_argument("--clients-per-gpu", type=int, default=1,
-                    help="federated round: clients per GPU (64 / N for the 64-client round)")
     ap.add_argument("--replay", default=None,
                     help="glob of captured replay rounds (.bin): time the closed loop on them instead")
     args = ap.parse_args()
@@ -799,8 +1085,6 @@ def main():
         return run_reference(args)
     if args.replay:
         return run_replay(args)
-    if int(os.environ.get("WORLD_SIZE", "1")) > 1 or args.federated:
-        return run_federated(args)
     return run_ours(args)
 
 

@@ -26,4 +26,6 @@ def main(ref_root: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
+    from oracle.reference_root import reference_root
+    main(sys.argv[1] if len(sys.argv) > 1 else reference_root())

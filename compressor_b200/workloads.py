@@ -8,7 +8,9 @@ architecture):
 * ``resnet18`` / ``resnet50``: round 0 per tensor N(0, (1e-3/sqrt(fan_in))^2);
   round t: d_t = rho * d_{t-1} + N(0, same sigma^2), rho = 0.9.
 * ``microbench``: one 512x512x3x3 tensor, sigma = 1e-4, rho = 0.9.
-* ``gpt2-medium``: Student-t (nu = 3) scaled by 1e-4, rho = 0.8.
+* ``gpt2-medium``: Student-t (nu = 3) scaled by 1e-4, rho = 0.8
+  (``gpt2-medium-slice``: the same for the embedding tables, the first block
+  and the final layer norm only).
 * multi-client federations add a shared N(0, (1e-3)^2) component per round.
 
 Draws are float32 from numpy PCG64 with fixed seeds; the same host bytes feed
@@ -35,8 +37,10 @@ def manifest(model: str) -> List[Tuple[str, Tuple[int, ...]]]:
         return out
     if model == "microbench":
         return [("layer4.0.conv2.weight", (512, 512, 3, 3))]
-    if model == "gpt2-medium":
-        d, vocab, npos, L = 1024, 50257, 1024, 24
+    if model in ("gpt2-medium", "gpt2-medium-slice"):
+        # the slice: both full-size embedding tables, the first block and the
+        # final layer norm (the parity tests' subset)
+        d, vocab, npos, L = 1024, 50257, 1024, 24 if model == "gpt2-medium" else 1
         out = [("transformer.wte.weight", (vocab, d)), ("transformer.wpe.weight", (npos, d))]
         for i in range(L):
             p = f"transformer.h.{i}."
@@ -95,7 +99,7 @@ class UpdateStream:
         self.rng = np.random.Generator(np.random.PCG64(seed))
         self.common = np.random.Generator(np.random.PCG64(common_seed)) if common_std > 0 else None
         self.common_std = common_std
-        if model == "gpt2-medium":
+        if model.startswith("gpt2-medium"):
             self.rho = 0.8 if rho is None else rho
             self.dist = dist or "student_t3"
         else:

@@ -1,6 +1,12 @@
 """Full-size parity on the model workloads: ResNet-18 (101 tensors, 5
 rounds) and ResNet-50 (266 tensors, 3 rounds) state-dict shapes with seeded
-AR(1) updates, and the 512x512x3x3 microbenchmark tensor (6 rounds).
+AR(1) updates, the 512x512x3x3 microbenchmark tensor (6 rounds), and a
+GPT-2-medium slice with Student-t updates (2 rounds): the full-size token
+embedding (50257x1024) and position embedding, the first transformer block
+and the final layer norm.  GPT-2 has no 4-D tensors, so under the
+reference's rules every weight above the cutoff takes the direct lossy path
+(momentum_compressor_openmp_simd_final.c:2436-2507 in round 1,
+:2337-2412 after) and everything else the lossless one.
 
 Against the reference build (oracle/_ref, the reference's own grouped
 OpenMP/SIMD codec with SZ3 stubbed):
@@ -22,7 +28,8 @@ from oracle import binding as ob
 
 pytestmark = pytest.mark.gpu
 
-CASES = [("resnet18", 5), ("resnet50", 3), ("microbench", 6)]
+CASES = [("resnet18", 5), ("resnet50", 3), ("microbench", 6), ("gpt2-medium-slice", 2)]
+CODE_CASES = [CASES[0], CASES[1], CASES[3]]
 
 
 def _rounds(model, n):
@@ -71,13 +78,16 @@ def test_model_bytes_identical_to_reference(product_lib, model, n_rounds):
         for name, ya, yb in zip(lay.names, YA, YB):
             assert ya.dtype == yb.dtype and ya.shape == yb.shape, name
             assert np.array_equal(ya.view(np.uint8), yb.view(np.uint8)), name
-    assert n_pred > 0
+    if model.startswith("gpt2"):
+        assert n_pred == 0     # no 4-D tensors: direct / direct_generic only
+    else:
+        assert n_pred > 0
     for c in (ours, ref, ours_d, ref_d):
         c.close()
 
 
 @pytest.mark.parametrize("codec,qmax", [("q8", 127), ("int4", 7)])
-@pytest.mark.parametrize("model,n_rounds", CASES[:2])
+@pytest.mark.parametrize("model,n_rounds", CODE_CASES)
 def test_model_codes_are_quantised_raw_residual(product_lib, model, n_rounds, codec, qmax):
     lay, rounds = _rounds(model, n_rounds)
     raw = Codec(product_lib, client="Client1")
