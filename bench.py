@@ -333,6 +333,7 @@ class FedRound:
         self.upd = self.lay.numel * 4
         self.launches = 0
         self.payload = 0
+        self.srv_state = None
 
     def close(self):
         for c in self.encs + [self.srv]:
@@ -354,10 +355,18 @@ class FedRound:
                 pb.set_pointers(ptrs[j], self.offs_b)
                 self.bound[j] = ptrs[j]
             r1 = pb.compress(self.encs[j].h, cid)
-            assert lib.falcom_set_aggregate(srv.h, ctypes.c_void_p(self.agg.data_ptr()), self.c_offs,
-                                            len(self.lay.offsets), self.w) == 0
-            lib.falcom_set_aggregate_store(srv.h, 1 if j == 0 else 0)
-            lib.falcom_set_aggregate_only(srv.h, 0 if outputs else 1)
+            # the server's aggregate settings, changed only when they differ
+            # (uniform weights: set once; the store flag for the first client)
+            want = (self.agg.data_ptr(), self.w, 1 if j == 0 else 0, 0 if outputs else 1)
+            if self.srv_state is None or self.srv_state[:2] != want[:2]:
+                assert lib.falcom_set_aggregate(srv.h, ctypes.c_void_p(want[0]), self.c_offs,
+                                                len(self.lay.offsets), want[1]) == 0
+                self.srv_state = (want[0], want[1], None, None)
+            if self.srv_state[2] != want[2]:
+                lib.falcom_set_aggregate_store(srv.h, want[2])
+            if self.srv_state[3] != want[3]:
+                lib.falcom_set_aggregate_only(srv.h, want[3])
+            self.srv_state = want
             r2 = pb.decompress(srv.h, cid)
             if r1 != 0 or r2 != 0:
                 raise RuntimeError(f"codec failed on rank {self.D.rank} client {cid}: {r1} {r2} "

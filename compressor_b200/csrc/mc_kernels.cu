@@ -1846,10 +1846,12 @@ __device__ void recon_tile(const mc_dec_launch &L, const StageDesc &d, const flo
                     if (M != 1 && o4) st_f4(o4 + q, rv, spol);
                     if (M != 0) {
                         if (avec) {
+                            // streamed like the other outputs: the aggregate is
+                            // read again only by the next client's decode
                             float4 a = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
                             if (!astore) a = a4[q];
-                            a4[q] = make_float4(__fmaf_rn(aw, rec[0], a.x), __fmaf_rn(aw, rec[1], a.y),
-                                                __fmaf_rn(aw, rec[2], a.z), __fmaf_rn(aw, rec[3], a.w));
+                            st_f4(a4 + q, make_float4(__fmaf_rn(aw, rec[0], a.x), __fmaf_rn(aw, rec[1], a.y),
+                                                      __fmaf_rn(aw, rec[2], a.z), __fmaf_rn(aw, rec[3], a.w)), spol);
                         } else {
                             agg_quad(I, tr.e0 + 4 * q, tr.e1, rec);
                         }
