@@ -59,9 +59,9 @@ NCU_TRAFFIC = {
         "enc_pass1_stats_sign": 246_334_464,
         "enc_pass2_variance": 193_776_128,
         "enc_pass3_predict": 342_665_216,
-        "enc_pass4_quantize_pack": 201_771_776,
+        "enc_pass4_quantize_pack": 201_046_528,
         "dec_prefix": 259_840,
-        "dec_reconstruct": 438_323_456,
+        "dec_reconstruct": 439_436_032,
     },
 }
 
