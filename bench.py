@@ -305,7 +305,7 @@ class FedRound:
     the aggregate over the ranks (N > 1)."""
 
     def __init__(self, torch, D: Dist, model: str, clients, n_total: int, codec: str, stream, so_path,
-                 host_inputs: bool = False):
+                 host_inputs: bool = False, peer: bool = False):
         from compressor_b200 import workloads as W
         from compressor_b200.abi import Codec, PreparedBatch
         self.torch, self.D, self.model = torch, D, model
@@ -329,15 +329,32 @@ class FedRound:
         self.bound = [None] * len(self.cids)
         self.offs_b = [4 * o for o in self.lay.offsets]
         self.c_offs = (ctypes.c_size_t * len(self.lay.offsets))(*self.lay.offsets)
-        self.agg = torch.zeros(self.lay.total, dtype=torch.float32, device=D.dev)
+        self.peer = None
+        self.collective = "none" if D.world == 1 else "nccl all-reduce"
+        if peer and D.world > 1:
+            from compressor_b200 import federated as F
+            try:   # every rank succeeds or every rank raises (PeerAggregate agrees first)
+                self.peer = F.PeerAggregate(torch, D.dist, self.lay.total, D.local)
+                self.collective = ("decoder stores into owner shards over NVLink peer memory, "
+                                   "shard sum + all-gather kernel")
+            except RuntimeError as e:
+                log(f"peer aggregate unavailable, NCCL all-reduce instead: {e}")
+        if self.peer is not None:
+            self.agg = self.peer.agg
+        else:
+            self.agg = torch.zeros(self.lay.total, dtype=torch.float32, device=D.dev)
         self.upd = self.lay.numel * 4
         self.launches = 0
         self.payload = 0
         self.srv_state = None
+        self.shard_on = False
 
     def close(self):
         for c in self.encs + [self.srv]:
             c.close()
+        if self.peer is not None:
+            self.peer.close()
+            self.peer = None
 
     def codec_part(self, ptrs, outputs: bool = False, check64=None, count_payload: bool = False):
         """Compress + decode of every local client (queued on the stream,
@@ -367,6 +384,14 @@ class FedRound:
             if self.srv_state[3] != want[3]:
                 lib.falcom_set_aggregate_only(srv.h, want[3])
             self.srv_state = want
+            if self.peer is not None:
+                # the rank's last client lands its partial sum in the owners' slots
+                last = j == len(self.cids) - 1
+                if last and not self.shard_on:
+                    self.peer.enable(lib, srv.h)
+                elif not last and self.shard_on:
+                    self.peer.disable(lib, srv.h)
+                self.shard_on = last
             r2 = pb.decompress(srv.h, cid)
             if r1 != 0 or r2 != 0:
                 raise RuntimeError(f"codec failed on rank {self.D.rank} client {cid}: {r1} {r2} "
@@ -387,7 +412,10 @@ class FedRound:
             pb.release()
 
     def allreduce(self):
-        self.D.sum_(self.agg)
+        if self.peer is not None:
+            self.peer.finish(self.srv.lib, self.stream.cuda_stream)
+        else:
+            self.D.sum_(self.agg)
 
 
 class E2ERound:
@@ -703,14 +731,14 @@ def closed_loop_line(torch, D, model, codec, K, W, flush, so, stream):
     return out
 
 
-def federated_line(torch, D, model, n_clients, codec, K, W, flush, so, stream, common_std):
+def federated_line(torch, D, model, n_clients, codec, K, W, flush, so, stream, common_std, peer=False):
     """n_clients clients block-distributed over the ranks; per step: every
     local client's compress + decode into the aggregate, then the NCCL
     all-reduce; value = all clients' update bytes / max-over-ranks step time.
     Ends with the FedAvg check of the reduced aggregate."""
     from compressor_b200 import federated as F
     mine = list(F.shard(n_clients, D.world, D.rank))
-    fr = FedRound(torch, D, model, mine, n_clients, codec, stream, so)
+    fr = FedRound(torch, D, model, mine, n_clients, codec, stream, so, peer=peer)
     data = DeviceUpdates(torch, model, mine, D.dev, common_std=common_std)
     step, codec_ms, wait, ar = timed_rounds(torch, D, fr, data, K, W, flush, split=D.world > 1)
     total = D.max(sum(step))
@@ -723,6 +751,7 @@ def federated_line(torch, D, model, n_clients, codec, K, W, flush, so, stream, c
            "peer_wait_ms_rank0": round(statistics.mean(wait), 4) if D.world > 1 else 0.0,
            "allreduce_ms_rank0": round(statistics.mean(ar), 4) if D.world > 1 else 0.0,
            "allreduce_bytes": 4 * fr.lay.total if D.world > 1 else 0,
+           "aggregate_collective": fr.collective,
            "aggregate_check": check, "gpu_launches_per_step_rank0": fr.launches // max(1, K)}
     fr.close()
     del data
@@ -927,7 +956,7 @@ def run_ours(args):
     world = D.world
 
     # ------------------------------------------------ headline (device value)
-    fr = FedRound(torch, D, model, [D.rank], world, codec, stream, so)
+    fr = FedRound(torch, D, model, [D.rank], world, codec, stream, so, peer=args.aggregate == "peer")
     data = DeviceUpdates(torch, model, [D.rank], D.dev, seed0=1000)
     local_gpus = list(range(int(os.environ.get("LOCAL_WORLD_SIZE", world))))
     with ClockSampler(local_gpus, interval_ms=20 if world == 1 else 50, enabled=D.local == 0) as clk:
@@ -960,6 +989,7 @@ def run_ours(args):
     roofline["closed_loop_frac"] = round(roofline["closed_loop_algorithmic_bytes"] /
                                          (codec_max * 1e-3) / 1e9 / peak, 4)
     check = fedavg_check(torch, D, fr, data)
+    collective = fr.collective
     fr.close()
 
     # ------------------------------------------------------------ e2e (host)
@@ -999,10 +1029,11 @@ def run_ours(args):
     if not args.skip_configs:
         # warm-up rounds: round 0 is direct, the first momentum rounds
         # allocate the state buffers; steady state from the fourth round
+        pa = args.aggregate == "peer"
         nested["federated_64"] = federated_line(torch, D, "resnet50", 64, codec, min(K, 5), 4, flush, so, stream,
-                                                common)
+                                                common, peer=pa)
         nested["gpt2_medium_16"] = federated_line(torch, D, "gpt2-medium", 16, "q8", min(K, 3), 3, flush, so,
-                                                  stream, 0.0)
+                                                  stream, 0.0, peer=pa)
     if world == 1 and not args.skip_configs:
         nested["resnet18"] = closed_loop_line(torch, D, "resnet18", codec, K, Wm, flush, so, stream)
         nested["int4"] = closed_loop_line(torch, D, "resnet50", "int4", K, Wm, flush, so, stream)
@@ -1031,19 +1062,20 @@ def run_ours(args):
                                    f"encoder + decompress_batch on a separate server decoder writing the decoded "
                                    f"update into the server aggregate (weight 1/{world}, fused into the "
                                    f"reconstruct kernel, no separate decoded copy)"
-                                   + (", NCCL sum all-reduce of the aggregate" if world > 1 else
+                                   + (", the aggregate summed over the GPUs" if world > 1 else
                                       "; at one GPU the aggregate is the decoded update itself"),
                        "elements_per_client": fr.lay.numel, "update_bytes_per_client": fr.upd,
                        "clients_per_gpu": 1, "codec": codec, "frames": "GPU zstd frames (Raw / RLE blocks)",
                        "l2": "flushed between steps (256 MiB write, then 256 MiB read of a second buffer; "
                              "outside the timed events)",
                        "parallelism": f"clients sharded over {world} GPU(s)" +
-                                      (", NCCL all-reduce of the aggregate" if world > 1 else "")},
+                                      (f", aggregate summed by {collective}" if world > 1 else "")},
             "gpu_launches": launches_timed,
             "payload_bytes_per_round": payload,
             "codec_ms_per_step_max": round(codec_max, 4),
             "allreduce_ms_rank0": round(statistics.mean(ar), 4) if world > 1 else 0.0,
             "allreduce_split": split,
+            "aggregate_collective": collective,
             "aggregate_check": check,
             "roofline": roofline,
             "e2e": {"value": round(e2e_val, 3), "unit": "GB/s", "ms_per_step": round(e2e_step, 4),
@@ -1156,6 +1188,9 @@ def main():
     ap.add_argument("--skip-configs", action="store_true",
                     help="headline step only (no federated / GPT-2 / per-config lines)")
     ap.add_argument("--cpu-budget-s", type=float, default=12.0)
+    ap.add_argument("--aggregate", default="peer", choices=["peer", "nccl"],
+                    help="N > 1: how the server aggregate is summed over the GPUs (peer: reduce-scatter fused "
+                         "into the decoder over NVLink + shard sum / all-gather kernel; nccl: all-reduce)")
     ap.add_argument("--e2e-chunks", type=int, default=3,
                     help="layer chunks of the pipelined host-buffer step (e2e)")
     ap.add_argument("--mode", default="full", choices=["full", "value"],

@@ -507,6 +507,12 @@ def bind_extensions(lib: ctypes.CDLL) -> None:
     lib.falcom_set_aggregate_store.restype = ctypes.c_int
     lib.falcom_set_aggregate_only.argtypes = [c_vp, ctypes.c_int]
     lib.falcom_set_aggregate_only.restype = ctypes.c_int
+    lib.falcom_set_aggregate_shards.argtypes = [c_vp, ctypes.POINTER(c_vp), ctypes.c_int, ctypes.c_int,
+                                                ctypes.c_size_t]
+    lib.falcom_set_aggregate_shards.restype = ctypes.c_int
+    lib.falcom_shard_reduce.argtypes = [c_vp, ctypes.c_int, ctypes.c_int, ctypes.c_size_t, ctypes.c_size_t,
+                                        ctypes.POINTER(c_vp), c_vp]
+    lib.falcom_shard_reduce.restype = ctypes.c_int
     lib.falcom_state_save.argtypes = [c_vp, ctypes.c_char_p]
     lib.falcom_state_save.restype = ctypes.c_int
     lib.falcom_state_load.argtypes = [c_vp, ctypes.c_char_p]

@@ -986,6 +986,7 @@ MC_EXPORT int falcom_set_aggregate(MomentumCompressor *mc, float *aggregate, con
         mc->agg_n = 0;
         mc->agg_store = 0;
         mc->agg_no_output = 0;
+        memset(&mc->agg_shards, 0, sizeof(mc->agg_shards));
         return ERROR_NONE;
     }
     int d = -1;
@@ -1015,6 +1016,51 @@ MC_EXPORT int falcom_set_aggregate_only(MomentumCompressor *mc, int on) {
     if (!mc || (on != 0 && on != 1)) return ERROR_INVALID_PARAM;
     mc->agg_no_output = on;
     return ERROR_NONE;
+}
+
+MC_EXPORT int falcom_set_aggregate_shards(MomentumCompressor *mc, float *const *landing, int nranks, int rank,
+                                          size_t shard_elems) {
+    if (!mc) return ERROR_INVALID_PARAM;
+    if (!landing || nranks == 0) {
+        memset(&mc->agg_shards, 0, sizeof(mc->agg_shards));
+        return ERROR_NONE;
+    }
+    if (nranks < 1 || nranks > MC_MAX_RANKS || rank < 0 || rank >= nranks || shard_elems % 64 != 0 ||
+        shard_elems < MC_TILE_ELEMS) {
+        mc_set_error(mc, "falcom_set_aggregate_shards: need 1..%d ranks, 0 <= rank < nranks and a shard of a "
+                         "multiple of 64 elements, at least %d", MC_MAX_RANKS, MC_TILE_ELEMS);
+        return ERROR_INVALID_PARAM;
+    }
+    for (int r = 0; r < nranks; r++) {
+        if (!landing[r] || ((uintptr_t)landing[r] & 15) != 0) {
+            mc_set_error(mc, "falcom_set_aggregate_shards: landing buffer %d is NULL or not 16-byte aligned", r);
+            return ERROR_INVALID_PARAM;
+        }
+    }
+    memset(&mc->agg_shards, 0, sizeof(mc->agg_shards));
+    for (int r = 0; r < nranks; r++) mc->agg_shards.landing[r] = landing[r];
+    mc->agg_shards.shard = (int64_t)shard_elems;
+    mc->agg_shards.nranks = nranks;
+    mc->agg_shards.rank = rank;
+    return ERROR_NONE;
+}
+
+MC_EXPORT int falcom_shard_reduce(const float *landing, int nranks, int rank, size_t shard_elems,
+                                  size_t total_elems, float *const *aggregates, void *stream) {
+    if (!landing || !aggregates || nranks < 1 || nranks > MC_MAX_RANKS || rank < 0 || rank >= nranks ||
+        shard_elems % 64 != 0 || shard_elems == 0 || total_elems > (size_t)nranks * shard_elems ||
+        ((uintptr_t)landing & 15) != 0) {
+        fprintf(stderr, "[ERROR] falcom_shard_reduce: invalid arguments\n");
+        return ERROR_INVALID_PARAM;
+    }
+    for (int r = 0; r < nranks; r++) {
+        if (!aggregates[r] || ((uintptr_t)aggregates[r] & 15) != 0) {
+            fprintf(stderr, "[ERROR] falcom_shard_reduce: aggregate %d is NULL or not 16-byte aligned\n", r);
+            return ERROR_INVALID_PARAM;
+        }
+    }
+    return mc_launch_shard_reduce(landing, nranks, rank, (int64_t)shard_elems, (int64_t)total_elems, aggregates,
+                                  stream) == 1 ? ERROR_NONE : ERROR_DECOMPRESSION;
 }
 
 /* ----------------------------------------------------------- kernel timing */

@@ -1133,6 +1133,7 @@ typedef struct {
     size_t sg_len;            /* sign content bytes of a Raw-block sign frame */
     int foreign;              /* a frame lives in device memory the library does not own */
     float *agg;               /* fused aggregate region of this item (float32 items), NULL */
+    size_t agg_off;           /* its element offset in the aggregate */
     int agg_only;             /* decoded into the aggregate only: no output array */
     const char *why;
 } dplan;
@@ -1490,7 +1491,20 @@ static int dec_segment(MomentumCompressor *mc, const BatchItem *items, size_t n,
          * get no output slot */
         if (mc->agg && d->dt == DTYPE_FLOAT32 && base + i < mc->agg_n) {
             d->agg = mc->agg + mc->agg_off[base + i];
+            d->agg_off = mc->agg_off[base + i];
             d->agg_only = mc->agg_no_output;
+            /* sharded: every element must fall in a shard, quads must not
+             * straddle two (offsets and shards are multiples of 4) */
+            if (mc->agg_shards.nranks > 0 &&
+                (d->agg_off % 4 != 0 ||
+                 d->agg_off + d->n > (size_t)mc->agg_shards.nranks * (size_t)mc->agg_shards.shard)) {
+                mc_set_error(mc, "Batch decompress: item %zu's aggregate region [%zu, %zu) does not fit the %d "
+                                 "shards of %lld elements (offsets must be multiples of 4)", base + i,
+                             d->agg_off, d->agg_off + d->n, mc->agg_shards.nranks,
+                             (long long)mc->agg_shards.shard);
+                rc = ERROR_INVALID_PARAM;
+                goto done;
+            }
         }
         d->out_off = out_bytes;
         if (!d->agg_only) out_bytes = ALIGN_UP(out_bytes + d->bytes, SLOT_ALIGN);
@@ -1571,6 +1585,8 @@ static int dec_segment(MomentumCompressor *mc, const BatchItem *items, size_t n,
             I->agg_w = mc->agg_w;
             I->agg_store = mc->agg_store;
             I->agg_vec = (((uintptr_t)d->agg) & 15) == 0;
+            I->agg_shard = mc->agg_shards.nranks > 0;
+            I->agg_off = (int64_t)d->agg_off;
         }
         if (d->dcodec == MC_DC_Q8 || d->dcodec == MC_DC_INT4) {
             I->scale_ptr = (const float *)d->d_data;
@@ -1693,6 +1709,7 @@ static int dec_segment(MomentumCompressor *mc, const BatchItem *items, size_t n,
         L.tile_count = d_count;
         L.tile_poff = d_poff;
         L.staged = dstaged;
+        L.shards = mc->agg_shards;
         L.item0 = 0;
         L.item1 = (int32_t)n;
         int k = mc_launch_decode(&L, st, tr);
@@ -1733,6 +1750,7 @@ static int dec_segment(MomentumCompressor *mc, const BatchItem *items, size_t n,
             L.tile_count = d_count;
             L.tile_poff = d_poff;
             L.staged = dstaged;
+            L.shards = mc->agg_shards;
             L.item0 = (int32_t)dstart[c];
             L.item1 = (int32_t)dstart[c + 1];
             all0 += na;

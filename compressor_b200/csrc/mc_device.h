@@ -135,6 +135,21 @@ enum {
 #define MC_ZBLOCK (1 << MC_ZBLOCK_LOG2)
 #define MC_ZHDR 9
 
+/* Sharded server aggregate over peer memory (a reduce-scatter fused into
+ * the decoder).  The aggregate's elements are split into nranks shards of
+ * `shard` elements; rank s owns shard s.  Every rank has a landing buffer of
+ * nranks * shard floats, slot r (elements [r * shard, (r + 1) * shard)) for
+ * rank r's contribution; landing[s] is rank s's buffer as addressed from
+ * this device (peer memory).  The decoder of rank `rank` writes the value of
+ * aggregate element x to landing[x / shard][rank * shard + x % shard]. */
+#define MC_MAX_RANKS 8
+typedef struct {
+    float *landing[MC_MAX_RANKS];
+    int64_t shard;              /* elements per shard: a multiple of 64, at least MC_TILE_ELEMS */
+    int32_t nranks;
+    int32_t rank;
+} mc_agg_shards;
+
 /* How the decoder reads a bitmap / sign / lossless payload. */
 enum {
     MC_BM_WORDS = 0,        /* contiguous content (expanded, or staged content) */
@@ -164,7 +179,8 @@ typedef struct {
     float agg_w;
     int32_t agg_store;
     int32_t agg_vec;            /* 1: agg is 16-byte aligned */
-    int32_t pad3;
+    int32_t agg_shard;          /* 1: the aggregate value goes to its owner's landing slot (mc_agg_shards) */
+    int64_t agg_off;            /* element offset of the item in the aggregate */
     int64_t n;
     int64_t K;
     int64_t bm_bits;            /* min(bitmap content bytes*8, K) */
@@ -214,6 +230,7 @@ typedef struct {
     int32_t staged;             /* 1: stage tiles of aligned items in shared memory (bulk copies) */
     int32_t item0, item1;       /* items [item0, item1) own this launch's tiles */
     int32_t pad;
+    mc_agg_shards shards;       /* sharded aggregate (items with agg_shard set) */
 } mc_dec_launch;
 
 
@@ -228,6 +245,14 @@ typedef struct {
     int kid[MC_KTRACE_MAX];
     int n;
 } mc_ktrace;
+
+/* Second half of the sharded aggregate: rank `rank` sums its shard over the
+ * nranks slots of its own landing buffer, in rank order, and stores the sum
+ * into aggregates[r][rank * shard + i] for every rank r (an all-gather by
+ * peer stores); elements at or beyond `total` are not written.  Returns 1,
+ * or a negative value when the launch failed. */
+int mc_launch_shard_reduce(const float *landing, int nranks, int rank, int64_t shard, int64_t total,
+                           float *const *aggregates, void *stream);
 
 /* Launchers: return the number of kernels launched, or a negative value
  * when a launch failed.  `tr` may be NULL. */

@@ -186,6 +186,7 @@ struct MomentumCompressor {
     float agg_w;
     int agg_store;      /* 1: the next batches store weight * decoded instead of adding */
     int agg_no_output;  /* 1: items added into the aggregate get no decoded array */
+    mc_agg_shards agg_shards;   /* nranks > 0: sharded aggregate (falcom_set_aggregate_shards) */
     int agg_failed;
 
     /* per-kernel device time (falcom_set_kernel_timing) */

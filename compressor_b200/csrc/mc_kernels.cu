@@ -1702,12 +1702,39 @@ __device__ __forceinline__ void dec_resid4(const mc_dec_item &I, const uint8_t *
 // agg = fma(w, decoded, agg), or fma(w, decoded, +0) in store mode (the old
 // value not read).  One rounding per element and client, the same bits as a
 // separate accumulate pass over the decoded tensor.
-__device__ __forceinline__ void agg_quad(const mc_dec_item &I, int64_t g, int64_t e1, const float (&v)[4]) {
+// Landing buffer of rank r (a select over the kernel-parameter array, so it
+// is not copied to local memory for a dynamic index).
+__device__ __forceinline__ float *landing_of(const mc_agg_shards &S, int r) {
+    float *p = nullptr;
+#pragma unroll
+    for (int k = 0; k < MC_MAX_RANKS; k++)
+        if (k == r) p = S.landing[k];
+    return p;
+}
+
+// With a sharded aggregate (the SHARD instantiation of the decoder) the
+// value, this rank's partial sum (the local aggregate, not read in store
+// mode, plus weight * decoded), goes to the owner's landing slot for this
+// rank instead (peer memory).
+template <bool SHARD>
+__device__ __forceinline__ void agg_quad(const mc_dec_launch &L, const mc_dec_item &I, int64_t g, int64_t e1,
+                                         const float (&v)[4]) {
     float a[4] = {0.0f, 0.0f, 0.0f, 0.0f};
     if (!I.agg_store) ld4(I.agg, g, e1, I.agg_vec != 0, a);
 #pragma unroll
     for (int j = 0; j < 4; j++) a[j] = __fmaf_rn(I.agg_w, v[j], a[j]);
-    st4(I.agg, g, e1, I.agg_vec != 0, a);
+    if constexpr (!SHARD) {
+        st4(I.agg, g, e1, I.agg_vec != 0, a);
+    } else {
+        const int64_t S = L.shards.shard;
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            if (g + j >= e1) break;
+            const int64_t x = I.agg_off + g + j;
+            const int64_t sh = x / S;
+            landing_of(L.shards, (int)sh)[(int64_t)L.shards.rank * S + (x - sh * S)] = a[j];
+        }
+    }
 }
 
 // Sign bytes a reconstruct tile needs: its predicted kernels' bits start at
@@ -1779,6 +1806,7 @@ __device__ void recon_pre(const mc_dec_launch &L, const StageDesc &d, uint32_t *
 
 // `codes`: the tile's payload bytes, staged or in place, indexed like
 // I.data; `scale`: the payload's scale header (1 without one).
+template <bool SHARD>
 __device__ void recon_tile(const mc_dec_launch &L, const StageDesc &d, const float *buf, const uint32_t *s_m,
                            const uint32_t *s_d, const uint8_t *codes, float scale) {
     const int gt = d.gt;
@@ -1823,13 +1851,27 @@ __device__ void recon_tile(const mc_dec_launch &L, const StageDesc &d, const flo
             float4 *mo4 = (float4 *)(I.mem_out + tr.e0), *h4 = (float4 *)(hist + tr.e0);
             const uint64_t spol = l2_stream();   // read again next round only
             // one loop per destination set, so each keeps only the pointers it
-            // writes live: 0 output copy (or none), 1 aggregate, 2 both
+            // writes live: 0 output copy (or none), 1 aggregate, 2 both (or a
+            // sharded aggregate through agg_quad), 3 sharded aggregate alone
             auto quads = [&](auto dst) {
                 constexpr int M = decltype(dst)::value;
-                float4 *o4 = (M != 1 && out) ? (float4 *)(out + tr.e0) : nullptr;
+                float4 *o4 = (M == 0 || M == 2) && out ? (float4 *)(out + tr.e0) : nullptr;
                 float4 *a4 = M != 0 ? (float4 *)(I.agg + tr.e0) : nullptr;
                 const float aw = I.agg_w;
                 const bool astore = I.agg_store != 0, avec = I.agg_vec != 0;
+                // sharded: the tile's elements lie in at most two shards (a
+                // shard holds at least a tile); x < sb1 goes to sp0 + x, the
+                // rest to sp1 + x
+                float *sp0 = nullptr, *sp1 = nullptr;
+                int64_t sb1 = 0;
+                if (M == 3) {
+                    const int64_t S = L.shards.shard, x0 = I.agg_off + tr.e0;
+                    const int s0 = (int)(x0 / S);
+                    sb1 = (int64_t)(s0 + 1) * S;
+                    sp0 = landing_of(L.shards, s0) + (int64_t)L.shards.rank * S - (int64_t)s0 * S;
+                    if (s0 + 1 < L.shards.nranks)
+                        sp1 = landing_of(L.shards, s0 + 1) + (int64_t)L.shards.rank * S - (int64_t)(s0 + 1) * S;
+                }
                 for (int q = threadIdx.x; q < nq; q += TPB) {
                     const QuadBits qb = quad_bits_full(s_m, s_d, (uint32_t)wb, k0, 4u * q, I.ks, I.ksdiv);
                     float r[4];
@@ -1843,9 +1885,17 @@ __device__ void recon_tile(const mc_dec_launch &L, const StageDesc &d, const flo
                     st_f4(mo4 + q, make_float4(mo[0], mo[1], mo[2], mo[3]), spol);
                     const float4 rv = make_float4(rec[0], rec[1], rec[2], rec[3]);
                     st_f4(h4 + q, rv, spol);
-                    if (M != 1 && o4) st_f4(o4 + q, rv, spol);
-                    if (M != 0) {
-                        if (avec) {
+                    if ((M == 0 || M == 2) && o4) st_f4(o4 + q, rv, spol);
+                    if (M == 3) {
+                        // this rank's partial sum into the owner's landing slot
+                        float4 a = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                        if (!astore) a = a4[q];
+                        const int64_t x = I.agg_off + tr.e0 + 4 * q;
+                        *(float4 *)((x < sb1 ? sp0 : sp1) + x) =
+                            make_float4(__fmaf_rn(aw, rec[0], a.x), __fmaf_rn(aw, rec[1], a.y),
+                                        __fmaf_rn(aw, rec[2], a.z), __fmaf_rn(aw, rec[3], a.w));
+                    } else if (M != 0) {
+                        if (avec && !SHARD) {
                             // streamed like the other outputs: the aggregate is
                             // read again only by the next client's decode
                             float4 a = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
@@ -1853,14 +1903,19 @@ __device__ void recon_tile(const mc_dec_launch &L, const StageDesc &d, const flo
                             st_f4(a4 + q, make_float4(__fmaf_rn(aw, rec[0], a.x), __fmaf_rn(aw, rec[1], a.y),
                                                       __fmaf_rn(aw, rec[2], a.z), __fmaf_rn(aw, rec[3], a.w)), spol);
                         } else {
-                            agg_quad(I, tr.e0 + 4 * q, tr.e1, rec);
+                            agg_quad<SHARD>(L, I, tr.e0 + 4 * q, tr.e1, rec);
                         }
                     }
                 }
             };
             if (!I.agg) quads(std::integral_constant<int, 0>());
-            else if (!out) quads(std::integral_constant<int, 1>());
-            else quads(std::integral_constant<int, 2>());
+            else if constexpr (SHARD) {
+                if (!out && I.agg_vec) quads(std::integral_constant<int, 3>());
+                else quads(std::integral_constant<int, 2>());
+            } else {
+                if (!out) quads(std::integral_constant<int, 1>());
+                else quads(std::integral_constant<int, 2>());
+            }
         }
         const int64_t gstart = I.vec ? tr.e0 + 4 * (int64_t)nq : tr.e0;
         const int owner = I.vec ? nq % TPB : 0;
@@ -1882,7 +1937,7 @@ __device__ void recon_tile(const mc_dec_launch &L, const StageDesc &d, const flo
             for (int64_t g = gstart + 4 * (int64_t)((threadIdx.x - owner + TPB) % TPB); g < tr.e1; g += 4 * TPB) {
                 float rec[4];
                 ld4(hist, g, tr.e1, I.vec, rec);
-                agg_quad(I, g, tr.e1, rec);
+                agg_quad<SHARD>(L, I, g, tr.e1, rec);
             }
         }
         return;
@@ -1890,12 +1945,38 @@ __device__ void recon_tile(const mc_dec_launch &L, const StageDesc &d, const flo
     const int64_t e0 = (int64_t)t * I.tile_kernels;
     const int64_t e1 = min(e0 + (int64_t)I.tile_kernels, I.n);
     if (I.kind == MC_D_RESIDUAL || I.kind == MC_D_QUANT) {
+        // sharded: the tile's (at most 4096) elements lie in at most two
+        // shards; whole aligned quads go to sp0 + x or sp1 + x
+        float *sp0 = nullptr, *sp1 = nullptr;
+        int64_t sb1 = 0;
+        bool sfast = false;
+        if constexpr (SHARD) {
+            if (I.agg) {
+                const int64_t S = L.shards.shard, x0 = I.agg_off + e0;
+                const int s0 = (int)(x0 / S);
+                sb1 = (int64_t)(s0 + 1) * S;
+                sp0 = landing_of(L.shards, s0) + (int64_t)L.shards.rank * S - (int64_t)s0 * S;
+                if (s0 + 1 < L.shards.nranks)
+                    sp1 = landing_of(L.shards, s0 + 1) + (int64_t)L.shards.rank * S - (int64_t)(s0 + 1) * S;
+                sfast = I.agg_vec && (I.agg_off & 3) == 0;
+            }
+        }
         for (int64_t g = e0 + 4 * (int64_t)threadIdx.x; g < e1; g += 4 * TPB) {
             float r[4];
             dec_resid4(I, I.data, g, e1, scale, r);
             st4(hist, g, e1, I.vec, r);
             if (out) st4(out, g, e1, I.vec, r);
-            if (I.agg) agg_quad(I, g, e1, r);
+            if (!I.agg) continue;
+            if (SHARD && sfast && g + 4 <= e1) {
+                float4 a = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                if (!I.agg_store) a = *(const float4 *)(I.agg + g);
+                const int64_t x = I.agg_off + g;
+                *(float4 *)((x < sb1 ? sp0 : sp1) + x) =
+                    make_float4(__fmaf_rn(I.agg_w, r[0], a.x), __fmaf_rn(I.agg_w, r[1], a.y),
+                                __fmaf_rn(I.agg_w, r[2], a.z), __fmaf_rn(I.agg_w, r[3], a.w));
+            } else {
+                agg_quad<SHARD>(L, I, g, e1, r);
+            }
         }
         return;
     }
@@ -1962,12 +2043,13 @@ __device__ void recon_tile(const mc_dec_launch &L, const StageDesc &d, const flo
         for (int64_t g = f0 + 4 * (int64_t)threadIdx.x; g < f1; g += 4 * TPB) {
             float v[4];
             ld4(hf, g, f1, true, v);
-            agg_quad(I, g, f1, v);
+            agg_quad<SHARD>(L, I, g, f1, v);
         }
     }
 }
 
-__global__ void __launch_bounds__(TPB, 4) k_dec_recon(mc_dec_launch L) {
+template <bool SHARD>
+__global__ void __launch_bounds__(TPB, SHARD ? 3 : 4) k_dec_recon(mc_dec_launch L) {
     __shared__ uint32_t s_m[TILE_WORDS], s_d[TILE_WORDS];
     __shared__ int scan_sh[NWARP + 1];
     __shared__ uint8_t s_sb[SIGN_WIN];
@@ -2006,8 +2088,50 @@ __global__ void __launch_bounds__(TPB, 4) k_dec_recon(mc_dec_launch L) {
                         const uint8_t *data = L.items[d.ii].data;
                         const uint8_t *xb = (const uint8_t *)(buf + 2 * STAGE_ELEMS);
                         const uint8_t *codes = d.x0 ? xb + ((intptr_t)data - (intptr_t)dn16(d.x0)) : data;
-                        recon_tile(L, d, buf, s_m, s_d, codes, s_scale);
+                        recon_tile<SHARD>(L, d, buf, s_m, s_d, codes, s_scale);
                     });
+}
+
+// ------------------------------------------------------- sharded aggregate
+// Second half of the sharded aggregate (the first is the decoder's stores
+// into the owners' landing slots): this rank sums its shard over the nranks
+// slots of its own landing buffer, in rank order, and stores the sum into
+// every rank's aggregate (an all-gather by peer stores over NVLink).  Quads
+// of 16-byte loads and stores: landing and aggregate bases are 16-byte
+// aligned and the shard a multiple of 64 elements.
+struct ShardDst {
+    float *agg[MC_MAX_RANKS];
+};
+__global__ void __launch_bounds__(TPB) k_shard_reduce(const float *__restrict__ land, int nranks, int rank,
+                                                     int64_t shard, int64_t total, ShardDst dst) {
+    const int64_t base = (int64_t)rank * shard;
+    const int64_t nq = shard >> 2;
+    for (int64_t q = blockIdx.x * (int64_t)TPB + threadIdx.x; q < nq; q += (int64_t)gridDim.x * TPB) {
+        const int64_t x = base + 4 * q;
+        if (x >= total) break;
+        float4 v = __ldcg((const float4 *)(land + 4 * q));
+#pragma unroll
+        for (int j = 1; j < MC_MAX_RANKS; j++) {
+            if (j >= nranks) break;
+            const float4 u = __ldcg((const float4 *)(land + (int64_t)j * shard + 4 * q));
+            v.x = __fadd_rn(v.x, u.x);
+            v.y = __fadd_rn(v.y, u.y);
+            v.z = __fadd_rn(v.z, u.z);
+            v.w = __fadd_rn(v.w, u.w);
+        }
+        if (x + 4 <= total) {
+#pragma unroll
+            for (int r = 0; r < MC_MAX_RANKS; r++)
+                if (r < nranks) *(float4 *)(dst.agg[r] + x) = v;
+        } else {
+            const float w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int r = 0; r < MC_MAX_RANKS; r++) {
+                if (r >= nranks) break;
+                for (int k = 0; k < 4 && x + k < total; k++) dst.agg[r][x + k] = w[k];
+            }
+        }
+    }
 }
 
 }  // namespace
@@ -2045,7 +2169,7 @@ static void launch_pdl(void (*kern)(P...), int grid, size_t smem, cudaStream_t s
 
 // Dynamic shared memory of the staged kernels (one stage of NA arrays),
 // opted in above the 48 KiB default once per kernel and device.
-enum { KF_P1 = 0, KF_P2, KF_P3, KF_P4, KF_RECON, KF_N };
+enum { KF_P1 = 0, KF_P2, KF_P3, KF_P4, KF_RECON, KF_RECON_SHARD, KF_N };
 #define MAX_DEVICES 64
 static int g_smem_set[KF_N][MAX_DEVICES];
 
@@ -2116,9 +2240,14 @@ extern "C" int mc_launch_decode(const mc_dec_launch *L, void *stream, mc_ktrace 
         n += 2;
     }
     if (L->nall_tiles > 0) {
-        smem_opt_in(KF_RECON, (const void *)k_dec_recon, RECON_SMEM);
         tr_begin(tr, MC_KT_DEC_RECON, s);
-        launch_pdl(k_dec_recon, L->nall_tiles, RECON_SMEM, s, *L);
+        if (L->shards.nranks > 0) {   // the sharded-aggregate instantiation
+            smem_opt_in(KF_RECON_SHARD, (const void *)k_dec_recon<true>, RECON_SMEM);
+            launch_pdl(k_dec_recon<true>, L->nall_tiles, RECON_SMEM, s, *L);
+        } else {
+            smem_opt_in(KF_RECON, (const void *)k_dec_recon<false>, RECON_SMEM);
+            launch_pdl(k_dec_recon<false>, L->nall_tiles, RECON_SMEM, s, *L);
+        }
         tr_end(tr, s);
         n++;
     }
@@ -2134,4 +2263,18 @@ extern "C" int mc_launch_unframe(const mc_unframe_job *jobs, int njobs, void *st
     tr_end(tr, s);
     if (cudaGetLastError() != cudaSuccess) return -1;
     return 1;
+}
+
+extern "C" int mc_launch_shard_reduce(const float *landing, int nranks, int rank, int64_t shard, int64_t total,
+                                      float *const *aggregates, void *stream) {
+    if (nranks < 1 || nranks > MC_MAX_RANKS || rank < 0 || rank >= nranks || shard <= 0) return -1;
+    ShardDst d;
+    for (int r = 0; r < MC_MAX_RANKS; r++) d.agg[r] = r < nranks ? aggregates[r] : nullptr;
+    const int64_t nq = shard >> 2;
+    int blocks = (int)((nq + TPB - 1) / TPB);
+    if (blocks > 148 * 8) blocks = 148 * 8;
+    if (blocks < 1) blocks = 1;
+    cudaStream_t s = (cudaStream_t)stream;
+    k_shard_reduce<<<blocks, TPB, 0, s>>>(landing, nranks, rank, shard, total, d);
+    return cudaGetLastError() == cudaSuccess ? 1 : -1;
 }

@@ -8,9 +8,11 @@ instance with the weighted aggregate fused into the decode
 (``falcom_set_aggregate``), and one sum all-reduce of the flat aggregate over
 NCCL finishes the global update.
 
-Everything here is plain host logic (which clients a rank owns, their
-weights, the aggregate layout and the collective); it runs the same under the
-``gloo`` backend on CPU tensors.
+Everything here but PeerAggregate is plain host logic (which clients a rank
+owns, their weights, the aggregate layout and the collective); it runs the
+same under the ``gloo`` backend on CPU tensors.  PeerAggregate maps the
+buffers of the sharded aggregate (the reduce-scatter fused into the decoder
+over NVLink peer memory) between the ranks' GPUs.
 """
 from __future__ import annotations
 
@@ -141,3 +143,125 @@ class ChunkedAllreduce:
         for w in self.works:
             w.wait()
         self.works = []
+
+
+def shard_elems(total: int, nranks: int) -> int:
+    """Elements per shard of a sharded aggregate: total / nranks rounded up
+    to a multiple of 64, at least one tile (4096)."""
+    if total < 0 or nranks < 1:
+        raise ValueError("bad shard request")
+    per = -(-total // nranks)
+    return max(4096, -(-per // 64) * 64)
+
+
+class PeerAggregate:
+    """The buffers of the sharded aggregate (falcom_set_aggregate_shards /
+    falcom_shard_reduce) on every rank, mapped into every other rank's
+    address space over CUDA IPC: this rank's aggregate and landing buffer
+    (nranks x shard floats each, zeroed, so padding between items stays 0),
+    and the peers' addresses of both.
+
+    One round: the decodes of every rank's last client store into the
+    owners' landing slots (the fused reduce-scatter), `finish` then orders a
+    barrier (a one-element all-reduce on the stream: every rank's decodes
+    have landed), every rank's falcom_shard_reduce (its shard summed in rank
+    order and stored into every rank's aggregate over NVLink), and a second
+    barrier, after which every rank's aggregate holds the global sum.
+    Every rank creates, uses and closes it at the same points."""
+
+    def __init__(self, torch, dist, total: int, device_index: int):
+        from cuda.bindings import runtime as rt
+        self.rt, self.torch, self.dist = rt, torch, dist
+        self._ok(rt.cudaSetDevice(int(device_index))[0], "cudaSetDevice")
+        self.nranks = dist.get_world_size()
+        self.rank = dist.get_rank()
+        self.total = int(total)
+        self.shard = shard_elems(self.total, self.nranks)
+        nbytes = 4 * self.nranks * self.shard
+        self.local = {}
+        for key in ("agg", "land"):
+            err, ptr = rt.cudaMalloc(nbytes)
+            self._ok(err, "cudaMalloc")
+            self._ok(rt.cudaMemset(ptr, 0, nbytes)[0], "cudaMemset")
+            self.local[key] = int(ptr)
+        self._ok(rt.cudaDeviceSynchronize()[0], "cudaDeviceSynchronize")
+        mine = {}
+        for key, ptr in self.local.items():
+            err, h = rt.cudaIpcGetMemHandle(ptr)
+            self._ok(err, "cudaIpcGetMemHandle")
+            mine[key] = bytes(h.reserved)
+        handles = [None] * self.nranks
+        dist.all_gather_object(handles, mine)
+        self.opened = []
+        self.ptrs = {"agg": [0] * self.nranks, "land": [0] * self.nranks}
+        failed = None
+        for r in range(self.nranks):
+            for key in ("agg", "land"):
+                if r == self.rank:
+                    self.ptrs[key][r] = self.local[key]
+                    continue
+                h = rt.cudaIpcMemHandle_t()
+                h.reserved = handles[r][key]
+                err, p = rt.cudaIpcOpenMemHandle(h, rt.cudaIpcMemLazyEnablePeerAccess)
+                if int(err) != 0:
+                    failed = f"cudaIpcOpenMemHandle of rank {r}'s {key} failed ({err})"
+                    continue
+                self.ptrs[key][r] = int(p)
+                self.opened.append(int(p))
+        # every rank learns whether every rank mapped every peer buffer
+        flag = torch.tensor([0 if failed else 1], dtype=torch.int32, device=torch.device("cuda", device_index))
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+        if int(flag.item()) != 1:
+            self.close()
+            raise RuntimeError(failed or "a peer could not map this rank's buffers")
+        c_vp = ctypes.c_void_p
+        self.c_land = (c_vp * self.nranks)(*self.ptrs["land"])
+        self.c_aggs = (c_vp * self.nranks)(*self.ptrs["agg"])
+        self.tiny = torch.zeros(1, device=torch.device("cuda", device_index))
+        self.agg = torch.as_tensor(_DeviceFloats(self.local["agg"], self.total), device=self.tiny.device)
+
+    @staticmethod
+    def _ok(err, what):
+        if int(err) != 0:
+            raise RuntimeError(f"{what} failed ({err})")
+
+    def enable(self, lib, decoder_handle) -> None:
+        """The decoder's next decodes go to the owners' landing slots."""
+        rc = lib.falcom_set_aggregate_shards(decoder_handle, self.c_land, self.nranks, self.rank, self.shard)
+        if rc != 0:
+            raise RuntimeError(f"falcom_set_aggregate_shards failed ({rc})")
+
+    @staticmethod
+    def disable(lib, decoder_handle) -> None:
+        lib.falcom_set_aggregate_shards(decoder_handle, None, 0, 0, 0)
+
+    def finish(self, lib, stream_ptr: int) -> None:
+        """After this rank's decodes are queued: barrier, shard sum and
+        all-gather, barrier (all on the current stream)."""
+        self.dist.all_reduce(self.tiny)
+        rc = lib.falcom_shard_reduce(ctypes.c_void_p(self.local["land"]), self.nranks, self.rank, self.shard,
+                                     self.total, self.c_aggs, ctypes.c_void_p(stream_ptr))
+        if rc != 0:
+            raise RuntimeError(f"falcom_shard_reduce failed ({rc})")
+        self.dist.all_reduce(self.tiny)
+
+    def close(self) -> None:
+        """Every rank: unmap the peers' buffers, then free its own once no
+        peer maps them any more."""
+        self.torch.cuda.synchronize()
+        self.dist.barrier()
+        for p in self.opened:
+            self.rt.cudaIpcCloseMemHandle(p)
+        self.opened = []
+        self.dist.barrier()
+        for p in self.local.values():
+            self.rt.cudaFree(p)
+        self.local = {}
+
+
+class _DeviceFloats:
+    """float32 device memory of `n` elements at `ptr`, for torch.as_tensor."""
+
+    def __init__(self, ptr: int, n: int):
+        self.__cuda_array_interface__ = {"shape": (int(n),), "typestr": "<f4", "data": (int(ptr), False),
+                                         "version": 3}

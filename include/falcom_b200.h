@@ -129,6 +129,46 @@ int falcom_set_aggregate_store(MomentumCompressor *mc, int store);
  * ERROR_INVALID_PARAM for mc NULL or on not 0 / 1. */
 int falcom_set_aggregate_only(MomentumCompressor *mc, int on);
 
+/* Sharded aggregate over several GPUs: the reduce-scatter of the
+ * aggregate's cross-GPU sum fused into the decoder.  No counterpart in the
+ * reference.
+ *
+ * The aggregate's elements are split into nranks shards of shard_elems
+ * elements (a multiple of 64, at least 4096); rank s owns shard s.  Every
+ * rank has a landing buffer of nranks * shard_elems floats; its slot r
+ * (elements [r * shard_elems, (r + 1) * shard_elems)) receives rank r's
+ * contribution to shard s.  landing[s] is rank s's landing buffer as
+ * addressed from this instance's device (peer memory mapped with CUDA IPC,
+ * 16-byte aligned; landing[rank] is this rank's own).  While set, the value
+ * each decode computes for aggregate element x -- this rank's partial sum,
+ * the local aggregate (not read in store mode) plus weight * decoded -- is
+ * written to landing[x / shard_elems][rank * shard_elems + x % shard_elems]
+ * over NVLink, by the reconstruct kernel as it decodes, instead of to the
+ * local aggregate.  Use it for a rank's last client of a round (its earlier
+ * clients go to the local aggregate as usual), then, once every rank's
+ * decodes are done (a barrier on the stream, for example a one-element
+ * all-reduce), falcom_shard_reduce on every rank, then a barrier again.
+ * Aggregate offsets must be multiples of 4 and every item must lie inside
+ * the nranks shards, else the decompress call fails with
+ * ERROR_INVALID_PARAM.  landing = NULL or nranks = 0 switches it off, as
+ * does falcom_set_aggregate(mc, NULL, ...).  Returns 0, or
+ * ERROR_INVALID_PARAM. */
+int falcom_set_aggregate_shards(MomentumCompressor *mc, float *const *landing, int nranks, int rank,
+                                size_t shard_elems);
+
+/* Second half of the sharded aggregate, on each rank after every rank's
+ * decodes have landed: sums shard `rank` over the nranks slots of this
+ * rank's own landing buffer, in rank order, and stores the sum into
+ * aggregates[r][rank * shard_elems + i] for every rank r (peer stores over
+ * NVLink, an all-gather), for elements below total_elems.  Every rank's
+ * aggregate then holds the whole sum once all ranks' calls have completed
+ * (a barrier on the stream).  aggregates[r] as addressed from the current
+ * device, 16-byte aligned.  Queued on `stream` (cudaStream_t) without
+ * waiting.  Returns 0, ERROR_INVALID_PARAM, or ERROR_DECOMPRESSION when the
+ * launch fails. */
+int falcom_shard_reduce(const float *landing, int nranks, int rank, size_t shard_elems, size_t total_elems,
+                        float *const *aggregates, void *stream);
+
 /* Residual quantiser that allocates no memory.  No counterpart in the
  * reference interface.
  *

@@ -157,3 +157,93 @@ def test_emulated_aggregate_add_and_store(emu_lib):
         c.close()
     for p in (pa, pb, pc):
         lib.emu_device_free(p)
+
+
+def test_emulated_sharded_aggregate_two_ranks(emu_lib):
+    """The sharded aggregate (a reduce-scatter fused into the decoder, then
+    the shard sum and all-gather kernel), with two ranks emulated in one
+    process: rank 0 decodes clients A1 (into its local aggregate) and A2
+    (added to it, the sum stored into the owners' landing slots), rank 1
+    decodes client B (stored into the landing slots); then each rank's
+    falcom_shard_reduce sums its shard and stores it into both aggregates.
+    With power-of-two weights every product is exact, so both aggregates
+    must equal (0.25 xA1 + 0.25 xA2) + 0.5 xB in float32 bit for bit, x the
+    clients' decodes from a plain decoder; padding between items stays 0."""
+    import ctypes
+    lib = ctypes.CDLL(emu_lib)
+    lib.emu_device_alloc.restype = ctypes.c_void_p
+    lib.emu_device_alloc.argtypes = [ctypes.c_size_t]
+    lib.emu_device_free.argtypes = [ctypes.c_void_p]
+    shapes = [("l1.conv.weight", (32, 16, 3, 3)), ("l1.bn.bias", (32,)), ("l2.conv.weight", (64, 32, 1, 1)),
+              ("fc.weight", (10, 300)), ("fc.bias", (10,))]
+    names = [n for n, _ in shapes]
+    sizes = [int(np.prod(s)) for _, s in shapes]
+    offs, o = [], 0
+    for n_ in sizes:
+        offs.append(o)
+        o = (o + n_ + 63) // 64 * 64
+    total = o
+    nranks, shard = 2, max(4096, ((total + 1) // 2 + 63) // 64 * 64)
+    off_c = (ctypes.c_size_t * len(names))(*offs)
+    c_vp = ctypes.c_void_p
+    land = [lib.emu_device_alloc(4 * nranks * shard) for _ in range(nranks)]
+    aggs = [lib.emu_device_alloc(4 * nranks * shard) for _ in range(nranks)]
+    view = lambda p, n: np.ctypeslib.as_array((ctypes.c_float * n).from_address(p))
+    for p in land + aggs:
+        view(p, nranks * shard)[:] = 0.0
+    land_arr = (c_vp * nranks)(*land)
+    agg_arr = (c_vp * nranks)(*aggs)
+    enc = {c: Codec(emu_lib, client=c, param_count_threshold=16) for c in ("A1", "A2", "B")}
+    srv = [Codec(emu_lib, client="server", param_count_threshold=16) for _ in range(nranks)]
+    plain = Codec(emu_lib, client="server", param_count_threshold=16)
+    w = {"A1": 0.25, "A2": 0.25, "B": 0.5}
+    rank_of = {"A1": 0, "A2": 0, "B": 1}
+    rng = np.random.default_rng(11)
+    for t in range(3):
+        dec = {}
+        for c in ("A1", "A2", "B"):
+            xs = [(rng.standard_normal(s) * 1e-3).astype(np.float32) for _, s in shapes]
+            ret, layers, errs = enc[c].compress_batch(names, xs)
+            assert ret == 0, errs
+            r = rank_of[c]
+            sv = srv[r]
+            assert sv.lib.falcom_set_aggregate(sv.h, c_vp(aggs[r]), off_c, len(names), w[c]) == 0
+            assert sv.lib.falcom_set_aggregate_store(sv.h, 0 if c == "A2" else 1) == 0
+            assert sv.lib.falcom_set_aggregate_only(sv.h, 1) == 0
+            last = c in ("A2", "B")   # the rank's last client writes into the landing slots
+            if last:
+                assert sv.lib.falcom_set_aggregate_shards(sv.h, land_arr, nranks, r, shard) == 0
+            else:
+                assert sv.lib.falcom_set_aggregate_shards(sv.h, None, 0, 0, 0) == 0
+            assert sv.decompress_batch(names, layers, client=c)[0] == 0
+            ret, outs = plain.decompress_batch(names, layers, client=c)
+            assert ret == 0
+            dec[c] = outs
+        for r in range(nranks):
+            assert lib.falcom_shard_reduce(c_vp(land[r]), nranks, r, shard, total, agg_arr, None) == 0
+        for i, n_ in enumerate(sizes):
+            xa1, xa2, xb = (dec[c][i].reshape(-1) for c in ("A1", "A2", "B"))
+            want = ((np.float32(0.25) * xa1) + (np.float32(0.25) * xa2)) + np.float32(0.5) * xb
+            for r in range(nranks):
+                got = view(aggs[r], total)[offs[i]:offs[i] + n_]
+                assert np.array_equal(got.view(np.uint32), want.astype(np.float32).view(np.uint32)), (t, r, names[i])
+        for r in range(nranks):
+            a = view(aggs[r], total).copy()
+            mask = np.ones(total, bool)
+            for i, n_ in enumerate(sizes):
+                mask[offs[i]:offs[i] + n_] = False
+            assert not a[mask].any()        # padding between items untouched
+    # an item outside the shards is refused before any launch
+    sv = srv[0]
+    assert 2 * 4096 < total
+    assert sv.lib.falcom_set_aggregate_shards(sv.h, land_arr, nranks, 0, 4096) == 0
+    ret, layers, _ = enc["A1"].compress_batch(names, [(rng.standard_normal(s) * 1e-3).astype(np.float32)
+                                                      for _, s in shapes])
+    assert ret == 0
+    assert sv.decompress_batch(names, layers, client="A1")[0] != 0
+    assert sv.lib.falcom_set_aggregate_shards(sv.h, land_arr, nranks, 2, shard) == -4      # rank out of range
+    assert sv.lib.falcom_set_aggregate_shards(sv.h, land_arr, nranks, 0, 100) == -4        # shard not a multiple of 64
+    for c in list(enc.values()) + srv + [plain]:
+        c.close()
+    for p in land + aggs:
+        lib.emu_device_free(p)
