@@ -956,6 +956,23 @@ def run_ours(args):
     world = D.world
 
     # ------------------------------------------------ headline (device value)
+    # N > 1, --aggregate auto: both ways of summing the aggregate over the
+    # GPUs run a few untimed rounds, and the faster (max over ranks) is used
+    # for the timed rounds and the nested lines
+    choice = None
+    if world > 1 and args.aggregate == "auto":
+        trial = {}
+        for mode in ("peer", "nccl"):
+            ft = FedRound(torch, D, model, [D.rank], world, codec, stream, so, peer=mode == "peer")
+            dt = DeviceUpdates(torch, model, [D.rank], D.dev, seed0=900)
+            st_, _, _, _ = timed_rounds(torch, D, ft, dt, 8, 4, flush)
+            trial[mode] = (D.max(statistics.median(st_)), ft.collective)
+            ft.close()
+            del dt
+        best = min(trial, key=lambda m: trial[m][0])
+        choice = {"chosen": best, "trial_ms_per_step": {m: round(v[0], 4) for m, v in trial.items()},
+                  "how": "8 untimed rounds each after 4 warm-up rounds, median, max over ranks"}
+        args.aggregate = best
     fr = FedRound(torch, D, model, [D.rank], world, codec, stream, so, peer=args.aggregate == "peer")
     data = DeviceUpdates(torch, model, [D.rank], D.dev, seed0=1000)
     local_gpus = list(range(int(os.environ.get("LOCAL_WORLD_SIZE", world))))
@@ -1076,6 +1093,7 @@ def run_ours(args):
             "allreduce_ms_rank0": round(statistics.mean(ar), 4) if world > 1 else 0.0,
             "allreduce_split": split,
             "aggregate_collective": collective,
+            "aggregate_choice": choice,
             "aggregate_check": check,
             "roofline": roofline,
             "e2e": {"value": round(e2e_val, 3), "unit": "GB/s", "ms_per_step": round(e2e_step, 4),
@@ -1188,9 +1206,10 @@ def main():
     ap.add_argument("--skip-configs", action="store_true",
                     help="headline step only (no federated / GPT-2 / per-config lines)")
     ap.add_argument("--cpu-budget-s", type=float, default=12.0)
-    ap.add_argument("--aggregate", default="peer", choices=["peer", "nccl"],
+    ap.add_argument("--aggregate", default="auto", choices=["auto", "peer", "nccl"],
                     help="N > 1: how the server aggregate is summed over the GPUs (peer: reduce-scatter fused "
-                         "into the decoder over NVLink + shard sum / all-gather kernel; nccl: all-reduce)")
+                         "into the decoder over NVLink + shard sum / all-gather kernel; nccl: all-reduce; "
+                         "auto: the faster of the two in untimed trial rounds)")
     ap.add_argument("--e2e-chunks", type=int, default=3,
                     help="layer chunks of the pipelined host-buffer step (e2e)")
     ap.add_argument("--mode", default="full", choices=["full", "value"],
