@@ -421,15 +421,21 @@ class FedRound:
 class E2ERound:
     """The headline step from host buffers, through the same public calls,
     pipelined over C layer chunks (contiguous layers of about equal size;
-    the codec's state is per layer, so chunking changes no result): chunk c's
-    compress_batch (pinned host inputs in, payloads returned in host memory),
-    its decompress_batch on the server (the payloads go up again and decode
-    into the aggregate), then for N > 1 the sum all-reduce of the chunk's
-    aggregate region, and the download of that region on a side stream,
-    which runs while chunk c+1's inputs go up: the copy engines move data in
-    both directions at once."""
+    the codec's state is per layer, so chunking changes no result).
 
-    def __init__(self, torch, D: Dist, model: str, codec: str, stream, so_path, n_chunks: int):
+    With `prefetch` (the default) the step first queues the uploads of every
+    chunk's pinned host inputs on an upload stream, one event per chunk, so
+    the host-to-device link streams the whole update while the codec works;
+    chunk c's compress_batch (on the device copy, payloads returned in host
+    memory) waits only for chunk c's upload.  Without it compress_batch reads
+    the pinned host inputs itself and uploads them inside the call.  Then
+    chunk c's decompress_batch on the server (the payloads go up again and
+    decode into the aggregate), for N > 1 the sum all-reduce of the chunk's
+    aggregate region, and the download of that region on a side stream: the
+    copy engines move data in both directions at once."""
+
+    def __init__(self, torch, D: Dist, model: str, codec: str, stream, so_path, n_chunks: int,
+                 prefetch: bool = True):
         from compressor_b200 import federated as F
         from compressor_b200 import workloads as W
         from compressor_b200.abi import Codec, PreparedBatch
@@ -455,15 +461,37 @@ class E2ERound:
         self.agg = torch.zeros(lay.total, dtype=torch.float32, device=D.dev)
         self.agg_host = torch.empty(lay.total, dtype=torch.float32, pin_memory=True)
         self.side = torch.cuda.Stream(device=D.dev)
+        self.prefetch = prefetch
+        if prefetch:
+            self.up = torch.cuda.Stream(device=D.dev)
+            self.dev_in = torch.empty(lay.total, dtype=torch.float32, device=D.dev)
         self.upd = lay.numel * 4
         self.payload = 0
 
-    def step(self, host_ptr: int, count_payload: bool = False):
+    def step(self, host, count_payload: bool = False):
+        """One round from the pinned float32 host tensor `host` (the flat
+        update in the layout's offsets)."""
         torch, lib, srv = self.torch, self.srv.lib, self.srv
         if count_payload:
             self.payload = 0
+        if self.prefetch:
+            # the previous round's compress calls have returned, so the
+            # device copy is free once the stream's earlier work is done
+            self.up.wait_stream(self.stream)
+            ready = []
+            with torch.cuda.stream(self.up):
+                for lo, hi in self.regions:
+                    self.dev_in[lo:hi].copy_(host[lo:hi], non_blocking=True)
+                    ev = torch.cuda.Event()
+                    ev.record(self.up)
+                    ready.append(ev)
+            src = self.dev_in.data_ptr()
+        else:
+            src = host.data_ptr()
         for c, pb in enumerate(self.pbs):
-            pb.set_pointers(host_ptr, self.offs_b[c])
+            if self.prefetch:
+                self.stream.wait_event(ready[c])
+            pb.set_pointers(src, self.offs_b[c])
             r1 = pb.compress(self.enc.h, self.cid)
             assert lib.falcom_set_aggregate(srv.h, ctypes.c_void_p(self.agg.data_ptr()), self.c_offs[c],
                                             len(self.offs_b[c]), self.w) == 0
@@ -483,6 +511,8 @@ class E2ERound:
             with torch.cuda.stream(self.side):
                 self.agg_host[lo:hi].copy_(self.agg[lo:hi], non_blocking=True)
         self.stream.wait_stream(self.side)
+        if self.prefetch:
+            self.stream.wait_stream(self.up)
 
     def close(self):
         self.enc.close()
@@ -1018,7 +1048,7 @@ def run_ours(args):
         h.copy_(data.x[0])
     torch.cuda.synchronize()
     for i in range(1 + Wm):
-        e2.step(hosts[i % n_host].data_ptr(), count_payload=(i == Wm))
+        e2.step(hosts[i % n_host], count_payload=(i == Wm))
     e2e_ms = []
     for j in range(K):
         h = hosts[(1 + Wm + j) % n_host]
@@ -1026,7 +1056,7 @@ def run_ours(args):
         flush()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
-        e2.step(h.data_ptr())
+        e2.step(h)
         e1.record(stream)
         e1.synchronize()
         e2e_ms.append(e0.elapsed_time(e1))
@@ -1099,9 +1129,10 @@ def run_ours(args):
             "e2e": {"value": round(e2e_val, 3), "unit": "GB/s", "ms_per_step": round(e2e_step, 4),
                     "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
                     "layer_chunks": n_e2e_chunks,
-                    "how": "pinned host inputs; per layer chunk compress_batch (payloads to host), "
-                           "decompress_batch into the aggregate, (N > 1) its all-reduce, its download on a "
-                           "side stream overlapping the next chunk's upload"},
+                    "how": "pinned host inputs, every chunk's upload queued at the start of the step on an "
+                           "upload stream; per layer chunk, once its upload is in, compress_batch (payloads to "
+                           "host), decompress_batch into the aggregate, (N > 1) its all-reduce, its download on "
+                           "a side stream"},
             "clocks": clk.summary(),
             "cpu_baseline": cpu,
             "cpu_baseline_8_threads": cpu8,
