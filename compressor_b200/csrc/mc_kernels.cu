@@ -1304,8 +1304,79 @@ struct P4Side {
     uint32_t blkpos;
 };
 
-__device__ void pass4_tile(const mc_enc_launch &L, const StageDesc &d, const float *buf, int *scan_sh,
-                           uint32_t *s_sg, const uint32_t *s_bw, const uint32_t *s_dw, const P4Side &S) {
+// The frames of a momentum tile in pass 4, from its bitmap and dominant-sign
+// words alone (no staged input), so it runs while the tile's bulk copies are
+// in flight: the tile's bitmap content into its block of the bitmap frame,
+// and its dense dominant signs into the sign frame.
+__device__ void pass4_frames(const mc_enc_launch &L, const StageDesc &d, int *scan_sh, uint32_t *s_sg,
+                             const uint32_t *s_bw, const uint32_t *s_dw, const P4Side &S) {
+    const mc_enc_item &I = L.items[d.ii];
+    const int t = d.gt - I.tile_base;
+    const TileRange tr = mom_range(I, t);
+    // bitmap content of this tile into its block of the bitmap frame
+    // (ref :2222-2253; RLE blocks were written whole by pass 1)
+    {
+        const int64_t c = (I.K + 7) >> 3;
+        const int64_t cb0 = tr.k0 >> 3, cb1 = min((tr.k1 + 7) >> 3, c);
+        const uint32_t pos = S.blkpos;
+        if (pos != 0xFFFFFFFFu) {
+            uint8_t *dst = I.bm_frame + pos - ((cb0 >> MC_ZBLOCK_LOG2) << MC_ZBLOCK_LOG2);  // + cb
+            // content byte b is byte b & 3 of the staged word (b >> 2) - wb0
+            const int64_t wb0 = tr.k0 >> 5;
+            if ((((uintptr_t)(dst + cb0)) & 3) == 0) {
+                for (int64_t w = (cb0 >> 2) + threadIdx.x; 4 * w < cb1; w += TPB) {
+                    const uint32_t v = s_bw[w - wb0];
+                    if (4 * w + 4 <= cb1) *(uint32_t *)(dst + 4 * w) = v;
+                    else
+                        for (int64_t b = 4 * w; b < cb1; b++) dst[b] = (uint8_t)(v >> (8 * (b & 3)));
+                }
+            } else {
+                for (int64_t b = cb0 + threadIdx.x; b < cb1; b += TPB)
+                    dst[b] = (uint8_t)(s_bw[(b >> 2) - wb0] >> (8 * (b & 3)));
+            }
+        }
+    }
+    // dense dominant signs of predicted kernels (ref :2258-2283): the
+    // tile's bits are assembled in shared memory, then written into the
+    // sign frame; the two edge bytes shared with neighbour tiles are ORed
+    const int64_t wb = tr.k0 >> 5, we = (tr.k1 + 31) >> 5;
+    const int i = threadIdx.x;
+    s_sg[i] = 0u;
+    if (i < 2) s_sg[TPB + i] = 0u;
+    uint32_t mw = 0, dv = 0;
+    if (wb + i < we && i < TILE_WORDS) {
+        mw = s_bw[i];
+        dv = s_dw[i];
+    }
+    const int pc = __popc(mw);
+    int tot;
+    const int off_l = block_excl_scan(pc, scan_sh, &tot);   // also orders the zeroing above
+    const int64_t poff = S.poff;
+    if (pc) {
+        const uint32_t bits = pext32(dv, mw);
+        const int lb = (int)(poff & 7) + off_l;
+        const int sh = lb & 31;
+        atomicOr(&s_sg[lb >> 5], bits << sh);
+        if (sh + pc > 32) atomicOr(&s_sg[(lb >> 5) + 1], bits >> (32 - sh));
+    }
+    __syncthreads();
+    if (tot > 0) {
+        const int64_t cb0 = poff >> 3;
+        const int64_t nbytes = ((poff + tot - 1) >> 3) - cb0 + 1;
+        for (int64_t j = threadIdx.x; j < nbytes; j += TPB) {
+            const uint32_t v = (s_sg[j >> 2] >> (8 * (j & 3))) & 0xFFu;
+            const int64_t fb = fpos_raw(cb0 + j);
+            if (j == 0 || j == nbytes - 1) {
+                if (v) atomicOr((uint32_t *)(I.sg_frame + (fb & ~(int64_t)3)), v << (8 * (fb & 3)));
+            } else {
+                I.sg_frame[fb] = (uint8_t)v;
+            }
+        }
+    }
+}
+
+__device__ void pass4_tile(const mc_enc_launch &L, const StageDesc &d, const float *buf, const uint32_t *s_bw,
+                           const uint32_t *s_dw) {
     const int gt = d.gt;
     const int ii = d.ii;
     const mc_enc_item I = L.items[ii];
@@ -1357,66 +1428,6 @@ __device__ void pass4_tile(const mc_enc_launch &L, const StageDesc &d, const flo
                 r[j] = ((qb.f >> j) & 1u) ? mom_residual(c[j], m[j], (qb.pos >> j) & 1u, mp) : c[j];
             put_codes(I.data_out, I.codec, g, tr.e1, I.vec, r, scale, inv, qm);
         }
-        // bitmap content of this tile into its block of the bitmap frame
-        // (ref :2222-2253; RLE blocks were written whole by pass 1)
-        {
-            const int64_t c = (I.K + 7) >> 3;
-            const int64_t cb0 = tr.k0 >> 3, cb1 = min((tr.k1 + 7) >> 3, c);
-            const uint32_t pos = S.blkpos;
-            if (pos != 0xFFFFFFFFu) {
-                uint8_t *dst = I.bm_frame + pos - ((cb0 >> MC_ZBLOCK_LOG2) << MC_ZBLOCK_LOG2);  // + cb
-                // content byte b is byte b & 3 of the staged word (b >> 2) - wb0
-                const int64_t wb0 = tr.k0 >> 5;
-                if ((((uintptr_t)(dst + cb0)) & 3) == 0) {
-                    for (int64_t w = (cb0 >> 2) + threadIdx.x; 4 * w < cb1; w += TPB) {
-                        const uint32_t v = s_bw[w - wb0];
-                        if (4 * w + 4 <= cb1) *(uint32_t *)(dst + 4 * w) = v;
-                        else
-                            for (int64_t b = 4 * w; b < cb1; b++) dst[b] = (uint8_t)(v >> (8 * (b & 3)));
-                    }
-                } else {
-                    for (int64_t b = cb0 + threadIdx.x; b < cb1; b += TPB)
-                        dst[b] = (uint8_t)(s_bw[(b >> 2) - wb0] >> (8 * (b & 3)));
-                }
-            }
-        }
-        // dense dominant signs of predicted kernels (ref :2258-2283): the
-        // tile's bits are assembled in shared memory, then written into the
-        // sign frame; the two edge bytes shared with neighbour tiles are ORed
-        const int64_t wb = tr.k0 >> 5, we = (tr.k1 + 31) >> 5;
-        const int i = threadIdx.x;
-        s_sg[i] = 0u;
-        if (i < 2) s_sg[TPB + i] = 0u;
-        uint32_t mw = 0, dv = 0;
-        if (wb + i < we && i < TILE_WORDS) {
-            mw = s_bw[i];
-            dv = s_dw[i];
-        }
-        const int pc = __popc(mw);
-        int tot;
-        const int off_l = block_excl_scan(pc, scan_sh, &tot);   // also orders the zeroing above
-        const int64_t poff = S.poff;
-        if (pc) {
-            const uint32_t bits = pext32(dv, mw);
-            const int lb = (int)(poff & 7) + off_l;
-            const int sh = lb & 31;
-            atomicOr(&s_sg[lb >> 5], bits << sh);
-            if (sh + pc > 32) atomicOr(&s_sg[(lb >> 5) + 1], bits >> (32 - sh));
-        }
-        __syncthreads();
-        if (tot > 0) {
-            const int64_t cb0 = poff >> 3;
-            const int64_t nbytes = ((poff + tot - 1) >> 3) - cb0 + 1;
-            for (int64_t j = threadIdx.x; j < nbytes; j += TPB) {
-                const uint32_t v = (s_sg[j >> 2] >> (8 * (j & 3))) & 0xFFu;
-                const int64_t fb = fpos_raw(cb0 + j);
-                if (j == 0 || j == nbytes - 1) {
-                    if (v) atomicOr((uint32_t *)(I.sg_frame + (fb & ~(int64_t)3)), v << (8 * (fb & 3)));
-                } else {
-                    I.sg_frame[fb] = (uint8_t)v;
-                }
-            }
-        }
         return;
     }
     if (I.kind == MC_K_QUANT) {
@@ -1458,10 +1469,10 @@ __global__ void __launch_bounds__(TPB, 5) k_enc_pass4(mc_enc_launch L) {
                             side.poff = L.tile_poff[d.gt];
                             side.blkpos = I.blk_pos[((int64_t)t * I.tile_kernels) >> (MC_ZBLOCK_LOG2 + 3)];
                         }
+                        __syncthreads();
+                        pass4_frames(L, d, scan_sh, s_sg, s_bw, s_dw, side);
                     },
-                    [&](const StageDesc &d, const float *buf) {
-                        pass4_tile(L, d, buf, scan_sh, s_sg, s_bw, s_dw, side);
-                    });
+                    [&](const StageDesc &d, const float *buf) { pass4_tile(L, d, buf, s_bw, s_dw); });
 }
 
 // ------------------------------------------------------------------ frames
@@ -2134,6 +2145,48 @@ __global__ void __launch_bounds__(TPB) k_shard_reduce(const float *__restrict__ 
     }
 }
 
+// One-shot in-place sum all-reduce of the ranks' aggregates over NVLink peer
+// memory: this rank owns elements [lo, hi); it loads them from every rank's
+// aggregate (peer loads, fetched again from the owner: ld.global.cv, so no
+// line of an earlier round is reused), sums them in rank order and stores the
+// sum into every rank's aggregate.  The ranks' ranges are disjoint, so no
+// element is touched by two ranks, and each thread loads all of an element's
+// values before it stores any.  Loads and stores go both ways over NVLink at
+// once: the reduce-scatter (ingress) and the all-gather (egress) overlap.
+struct PeerAggs {
+    float *agg[MC_MAX_RANKS];
+};
+__global__ void __launch_bounds__(TPB) k_peer_allreduce(PeerAggs a, int nranks, int64_t lo, int64_t hi) {
+    const int64_t nq = (hi - lo) >> 2;
+    for (int64_t q = blockIdx.x * (int64_t)TPB + threadIdx.x; q < nq; q += (int64_t)gridDim.x * TPB) {
+        const int64_t x = lo + 4 * q;
+        float4 u[MC_MAX_RANKS];
+#pragma unroll
+        for (int r = 0; r < MC_MAX_RANKS; r++)
+            if (r < nranks) u[r] = __ldcv((const float4 *)(a.agg[r] + x));
+        float4 v = u[0];
+#pragma unroll
+        for (int r = 1; r < MC_MAX_RANKS; r++) {
+            if (r >= nranks) break;
+            v.x = __fadd_rn(v.x, u[r].x);
+            v.y = __fadd_rn(v.y, u[r].y);
+            v.z = __fadd_rn(v.z, u[r].z);
+            v.w = __fadd_rn(v.w, u[r].w);
+        }
+#pragma unroll
+        for (int r = 0; r < MC_MAX_RANKS; r++)
+            if (r < nranks) *(float4 *)(a.agg[r] + x) = v;
+    }
+    // the last 0-3 elements of the range
+    const int64_t x = lo + 4 * nq;
+    if (blockIdx.x == 0 && x + threadIdx.x < hi) {
+        const int64_t e = x + threadIdx.x;
+        float v = __ldcv(a.agg[0] + e);
+        for (int r = 1; r < nranks; r++) v = __fadd_rn(v, __ldcv(a.agg[r] + e));
+        for (int r = 0; r < nranks; r++) a.agg[r][e] = v;
+    }
+}
+
 }  // namespace
 
 // ---------------------------------------------------------------- launchers
@@ -2276,5 +2329,23 @@ extern "C" int mc_launch_shard_reduce(const float *landing, int nranks, int rank
     if (blocks < 1) blocks = 1;
     cudaStream_t s = (cudaStream_t)stream;
     k_shard_reduce<<<blocks, TPB, 0, s>>>(landing, nranks, rank, shard, total, d);
+    return cudaGetLastError() == cudaSuccess ? 1 : -1;
+}
+
+extern "C" int mc_launch_peer_allreduce(float *const *aggregates, int nranks, int rank, int64_t shard, int64_t total,
+                                        void *stream) {
+    if (nranks < 1 || nranks > MC_MAX_RANKS || rank < 0 || rank >= nranks || shard <= 0 || (shard & 3) != 0)
+        return -1;
+    PeerAggs a;
+    for (int r = 0; r < MC_MAX_RANKS; r++) a.agg[r] = r < nranks ? aggregates[r] : nullptr;
+    const int64_t lo = (int64_t)rank * shard;
+    const int64_t hi = lo + shard < total ? lo + shard : total;
+    if (hi <= lo) return 0;
+    const int64_t nq = (hi - lo) >> 2;
+    int blocks = (int)((nq + TPB - 1) / TPB);
+    if (blocks > 148 * 8) blocks = 148 * 8;
+    if (blocks < 1) blocks = 1;
+    cudaStream_t s = (cudaStream_t)stream;
+    k_peer_allreduce<<<blocks, TPB, 0, s>>>(a, nranks, lo, hi);
     return cudaGetLastError() == cudaSuccess ? 1 : -1;
 }
