@@ -296,6 +296,14 @@ class DeviceUpdates:
 
 
 # ------------------------------------------------------------ the round
+# --aggregate modes that sum over NVLink peer memory, and their PeerAggregate mode
+PEER_MODES = {"peer": "fused", "oneshot": "oneshot"}
+COLLECTIVES = {"peer": "decoder stores into owner shards over NVLink peer memory, shard sum + all-gather kernel",
+               "oneshot": "one-shot in-place all-reduce kernel over NVLink peer memory (peer loads of the "
+                          "rank's shard, sum, peer stores)",
+               "nccl": "nccl all-reduce"}
+
+
 class FedRound:
     """One federated round on this rank: every local client's update through
     its own encoder instance (compress_batch), then through this rank's server
@@ -305,7 +313,7 @@ class FedRound:
     the aggregate over the ranks (N > 1)."""
 
     def __init__(self, torch, D: Dist, model: str, clients, n_total: int, codec: str, stream, so_path,
-                 host_inputs: bool = False, peer: bool = False):
+                 host_inputs: bool = False, peer: str = "nccl"):
         from compressor_b200 import workloads as W
         from compressor_b200.abi import Codec, PreparedBatch
         self.torch, self.D, self.model = torch, D, model
@@ -331,12 +339,11 @@ class FedRound:
         self.c_offs = (ctypes.c_size_t * len(self.lay.offsets))(*self.lay.offsets)
         self.peer = None
         self.collective = "none" if D.world == 1 else "nccl all-reduce"
-        if peer and D.world > 1:
+        if peer in PEER_MODES and D.world > 1:
             from compressor_b200 import federated as F
             try:   # every rank succeeds or every rank raises (PeerAggregate agrees first)
-                self.peer = F.PeerAggregate(torch, D.dist, self.lay.total, D.local)
-                self.collective = ("decoder stores into owner shards over NVLink peer memory, "
-                                   "shard sum + all-gather kernel")
+                self.peer = F.PeerAggregate(torch, D.dist, self.lay.total, D.local, mode=PEER_MODES[peer])
+                self.collective = COLLECTIVES[peer]
             except RuntimeError as e:
                 log(f"peer aggregate unavailable, NCCL all-reduce instead: {e}")
         if self.peer is not None:
@@ -423,19 +430,24 @@ class E2ERound:
     pipelined over C layer chunks (contiguous layers of about equal size;
     the codec's state is per layer, so chunking changes no result).
 
-    With `prefetch` (the default) the step first queues the uploads of every
-    chunk's pinned host inputs on an upload stream, one event per chunk, so
-    the host-to-device link streams the whole update while the codec works;
-    chunk c's compress_batch (on the device copy, payloads returned in host
-    memory) waits only for chunk c's upload.  Without it compress_batch reads
-    the pinned host inputs itself and uploads them inside the call.  Then
-    chunk c's decompress_batch on the server (the payloads go up again and
-    decode into the aggregate), for N > 1 the sum all-reduce of the chunk's
-    aggregate region, and the download of that region on a side stream: the
-    copy engines move data in both directions at once."""
+    `xfer` = "sm" (the default) or "ce": the step first queues the uploads
+    of every chunk's pinned host inputs on an upload stream, one event per
+    chunk, so the host-to-device link streams the whole update while the
+    codec works; chunk c's compress_batch (on the device copy, payloads
+    returned in host memory) waits only for chunk c's upload.  "sm" moves the
+    inputs up and the aggregate down with falcom_copy_sm (kernels, no copy
+    engine), so the small copies the codec calls queue on the copy engines
+    never wait behind them; "ce" with copy-engine copies.  "lib":
+    compress_batch reads the pinned host inputs itself and uploads them
+    inside the call.  Then chunk c's decompress_batch on the server (the
+    payloads go up again and decode into the aggregate), for N > 1 the sum
+    all-reduce of the chunk's aggregate region, and the download of that
+    region on a side stream: the link carries data both ways at once."""
+
+    XFER = ("sm", "ce", "lib")
 
     def __init__(self, torch, D: Dist, model: str, codec: str, stream, so_path, n_chunks: int,
-                 prefetch: bool = True):
+                 xfer: str = "sm", fracs=None, down_blocks: int = 4, up_blocks: int = 0):
         from compressor_b200 import federated as F
         from compressor_b200 import workloads as W
         from compressor_b200.abi import Codec, PreparedBatch
@@ -450,7 +462,12 @@ class E2ERound:
             c.lib.falcom_set_stream(c.h, ctypes.c_void_p(stream.cuda_stream))
             return c
         self.enc, self.srv = mk(self.cid.decode()), mk("server")
-        self.chunks = F.layer_chunks([int(np.prod(sh)) for sh in lay.shapes], n_chunks)
+        self.chunks = F.layer_chunks([int(np.prod(sh)) for sh in lay.shapes], n_chunks, fracs)
+        # falcom_copy_sm CTAs of the uploads (0: the library's default) and
+        # of the aggregate downloads: few download CTAs leave the
+        # device-to-host link to the payload copies of the next chunk's
+        # compress_batch, which are on the critical path
+        self.down_blocks, self.up_blocks = down_blocks, up_blocks
         self.pbs, self.offs_b, self.c_offs, self.regions = [], [], [], []
         for i0, i1 in self.chunks:
             self.pbs.append(PreparedBatch(self.srv.lib, lay.names[i0:i1], lay.shapes[i0:i1]))
@@ -461,12 +478,24 @@ class E2ERound:
         self.agg = torch.zeros(lay.total, dtype=torch.float32, device=D.dev)
         self.agg_host = torch.empty(lay.total, dtype=torch.float32, pin_memory=True)
         self.side = torch.cuda.Stream(device=D.dev)
-        self.prefetch = prefetch
-        if prefetch:
+        if xfer not in self.XFER:
+            raise ValueError(f"unknown e2e transfer mode {xfer!r}")
+        self.xfer = xfer
+        self.prefetch = xfer != "lib"
+        if self.prefetch:
             self.up = torch.cuda.Stream(device=D.dev)
             self.dev_in = torch.empty(lay.total, dtype=torch.float32, device=D.dev)
         self.upd = lay.numel * 4
         self.payload = 0
+        self.sm_copies = 0
+        if xfer == "sm":   # pinned memory that is not mapped into the device address space: copy engines
+            probe = torch.empty(4, dtype=torch.float32, pin_memory=True)
+            rc = self.srv.lib.falcom_copy_sm(ctypes.c_void_p(self.agg.data_ptr()), ctypes.c_void_p(probe.data_ptr()),
+                                             16, 0, ctypes.c_void_p(stream.cuda_stream))
+            torch.cuda.current_stream().synchronize()
+            if rc != 0:
+                log(f"falcom_copy_sm refused pinned memory ({rc}); e2e transfers by copy engines")
+                self.xfer = "ce"
 
     def step(self, host, count_payload: bool = False):
         """One round from the pinned float32 host tensor `host` (the flat
@@ -481,7 +510,7 @@ class E2ERound:
             ready = []
             with torch.cuda.stream(self.up):
                 for lo, hi in self.regions:
-                    self.dev_in[lo:hi].copy_(host[lo:hi], non_blocking=True)
+                    self._move(self.dev_in[lo:hi], host[lo:hi], self.up, self.up_blocks)
                     ev = torch.cuda.Event()
                     ev.record(self.up)
                     ready.append(ev)
@@ -509,10 +538,21 @@ class E2ERound:
             ev.record(self.stream)
             self.side.wait_event(ev)
             with torch.cuda.stream(self.side):
-                self.agg_host[lo:hi].copy_(self.agg[lo:hi], non_blocking=True)
+                self._move(self.agg_host[lo:hi], self.agg[lo:hi], self.side, self.down_blocks)
         self.stream.wait_stream(self.side)
         if self.prefetch:
             self.stream.wait_stream(self.up)
+
+    def _move(self, dst, src, stream, blocks: int = 0):
+        """dst <- src (float32, one of them pinned host memory) on `stream`."""
+        if self.xfer == "sm":
+            rc = self.srv.lib.falcom_copy_sm(ctypes.c_void_p(dst.data_ptr()), ctypes.c_void_p(src.data_ptr()),
+                                             4 * src.numel(), blocks, ctypes.c_void_p(stream.cuda_stream))
+            if rc != 0:
+                raise RuntimeError(f"falcom_copy_sm failed ({rc})")
+            self.sm_copies += 1
+        else:
+            dst.copy_(src, non_blocking=True)
 
     def close(self):
         self.enc.close()
@@ -761,7 +801,7 @@ def closed_loop_line(torch, D, model, codec, K, W, flush, so, stream):
     return out
 
 
-def federated_line(torch, D, model, n_clients, codec, K, W, flush, so, stream, common_std, peer=False):
+def federated_line(torch, D, model, n_clients, codec, K, W, flush, so, stream, common_std, peer="nccl"):
     """n_clients clients block-distributed over the ranks; per step: every
     local client's compress + decode into the aggregate, then the NCCL
     all-reduce; value = all clients' update bytes / max-over-ranks step time.
@@ -992,18 +1032,25 @@ def run_ours(args):
     choice = None
     if world > 1 and args.aggregate == "auto":
         trial = {}
-        for mode in ("peer", "nccl"):
-            ft = FedRound(torch, D, model, [D.rank], world, codec, stream, so, peer=mode == "peer")
+        checks = {}
+        for mode in ("peer", "oneshot", "nccl"):
+            ft = FedRound(torch, D, model, [D.rank], world, codec, stream, so, peer=mode)
             dt = DeviceUpdates(torch, model, [D.rank], D.dev, seed0=900)
             st_, _, _, _ = timed_rounds(torch, D, ft, dt, 8, 4, flush)
-            trial[mode] = (D.max(statistics.median(st_)), ft.collective)
+            # a mode whose sum fails the FedAvg check is not chosen
+            ok = D.max(0.0 if fedavg_check(torch, D, ft, dt)["pass"] else 1.0) == 0.0
+            if ft.collective == COLLECTIVES[mode]:     # not fallen back to NCCL
+                trial[mode] = D.max(statistics.median(st_))
+                checks[mode] = ok
             ft.close()
             del dt
-        best = min(trial, key=lambda m: trial[m][0])
-        choice = {"chosen": best, "trial_ms_per_step": {m: round(v[0], 4) for m, v in trial.items()},
-                  "how": "8 untimed rounds each after 4 warm-up rounds, median, max over ranks"}
+        best = min((m for m in trial if checks[m]), key=lambda m: trial[m], default="nccl")
+        choice = {"chosen": best, "trial_ms_per_step": {m: round(v, 4) for m, v in trial.items()},
+                  "trial_fedavg_pass": checks,
+                  "how": "8 untimed rounds each after 4 warm-up rounds, median, max over ranks; then one "
+                         "FedAvg-checked round"}
         args.aggregate = best
-    fr = FedRound(torch, D, model, [D.rank], world, codec, stream, so, peer=args.aggregate == "peer")
+    fr = FedRound(torch, D, model, [D.rank], world, codec, stream, so, peer=args.aggregate)
     data = DeviceUpdates(torch, model, [D.rank], D.dev, seed0=1000)
     local_gpus = list(range(int(os.environ.get("LOCAL_WORLD_SIZE", world))))
     with ClockSampler(local_gpus, interval_ms=20 if world == 1 else 50, enabled=D.local == 0) as clk:
@@ -1040,7 +1087,7 @@ def run_ours(args):
     fr.close()
 
     # ------------------------------------------------------------ e2e (host)
-    e2 = E2ERound(torch, D, model, codec, stream, so, args.e2e_chunks)
+    e2 = E2ERound(torch, D, model, codec, stream, so, args.e2e_chunks, xfer=args.e2e_xfer)
     n_host = min(K, 8) + 1
     hosts = [torch.empty(e2.lay.total, dtype=torch.float32, pin_memory=True) for _ in range(n_host)]
     for i, h in enumerate(hosts):
@@ -1061,6 +1108,7 @@ def run_ours(args):
         e1.synchronize()
         e2e_ms.append(e0.elapsed_time(e1))
     pbytes = e2.payload
+    e2e_xfer = e2.xfer
     e2.close()
     e2e_step = D.max(sum(e2e_ms)) / K
     e2e_val = world * e2.upd / (e2e_step * 1e-3) / 1e9
@@ -1076,7 +1124,7 @@ def run_ours(args):
     if not args.skip_configs:
         # warm-up rounds: round 0 is direct, the first momentum rounds
         # allocate the state buffers; steady state from the fourth round
-        pa = args.aggregate == "peer"
+        pa = args.aggregate
         nested["federated_64"] = federated_line(torch, D, "resnet50", 64, codec, min(K, 5), 4, flush, so, stream,
                                                 common, peer=pa)
         nested["gpt2_medium_16"] = federated_line(torch, D, "gpt2-medium", 16, "q8", min(K, 3), 3, flush, so,
@@ -1129,10 +1177,12 @@ def run_ours(args):
             "e2e": {"value": round(e2e_val, 3), "unit": "GB/s", "ms_per_step": round(e2e_step, 4),
                     "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
                     "layer_chunks": n_e2e_chunks,
+                    "transfers": e2e_xfer,
                     "how": "pinned host inputs, every chunk's upload queued at the start of the step on an "
                            "upload stream; per layer chunk, once its upload is in, compress_batch (payloads to "
                            "host), decompress_batch into the aggregate, (N > 1) its all-reduce, its download on "
-                           "a side stream"},
+                           "a side stream; inputs up and aggregate down by falcom_copy_sm kernels (sm) or "
+                           "copy-engine copies (ce), payloads by the codec's own copies"},
             "clocks": clk.summary(),
             "cpu_baseline": cpu,
             "cpu_baseline_8_threads": cpu8,
@@ -1237,12 +1287,16 @@ def main():
     ap.add_argument("--skip-configs", action="store_true",
                     help="headline step only (no federated / GPT-2 / per-config lines)")
     ap.add_argument("--cpu-budget-s", type=float, default=12.0)
-    ap.add_argument("--aggregate", default="auto", choices=["auto", "peer", "nccl"],
+    ap.add_argument("--aggregate", default="auto", choices=["auto", "peer", "oneshot", "nccl"],
                     help="N > 1: how the server aggregate is summed over the GPUs (peer: reduce-scatter fused "
-                         "into the decoder over NVLink + shard sum / all-gather kernel; nccl: all-reduce; "
-                         "auto: the faster of the two in untimed trial rounds)")
+                         "into the decoder over NVLink + shard sum / all-gather kernel; oneshot: local "
+                         "aggregates, then one in-place all-reduce kernel over NVLink peer memory; nccl: "
+                         "all-reduce; auto: the fastest in untimed trial rounds whose FedAvg check passes)")
     ap.add_argument("--e2e-chunks", type=int, default=3,
                     help="layer chunks of the pipelined host-buffer step (e2e)")
+    ap.add_argument("--e2e-xfer", default="sm", choices=list(E2ERound.XFER),
+                    help="e2e bulk transfers: sm = falcom_copy_sm kernels, ce = copy-engine copies, lib = inputs "
+                         "uploaded inside compress_batch")
     ap.add_argument("--mode", default="full", choices=["full", "value"],
                     help="value: only the device-resident timed loop (for profiler runs)")
     ap.add_argument("--replay", default=None,

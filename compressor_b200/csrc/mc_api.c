@@ -1063,6 +1063,72 @@ MC_EXPORT int falcom_shard_reduce(const float *landing, int nranks, int rank, si
                                   stream) == 1 ? ERROR_NONE : ERROR_DECOMPRESSION;
 }
 
+MC_EXPORT int falcom_peer_allreduce(float *const *aggregates, int nranks, int rank, size_t shard_elems,
+                                    size_t total_elems, void *stream) {
+    if (!aggregates || nranks < 1 || nranks > MC_MAX_RANKS || rank < 0 || rank >= nranks ||
+        shard_elems % 64 != 0 || shard_elems == 0 || total_elems > (size_t)nranks * shard_elems) {
+        fprintf(stderr, "[ERROR] falcom_peer_allreduce: invalid arguments\n");
+        return ERROR_INVALID_PARAM;
+    }
+    for (int r = 0; r < nranks; r++) {
+        if (!aggregates[r] || ((uintptr_t)aggregates[r] & 15) != 0) {
+            fprintf(stderr, "[ERROR] falcom_peer_allreduce: aggregate %d is NULL or not 16-byte aligned\n", r);
+            return ERROR_INVALID_PARAM;
+        }
+    }
+    return mc_launch_peer_allreduce(aggregates, nranks, rank, (int64_t)shard_elems, (int64_t)total_elems,
+                                    stream) >= 0 ? ERROR_NONE : ERROR_DECOMPRESSION;
+}
+
+/* Device address of [p, p + bytes) for a kernel of the current device:
+ * device memory of that device as is, pinned host memory through its mapped
+ * device pointer; NULL (with a message) for anything else. */
+static void *sm_copy_addr(const void *p, size_t bytes, const char *what) {
+    int cur = -1;
+    if (cudaGetDevice(&cur) != cudaSuccess) {
+        (void)cudaGetLastError();
+        return NULL;
+    }
+    void *res = NULL;
+    for (int end = 0; end < 2; end++) {
+        const void *q = end ? (const void *)((const uint8_t *)p + bytes - 1) : p;
+        struct cudaPointerAttributes at;
+        if (cudaPointerGetAttributes(&at, q) != cudaSuccess) {
+            (void)cudaGetLastError();
+            at.type = cudaMemoryTypeUnregistered;
+        }
+        void *a = NULL;
+        if ((at.type == cudaMemoryTypeDevice || at.type == cudaMemoryTypeManaged) && at.device == cur)
+            a = (void *)q;
+        else if (at.type == cudaMemoryTypeHost && at.devicePointer)
+            a = at.devicePointer;
+        if (!a) {
+            fprintf(stderr, "[ERROR] falcom_copy_sm: %s is neither device memory of the current device nor pinned "
+                            "host memory\n", what);
+            return NULL;
+        }
+        if (!end) res = a;
+        else if ((uint8_t *)a != (uint8_t *)res + bytes - 1) {
+            fprintf(stderr, "[ERROR] falcom_copy_sm: %s range is not contiguous in the device address space\n", what);
+            return NULL;
+        }
+    }
+    return res;
+}
+
+MC_EXPORT int falcom_copy_sm(void *dst, const void *src, size_t bytes, int nblocks, void *stream) {
+    if (bytes == 0) return ERROR_NONE;
+    if (!dst || !src) {
+        fprintf(stderr, "[ERROR] falcom_copy_sm: NULL pointer\n");
+        return ERROR_INVALID_PARAM;
+    }
+    void *d = sm_copy_addr(dst, bytes, "destination");
+    const void *s = d ? sm_copy_addr(src, bytes, "source") : NULL;
+    if (!d || !s) return ERROR_INVALID_PARAM;
+    return mc_launch_copy(d, s, (int64_t)bytes, nblocks > 0 ? nblocks : 32, stream) >= 0 ? ERROR_NONE
+                                                                                          : ERROR_COMPRESSION;
+}
+
 /* ----------------------------------------------------------- kernel timing */
 static const char *k_names[MC_NKERN] = {"enc_pass1_stats_sign", "enc_pass2_variance", "enc_pass3_predict",
                                         "enc_pass4_quantize_pack", "frames_expand",

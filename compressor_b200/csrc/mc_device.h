@@ -253,6 +253,13 @@ typedef struct {
  * or a negative value when the launch failed. */
 int mc_launch_shard_reduce(const float *landing, int nranks, int rank, int64_t shard, int64_t total,
                            float *const *aggregates, void *stream);
+/* one-shot in-place sum all-reduce of elements [rank*shard, min((rank+1)*shard, total)) over the ranks'
+ * aggregates (peer loads and stores); 1 launched, 0 nothing to do, -1 error */
+/* copy of `bytes` bytes by a kernel of `nblocks` CTAs (device addresses; pinned host memory mapped into the
+ * device address space included); 1 launched, 0 nothing to do, -1 error */
+int mc_launch_copy(void *dst, const void *src, int64_t bytes, int nblocks, void *stream);
+int mc_launch_peer_allreduce(float *const *aggregates, int nranks, int rank, int64_t shard, int64_t total,
+                             void *stream);
 
 /* Launchers: return the number of kernels launched, or a negative value
  * when a launch failed.  `tr` may be NULL. */

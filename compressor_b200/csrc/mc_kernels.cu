@@ -2187,6 +2187,38 @@ __global__ void __launch_bounds__(TPB) k_peer_allreduce(PeerAggs a, int nranks, 
     }
 }
 
+// Copy of `bytes` bytes by the SMs: a transfer between pinned host memory
+// (mapped into the device address space) and device memory that occupies
+// no copy engine, so the copies the codec queues on the copy engines never
+// wait behind it.  When source and destination are congruent modulo 16 the
+// body moves in 16-byte loads and stores (up to four in flight per thread)
+// and block 0 copies the ragged head and tail bytewise; otherwise every byte
+// is copied on its own.
+__global__ void __launch_bounds__(TPB) k_copy(const uint8_t *__restrict__ src, uint8_t *__restrict__ dst,
+                                              int64_t bytes, int64_t head, int64_t nq) {
+    if (nq < 0) {   // incongruent ends
+        for (int64_t i = blockIdx.x * (int64_t)TPB + threadIdx.x; i < bytes; i += (int64_t)gridDim.x * TPB)
+            dst[i] = src[i];
+        return;
+    }
+    const uint4 *s4 = (const uint4 *)(src + head);
+    uint4 *d4 = (uint4 *)(dst + head);
+    const int64_t stride = (int64_t)gridDim.x * TPB;
+    for (int64_t q0 = blockIdx.x * (int64_t)TPB + threadIdx.x; q0 < nq; q0 += 4 * stride) {
+        uint4 v[4];
+#pragma unroll
+        for (int k = 0; k < 4; k++)
+            if (q0 + k * stride < nq) v[k] = __ldcs(s4 + q0 + k * stride);
+#pragma unroll
+        for (int k = 0; k < 4; k++)
+            if (q0 + k * stride < nq) __stcs(d4 + q0 + k * stride, v[k]);
+    }
+    if (blockIdx.x == 0) {
+        for (int64_t i = threadIdx.x; i < head; i += TPB) dst[i] = src[i];
+        for (int64_t i = head + 16 * nq + threadIdx.x; i < bytes; i += TPB) dst[i] = src[i];
+    }
+}
+
 }  // namespace
 
 // ---------------------------------------------------------------- launchers
@@ -2329,6 +2361,23 @@ extern "C" int mc_launch_shard_reduce(const float *landing, int nranks, int rank
     if (blocks < 1) blocks = 1;
     cudaStream_t s = (cudaStream_t)stream;
     k_shard_reduce<<<blocks, TPB, 0, s>>>(landing, nranks, rank, shard, total, d);
+    return cudaGetLastError() == cudaSuccess ? 1 : -1;
+}
+
+extern "C" int mc_launch_copy(void *dst, const void *src, int64_t bytes, int nblocks, void *stream) {
+    if (bytes <= 0) return 0;
+    if (!dst || !src) return -1;
+    const uintptr_t d = (uintptr_t)dst, s = (uintptr_t)src;
+    int64_t head = 0, nq = -1;
+    if (((d - s) & 15) == 0) {
+        head = (int64_t)((16 - (d & 15)) & 15);
+        if (head > bytes) head = bytes;
+        nq = (bytes - head) >> 4;
+    }
+    if (nblocks < 1) nblocks = 1;
+    if (nblocks > 148 * 8) nblocks = 148 * 8;
+    cudaStream_t st = (cudaStream_t)stream;
+    k_copy<<<nblocks, TPB, 0, st>>>((const uint8_t *)src, (uint8_t *)dst, bytes, head, nq);
     return cudaGetLastError() == cudaSuccess ? 1 : -1;
 }
 

@@ -11,8 +11,9 @@ NCCL finishes the global update.
 Everything here but PeerAggregate is plain host logic (which clients a rank
 owns, their weights, the aggregate layout and the collective); it runs the
 same under the ``gloo`` backend on CPU tensors.  PeerAggregate maps the
-buffers of the sharded aggregate (the reduce-scatter fused into the decoder
-over NVLink peer memory) between the ranks' GPUs.
+aggregate buffers between the ranks' GPUs for the two NVLink peer-memory
+sums (the reduce-scatter fused into the decoder, or the one-shot in-place
+all-reduce kernel).
 """
 from __future__ import annotations
 
@@ -85,20 +86,31 @@ def allreduce_aggregate(aggregate, dist=None, group=None) -> None:
         dist.all_reduce(aggregate, op=dist.ReduceOp.SUM, group=group)
 
 
-def layer_chunks(numels: Sequence[int], n_chunks: int) -> List[tuple]:
+def layer_chunks(numels: Sequence[int], n_chunks: int, fracs: Sequence[float] = None) -> List[tuple]:
     """Splits items 0..len(numels)-1, in order, into at most n_chunks
-    contiguous runs [i0, i1) of about equal element counts (a run ends once
-    it reaches its share of the total; every run holds at least one item)."""
+    contiguous runs [i0, i1) of about equal element counts, or of about the
+    shares `fracs` of the elements (one per run, normalised; n_chunks is then
+    len(fracs)): a run ends once the elements so far reach the share of the
+    runs so far; every run holds at least one item."""
     n = len(numels)
     if n == 0:
         return []
+    if fracs is not None:
+        if len(fracs) == 0 or any(f <= 0 for f in fracs):
+            raise ValueError("chunk shares must be positive")
+        n_chunks = len(fracs)
     n_chunks = max(1, min(int(n_chunks), n))
+    shares = [float(f) for f in fracs[:n_chunks]] if fracs is not None else [1.0] * n_chunks
+    ends, c = [], 0.0
+    for f in shares:
+        c += f
+        ends.append(c / sum(shares))
     total = float(sum(int(x) for x in numels))
     out, i0, acc = [], 0, 0
     for i, x in enumerate(numels):
         acc += int(x)
         left_items, left_chunks = n - (i + 1), n_chunks - len(out) - 1
-        if left_chunks > 0 and (acc >= total * (len(out) + 1) / n_chunks or left_items == left_chunks):
+        if left_chunks > 0 and (acc >= total * ends[len(out)] or left_items == left_chunks):
             out.append((i0, i + 1))
             i0 = i + 1
     out.append((i0, n))
@@ -155,22 +167,36 @@ def shard_elems(total: int, nranks: int) -> int:
 
 
 class PeerAggregate:
-    """The buffers of the sharded aggregate (falcom_set_aggregate_shards /
-    falcom_shard_reduce) on every rank, mapped into every other rank's
-    address space over CUDA IPC: this rank's aggregate and landing buffer
-    (nranks x shard floats each, zeroed, so padding between items stays 0),
-    and the peers' addresses of both.
+    """The server aggregate summed over the ranks' GPUs through NVLink peer
+    memory, in one of two ways (`mode`):
 
-    One round: the decodes of every rank's last client store into the
-    owners' landing slots (the fused reduce-scatter), `finish` then orders a
-    barrier (a one-element all-reduce on the stream: every rank's decodes
-    have landed), every rank's falcom_shard_reduce (its shard summed in rank
-    order and stored into every rank's aggregate over NVLink), and a second
-    barrier, after which every rank's aggregate holds the global sum.
-    Every rank creates, uses and closes it at the same points."""
+    "fused": the sharded aggregate (falcom_set_aggregate_shards /
+    falcom_shard_reduce).  The decodes of every rank's last client store into
+    the owners' landing slots (the reduce-scatter fused into the decoder);
+    `finish` then orders a barrier (a one-element all-reduce on the stream:
+    every rank's decodes have landed), every rank's falcom_shard_reduce (its
+    shard summed in rank order and stored into every rank's aggregate) and a
+    second barrier.
 
-    def __init__(self, torch, dist, total: int, device_index: int):
+    "oneshot": the decodes write local aggregates as without peers;
+    `finish` orders a barrier, every rank's falcom_peer_allreduce (its shard
+    loaded from every rank's aggregate, summed in rank order and stored back
+    into every rank's aggregate: reduce-scatter and all-gather in one
+    kernel, both directions of the links at once) and a second barrier.
+
+    The buffers, on every rank: its aggregate and (fused) its landing buffer,
+    nranks x shard floats each, zeroed, so padding between items stays 0,
+    mapped into every other rank's address space over CUDA IPC.  After
+    `finish` every rank's aggregate holds the global sum.  Every rank
+    creates, uses and closes it at the same points, in the same mode."""
+
+    MODES = ("fused", "oneshot")
+
+    def __init__(self, torch, dist, total: int, device_index: int, mode: str = "fused"):
         from cuda.bindings import runtime as rt
+        if mode not in self.MODES:
+            raise ValueError(f"unknown peer aggregate mode {mode!r}")
+        self.mode = mode
         self.rt, self.torch, self.dist = rt, torch, dist
         self._ok(rt.cudaSetDevice(int(device_index))[0], "cudaSetDevice")
         self.nranks = dist.get_world_size()
@@ -178,8 +204,9 @@ class PeerAggregate:
         self.total = int(total)
         self.shard = shard_elems(self.total, self.nranks)
         nbytes = 4 * self.nranks * self.shard
+        keys = ("agg", "land") if mode == "fused" else ("agg",)
         self.local = {}
-        for key in ("agg", "land"):
+        for key in keys:
             err, ptr = rt.cudaMalloc(nbytes)
             self._ok(err, "cudaMalloc")
             self._ok(rt.cudaMemset(ptr, 0, nbytes)[0], "cudaMemset")
@@ -193,10 +220,10 @@ class PeerAggregate:
         handles = [None] * self.nranks
         dist.all_gather_object(handles, mine)
         self.opened = []
-        self.ptrs = {"agg": [0] * self.nranks, "land": [0] * self.nranks}
+        self.ptrs = {k: [0] * self.nranks for k in keys}
         failed = None
         for r in range(self.nranks):
-            for key in ("agg", "land"):
+            for key in keys:
                 if r == self.rank:
                     self.ptrs[key][r] = self.local[key]
                     continue
@@ -215,7 +242,7 @@ class PeerAggregate:
             self.close()
             raise RuntimeError(failed or "a peer could not map this rank's buffers")
         c_vp = ctypes.c_void_p
-        self.c_land = (c_vp * self.nranks)(*self.ptrs["land"])
+        self.c_land = (c_vp * self.nranks)(*self.ptrs["land"]) if mode == "fused" else None
         self.c_aggs = (c_vp * self.nranks)(*self.ptrs["agg"])
         self.tiny = torch.zeros(1, device=torch.device("cuda", device_index))
         self.agg = torch.as_tensor(_DeviceFloats(self.local["agg"], self.total), device=self.tiny.device)
@@ -226,23 +253,33 @@ class PeerAggregate:
             raise RuntimeError(f"{what} failed ({err})")
 
     def enable(self, lib, decoder_handle) -> None:
-        """The decoder's next decodes go to the owners' landing slots."""
+        """Fused mode: the decoder's next decodes go to the owners' landing
+        slots (no-op in oneshot mode)."""
+        if self.mode != "fused":
+            return
         rc = lib.falcom_set_aggregate_shards(decoder_handle, self.c_land, self.nranks, self.rank, self.shard)
         if rc != 0:
             raise RuntimeError(f"falcom_set_aggregate_shards failed ({rc})")
 
-    @staticmethod
-    def disable(lib, decoder_handle) -> None:
-        lib.falcom_set_aggregate_shards(decoder_handle, None, 0, 0, 0)
+    def disable(self, lib, decoder_handle) -> None:
+        if self.mode == "fused":
+            lib.falcom_set_aggregate_shards(decoder_handle, None, 0, 0, 0)
 
     def finish(self, lib, stream_ptr: int) -> None:
-        """After this rank's decodes are queued: barrier, shard sum and
-        all-gather, barrier (all on the current stream)."""
+        """After this rank's decodes are queued: barrier, the cross-rank sum
+        (shard sum + all-gather, or the one-shot all-reduce), barrier (all on
+        the current stream)."""
         self.dist.all_reduce(self.tiny)
-        rc = lib.falcom_shard_reduce(ctypes.c_void_p(self.local["land"]), self.nranks, self.rank, self.shard,
-                                     self.total, self.c_aggs, ctypes.c_void_p(stream_ptr))
+        if self.mode == "fused":
+            rc = lib.falcom_shard_reduce(ctypes.c_void_p(self.local["land"]), self.nranks, self.rank, self.shard,
+                                         self.total, self.c_aggs, ctypes.c_void_p(stream_ptr))
+            what = "falcom_shard_reduce"
+        else:
+            rc = lib.falcom_peer_allreduce(self.c_aggs, self.nranks, self.rank, self.shard, self.total,
+                                           ctypes.c_void_p(stream_ptr))
+            what = "falcom_peer_allreduce"
         if rc != 0:
-            raise RuntimeError(f"falcom_shard_reduce failed ({rc})")
+            raise RuntimeError(f"{what} failed ({rc})")
         self.dist.all_reduce(self.tiny)
 
     def close(self) -> None:

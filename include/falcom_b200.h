@@ -169,6 +169,36 @@ int falcom_set_aggregate_shards(MomentumCompressor *mc, float *const *landing, i
 int falcom_shard_reduce(const float *landing, int nranks, int rank, size_t shard_elems, size_t total_elems,
                         float *const *aggregates, void *stream);
 
+/* One-shot in-place sum all-reduce of float32 aggregates over NVLink peer
+ * memory, the alternative to the sharded aggregate when the decodes write
+ * local aggregates (plain falcom_set_aggregate): after every rank's decodes
+ * are done (a barrier on the stream), each rank calls it once; rank `rank`
+ * loads elements [rank * shard_elems, (rank + 1) * shard_elems) below
+ * total_elems from every rank's aggregate, sums them in rank order and
+ * stores the sum into every rank's aggregate, so every aggregate holds the
+ * whole sum once all ranks' calls have completed (a barrier again, which
+ * also keeps any rank from overwriting its aggregate while a peer still
+ * reads it).  aggregates[r] as addressed from the current device (CUDA IPC
+ * mappings of the peers' buffers), 16-byte aligned; shard_elems a multiple
+ * of 64.  Queued on `stream` (cudaStream_t) without waiting.  Returns 0,
+ * ERROR_INVALID_PARAM, or ERROR_DECOMPRESSION when the launch fails. */
+int falcom_peer_allreduce(float *const *aggregates, int nranks, int rank, size_t shard_elems,
+                          size_t total_elems, void *stream);
+
+/* Copies `bytes` bytes from src to dst with a kernel of `nblocks` CTAs (0:
+ * 32) on `stream` (cudaStream_t) instead of a copy engine, returning without
+ * waiting.  Each side is device memory of the current device or pinned host
+ * memory (cudaHostAlloc / cudaHostRegister, read and written through its
+ * mapped device address); pageable host memory is refused.  For callers
+ * that pipeline host transfers around the codec calls: a large upload of the
+ * next inputs or download of the aggregate issued as a copy-engine copy can
+ * hold up the small table uploads and payload copies a compress or
+ * decompress call queues on the copy engines behind it, while this copy
+ * leaves the copy engines to them (at about 51 GB/s over PCIe 5 x16 on a
+ * B200, against 55 for a copy engine).  Returns 0, ERROR_INVALID_PARAM, or
+ * ERROR_COMPRESSION when the launch fails. */
+int falcom_copy_sm(void *dst, const void *src, size_t bytes, int nblocks, void *stream);
+
 /* Residual quantiser that allocates no memory.  No counterpart in the
  * reference interface.
  *

@@ -136,6 +136,25 @@ inline float4 __ldcg(const float4 *p) {
     return *p;
 }
 
+template <class T>
+inline T __ldcv(const T *p) { return __ldcg(p); }
+template <class T>
+inline T __ldcs(const T *p) {
+    if (sizeof(T) == 16 && (((uintptr_t)p) & 15)) {
+        fprintf(stderr, "emu: misaligned 16-byte load %p\n", (const void *)p);
+        abort();
+    }
+    return *p;
+}
+template <class T>
+inline void __stcs(T *p, T v) {
+    if (sizeof(T) == 16 && (((uintptr_t)p) & 15)) {
+        fprintf(stderr, "emu: misaligned 16-byte store %p\n", (void *)p);
+        abort();
+    }
+    *p = v;
+}
+
 inline float __fmaf_rn(float a, float b, float c) { return fmaf(a, b, c); }
 inline float __fmul_rn(float a, float b) { volatile float r = a * b; return r; }
 inline float __fadd_rn(float a, float b) { volatile float r = a + b; return r; }

@@ -152,6 +152,7 @@ cudaError_t cudaPointerGetAttributes(cudaPointerAttributes *a, const void *p) {
     } else if (inside(g_host, p)) {
         a->type = cudaMemoryTypeHost;
         a->hostPointer = (void *)p;
+        a->devicePointer = (void *)p;   // mapped at the same address (unified addressing)
     } else {
         a->type = cudaMemoryTypeUnregistered;
     }
@@ -227,9 +228,15 @@ cudaError_t cudaGetDriverEntryPoint(const char *, void **fp, unsigned long long,
 }  // extern "C"
 
 // Test hooks of the emulation library: "device" memory for arguments that
-// the library checks to be device memory (the fused aggregate).
+// the library checks to be device memory (the fused aggregate), and pinned
+// "host" memory.
 extern "C" __attribute__((visibility("default"))) void *emu_device_alloc(size_t n) {
     void *p = nullptr;
     return cudaMalloc(&p, n) == cudaSuccess ? p : nullptr;
 }
 extern "C" __attribute__((visibility("default"))) void emu_device_free(void *p) { cudaFree(p); }
+extern "C" __attribute__((visibility("default"))) void *emu_host_alloc(size_t n) {
+    void *p = nullptr;
+    return cudaHostAlloc(&p, n, 0) == cudaSuccess ? p : nullptr;
+}
+extern "C" __attribute__((visibility("default"))) void emu_host_free(void *p) { cudaFreeHost(p); }

@@ -84,6 +84,12 @@ def test_layer_chunks_cover_items_in_order():
         assert all(i1 > i0 for i0, i1 in ch) and len(ch) <= g
     assert F.layer_chunks([3, 3, 3, 3], 2) == [(0, 2), (2, 4)]
     assert F.layer_chunks([], 3) == []
+    # shares: a run ends once the cumulative share is reached
+    assert F.layer_chunks([1] * 12, 3, fracs=[1, 2, 3]) == [(0, 2), (2, 6), (6, 12)]
+    assert F.layer_chunks([5, 1, 1, 1], 2, fracs=[1, 1]) == [(0, 1), (1, 4)]
+    assert F.layer_chunks([1, 1], 2, fracs=[1, 100, 100]) == [(0, 1), (1, 2)]
+    with pytest.raises(ValueError):
+        F.layer_chunks([1, 1], 2, fracs=[1, 0])
 
 
 def _chunked_worker(rank, world, port, out_path):

@@ -226,3 +226,30 @@ def test_reference_frames_with_compressed_blocks(product_lib):
         _, yb = db.decompress_batch(names, LB)
         for x, y in zip(ya, yb):
             assert np.array_equal(x.view(np.uint32), y.view(np.uint32))
+
+
+def test_copy_sm_pinned_host_and_device(product_lib):
+    """falcom_copy_sm between torch's pinned host memory and device memory in
+    both directions: sizes with ragged heads and tails, congruent and
+    incongruent offsets, device to device; bytes outside the range untouched;
+    pageable host memory refused."""
+    lib = ctypes.CDLL(product_lib)
+    lib.falcom_copy_sm.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int, ctypes.c_void_p]
+    lib.falcom_copy_sm.restype = ctypes.c_int
+    cap = 1 << 22
+    g = torch.Generator().manual_seed(7)
+    h = torch.randint(0, 256, (cap,), dtype=torch.uint8, generator=g).pin_memory()
+    d = torch.randint(0, 256, (cap,), dtype=torch.uint8, generator=g).cuda()
+    d2 = torch.zeros(cap, dtype=torch.uint8, device="cuda")
+    s = torch.cuda.current_stream().cuda_stream
+    for n, so, do in ((0, 0, 0), (1, 0, 0), (15, 1, 1), (17, 3, 3), (1000, 5, 9), (3_000_001, 16, 48),
+                      (3_000_000, 7, 7), (1 << 21, 0, 0)):
+        for src, dst in ((h, d), (d, h), (d, d2)):
+            before = dst.cpu().clone()
+            assert lib.falcom_copy_sm(dst.data_ptr() + do, src.data_ptr() + so, n, 0, s) == 0
+            torch.cuda.synchronize()
+            got = dst.cpu()
+            assert torch.equal(got[do:do + n], src.cpu()[so:so + n]), (n, so, do)
+            assert torch.equal(got[:do], before[:do]) and torch.equal(got[do + n:], before[do + n:])
+    pageable = torch.zeros(64, dtype=torch.uint8)
+    assert lib.falcom_copy_sm(d.data_ptr(), pageable.data_ptr(), 64, 0, s) == -4

@@ -1,13 +1,15 @@
-"""GPU test of the sharded server aggregate on two GPUs (skipped with fewer):
-the reduce-scatter of the cross-GPU sum fused into the decoder over NVLink
-peer memory (falcom_set_aggregate_shards), then each rank's shard sum and
-all-gather (falcom_shard_reduce), against NCCL's all-reduce of the same
-per-rank aggregates.
+"""GPU test of the two NVLink peer-memory sums of the server aggregate on
+two GPUs (skipped with fewer), against NCCL's all-reduce of the same
+per-rank aggregates: "fused", the reduce-scatter of the cross-GPU sum fused
+into the decoder (falcom_set_aggregate_shards), then each rank's shard sum
+and all-gather (falcom_shard_reduce); "oneshot", local aggregates, then
+each rank's one-shot in-place all-reduce of its shard
+(falcom_peer_allreduce).
 
 Two ranks, one process per GPU (spawned, NCCL on 127.0.0.1).  Rank r
 compresses two clients and decodes them on its server: the first into its
-local aggregate (store mode), the second added to it and landed in the
-owners' slots.  A second server on each rank decodes the same payloads into
+local aggregate (store mode), the second added to it (fused mode: landed in the
+owners' slots).  A second server on each rank decodes the same payloads into
 a plain local aggregate, which NCCL then all-reduces.  With two ranks both
 sums add the same two float32 values, so the aggregates must be equal bit
 for bit on both ranks, for three rounds (round 0 direct, then momentum)."""
@@ -31,7 +33,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _rank_main(rank, world, port, lib_path, out_dir):
+def _rank_main(rank, world, port, lib_path, out_dir, mode):
     import datetime
     import torch.distributed as dist
     from compressor_b200 import federated as F
@@ -48,7 +50,7 @@ def _rank_main(rank, world, port, lib_path, out_dir):
     lay = F.AggregateLayout.of(NAMES, SHAPES, align=64)
     offs_b = [4 * o for o in lay.offsets]
     c_offs = lay.c_offsets()
-    peer = F.PeerAggregate(torch, dist, lay.total, rank)
+    peer = F.PeerAggregate(torch, dist, lay.total, rank, mode=mode)
     plain = torch.zeros(lay.total, dtype=torch.float32, device=dev)
 
     def mk(cid):
@@ -100,10 +102,11 @@ def _rank_main(rank, world, port, lib_path, out_dir):
     dist.destroy_process_group()
 
 
-def test_sharded_aggregate_equals_nccl_allreduce(product_lib, tmp_path):
+@pytest.mark.parametrize("mode", ["fused", "oneshot"])
+def test_peer_aggregate_equals_nccl_allreduce(product_lib, tmp_path, mode):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     import torch.multiprocessing as mp
-    mp.spawn(_rank_main, args=(2, _free_port(), product_lib, str(tmp_path)), nprocs=2, join=True)
+    mp.spawn(_rank_main, args=(2, _free_port(), product_lib, str(tmp_path), mode), nprocs=2, join=True)
     for r in range(2):
         assert (tmp_path / f"rank{r}.txt").read_text() == "ok", r

@@ -247,3 +247,79 @@ def test_emulated_sharded_aggregate_two_ranks(emu_lib):
         c.close()
     for p in land + aggs:
         lib.emu_device_free(p)
+
+
+def test_emulated_peer_allreduce_in_place(emu_lib):
+    """The one-shot in-place all-reduce (falcom_peer_allreduce) over three
+    emulated ranks' aggregates, a total that is not a multiple of 4 (the
+    last rank's range ends in a partial quad) and a rank whose range is
+    empty: after every rank's call every aggregate holds (a0 + a1) + a2 in
+    float32 bit for bit, elements past `total` untouched."""
+    import ctypes
+    lib = ctypes.CDLL(emu_lib)
+    lib.emu_device_alloc.restype = ctypes.c_void_p
+    lib.emu_device_alloc.argtypes = [ctypes.c_size_t]
+    lib.emu_device_free.argtypes = [ctypes.c_void_p]
+    lib.falcom_peer_allreduce.argtypes = [ctypes.POINTER(ctypes.c_void_p), ctypes.c_int, ctypes.c_int,
+                                          ctypes.c_size_t, ctypes.c_size_t, ctypes.c_void_p]
+    c_vp = ctypes.c_void_p
+    view = lambda p, n: np.ctypeslib.as_array((ctypes.c_float * n).from_address(p))
+    rng = np.random.default_rng(5)
+    for nranks, shard, total in ((3, 4096, 2 * 4096 + 1234 + 3), (3, 8192, 8192 + 77), (2, 4096, 4096)):
+        cap = nranks * shard
+        aggs = [lib.emu_device_alloc(4 * cap) for _ in range(nranks)]
+        init = [(rng.standard_normal(cap) * 1e-3).astype(np.float32) for _ in range(nranks)]
+        for p, a in zip(aggs, init):
+            view(p, cap)[:] = a
+        arr = (c_vp * nranks)(*aggs)
+        for r in range(nranks):
+            assert lib.falcom_peer_allreduce(arr, nranks, r, shard, total, None) == 0
+        want = init[0][:total].copy()
+        for a in init[1:]:
+            want = want + a[:total]
+        for r in range(nranks):
+            got = view(aggs[r], cap)
+            assert np.array_equal(got[:total].view(np.uint32), want.view(np.uint32)), (nranks, shard, total, r)
+            assert np.array_equal(got[total:].view(np.uint32), init[r][total:].view(np.uint32))
+        for p in aggs:
+            lib.emu_device_free(p)
+    arr = (c_vp * 2)(None, None)
+    assert lib.falcom_peer_allreduce(arr, 2, 0, 4096, 4096, None) == -4      # NULL aggregates
+    assert lib.falcom_peer_allreduce(arr, 9, 0, 4096, 4096, None) == -4      # too many ranks
+
+
+def test_emulated_copy_sm(emu_lib):
+    """falcom_copy_sm (the SM copy kernel) between pinned host and device
+    buffers of the emulator: every size from 0 to 70 bytes and a large one,
+    congruent and incongruent offsets of source and destination, bytes
+    outside the range untouched; pageable memory and NULL refused."""
+    import ctypes
+    lib = ctypes.CDLL(emu_lib)
+    lib.emu_device_alloc.restype = ctypes.c_void_p
+    lib.emu_device_alloc.argtypes = [ctypes.c_size_t]
+    lib.emu_device_free.argtypes = [ctypes.c_void_p]
+    lib.emu_host_alloc.restype = ctypes.c_void_p
+    lib.emu_host_alloc.argtypes = [ctypes.c_size_t]
+    lib.emu_host_free.argtypes = [ctypes.c_void_p]
+    lib.falcom_copy_sm.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int, ctypes.c_void_p]
+    cap = 1 << 16
+    h = lib.emu_host_alloc(cap)
+    d = lib.emu_device_alloc(cap)
+    view = lambda p: np.ctypeslib.as_array((ctypes.c_uint8 * cap).from_address(p))
+    rng = np.random.default_rng(3)
+    cases = [(n, so, do) for n in range(0, 71) for so, do in ((0, 0), (3, 3), (5, 9))]
+    cases += [(40000, 16, 48), (40000, 7, 7), (40001, 1, 2)]
+    for n, so, do in cases:
+        for src, dst in ((h, d), (d, h)):
+            view(src)[:] = rng.integers(0, 256, cap, dtype=np.uint8)
+            before = view(dst).copy()
+            assert lib.falcom_copy_sm(dst + do, src + so, n, 3, None) == 0
+            got = view(dst)
+            assert np.array_equal(got[do:do + n], view(src)[so:so + n]), (n, so, do)
+            assert np.array_equal(got[:do], before[:do]) and np.array_equal(got[do + n:], before[do + n:])
+    pageable = (ctypes.c_uint8 * 64)()
+    assert lib.falcom_copy_sm(d, ctypes.addressof(pageable), 64, 0, None) == -4
+    assert lib.falcom_copy_sm(None, h, 64, 0, None) == -4
+    assert lib.falcom_copy_sm(d, h, cap + 1, 0, None) == -4     # the source range ends outside the pinned buffer
+    lib.emu_host_free(h)
+    lib.emu_device_free(d)
