@@ -323,3 +323,79 @@ def test_emulated_copy_sm(emu_lib):
     assert lib.falcom_copy_sm(d, h, cap + 1, 0, None) == -4     # the source range ends outside the pinned buffer
     lib.emu_host_free(h)
     lib.emu_device_free(d)
+
+
+@pytest.mark.parametrize("nranks", [8])
+def test_emulated_sharded_aggregate_many_ranks(emu_lib, nranks):
+    """The fused sharded aggregate and the one-shot all-reduce with 8
+    emulated ranks (the most either supports), one client per rank, weight 1/nranks (a power of two, so
+    every weighted decode is exact): after each rank's falcom_shard_reduce
+    every aggregate equals the rank-order float32 sum of the weighted
+    decodes bit for bit, and so does the one-shot all-reduce of plain local
+    aggregates; ranks whose shards lie past the last element store nothing."""
+    import ctypes
+    lib = ctypes.CDLL(emu_lib)
+    lib.emu_device_alloc.restype = ctypes.c_void_p
+    lib.emu_device_alloc.argtypes = [ctypes.c_size_t]
+    lib.emu_device_free.argtypes = [ctypes.c_void_p]
+    lib.falcom_peer_allreduce.argtypes = [ctypes.POINTER(ctypes.c_void_p), ctypes.c_int, ctypes.c_int,
+                                          ctypes.c_size_t, ctypes.c_size_t, ctypes.c_void_p]
+    shapes = [("l1.conv.weight", (32, 16, 3, 3)), ("l1.bn.bias", (32,)), ("l2.conv.weight", (64, 32, 1, 1)),
+              ("fc.weight", (10, 300)), ("fc.bias", (10,))]
+    names = [n for n, _ in shapes]
+    sizes = [int(np.prod(s)) for _, s in shapes]
+    offs, o = [], 0
+    for n_ in sizes:
+        offs.append(o)
+        o = (o + n_ + 63) // 64 * 64
+    total = o
+    shard = max(4096, ((total + nranks - 1) // nranks + 63) // 64 * 64)
+    assert total <= (nranks - 1) * shard            # the last rank's shard is empty
+    off_c = (ctypes.c_size_t * len(names))(*offs)
+    c_vp = ctypes.c_void_p
+    cap = nranks * shard
+    land = [lib.emu_device_alloc(4 * cap) for _ in range(nranks)]
+    aggs = [lib.emu_device_alloc(4 * cap) for _ in range(nranks)]
+    plain = [lib.emu_device_alloc(4 * cap) for _ in range(nranks)]
+    view = lambda p, n: np.ctypeslib.as_array((ctypes.c_float * n).from_address(p))
+    for p in land + aggs + plain:
+        view(p, cap)[:] = 0.0
+    land_arr = (c_vp * nranks)(*land)
+    agg_arr = (c_vp * nranks)(*aggs)
+    plain_arr = (c_vp * nranks)(*plain)
+    w = 1.0 / nranks
+    rng = np.random.default_rng(21)
+    mk = lambda cid: Codec(emu_lib, client=cid, param_count_threshold=16)
+    encs = [mk(f"C{r}") for r in range(nranks)]
+    srvs = [mk("server") for r in range(nranks)]
+    refs = [mk("server") for r in range(nranks)]
+    for t in range(3):   # round 0 direct, then momentum
+        want = np.zeros(total, np.float32)
+        for r in range(nranks):
+            cid = f"C{r}"
+            enc, srv, ref = encs[r], srvs[r], refs[r]
+            xs = [(rng.standard_normal(s) * 1e-3).astype(np.float32) for _, s in shapes]
+            ret, layers, errs = enc.compress_batch(names, xs)
+            assert ret == 0, errs
+            for sv, agg in ((srv, aggs[r]), (ref, plain[r])):
+                assert sv.lib.falcom_set_aggregate(sv.h, c_vp(agg), off_c, len(names), w) == 0
+                assert sv.lib.falcom_set_aggregate_store(sv.h, 1) == 0
+                assert sv.lib.falcom_set_aggregate_only(sv.h, 1) == 0
+            assert srv.lib.falcom_set_aggregate_shards(srv.h, land_arr, nranks, r, shard) == 0
+            assert srv.decompress_batch(names, layers, client=cid)[0] == 0
+            assert ref.decompress_batch(names, layers, client=cid)[0] == 0
+            flat = view(plain[r], cap)[:total].copy()
+            want = want + flat          # rank order
+        for r in range(nranks):
+            assert lib.falcom_shard_reduce(c_vp(land[r]), nranks, r, shard, total, agg_arr, None) == 0
+        for r in range(nranks):
+            assert lib.falcom_peer_allreduce(plain_arr, nranks, r, shard, total, None) == 0
+        for r in range(nranks):
+            assert np.array_equal(view(aggs[r], cap)[:total].view(np.uint32), want.view(np.uint32)), (t, r)
+            assert np.array_equal(view(plain[r], cap)[:total].view(np.uint32), want.view(np.uint32)), (t, r)
+        for p in plain:   # the next round's plain aggregates start from zero padding again
+            view(p, cap)[:] = 0.0
+    for c in encs + srvs + refs:
+        c.close()
+    for p in land + aggs + plain:
+        lib.emu_device_free(p)
