@@ -486,6 +486,12 @@ __device__ __forceinline__ const float *staged_or(const StageDesc &d, const floa
 // buf + NA * STAGE_ELEMS); pre(const StageDesc&) runs on all threads between
 // the issue and the wait.  A copy that does not complete within the spin
 // limit sets the item's error flag and skips the tile.
+// Under programmatic dependent launch the plan and the bulk copies run
+// before the wait on the previous kernel of the stream, so they may read
+// only what was complete before that kernel started: the inputs, the state
+// of earlier calls, and the output of kernels two or more launches back
+// (pass 4 stages the new memory of pass 3 with the finalize kernel of pass 3
+// between them).
 template <int NA, bool REVERSE, class Plan, class Pre, class Body>
 __device__ void run_tile(const int2 *list, float *stage_mem, uint64_t *bar, StageDesc *sd, int32_t *err_of_item,
                          int err_stride_words, Plan plan, Pre pre, Body body) {
