@@ -758,6 +758,11 @@ int mc_compress_grouped(MomentumCompressor *mc, BatchItem *items, size_t n, cons
             cgroup *grp = &G[p->group];
             if (p->prev_item >= 0) I->prev = (const float *)P[p->prev_item].dev_in;
             else I->prev = (const float *)p->prev_t->dev;
+            if (p->prev_item < 0 && p->prev_t->st_valid) {
+                I->prev_known = 1;
+                I->pm_known = p->prev_t->st_mean;
+                I->ps_known = p->prev_t->st_std;
+            }
             /* the first momentum item of a group reads the committed memory;
              * later ones continue in the group's new buffer */
             I->mem_in = p->wave == 0 ? (grp->mem_committed ? (const float *)grp->mem_committed->dev
@@ -1060,6 +1065,14 @@ int mc_compress_grouped(MomentumCompressor *mc, BatchItem *items, size_t n, cons
         for (size_t i = 0; i < n; i++) {
             mc_layer_rec *r = P[i].lrec;
             r->step++;
+            /* a momentum item's history is an exact copy of its input, whose
+             * |x| statistics the item just computed: the next round's
+             * encode of this layer takes them instead of recomputing */
+            if (P[i].hist) {
+                P[i].hist->st_valid = P[i].kind == MC_K_MOMENTUM;
+                P[i].hist->st_mean = hres[i].cm;
+                P[i].hist->st_std = hres[i].cs;
+            }
             /* the last item of a history key becomes the head (ref :2902) */
             rec_commit(&r->hist, &r->spare, P[i].hist);
             P[i].hist = NULL;

@@ -65,6 +65,13 @@ typedef struct {
     mc_fastdiv ksdiv;
     float lr;
     float thr;
+    /* MOMENTUM: 1 when the history head `prev` is an exact copy of an input
+     * whose mean and population std of |x| an earlier momentum encode of the
+     * same layer computed (pm_known, ps_known): the passes then take them
+     * instead of reading prev for them.  Same values, same reduction order:
+     * the history has the input's shape and so its tiling. */
+    int32_t prev_known;
+    float pm_known, ps_known;
 } mc_enc_item;
 
 typedef struct {

@@ -72,6 +72,11 @@ typedef struct {
     size_t bytes;
     int device;
     void *dev;         /* device copy */
+    /* mean and population std of |x| of exactly these values as a momentum
+     * encode computed them (st_valid 1), set when the encode commits the
+     * tensor as a layer's history head; 0 for any other writer */
+    int st_valid;
+    float st_mean, st_std;
 } mc_tensor;
 
 mc_tensor *tensor_new(DataType dt, size_t ndim, const size_t *shape, int device);

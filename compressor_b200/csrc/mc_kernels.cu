@@ -639,31 +639,40 @@ __device__ void pass1_tile(const mc_enc_launch &L, const StageDesc &d, const flo
             const float4 *c4 = (const float4 *)(cur + tr.e0), *p4 = (const float4 *)(prev + tr.e0);
             float4 *h4 = hist ? (float4 *)(hist + tr.e0) : nullptr;
             const uint64_t hpol = l2_stream();   // the history copy is read next round
-            for (int q = threadIdx.x; q < nq; q += TPB) {
-                const float4 c = c4[q], p = p4[q];
-                dd[0] += (double)fabsf(c.x);
-                dd[1] += (double)fabsf(p.x);
-                dd[0] += (double)fabsf(c.y);
-                dd[1] += (double)fabsf(p.y);
-                dd[0] += (double)fabsf(c.z);
-                dd[1] += (double)fabsf(p.z);
-                dd[0] += (double)fabsf(c.w);
-                dd[1] += (double)fabsf(p.w);
-                mn = c.x < mn ? c.x : mn;
-                mx = c.x > mx ? c.x : mx;
-                mn = c.y < mn ? c.y : mn;
-                mx = c.y > mx ? c.y : mx;
-                mn = c.z < mn ? c.z : mn;
-                mx = c.z > mx ? c.z : mx;
-                mn = c.w < mn ? c.w : mn;
-                mx = c.w > mx ? c.w : mx;
-                if (h4) st_f4(h4 + q, c, hpol);
-            }
+            // WP: the |prev| sum is computed here (its statistics are not known)
+            auto quads = [&](auto wp) {
+                constexpr bool WP = decltype(wp)::value;
+                for (int q = threadIdx.x; q < nq; q += TPB) {
+                    const float4 c = c4[q];
+                    dd[0] += (double)fabsf(c.x);
+                    dd[0] += (double)fabsf(c.y);
+                    dd[0] += (double)fabsf(c.z);
+                    dd[0] += (double)fabsf(c.w);
+                    if (WP) {
+                        const float4 p = p4[q];
+                        dd[1] += (double)fabsf(p.x);
+                        dd[1] += (double)fabsf(p.y);
+                        dd[1] += (double)fabsf(p.z);
+                        dd[1] += (double)fabsf(p.w);
+                    }
+                    mn = c.x < mn ? c.x : mn;
+                    mx = c.x > mx ? c.x : mx;
+                    mn = c.y < mn ? c.y : mn;
+                    mx = c.y > mx ? c.y : mx;
+                    mn = c.z < mn ? c.z : mn;
+                    mx = c.z > mx ? c.z : mx;
+                    mn = c.w < mn ? c.w : mn;
+                    mx = c.w > mx ? c.w : mx;
+                    if (h4) st_f4(h4 + q, c, hpol);
+                }
+            };
+            if (I.prev_known) quads(std::false_type());
+            else quads(std::true_type());
             if ((len & 3) && threadIdx.x == (nq % TPB)) {
                 for (int64_t g = tr.e0 + 4 * (int64_t)nq; g < tr.e1; g++) {
                     const float c = cur[g];
                     dd[0] += (double)fabsf(c);
-                    dd[1] += (double)fabsf(prev[g]);
+                    if (!I.prev_known) dd[1] += (double)fabsf(prev[g]);
                     mn = c < mn ? c : mn;
                     mx = c > mx ? c : mx;
                     if (hist) hist[g] = c;
@@ -671,9 +680,9 @@ __device__ void pass1_tile(const mc_enc_launch &L, const StageDesc &d, const flo
             }
         } else {
             for (int64_t g = tr.e0 + 4 * (int64_t)threadIdx.x; g < tr.e1; g += 4 * TPB) {
-                float c[4], p[4];
+                float c[4], p[4] = {0.0f, 0.0f, 0.0f, 0.0f};
                 ld4(cur, g, tr.e1, false, c);
-                ld4(prev, g, tr.e1, false, p);
+                if (!I.prev_known) ld4(prev, g, tr.e1, false, p);
 #pragma unroll
                 for (int j = 0; j < 4; j++) {
                     if (g + j < tr.e1) {
@@ -908,7 +917,7 @@ __global__ void __launch_bounds__(TPB, 4) k_enc_pass1(mc_enc_launch L) {
                     const mc_enc_item &I = enc_plan_range(L, d);
                     if ((I.kind == MC_K_MOMENTUM || I.kind == MC_K_QUANT) && stageable(L.staged, I, d)) {
                         d.src[0] = (const float *)I.cur;
-                        if (I.kind == MC_K_MOMENTUM) d.src[1] = I.prev;
+                        if (I.kind == MC_K_MOMENTUM && !I.prev_known) d.src[1] = I.prev;
                     }
                 },
                 [](const StageDesc &) {},
@@ -960,7 +969,7 @@ __global__ void __launch_bounds__(TPB) k_enc_final1(mc_enc_launch L) {
         if (threadIdx.x == 0) {
             const double dn = (double)I.n;
             R->cm = __double2float_rn(__ddiv_rn(a[0], dn));
-            R->pm = __double2float_rn(__ddiv_rn(a[1], dn));
+            R->pm = I.prev_known ? I.pm_known : __double2float_rn(__ddiv_rn(a[1], dn));
             R->gmin = tmn;
             R->gmax = tmx;
             R->P = total;
@@ -987,7 +996,7 @@ __global__ void __launch_bounds__(TPB, 6) k_enc_pass2(mc_enc_launch L) {
                         const mc_enc_item &I = enc_plan_range(L, d);
                         if (stageable(L.staged, I, d)) {
                             d.src[0] = (const float *)I.cur;
-                            d.src[1] = I.prev;
+                            if (!I.prev_known) d.src[1] = I.prev;
                         }
                     },
                     [](const StageDesc &) {},
@@ -1000,27 +1009,49 @@ __global__ void __launch_bounds__(TPB, 6) k_enc_pass2(mc_enc_launch L) {
                         double dd[4] = {0.0, 0.0, 0.0, 0.0};
                         long long l[2] = {0, 0};
                         float mn = FLT_MAX, mx = -FLT_MAX, mx2 = 0.0f;
-                        auto acc = [&](float c, float p) {
+                        // with the previous gradient's statistics known only |cur| is summed
+                        const bool wp = !I.prev_known;
+                        auto accc = [&](float c) {
                             const double dc = (double)__fsub_rn(fabsf(c), cm);
-                            const double dp = (double)__fsub_rn(fabsf(p), pm);
                             dd[0] = __fma_rn(dc, dc, dd[0]);
+                        };
+                        auto accp = [&](float p) {
+                            const double dp = (double)__fsub_rn(fabsf(p), pm);
                             dd[1] = __fma_rn(dp, dp, dd[1]);
                         };
                         const int len = (int)(d.e1 - d.e0), nq = len >> 2;
                         if (I.vec) {
                             const float4 *c4 = (const float4 *)(cur + d.e0), *p4 = (const float4 *)(prev + d.e0);
-                            for (int q = threadIdx.x; q < nq; q += TPB) {
-                                const float4 c = c4[q], p = p4[q];
-                                acc(c.x, p.x);
-                                acc(c.y, p.y);
-                                acc(c.z, p.z);
-                                acc(c.w, p.w);
-                            }
+                            auto quads = [&](auto wpc) {
+                                constexpr bool WP = decltype(wpc)::value;
+                                for (int q = threadIdx.x; q < nq; q += TPB) {
+                                    const float4 c = c4[q];
+                                    accc(c.x);
+                                    accc(c.y);
+                                    accc(c.z);
+                                    accc(c.w);
+                                    if (WP) {
+                                        const float4 p = p4[q];
+                                        accp(p.x);
+                                        accp(p.y);
+                                        accp(p.z);
+                                        accp(p.w);
+                                    }
+                                }
+                            };
+                            if (wp) quads(std::true_type());
+                            else quads(std::false_type());
                             if ((len & 3) && threadIdx.x == (nq % TPB))
-                                for (int64_t g = d.e0 + 4 * (int64_t)nq; g < d.e1; g++) acc(cur[g], prev[g]);
+                                for (int64_t g = d.e0 + 4 * (int64_t)nq; g < d.e1; g++) {
+                                    accc(cur[g]);
+                                    if (wp) accp(prev[g]);
+                                }
                         } else {
                             for (int64_t g = d.e0 + threadIdx.x * 4; g < d.e1; g += 4 * TPB)
-                                for (int64_t e = g; e < g + 4 && e < d.e1; e++) acc(cur[e], prev[e]);
+                                for (int64_t e = g; e < g + 4 && e < d.e1; e++) {
+                                    accc(cur[e]);
+                                    if (wp) accp(prev[e]);
+                                }
                         }
                         block_reduce<2, 0, 0>(red, dd, mn, mx, mx2, l);
                         if (threadIdx.x == 0) {
@@ -1050,7 +1081,7 @@ __global__ void __launch_bounds__(TPB) k_enc_final2(mc_enc_launch L) {
     if (threadIdx.x == 0) {
         const double dn = (double)I.n;
         const float cs = __fsqrt_rn(__double2float_rn(__ddiv_rn(a[0], dn)));
-        const float ps = __fsqrt_rn(__double2float_rn(__ddiv_rn(a[1], dn)));
+        const float ps = I.prev_known ? I.ps_known : __fsqrt_rn(__double2float_rn(__ddiv_rn(a[1], dn)));
         R->cs = cs;
         R->ps = ps;
         R->inv_ps = (ps > 1e-8f) ? __fdiv_rn(1.0f, ps) : 1.0f;

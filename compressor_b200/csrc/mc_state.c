@@ -72,6 +72,7 @@ static int same_layout(const mc_tensor *t, DataType dt, size_t ndim, const size_
 mc_tensor *rec_take(mc_tensor **spare, DataType dt, size_t ndim, const size_t *shape, int device) {
     if (spare && *spare) {
         mc_tensor *s = *spare;
+        s->st_valid = 0;   /* about to be rewritten */
         if (same_layout(s, dt, ndim, shape)) {
             *spare = NULL;
             return s;
