@@ -56,8 +56,6 @@ PEAK_FALLBACK_GBS = 6650.0
 # whenever a kernel changes; None for workloads that were not captured.
 NCU_TRAFFIC = {
     ("resnet50", "q8"): {
-        "enc_pass1_stats_sign": 246_334_464,
-        "enc_pass2_variance": 193_776_128,
         "enc_pass3_predict": 342_665_216,
         "enc_pass4_quantize_pack": 201_046_528,
         "dec_prefix": 259_840,
@@ -753,12 +751,14 @@ def kernel_roofline(torch, D, fr: FedRound, data: DeviceUpdates, K: int, flush, 
     q = {"q8": 1.0, "int4": 0.5, "raw": 4.0}[codec]
     me, de = ab["momentum_elements"], ab["direct_elements"]
     nc = len(fr.clients)
-    # algorithmic bytes per launch of each kernel (all kernels predicted);
-    # the decoder writes memory, history and the aggregate (store mode: the
-    # old value is not read; first client of a round)
+    # algorithmic bytes per launch of each kernel (all kernels predicted,
+    # steady state: the previous gradient's |x| statistics come from the
+    # round that wrote it, so passes 1 and 2 do not read it); the decoder
+    # writes memory, history and the aggregate (store mode: the old value is
+    # not read; first client of a round)
     alg = {
-        "enc_pass1_stats_sign": me * 12 + de * 8,          # read cur, prev; write history copy
-        "enc_pass2_variance": me * 8,                       # read cur, prev
+        "enc_pass1_stats_sign": me * 8 + de * 8,           # read cur; write history copy
+        "enc_pass2_variance": me * 4,                       # read cur
         "enc_pass3_predict": me * 16,                       # read cur, prev, mem; write mem
         "enc_pass4_quantize_pack": me * (8 + q) + de * (4 + q),   # read cur, mem; write codes
         "dec_reconstruct": me * (20 + q) + de * (8 + q),    # read q, prev, mem; write mem, history, aggregate
@@ -854,11 +854,12 @@ def microbench_line(torch, D, K, flush, so, stream, codec="q8"):
             tot[k] = (a[0] + v[0], a[1] + v[1])
     n = 512 * 512 * 9
     kern = 512 * 512
-    # algorithmic bytes per launch (all kernels predicted) and the reference
+    # algorithmic bytes per launch (all kernels predicted; from the third round on the previous
+    # gradient's statistics are known, so passes 1 and 2 read only cur) and the reference
     # microbench kernels each of ours covers
     alg = {
-        "enc_pass1_stats_sign": (12 * n + kern / 8 * 2, "threshold_scan + bitmap_pack (+ stats sums, history copy)"),
-        "enc_pass2_variance": (8 * n, "(stats second pass)"),
+        "enc_pass1_stats_sign": (8 * n + kern / 8 * 2, "threshold_scan + bitmap_pack (+ stats sums, history copy)"),
+        "enc_pass2_variance": (4 * n, "(stats second pass)"),
         "enc_pass3_predict": (16 * n, "momentum_update + residual_predmem_update"),
         "enc_pass4_quantize_pack": (9 * n + kern / 8 * 2, "dominant_sign_pack (+ q8 codes, bitmap frame)"),
         "dec_reconstruct": (21 * n, "decompress_reconstruct (+ q8 decode, memory update)"),

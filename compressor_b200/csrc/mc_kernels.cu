@@ -908,7 +908,7 @@ __device__ __forceinline__ bool stageable(int staged, const mc_enc_item &I, cons
 }
 #define ENC_ERR(L) &(L).results[0].err, (int)(sizeof(mc_enc_result) / 4)
 
-__global__ void __launch_bounds__(TPB, 4) k_enc_pass1(mc_enc_launch L) {
+__global__ void __launch_bounds__(TPB, 5) k_enc_pass1(mc_enc_launch L) {
     __shared__ Red red;
     __shared__ TileShared ts;
     extern __shared__ __align__(128) float s_stage[];
