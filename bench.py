@@ -295,10 +295,12 @@ class DeviceUpdates:
 
 # ------------------------------------------------------------ the round
 # --aggregate modes that sum over NVLink peer memory, and their PeerAggregate mode
-PEER_MODES = {"peer": "fused", "oneshot": "oneshot"}
+PEER_MODES = {"peer": "fused", "oneshot": "oneshot", "synced": "synced"}
 COLLECTIVES = {"peer": "decoder stores into owner shards over NVLink peer memory, shard sum + all-gather kernel",
                "oneshot": "one-shot in-place all-reduce kernel over NVLink peer memory (peer loads of the "
                           "rank's shard, sum, peer stores)",
+               "synced": "one-shot in-place all-reduce kernel over NVLink peer memory with its barriers on "
+                         "peer flag words inside the kernel (no NCCL call per round)",
                "nccl": "nccl all-reduce"}
 
 
@@ -610,8 +612,13 @@ def fedavg_check(torch, D: Dist, fr: FedRound, data: DeviceUpdates):
     den = float(torch.linalg.vector_norm(acc).item())
     exact = bool(torch.equal(fr.agg, acc.float())) if D.world == 1 and len(fr.clients) == 1 else None
     rel = num / den if den > 0 else num
-    return {"rel_l2": rel, "pass": rel <= 1e-6, "bar": 1e-6, "bit_exact_single_client": exact,
-            "against": "float64 sum over all clients of weight x decoded update (FedAvg), all-reduced in float64"}
+    # synced peer mode: a barrier wait that ran out inside the kernel, on any rank
+    sync_err = D.max(float(fr.peer.errors())) if fr.peer is not None else 0.0
+    out = {"rel_l2": rel, "pass": rel <= 1e-6 and sync_err == 0.0, "bar": 1e-6, "bit_exact_single_client": exact,
+           "against": "float64 sum over all clients of weight x decoded update (FedAvg), all-reduced in float64"}
+    if fr.peer is not None and fr.peer.mode == "synced":
+        out["barrier_timeouts"] = int(sync_err)
+    return out
 
 
 # ------------------------------------------------------------ reference CPU
@@ -1034,7 +1041,7 @@ def run_ours(args):
     if world > 1 and args.aggregate == "auto":
         trial = {}
         checks = {}
-        for mode in ("peer", "oneshot", "nccl"):
+        for mode in ("peer", "oneshot", "synced", "nccl"):
             ft = FedRound(torch, D, model, [D.rank], world, codec, stream, so, peer=mode)
             dt = DeviceUpdates(torch, model, [D.rank], D.dev, seed0=900)
             st_, _, _, _ = timed_rounds(torch, D, ft, dt, 8, 4, flush)
@@ -1288,10 +1295,11 @@ def main():
     ap.add_argument("--skip-configs", action="store_true",
                     help="headline step only (no federated / GPT-2 / per-config lines)")
     ap.add_argument("--cpu-budget-s", type=float, default=12.0)
-    ap.add_argument("--aggregate", default="auto", choices=["auto", "peer", "oneshot", "nccl"],
+    ap.add_argument("--aggregate", default="auto", choices=["auto", "peer", "oneshot", "synced", "nccl"],
                     help="N > 1: how the server aggregate is summed over the GPUs (peer: reduce-scatter fused "
                          "into the decoder over NVLink + shard sum / all-gather kernel; oneshot: local "
-                         "aggregates, then one in-place all-reduce kernel over NVLink peer memory; nccl: "
+                         "aggregates, then one in-place all-reduce kernel over NVLink peer memory between two "
+                         "NCCL barriers; synced: the same kernel with its barriers on peer flags; nccl: "
                          "all-reduce; auto: the fastest in untimed trial rounds whose FedAvg check passes)")
     ap.add_argument("--e2e-chunks", type=int, default=3,
                     help="layer chunks of the pipelined host-buffer step (e2e)")

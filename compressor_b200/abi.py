@@ -516,6 +516,9 @@ def bind_extensions(lib: ctypes.CDLL) -> None:
     lib.falcom_peer_allreduce.argtypes = [ctypes.POINTER(c_vp), ctypes.c_int, ctypes.c_int, ctypes.c_size_t,
                                           ctypes.c_size_t, c_vp]
     lib.falcom_peer_allreduce.restype = ctypes.c_int
+    lib.falcom_peer_allreduce_sync.argtypes = [ctypes.POINTER(c_vp), ctypes.POINTER(c_vp), ctypes.c_int,
+                                               ctypes.c_int, ctypes.c_size_t, ctypes.c_size_t, ctypes.c_uint32, c_vp]
+    lib.falcom_peer_allreduce_sync.restype = ctypes.c_int
     lib.falcom_copy_sm.argtypes = [c_vp, c_vp, ctypes.c_size_t, ctypes.c_int, c_vp]
     lib.falcom_copy_sm.restype = ctypes.c_int
     lib.falcom_state_save.argtypes = [c_vp, ctypes.c_char_p]

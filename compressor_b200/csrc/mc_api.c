@@ -1080,6 +1080,24 @@ MC_EXPORT int falcom_peer_allreduce(float *const *aggregates, int nranks, int ra
                                     stream) >= 0 ? ERROR_NONE : ERROR_DECOMPRESSION;
 }
 
+MC_EXPORT int falcom_peer_allreduce_sync(float *const *aggregates, uint32_t *const *flags, int nranks, int rank,
+                                         size_t shard_elems, size_t total_elems, uint32_t epoch, void *stream) {
+    if (!aggregates || !flags || nranks < 1 || nranks > MC_MAX_RANKS || rank < 0 || rank >= nranks ||
+        shard_elems % 64 != 0 || shard_elems == 0 || total_elems > (size_t)nranks * shard_elems) {
+        fprintf(stderr, "[ERROR] falcom_peer_allreduce_sync: invalid arguments\n");
+        return ERROR_INVALID_PARAM;
+    }
+    for (int r = 0; r < nranks; r++) {
+        if (!aggregates[r] || ((uintptr_t)aggregates[r] & 15) != 0 || !flags[r] || ((uintptr_t)flags[r] & 3) != 0) {
+            fprintf(stderr, "[ERROR] falcom_peer_allreduce_sync: aggregate or flag block %d is NULL or misaligned\n",
+                    r);
+            return ERROR_INVALID_PARAM;
+        }
+    }
+    return mc_launch_peer_allreduce_sync(aggregates, flags, nranks, rank, (int64_t)shard_elems, (int64_t)total_elems,
+                                         epoch, stream) >= 0 ? ERROR_NONE : ERROR_DECOMPRESSION;
+}
+
 /* Device address of [p, p + bytes) for a kernel of the current device:
  * device memory of that device as is, pinned host memory through its mapped
  * device pointer; NULL (with a message) for anything else. */

@@ -267,6 +267,10 @@ int mc_launch_shard_reduce(const float *landing, int nranks, int rank, int64_t s
 int mc_launch_copy(void *dst, const void *src, int64_t bytes, int nblocks, void *stream);
 int mc_launch_peer_allreduce(float *const *aggregates, int nranks, int rank, int64_t shard, int64_t total,
                              void *stream);
+/* the same with the barriers before and after it done by the kernel over the ranks' flag blocks (18 words each,
+ * zeroed before the first round); 1 launched, -1 error */
+int mc_launch_peer_allreduce_sync(float *const *aggregates, uint32_t *const *flags, int nranks, int rank,
+                                  int64_t shard, int64_t total, uint32_t epoch, void *stream);
 
 /* Launchers: return the number of kernels launched, or a negative value
  * when a launch failed.  `tr` may be NULL. */

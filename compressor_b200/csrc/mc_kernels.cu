@@ -2224,6 +2224,111 @@ __global__ void __launch_bounds__(TPB) k_peer_allreduce(PeerAggs a, int nranks, 
     }
 }
 
+// The one-shot all-reduce with its two barriers in the kernel itself, over
+// flag words in every rank's memory (block f of rank r, mapped into every
+// rank: words [0, 8) arrival of rank q, [8, 16) completion of rank q, word
+// 16 this launch's CTA count, word 17 an error flag).  Each launch carries a
+// round number `epoch`, larger than the last one; a flag is set when it
+// holds epoch (compared modulo 2^32).
+//  * arrival: block 0 of every rank, once its kernel starts (so its decodes,
+//    earlier on its stream, are complete), stores epoch into word `rank` of
+//    every rank's block (system-scope release after a system fence); every
+//    CTA waits until its own block shows all ranks arrived, then sums its
+//    share of the rank's shard as k_peer_allreduce does;
+//  * completion: every CTA fences its peer stores and counts itself in word
+//    16; the last one stores epoch into word 8 + rank of every rank's block
+//    and waits until all ranks completed, so no kernel after this one on the
+//    stream (the next round's decodes into the aggregate) starts while a
+//    peer still reads or writes this rank's aggregate.
+// Every wait is bounded (about a second); one that runs out sets word 17
+// and the CTA stops, so a missing rank ends in an error flag, not a hang.
+struct PeerFlags {
+    uint32_t *blk[MC_MAX_RANKS];
+};
+#define PF_ARRIVE 0
+#define PF_DONE 8
+#define PF_COUNT 16
+#define PF_ERR 17
+__device__ __forceinline__ void st_release_sys(uint32_t *p, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+// true once p[k] has reached `epoch` for every k < n; false after about a second
+__device__ bool wait_flags(const uint32_t *p, int n, uint32_t epoch) {
+    uint64_t t0;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+    for (int k = 0; k < n; k++) {
+        for (uint32_t i = 0;; i++) {
+            if ((int32_t)(ld_acquire_sys(p + k) - epoch) >= 0) break;
+            if (i >= (1u << 22)) return false;
+            __nanosleep(128);
+            if ((i & 63) == 63) {
+                uint64_t t;
+                asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+                if (t - t0 > 1000000000ull) return false;
+            }
+        }
+    }
+    return true;
+}
+__global__ void __launch_bounds__(TPB) k_peer_allreduce_sync(PeerAggs a, PeerFlags f, int nranks, int rank,
+                                                             int64_t lo, int64_t hi, uint32_t epoch) {
+    __shared__ int s_ok;
+    uint32_t *mine = f.blk[rank];
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+        __threadfence_system();
+        for (int r = 0; r < nranks; r++) st_release_sys(f.blk[r] + PF_ARRIVE + rank, epoch);
+    }
+    if (threadIdx.x == 0) {
+        s_ok = wait_flags(mine + PF_ARRIVE, nranks, epoch);
+        if (!s_ok) atomicExch(mine + PF_ERR, 1u);
+    }
+    __syncthreads();
+    // a CTA whose wait ran out skips the sum but still counts itself, so the
+    // count resets and every rank is released; the error flag reports it
+    const int64_t nq = s_ok ? (hi - lo) >> 2 : 0;
+    for (int64_t q = blockIdx.x * (int64_t)TPB + threadIdx.x; q < nq; q += (int64_t)gridDim.x * TPB) {
+        const int64_t x = lo + 4 * q;
+        float4 u[MC_MAX_RANKS];
+#pragma unroll
+        for (int r = 0; r < MC_MAX_RANKS; r++)
+            if (r < nranks) u[r] = __ldcv((const float4 *)(a.agg[r] + x));
+        float4 v = u[0];
+#pragma unroll
+        for (int r = 1; r < MC_MAX_RANKS; r++) {
+            if (r >= nranks) break;
+            v.x = __fadd_rn(v.x, u[r].x);
+            v.y = __fadd_rn(v.y, u[r].y);
+            v.z = __fadd_rn(v.z, u[r].z);
+            v.w = __fadd_rn(v.w, u[r].w);
+        }
+#pragma unroll
+        for (int r = 0; r < MC_MAX_RANKS; r++)
+            if (r < nranks) *(float4 *)(a.agg[r] + x) = v;
+    }
+    const int64_t xt = lo + 4 * nq;
+    if (s_ok && blockIdx.x == 0 && xt + threadIdx.x < hi) {
+        const int64_t e = xt + threadIdx.x;
+        float v = __ldcv(a.agg[0] + e);
+        for (int r = 1; r < nranks; r++) v = __fadd_rn(v, __ldcv(a.agg[r] + e));
+        for (int r = 0; r < nranks; r++) a.agg[r][e] = v;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence_system();
+        if (atomicAdd(mine + PF_COUNT, 1u) == gridDim.x - 1) {
+            __threadfence_system();
+            mine[PF_COUNT] = 0;   // the next launch comes after this one on the stream
+            for (int r = 0; r < nranks; r++) st_release_sys(f.blk[r] + PF_DONE + rank, epoch);
+            if (!wait_flags(mine + PF_DONE, nranks, epoch)) atomicExch(mine + PF_ERR, 1u);
+        }
+    }
+}
+
 // Copy of `bytes` bytes by the SMs: a transfer between pinned host memory
 // (mapped into the device address space) and device memory that occupies
 // no copy engine, so the copies the codec queues on the copy engines never
@@ -2415,6 +2520,28 @@ extern "C" int mc_launch_copy(void *dst, const void *src, int64_t bytes, int nbl
     if (nblocks > 148 * 8) nblocks = 148 * 8;
     cudaStream_t st = (cudaStream_t)stream;
     k_copy<<<nblocks, TPB, 0, st>>>((const uint8_t *)src, (uint8_t *)dst, bytes, head, nq);
+    return cudaGetLastError() == cudaSuccess ? 1 : -1;
+}
+
+extern "C" int mc_launch_peer_allreduce_sync(float *const *aggregates, uint32_t *const *flags, int nranks, int rank,
+                                             int64_t shard, int64_t total, uint32_t epoch, void *stream) {
+    if (nranks < 1 || nranks > MC_MAX_RANKS || rank < 0 || rank >= nranks || shard <= 0 || (shard & 3) != 0)
+        return -1;
+    PeerAggs a;
+    PeerFlags f;
+    for (int r = 0; r < MC_MAX_RANKS; r++) {
+        a.agg[r] = r < nranks ? aggregates[r] : nullptr;
+        f.blk[r] = r < nranks ? flags[r] : nullptr;
+    }
+    const int64_t lo = (int64_t)rank * shard;
+    int64_t hi = lo + shard < total ? lo + shard : total;
+    if (hi < lo) hi = lo;   // an empty shard still takes part in both barriers
+    const int64_t nq = (hi - lo) >> 2;
+    int blocks = (int)((nq + TPB - 1) / TPB);
+    if (blocks > 148 * 8) blocks = 148 * 8;
+    if (blocks < 1) blocks = 1;
+    cudaStream_t s = (cudaStream_t)stream;
+    k_peer_allreduce_sync<<<blocks, TPB, 0, s>>>(a, f, nranks, rank, lo, hi, epoch);
     return cudaGetLastError() == cudaSuccess ? 1 : -1;
 }
 

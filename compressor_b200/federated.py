@@ -184,13 +184,19 @@ class PeerAggregate:
     into every rank's aggregate: reduce-scatter and all-gather in one
     kernel, both directions of the links at once) and a second barrier.
 
+    "synced": as "oneshot", with both barriers done inside the kernel
+    (falcom_peer_allreduce_sync) over a block of flag words that follows
+    each rank's aggregate in the same allocation; no NCCL call per round.
+    `errors()` reads the rank's error word (a barrier wait that ran out).
+
     The buffers, on every rank: its aggregate and (fused) its landing buffer,
     nranks x shard floats each, zeroed, so padding between items stays 0,
     mapped into every other rank's address space over CUDA IPC.  After
     `finish` every rank's aggregate holds the global sum.  Every rank
     creates, uses and closes it at the same points, in the same mode."""
 
-    MODES = ("fused", "oneshot")
+    MODES = ("fused", "oneshot", "synced")
+    FLAG_BYTES = 256   # flag block behind a synced aggregate (18 words used)
 
     def __init__(self, torch, dist, total: int, device_index: int, mode: str = "fused"):
         from cuda.bindings import runtime as rt
@@ -207,10 +213,12 @@ class PeerAggregate:
         keys = ("agg", "land") if mode == "fused" else ("agg",)
         self.local = {}
         for key in keys:
-            err, ptr = rt.cudaMalloc(nbytes)
+            size = nbytes + (self.FLAG_BYTES if key == "agg" and mode == "synced" else 0)
+            err, ptr = rt.cudaMalloc(size)
             self._ok(err, "cudaMalloc")
-            self._ok(rt.cudaMemset(ptr, 0, nbytes)[0], "cudaMemset")
+            self._ok(rt.cudaMemset(ptr, 0, size)[0], "cudaMemset")
             self.local[key] = int(ptr)
+        self.epoch = 0
         self._ok(rt.cudaDeviceSynchronize()[0], "cudaDeviceSynchronize")
         mine = {}
         for key, ptr in self.local.items():
@@ -244,6 +252,9 @@ class PeerAggregate:
         c_vp = ctypes.c_void_p
         self.c_land = (c_vp * self.nranks)(*self.ptrs["land"]) if mode == "fused" else None
         self.c_aggs = (c_vp * self.nranks)(*self.ptrs["agg"])
+        # the flag blocks sit behind the nranks x shard floats of each aggregate
+        self.c_flags = (c_vp * self.nranks)(*[p + nbytes for p in self.ptrs["agg"]]) if mode == "synced" else None
+        self.flag_off = nbytes
         self.tiny = torch.zeros(1, device=torch.device("cuda", device_index))
         self.agg = torch.as_tensor(_DeviceFloats(self.local["agg"], self.total), device=self.tiny.device)
 
@@ -269,6 +280,13 @@ class PeerAggregate:
         """After this rank's decodes are queued: barrier, the cross-rank sum
         (shard sum + all-gather, or the one-shot all-reduce), barrier (all on
         the current stream)."""
+        if self.mode == "synced":
+            self.epoch = (self.epoch + 1) & 0xFFFFFFFF
+            rc = lib.falcom_peer_allreduce_sync(self.c_aggs, self.c_flags, self.nranks, self.rank, self.shard,
+                                                self.total, self.epoch, ctypes.c_void_p(stream_ptr))
+            if rc != 0:
+                raise RuntimeError(f"falcom_peer_allreduce_sync failed ({rc})")
+            return
         self.dist.all_reduce(self.tiny)
         if self.mode == "fused":
             rc = lib.falcom_shard_reduce(ctypes.c_void_p(self.local["land"]), self.nranks, self.rank, self.shard,
@@ -281,6 +299,18 @@ class PeerAggregate:
         if rc != 0:
             raise RuntimeError(f"{what} failed ({rc})")
         self.dist.all_reduce(self.tiny)
+
+    def errors(self) -> int:
+        """Synced mode: this rank's error word (nonzero once a barrier wait in
+        the kernel ran out); 0 in the other modes.  Synchronises the device."""
+        if self.mode != "synced":
+            return 0
+        self.torch.cuda.synchronize()
+        buf = (ctypes.c_uint32 * 1)()
+        err = self.rt.cudaMemcpy(ctypes.addressof(buf), self.local["agg"] + self.flag_off + 4 * 17, 4,
+                                 self.rt.cudaMemcpyKind.cudaMemcpyDeviceToHost)[0]
+        self._ok(err, "cudaMemcpy")
+        return int(buf[0])
 
     def close(self) -> None:
         """Every rank: unmap the peers' buffers, then free its own once no

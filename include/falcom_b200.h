@@ -185,6 +185,24 @@ int falcom_shard_reduce(const float *landing, int nranks, int rank, size_t shard
 int falcom_peer_allreduce(float *const *aggregates, int nranks, int rank, size_t shard_elems,
                           size_t total_elems, void *stream);
 
+/* falcom_peer_allreduce with its two barriers done by the kernel itself over
+ * flag words in peer memory, without the caller's barriers: flags[r] is
+ * rank r's block of 18 uint32 (as addressed from the current device, 4-byte
+ * aligned, zeroed before the first call), `epoch` the round number, larger
+ * on every call (1, 2, ...; compared modulo 2^32), the same on every rank.
+ * The kernel announces the rank's arrival to every rank when it starts (the
+ * caller's decodes earlier on `stream` are then complete), waits for every
+ * rank's arrival, sums the rank's shard in rank order into every rank's
+ * aggregate, and returns once every rank has finished, so work queued after
+ * it on `stream` sees the whole sum and cannot overwrite the aggregate
+ * while a peer still uses it.  Every wait is bounded (about one second): a
+ * rank that never arrives sets word 17 of the waiting ranks' blocks, and
+ * their aggregates are then incomplete.  Queued on `stream` without
+ * waiting.  Returns 0, ERROR_INVALID_PARAM, or ERROR_DECOMPRESSION when the
+ * launch fails. */
+int falcom_peer_allreduce_sync(float *const *aggregates, uint32_t *const *flags, int nranks, int rank,
+                               size_t shard_elems, size_t total_elems, uint32_t epoch, void *stream);
+
 /* Copies `bytes` bytes from src to dst with a kernel of `nblocks` CTAs (0:
  * 32) on `stream` (cudaStream_t) instead of a copy engine, returning without
  * waiting.  Each side is device memory of the current device or pinned host

@@ -4,7 +4,9 @@ per-rank aggregates: "fused", the reduce-scatter of the cross-GPU sum fused
 into the decoder (falcom_set_aggregate_shards), then each rank's shard sum
 and all-gather (falcom_shard_reduce); "oneshot", local aggregates, then
 each rank's one-shot in-place all-reduce of its shard
-(falcom_peer_allreduce).
+(falcom_peer_allreduce) between NCCL barriers; "synced", the same with the
+barriers on peer flag words inside the kernel
+(falcom_peer_allreduce_sync).
 
 Two ranks, one process per GPU (spawned, NCCL on 127.0.0.1).  Rank r
 compresses two clients and decodes them on its server: the first into its
@@ -92,7 +94,7 @@ def _rank_main(rank, world, port, lib_path, out_dir, mode):
         dist.all_reduce(plain)
         torch.cuda.synchronize()
         a, b = peer.agg.cpu().numpy(), plain.cpu().numpy()
-        ok = ok and np.array_equal(a.view(np.uint32), b.view(np.uint32))
+        ok = ok and np.array_equal(a.view(np.uint32), b.view(np.uint32)) and peer.errors() == 0
     for c in list(encs.values()) + [srv, ref]:
         c.close()
     peer.close()
@@ -102,7 +104,7 @@ def _rank_main(rank, world, port, lib_path, out_dir, mode):
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("mode", ["fused", "oneshot"])
+@pytest.mark.parametrize("mode", ["fused", "oneshot", "synced"])
 def test_peer_aggregate_equals_nccl_allreduce(product_lib, tmp_path, mode):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
