@@ -79,6 +79,7 @@ inline void __syncthreads() { emu_cta->cta.wait(); }
 inline int __syncthreads_and(int v) { return emu_cta->cta.wait(v); }
 inline void __syncwarp(unsigned = 0xffffffffu) { emu_cta->warp[threadIdx.x >> 5]->wait(); }
 inline void __threadfence() { __atomic_thread_fence(__ATOMIC_SEQ_CST); }
+inline void __threadfence_system() { __atomic_thread_fence(__ATOMIC_SEQ_CST); }
 inline void __nanosleep(unsigned) { std::this_thread::yield(); }
 // Callers vote only to skip work that each lane guards by its own predicate,
 // so a per-lane answer gives the same result.

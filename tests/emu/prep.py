@@ -65,6 +65,15 @@ HELPERS = {
     # bulk copies complete at issue, so every phase a tile waits for is done
     "mbar_try_wait": "(void)bar; (void)parity; return true;",
     "mbar_wait": "(void)bar; (void)parity; return true;",
+    # peer flags: kernels run one after another here, so a flag that is not
+    # set yet never will be (one rank, or flags set beforehand)
+    "st_release_sys": "__atomic_store_n(p, v, __ATOMIC_RELEASE);",
+    "ld_acquire_sys": "return __atomic_load_n(p, __ATOMIC_ACQUIRE);",
+    "wait_flags": r"""
+    for (int k = 0; k < n; k++)
+        if ((int32_t)(__atomic_load_n(p + k, __ATOMIC_ACQUIRE) - epoch) < 0) return false;
+    return true;
+""",
 }
 
 LAUNCH = re.compile(r"(\w+)<<<([^,]+),\s*(\w+),\s*([^,]+),\s*(\w+)>>>\((.*)\);")

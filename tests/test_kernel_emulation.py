@@ -399,3 +399,39 @@ def test_emulated_sharded_aggregate_many_ranks(emu_lib, nranks):
         c.close()
     for p in land + aggs + plain:
         lib.emu_device_free(p)
+
+
+def test_emulated_peer_allreduce_sync_one_rank(emu_lib):
+    """falcom_peer_allreduce_sync on one emulated rank (its own arrival and
+    completion flags release it): the aggregate is unchanged, the flag block
+    holds the round number in word 0 (arrival) and word 8 (completion), the
+    CTA count is back to 0 and no error is set, for three rounds (a waiter
+    compares modulo 2^32, so a round number the flags already passed does
+    not wait either); bad arguments are refused."""
+    import ctypes
+    lib = ctypes.CDLL(emu_lib)
+    lib.emu_device_alloc.restype = ctypes.c_void_p
+    lib.emu_device_alloc.argtypes = [ctypes.c_size_t]
+    lib.emu_device_free.argtypes = [ctypes.c_void_p]
+    c_vp = ctypes.c_void_p
+    lib.falcom_peer_allreduce_sync.argtypes = [ctypes.POINTER(c_vp), ctypes.POINTER(c_vp), ctypes.c_int,
+                                               ctypes.c_int, ctypes.c_size_t, ctypes.c_size_t, ctypes.c_uint32,
+                                               c_vp]
+    shard, total = 8192, 8192 - 3
+    agg = lib.emu_device_alloc(4 * shard + 256)
+    view = np.ctypeslib.as_array((ctypes.c_float * shard).from_address(agg))
+    flags = np.ctypeslib.as_array((ctypes.c_uint32 * 64).from_address(agg + 4 * shard))
+    x = np.random.default_rng(2).standard_normal(shard).astype(np.float32)
+    view[:] = x
+    flags[:] = 0
+    aggs = (c_vp * 1)(agg)
+    fl = (c_vp * 1)(agg + 4 * shard)
+    for epoch in (1, 2, 3):
+        assert lib.falcom_peer_allreduce_sync(aggs, fl, 1, 0, shard, total, epoch, None) == 0
+        assert np.array_equal(view.view(np.uint32), x.view(np.uint32))
+        assert flags[0] == epoch and flags[8] == epoch and flags[16] == 0 and flags[17] == 0
+    assert lib.falcom_peer_allreduce_sync(aggs, fl, 1, 0, shard, total, 2, None) == 0   # below the flags: passes
+    assert flags[17] == 0
+    assert lib.falcom_peer_allreduce_sync(aggs, (c_vp * 1)(None), 1, 0, shard, total, 4, None) == -4
+    assert lib.falcom_peer_allreduce_sync(aggs, fl, 1, 1, shard, total, 4, None) == -4
+    lib.emu_device_free(agg)
