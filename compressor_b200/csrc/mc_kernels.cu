@@ -180,10 +180,15 @@ __device__ __forceinline__ int qmax_of(int codec) {
 // There rint(y) equals rint(r / scale) unless y lies within 2^-15 of a
 // half-integer; those elements (about 6 in 10^5), and every NaN / Inf case
 // (inv = Inf for a subnormal scale), take the exact quotient.
+// The product r * (1/scale) rounds like the quotient r / scale except,
+// possibly, next to a half-integer: |y - rint(y)| (exact, at most 0.5) of at
+// least 0.5 - 2^-15 -- or NaN, when 1/scale overflowed -- takes the exact
+// quotient.
+#define QUANT_NEAR_HALF 0.499969482421875f
 __device__ __forceinline__ int quant1(float r, float scale, float inv, float qm) {
     const float y = __fmul_rn(r, inv);
     float v = rintf(y);
-    if (!(fabsf(fabsf(__fsub_rn(y, v)) - 0.5f) > 3.0517578125e-5f)) v = rintf(__fdiv_rn(r, scale));
+    if (!(fabsf(__fsub_rn(y, v)) < QUANT_NEAR_HALF)) v = rintf(__fdiv_rn(r, scale));
     v = fminf(qm, fmaxf(-qm, v));
     return (int)v;
 }
@@ -1305,13 +1310,13 @@ __device__ __forceinline__ void put_codes_full(uint8_t *data_out, int64_t g, con
     for (int j = 0; j < 4; j++) {
         const float y = __fmul_rn(r[j], inv);
         v[j] = rintf(y);
-        need |= !(fabsf(fabsf(__fsub_rn(y, v[j])) - 0.5f) > 3.0517578125e-5f);
+        need |= !(fabsf(__fsub_rn(y, v[j])) < QUANT_NEAR_HALF);
     }
     if (__any_sync(__activemask(), need)) {   // the lanes still in the quad loop
 #pragma unroll
         for (int j = 0; j < 4; j++) {
             const float y = __fmul_rn(r[j], inv);
-            if (!(fabsf(fabsf(__fsub_rn(y, v[j])) - 0.5f) > 3.0517578125e-5f)) v[j] = rintf(__fdiv_rn(r[j], scale));
+            if (!(fabsf(__fsub_rn(y, v[j])) < QUANT_NEAR_HALF)) v[j] = rintf(__fdiv_rn(r[j], scale));
         }
     }
 #pragma unroll
