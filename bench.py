@@ -294,6 +294,15 @@ class DeviceUpdates:
 
 
 # ------------------------------------------------------------ the round
+def choose_aggregate(trial_ms: dict, passed: dict) -> str:
+    """The --aggregate mode to use after the trial rounds: the fastest (max
+    over ranks of the median step) among the modes whose FedAvg check passed;
+    NCCL when none did.  A mode missing from trial_ms fell back to NCCL at
+    set-up and is not a candidate."""
+    ok = [m for m in trial_ms if passed.get(m)]
+    return min(ok, key=lambda m: (trial_ms[m], m)) if ok else "nccl"
+
+
 # --aggregate modes that sum over NVLink peer memory, and their PeerAggregate mode
 PEER_MODES = {"peer": "fused", "oneshot": "oneshot", "synced": "synced"}
 COLLECTIVES = {"peer": "decoder stores into owner shards over NVLink peer memory, shard sum + all-gather kernel",
@@ -1052,7 +1061,7 @@ def run_ours(args):
                 checks[mode] = ok
             ft.close()
             del dt
-        best = min((m for m in trial if checks[m]), key=lambda m: trial[m], default="nccl")
+        best = choose_aggregate(trial, checks)
         choice = {"chosen": best, "trial_ms_per_step": {m: round(v, 4) for m, v in trial.items()},
                   "trial_fedavg_pass": checks,
                   "how": "8 untimed rounds each after 4 warm-up rounds, median, max over ranks; then one "
