@@ -130,9 +130,10 @@ enum {
 
 /* Elements of one tile: the unit of work of one CTA of the streaming
  * kernels and the capacity of one array of its shared-memory stage.  A
- * momentum tile holds a power-of-two number of whole kernels (at least 32)
- * with at most MC_TILE_ELEMS elements; other tiles hold MC_TILE_ELEMS
- * elements (4x that for byte copies). */
+ * momentum tile holds a multiple of 32 whole kernels (at least 32; a power
+ * of two when the layer's bitmap frame has more than one block) with at
+ * most MC_TILE_ELEMS elements; other tiles hold MC_TILE_ELEMS elements (4x
+ * that for byte copies). */
 #define MC_TILE_ELEMS 4096
 
 /* zstd framing shared by encoder and decoder: single-segment frame header
