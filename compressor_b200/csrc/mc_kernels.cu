@@ -995,6 +995,7 @@ __global__ void __launch_bounds__(TPB) k_enc_final1(mc_enc_launch L) {
 __global__ void __launch_bounds__(TPB, 6) k_enc_pass2(mc_enc_launch L) {
     __shared__ Red red;
     __shared__ TileShared ts;
+    __shared__ float s_par[2];
     extern __shared__ __align__(128) float s_stage[];
     run_tile<2, true>((const int2 *)L.mom_tiles, s_stage, &ts.bar, &ts.d, ENC_ERR(L),
                     [&](StageDesc &d) {
@@ -1004,11 +1005,17 @@ __global__ void __launch_bounds__(TPB, 6) k_enc_pass2(mc_enc_launch L) {
                             if (!I.prev_known) d.src[1] = I.prev;
                         }
                     },
-                    [](const StageDesc &) {},
+                    [&](const StageDesc &d) {
+                        // the item's means (final1), read while the copies are in flight
+                        if (threadIdx.x == 0) {
+                            const mc_enc_result *R = L.results + d.ii;
+                            s_par[0] = R->cm;
+                            s_par[1] = R->pm;
+                        }
+                    },
                     [&](const StageDesc &d, const float *buf) {
                         const mc_enc_item I = L.items[d.ii];
-                        const mc_enc_result *R = L.results + d.ii;
-                        const float cm = R->cm, pm = R->pm;
+                        const float cm = s_par[0], pm = s_par[1];
                         const float *cur = staged_or(d, buf, 0, (const float *)I.cur);
                         const float *prev = staged_or(d, buf, 1, I.prev);
                         double dd[4] = {0.0, 0.0, 0.0, 0.0};
