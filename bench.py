@@ -606,6 +606,25 @@ def timed_rounds(torch, D: Dist, fr: FedRound, data: DeviceUpdates, K: int, W: i
     return step, codec, wait, ar
 
 
+def first_rounds(torch, D: Dist, model, world, codec, stream, so, aggregate, flush, hot_steps):
+    """Rounds 0, 1 and 2 of fresh encoder / decoder instances, each timed
+    like a hot step (L2 flushed before it, CUDA events, max over ranks),
+    beside the median of the hot steps.  Round 0 has no history: every
+    tensor takes the direct path and the state is allocated; round 1 is the
+    first momentum round (the previous gradient's statistics not yet
+    known); from round 2 on the rounds are hot."""
+    fr0 = FedRound(torch, D, model, [D.rank], world, codec, stream, so, peer=aggregate)
+    d0 = DeviceUpdates(torch, model, [D.rank], D.dev, seed0=1500)
+    s0, _, _, _ = timed_rounds(torch, D, fr0, d0, 3, 0, flush)
+    fr0.close()
+    del d0
+    return {"round0_ms": round(D.max(s0[0]), 4), "round1_ms": round(D.max(s0[1]), 4),
+            "round2_ms": round(D.max(s0[2]), 4), "hot_median_ms": round(D.max(statistics.median(hot_steps)), 4),
+            "how": "fresh instances, rounds 0-2 timed like the hot steps (L2 flushed before each, CUDA events, "
+                   "max over ranks); round 0: no history, every tensor direct, state allocated; round 1: first "
+                   "momentum round; hot median: the timed steps of the headline"}
+
+
 def fedavg_check(torch, D: Dist, fr: FedRound, data: DeviceUpdates):
     """One more round in which the server also returns the decoded arrays:
     rank 0 compares the NCCL-reduced float32 aggregate with the float64 sum
@@ -1102,6 +1121,7 @@ def run_ours(args):
     check = fedavg_check(torch, D, fr, data)
     collective = fr.collective
     fr.close()
+    first = first_rounds(torch, D, model, world, codec, stream, so, args.aggregate, flush, step)
 
     # ------------------------------------------------------------ e2e (host)
     e2 = E2ERound(torch, D, model, codec, stream, so, args.e2e_chunks, xfer=args.e2e_xfer)
@@ -1190,6 +1210,7 @@ def run_ours(args):
             "aggregate_collective": collective,
             "aggregate_choice": choice,
             "aggregate_check": check,
+            "rounds": first,
             "roofline": roofline,
             "e2e": {"value": round(e2e_val, 3), "unit": "GB/s", "ms_per_step": round(e2e_step, 4),
                     "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
