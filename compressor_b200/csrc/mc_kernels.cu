@@ -412,6 +412,8 @@ struct StageDesc {
     const uint8_t *x0, *x1;
     int gt;                         // tile id
     int ii;                         // item index
+    int late;                       // bit k: array k is the previous kernel's output, copied after
+                                    // the dependent-launch wait (see run_tile)
 };
 
 struct TileShared {
@@ -443,11 +445,24 @@ __device__ void pipe_issue(uint32_t bar, float *buf, uint8_t *xb, const StageDes
     if (body) {
 #pragma unroll
         for (int k = 0; k < NA; k++)
-            if (d.src[k])
+            if (d.src[k] && !((d.late >> k) & 1))
                 bulk_g2s(smem_u32(buf + k * STAGE_ELEMS), d.src[k] + d.e0, body, bar,
                          stream);
     }
     if (xbytes) bulk_g2s(smem_u32(xb + (xa - dn16(d.x0))), (const void *)xa, xbytes, bar, stream);
+}
+// Thread 0, after the dependent-launch wait: the copies of the arrays in
+// d.late (their bytes were announced with the others by pipe_issue, on the
+// same mbarrier phase).
+template <int NA>
+__device__ void pipe_issue_late(uint32_t bar, float *buf, const StageDesc &d) {
+    const uint32_t body = stage_body_bytes(d);
+    if (!d.late || !body) return;
+    const uint64_t stream = l2_stream();
+#pragma unroll
+    for (int k = 0; k < NA; k++)
+        if (d.src[k] && ((d.late >> k) & 1))
+            bulk_g2s(smem_u32(buf + k * STAGE_ELEMS), d.src[k] + d.e0, body, bar, stream);
 }
 
 // All threads, while the copies are in flight: what the bulk copies leave
@@ -496,7 +511,9 @@ __device__ __forceinline__ const float *staged_or(const StageDesc &d, const floa
 // only what was complete before that kernel started: the inputs, the state
 // of earlier calls, and the output of kernels two or more launches back
 // (pass 4 stages the new memory of pass 3 with the finalize kernel of pass 3
-// between them).
+// between them).  Arrays the plan marks in d.late are copied after the wait,
+// so they may be the previous kernel's output (the server aggregate, which
+// the previous decode on the stream may still be writing).
 template <int NA, bool REVERSE, class Plan, class Pre, class Body>
 __device__ void run_tile(const int2 *list, float *stage_mem, uint64_t *bar, StageDesc *sd, int32_t *err_of_item,
                          int err_stride_words, Plan plan, Pre pre, Body body) {
@@ -508,6 +525,7 @@ __device__ void run_tile(const int2 *list, float *stage_mem, uint64_t *bar, Stag
         d.gt = e.x;
         d.ii = e.y;
         d.x0 = d.x1 = nullptr;
+        d.late = 0;
         plan(d);
         *sd = d;
         mbar_init(b, 1);
@@ -517,6 +535,7 @@ __device__ void run_tile(const int2 *list, float *stage_mem, uint64_t *bar, Stag
     pdl_wait();
     pdl_release();
     const StageDesc d = *sd;
+    if (threadIdx.x == 0) pipe_issue_late<NA>(b, stage_mem, d);
     pipe_tail<NA>(stage_mem, xb, d);
     pre(d);   // the tile's own global reads, while its bulk copies are in flight
     // warp 0 waits for the copies; the other warps wait in the CTA barrier
@@ -1776,11 +1795,13 @@ __device__ __forceinline__ float *landing_of(const mc_agg_shards &S, int r) {
 // value, this rank's partial sum (the local aggregate, not read in store
 // mode, plus weight * decoded), goes to the owner's landing slot for this
 // rank instead (peer memory).
+// `agg_in`: the aggregate's old values, element-indexed like I.agg (its
+// staged copy, or I.agg itself).
 template <bool SHARD>
 __device__ __forceinline__ void agg_quad(const mc_dec_launch &L, const mc_dec_item &I, int64_t g, int64_t e1,
-                                         const float (&v)[4]) {
+                                         const float (&v)[4], const float *agg_in) {
     float a[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-    if (!I.agg_store) ld4(I.agg, g, e1, I.agg_vec != 0, a);
+    if (!I.agg_store) ld4(agg_in, g, e1, I.agg_vec != 0, a);
 #pragma unroll
     for (int j = 0; j < 4; j++) a[j] = __fmaf_rn(I.agg_w, v[j], a[j]);
     if constexpr (!SHARD) {
@@ -1963,7 +1984,7 @@ __device__ void recon_tile(const mc_dec_launch &L, const StageDesc &d, const flo
                             st_f4(a4 + q, make_float4(__fmaf_rn(aw, rec[0], a.x), __fmaf_rn(aw, rec[1], a.y),
                                                       __fmaf_rn(aw, rec[2], a.z), __fmaf_rn(aw, rec[3], a.w)), spol);
                         } else {
-                            agg_quad<SHARD>(L, I, tr.e0 + 4 * q, tr.e1, rec);
+                            agg_quad<SHARD>(L, I, tr.e0 + 4 * q, tr.e1, rec, I.agg);
                         }
                     }
                 }
@@ -1997,7 +2018,7 @@ __device__ void recon_tile(const mc_dec_launch &L, const StageDesc &d, const flo
             for (int64_t g = gstart + 4 * (int64_t)((threadIdx.x - owner + TPB) % TPB); g < tr.e1; g += 4 * TPB) {
                 float rec[4];
                 ld4(hist, g, tr.e1, I.vec, rec);
-                agg_quad<SHARD>(L, I, g, tr.e1, rec);
+                agg_quad<SHARD>(L, I, g, tr.e1, rec, I.agg);
             }
         }
         return;
@@ -2021,21 +2042,23 @@ __device__ void recon_tile(const mc_dec_launch &L, const StageDesc &d, const flo
                 sfast = I.agg_vec && (I.agg_off & 3) == 0;
             }
         }
+        // the old aggregate, staged as array 0 when the plan staged it
+        const float *agg_in = staged_or(d, buf, 0, I.agg);
         for (int64_t g = e0 + 4 * (int64_t)threadIdx.x; g < e1; g += 4 * TPB) {
             float r[4];
-            dec_resid4(I, I.data, g, e1, scale, r);
+            dec_resid4(I, codes, g, e1, scale, r);
             st4(hist, g, e1, I.vec, r);
             if (out) st4(out, g, e1, I.vec, r);
             if (!I.agg) continue;
             if (SHARD && sfast && g + 4 <= e1) {
                 float4 a = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-                if (!I.agg_store) a = *(const float4 *)(I.agg + g);
+                if (!I.agg_store) a = *(const float4 *)(agg_in + g);
                 const int64_t x = I.agg_off + g;
                 *(float4 *)((x < sb1 ? sp0 : sp1) + x) =
                     make_float4(__fmaf_rn(I.agg_w, r[0], a.x), __fmaf_rn(I.agg_w, r[1], a.y),
                                 __fmaf_rn(I.agg_w, r[2], a.z), __fmaf_rn(I.agg_w, r[3], a.w));
             } else {
-                agg_quad<SHARD>(L, I, g, e1, r);
+                agg_quad<SHARD>(L, I, g, e1, r, agg_in);
             }
         }
         return;
@@ -2103,7 +2126,7 @@ __device__ void recon_tile(const mc_dec_launch &L, const StageDesc &d, const flo
         for (int64_t g = f0 + 4 * (int64_t)threadIdx.x; g < f1; g += 4 * TPB) {
             float v[4];
             ld4(hf, g, f1, true, v);
-            agg_quad<SHARD>(L, I, g, f1, v);
+            agg_quad<SHARD>(L, I, g, f1, v, I.agg);
         }
     }
 }
@@ -2141,6 +2164,23 @@ __global__ void __launch_bounds__(TPB, SHARD ? 3 : 4) k_dec_recon(mc_dec_launch 
                         } else {
                             d.e0 = (int64_t)t * I.tile_kernels;
                             d.e1 = min(d.e0 + (int64_t)I.tile_kernels, I.n);
+                            // direct codes: staged like a momentum tile's; the old
+                            // aggregate (add mode) too, after the dependent-launch
+                            // wait: the previous decode on the stream may write it
+                            if (I.kind == MC_D_QUANT && L.staged && I.vec && d.e1 - d.e0 <= STAGE_ELEMS &&
+                                (I.codec == MC_DC_Q8 || I.codec == MC_DC_INT4)) {
+                                if (I.codec == MC_DC_Q8) {
+                                    d.x0 = I.data + d.e0;
+                                    d.x1 = I.data + d.e1;
+                                } else {
+                                    d.x0 = I.data + (d.e0 >> 1);
+                                    d.x1 = I.data + ((d.e1 + 1) >> 1);
+                                }
+                                if (I.agg && !I.agg_store && I.agg_vec) {
+                                    d.src[0] = I.agg;
+                                    d.late = 1;
+                                }
+                            }
                         }
                     },
                     [&](const StageDesc &d) { recon_pre(L, d, s_m, s_d, scan_sh, s_sb, &s_scale); },
