@@ -1505,7 +1505,30 @@ __device__ void pass4_tile(const mc_enc_launch &L, const StageDesc &d, const flo
         const float inv = __fdiv_rn(1.0f, scale);
         const float qm = (float)qmax_of(I.codec);
         const float *cur = staged_or(d, buf, 0, (const float *)I.cur);
-        for (int64_t g = e0 + 4 * (int64_t)threadIdx.x; g < e1; g += 4 * TPB) {
+        int64_t gstart = e0;
+        int owner = 0;
+        if (I.vec) {   // whole quads, no range checks, the codec a template argument
+            const int nq = (int)((e1 - e0) >> 2);
+            const float4 *c4 = (const float4 *)(cur + e0);
+            auto quads = [&](auto codec) {
+                for (int q = threadIdx.x; q < nq; q += TPB) {
+                    const float4 cv = c4[q];
+                    const float c[4] = {cv.x, cv.y, cv.z, cv.w};
+                    put_codes_full<decltype(codec)::value>(I.data_out, e0 + 4 * q, c, scale, inv, qm);
+                }
+            };
+            switch (I.codec) {
+                case MC_DC_Q8: quads(std::integral_constant<int, MC_DC_Q8>()); break;
+                case MC_DC_INT4: quads(std::integral_constant<int, MC_DC_INT4>()); break;
+                case MC_DC_RAW: quads(std::integral_constant<int, MC_DC_RAW>()); break;
+                case MC_DC_Q8_RAW: quads(std::integral_constant<int, MC_DC_Q8_RAW>()); break;
+                default: quads(std::integral_constant<int, MC_DC_INT4_RAW>()); break;
+            }
+            gstart = e0 + 4 * (int64_t)nq;
+            owner = nq % TPB;
+        }
+        // the ragged end (or every quad of an unaligned item)
+        for (int64_t g = gstart + 4 * (int64_t)((threadIdx.x - owner + TPB) % TPB); g < e1; g += 4 * TPB) {
             float c[4];
             ld4(cur, g, e1, I.vec, c);
             put_codes(I.data_out, I.codec, g, e1, I.vec, c, scale, inv, qm);
