@@ -1203,6 +1203,8 @@ def run_ours(args):
                        "parallelism": f"clients sharded over {world} GPU(s)" +
                                       (f", aggregate summed by {collective}" if world > 1 else "")},
             "gpu_launches": launches_timed,
+            # `value` is the whole job's raw-update rate (all GPUs); per GPU:
+            "value_per_gpu": round(value / world, 3),
             "payload_bytes_per_round": payload,
             "codec_ms_per_step_max": round(codec_max, 4),
             "allreduce_ms_rank0": round(statistics.mean(ar), 4) if world > 1 else 0.0,
