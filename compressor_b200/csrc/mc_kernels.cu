@@ -2067,7 +2067,50 @@ __device__ void recon_tile(const mc_dec_launch &L, const StageDesc &d, const flo
         }
         // the old aggregate, staged as array 0 when the plan staged it
         const float *agg_in = staged_or(d, buf, 0, I.agg);
-        for (int64_t g = e0 + 4 * (int64_t)threadIdx.x; g < e1; g += 4 * TPB) {
+        int64_t gstart = e0;
+        int owner = 0;
+        if (!SHARD && I.vec && (I.codec == MC_DC_Q8 || I.codec == MC_DC_INT4) && (!I.agg || I.agg_vec)) {
+            // whole quads, no range checks; codec and aggregate mode as template arguments
+            const int nq = (int)((e1 - e0) >> 2);
+            auto quads = [&](auto codec, auto store) {
+                constexpr int C = decltype(codec)::value;
+                constexpr bool ST = decltype(store)::value;
+                for (int q = threadIdx.x; q < nq; q += TPB) {
+                    const int64_t g = e0 + 4 * (int64_t)q;
+                    float r[4];
+                    if (C == MC_DC_Q8) {
+                        const uint32_t w = *(const uint32_t *)(codes + g);
+#pragma unroll
+                        for (int j = 0; j < 4; j++) r[j] = __fmul_rn((float)(int8_t)(uint8_t)(w >> (8 * j)), scale);
+                    } else {
+                        const uint32_t w = *(const uint16_t *)(codes + (g >> 1));
+#pragma unroll
+                        for (int j = 0; j < 4; j++) r[j] = __fmul_rn((float)((int)((w >> (4 * j)) & 15u) - 8), scale);
+                    }
+                    const float4 rv = make_float4(r[0], r[1], r[2], r[3]);
+                    *(float4 *)(hist + g) = rv;
+                    if (out) *(float4 *)(out + g) = rv;
+                    if (I.agg) {
+                        float4 a = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                        if (!ST) a = *(const float4 *)(agg_in + g);
+                        *(float4 *)(I.agg + g) = make_float4(__fmaf_rn(I.agg_w, r[0], a.x), __fmaf_rn(I.agg_w, r[1], a.y),
+                                                             __fmaf_rn(I.agg_w, r[2], a.z), __fmaf_rn(I.agg_w, r[3], a.w));
+                    }
+                }
+            };
+            const bool st = I.agg_store != 0;
+            if (I.codec == MC_DC_Q8) {
+                if (st) quads(std::integral_constant<int, MC_DC_Q8>(), std::true_type());
+                else quads(std::integral_constant<int, MC_DC_Q8>(), std::false_type());
+            } else {
+                if (st) quads(std::integral_constant<int, MC_DC_INT4>(), std::true_type());
+                else quads(std::integral_constant<int, MC_DC_INT4>(), std::false_type());
+            }
+            gstart = e0 + 4 * (int64_t)nq;
+            owner = nq % TPB;
+        }
+        // the ragged end (or every quad, where the fast loop does not apply)
+        for (int64_t g = gstart + 4 * (int64_t)((threadIdx.x - owner + TPB) % TPB); g < e1; g += 4 * TPB) {
             float r[4];
             dec_resid4(I, codes, g, e1, scale, r);
             st4(hist, g, e1, I.vec, r);
