@@ -512,8 +512,10 @@ int mc_compress_grouped(MomentumCompressor *mc, BatchItem *items, size_t n, cons
             p->dcodec = dcodec;
             p->codec_tag = codec_tag_of(dcodec);
             p->kind = MC_K_QUANT;
-            p->tile_param = TILE_ELEMS;
-            p->ntiles = (int)((p->n + TILE_ELEMS - 1) / TILE_ELEMS);
+            /* the encoder stages only the input of a direct quantised tile,
+             * so its tile fills both arrays of the two-array stage */
+            p->tile_param = 2 * TILE_ELEMS;
+            p->ntiles = (int)((p->n + 2 * TILE_ELEMS - 1) / (2 * TILE_ELEMS));
         } else if (p->use_lossy) {
             /* raw residual codec, and float64 lossy tensors: raw copy (the
              * reference's result when SZ3 is unavailable) */

@@ -132,8 +132,9 @@ enum {
  * kernels and the capacity of one array of its shared-memory stage.  A
  * momentum tile holds a multiple of 32 whole kernels (at least 32; a power
  * of two when the layer's bitmap frame has more than one block) with at
- * most MC_TILE_ELEMS elements; other tiles hold MC_TILE_ELEMS elements (4x
- * that for byte copies). */
+ * most MC_TILE_ELEMS elements; other tiles hold MC_TILE_ELEMS elements (2x
+ * that for the encoder's direct quantised tiles, whose input fills a
+ * two-array stage; 4x for byte copies). */
 #define MC_TILE_ELEMS 4096
 
 /* zstd framing shared by encoder and decoder: single-segment frame header

@@ -928,7 +928,10 @@ __device__ __forceinline__ const mc_enc_item &enc_plan_range(const mc_enc_launch
     return I;
 }
 __device__ __forceinline__ bool stageable(int staged, const mc_enc_item &I, const StageDesc &d) {
-    return staged && I.vec && d.e1 - d.e0 <= STAGE_ELEMS;
+    // a direct quantised tile stages its input alone, across both arrays of
+    // the two-array stages of passes 1 and 4
+    const int64_t cap = I.kind == MC_K_QUANT ? 2 * STAGE_ELEMS : STAGE_ELEMS;
+    return staged && I.vec && d.e1 - d.e0 <= cap;
 }
 #define ENC_ERR(L) &(L).results[0].err, (int)(sizeof(mc_enc_result) / 4)
 
