@@ -25,6 +25,7 @@ SHAPES = [
     ("five.weight", (5, 3, 5, 5)),        # ks = 25
     ("bn.bias", (64,)),                   # lossless
     ("fc.weight", (10, 512)),             # 2-D lossy, direct_generic
+    ("head.weight", (9, 1001)),           # 2-D lossy, ragged: an 8192-element encoder tile plus 817
 ]
 THRESHOLD = 4   # momentum path on the toy shapes, as the reference tests do
 
