@@ -606,6 +606,17 @@ def timed_rounds(torch, D: Dist, fr: FedRound, data: DeviceUpdates, K: int, W: i
     return step, codec, wait, ar
 
 
+def e2e_link_bound(h2d_bytes: float, d2h_bytes: float, pcie: dict) -> float:
+    """Lower bound in ms of an e2e step's host transfers from the pinned copy
+    rates measured in the same run: the slower of the upload alone, the
+    download alone, and both directions sharing the link at their measured
+    combined rate."""
+    up = h2d_bytes / (pcie["h2d_gbs"] * 1e9)
+    down = d2h_bytes / (pcie["d2h_gbs"] * 1e9)
+    both = (h2d_bytes + d2h_bytes) / (pcie["duplex_gbs"] * 1e9)
+    return 1e3 * max(up, down, both)
+
+
 def first_rounds(torch, D: Dist, model, world, codec, stream, so, aggregate, flush, hot_steps):
     """Rounds 0, 1 and 2 of fresh encoder / decoder instances, each timed
     like a hot step (L2 flushed before it, CUDA events, max over ranks),
@@ -1228,6 +1239,10 @@ def run_ours(args):
             "cpu_baseline_8_threads": cpu8,
         }
         del ab_gpu
+        if "pcie" in nested:
+            bound = e2e_link_bound(h2d, d2h, nested["pcie"])
+            out["e2e"]["link_bound_ms"] = round(bound, 4)
+            out["e2e"]["link_bound_frac"] = round(bound / e2e_step, 4)
         out.update(nested)
         print(json.dumps(out))
     D.close()

@@ -1,5 +1,5 @@
 """Host logic of bench.py that needs no GPU: the choice of the cross-GPU sum
-after the trial rounds, and the e2e layer chunks."""
+after the trial rounds, the e2e layer chunks and the e2e link bound."""
 import numpy as np
 
 import bench
@@ -28,3 +28,12 @@ def test_e2e_chunks_cover_resnet50_in_order():
     assert all(a[1] == b[0] for a, b in zip(ch, ch[1:]))
     sizes = [sum(numels[a:b]) for a, b in ch]
     assert len(ch) == 3 and max(sizes) < 0.5 * sum(numels)
+
+
+def test_e2e_link_bound():
+    pcie = {"h2d_gbs": 50.0, "d2h_gbs": 50.0, "duplex_gbs": 80.0}
+    # 1 GB each way: 20 ms alone per direction, 25 ms sharing the link
+    assert abs(bench.e2e_link_bound(1e9, 1e9, pcie) - 25.0) < 1e-9
+    # one direction only: its own rate binds
+    assert abs(bench.e2e_link_bound(1e9, 0.0, pcie) - 20.0) < 1e-9
+    assert abs(bench.e2e_link_bound(0.0, 2e9, pcie) - 40.0) < 1e-9
